@@ -1,0 +1,218 @@
+/*
+ * mergenet_b200.h -- C ABI of the B200 (sm_100a) DTEM spatial-routing library.
+ *
+ * Every entry point takes plain device pointers, explicit sizes and a
+ * cudaStream_t (passed as void*), launches asynchronously on that stream and
+ * returns an int status: 0 = launched, negative = argument error (nothing was
+ * launched), positive = a data condition detected on the host.  Outputs and
+ * workspaces are allocated by the caller; inputs are never written.  Kernels
+ * report data conditions found on the device by OR-ing bits into the caller's
+ * device status word (MN_STATUS_* below), which the caller reads when it
+ * synchronises.  No entry point allocates device memory or synchronises.
+ *
+ * Tensors are dense row-major (C-contiguous) unless a stride argument says
+ * otherwise.  Index tensors are int64 like the reference's torch.long tensors;
+ * boolean tensors are one byte per element like torch.bool.
+ *
+ * Reference interfaces cited below are files of the MergeNet project.
+ */
+#ifndef MERGENET_B200_H
+#define MERGENET_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define MN_F32 0
+#define MN_F16 1
+#define MN_BF16 2
+
+/* host-side return codes */
+#define MN_OK 0
+#define MN_ERR_ARG (-1)          /* bad size, pointer or dtype                 */
+#define MN_ERR_UNSUPPORTED (-2)  /* shape outside what the kernels are built for */
+#define MN_ERR_WORKSPACE (-3)    /* workspace smaller than the size query says  */
+#define MN_ERR_LAUNCH (-4)       /* cudaGetLastError reported a launch failure   */
+#define MN_INFEASIBLE_BUDGET 1   /* fewer donor rows with a legal receiver than k */
+
+/* device status bits (OR-ed into the caller's int) */
+#define MN_STATUS_INFEASIBLE_BUDGET 1
+#define MN_STATUS_DEGENERATE_RANGE 2 /* ThreTopK global max == min */
+#define MN_STATUS_TOO_MANY_EDGES 4
+
+/* Library version, for the loader's sanity check. */
+int mn_version(void);
+
+/* ------------------------------------------------------------------------
+ * Geometry (host).  Replaces build_patch_spatial_adjacency +
+ * adjacency_to_padded_neighbors, opentome/timm/dtem.py:50-127.
+ * ------------------------------------------------------------------------ */
+
+/* Width K of the padded [P,K] neighbour table of a grid and radius. */
+int mn_neighbor_table_width(int grid_h, int grid_w, double radius, int* k_out);
+
+/* Fill the [P,K] table (ascending patch order, index 0 / valid 0 padding). */
+int mn_neighbor_table_fill(int grid_h, int grid_w, double radius, int k,
+                           int64_t* indices, uint8_t* valid);
+
+/* ------------------------------------------------------------------------
+ * Fused routing for the canonical eval grouping (alternating_per_layer_fast,
+ * even patch count): L merge layers of DTEMBlock._merge_train
+ * (opentome/timm/dtem.py:1687-2223, called from LocalEncoder.forward,
+ * opentome/models/mergenet/model.py:574-590) followed by the carrier block of
+ * CLSHybridToMeModel.forward (model.py:1157-1183).
+ * ------------------------------------------------------------------------ */
+typedef struct mn_route_dims {
+  int grid_h, grid_w;
+  int num_patches;   /* P = grid_h * grid_w (even)                          */
+  int half;          /* P / 2 = donors = receivers per layer                */
+  int k_static;      /* K: width of the padded neighbour table              */
+  int kc;            /* compact donor slots: max legal receivers of a donor */
+  int kin;           /* max donors of one receiver                          */
+  int radius_rows;   /* largest row offset between two neighbours           */
+  int valid_rows[2]; /* donors with >= 1 legal receiver, per layer parity   */
+  int64_t table_ints;/* int32 entries of the routing table buffer           */
+} mn_route_dims;
+
+int mn_route_dims_query(int grid_h, int grid_w, double radius, mn_route_dims* dims);
+
+/* Host-side fill of the routing table buffer (int32[table_ints]); the caller
+ * copies it to the device once and passes it to every routing call.  Layout,
+ * per layer parity q in {0,1} (q = layer % 2):
+ *   slot_k  [half][kc]  static slot of each compact donor slot (or -1)
+ *   slot_rx [half][kc]  receiver local index of that slot (or -1)
+ *   rx_in   [half][kin] edge ids d*kc+c feeding each receiver, ascending
+ *                       (the reference's sequential scatter order), or -1 */
+int mn_route_tables_fill(int grid_h, int grid_w, double radius,
+                         const mn_route_dims* dims, int32_t* host_table);
+
+/* Bytes of device workspace mn_route_and_gather needs. */
+size_t mn_route_workspace_bytes(const mn_route_dims* dims, int batch,
+                                int num_layers);
+
+/*
+ * x        [B, T, C]     tokens after the local blocks (T = 1 + P, CLS first),
+ *                        MN_F32 / MN_F16 / MN_BF16 (routing math is fp32)
+ * metrics  [L, B, T, Cm] metric-head outputs, any of the three dtypes
+ * r_list   host int[L]   per-layer merge budget (parse_r schedule)
+ * k        carriers      (T - 1 - sum(r_list) in the canonical model)
+ * outputs: topk_x [B, k+1, C] (x dtype, CLS row first, carriers ordered by
+ *          centre of mass), topk_size f32 [B, k+1], topk_idx int64 [B, k]
+ *          (patch indices, aux["topk_patch_indices"]), size_out f32 [B, T],
+ *          center_out f32 [B, T] (token_center after the last layer).
+ * tau1/tau2: _tome_info tau1 (1.0) and ThreTopK temperature tau2 (30.0).
+ * Ties: equal masses keep the lower patch index; equal centres keep the
+ * lower patch index (the reference leaves both unspecified).
+ */
+int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev_table,
+                        int batch, int channels, int metric_dim, int num_layers,
+                        const int* r_list, int k, float tau1, float tau2,
+                        const void* x, int x_dtype,
+                        const void* metrics, int metric_dtype,
+                        void* workspace, size_t workspace_bytes,
+                        void* topk_x, float* topk_size, int64_t* topk_idx,
+                        float* size_out, float* center_out,
+                        int* status, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Function-level drop-ins (arbitrary donor/receiver partitions).
+ * ------------------------------------------------------------------------ */
+
+/* sparse_spatial_score, opentome/timm/dtem.py:813-848 (kernel :361-433):
+ * a [B,Na,C], b [B,Nb,C] (dtype), table [P,K] int64 + uint8, donor_patch
+ * int64 [B,Na], receiver_patch int64 [B,Nb] sorted ascending per row.
+ * Outputs scores [B,Na,K] (dtype), receiver_indices int64 [B,Na,K],
+ * receiver_valid uint8 [B,Na,K]. */
+int mn_sparse_spatial_score(int batch, int num_donors, int num_receivers,
+                            int num_patches, int k, int channels, int dtype,
+                            const void* a, const void* b,
+                            const int64_t* neighbor_indices,
+                            const uint8_t* neighbor_valid,
+                            const int64_t* donor_patch,
+                            const int64_t* receiver_patch, void* scores,
+                            int64_t* receiver_indices, uint8_t* receiver_valid,
+                            void* stream);
+
+/* sparse_neighbor_dot, opentome/timm/dtem.py:680-687 (kernel :286-315). */
+int mn_sparse_neighbor_dot(int batch, int num_donors, int num_receivers, int k,
+                           int channels, int dtype, const void* a,
+                           const void* b, const int64_t* receiver_indices,
+                           const uint8_t* receiver_valid, void* scores,
+                           void* stream);
+
+/* sparse_weighted_transport, opentome/timm/dtem.py:1035-1067 (kernel
+ * :436-468): out [B,Nb,C] = sum over edges (d,k) into slot s of
+ * assignment[b,d,k] * values[b,d,:], accumulated per receiver in ascending
+ * edge order without atomics.  Invalid edges contribute nothing. */
+int mn_sparse_weighted_transport(int batch, int num_donors, int num_receivers,
+                                 int k, int channels, int dtype,
+                                 const void* assignment, const void* values,
+                                 const int64_t* receiver_indices,
+                                 const uint8_t* receiver_valid, void* out,
+                                 int* status, void* stream);
+
+/* Adjoint of the transport (the reference's backward, dtem.py:962-973):
+ * grad_assignment [B,Na,K] = <values[b,d,:], grad_out[b,slot,:]>,
+ * grad_values [B,Na,C] = sum_k assignment * grad_out[b,slot,:]. */
+int mn_sparse_transport_adjoint(int batch, int num_donors, int num_receivers,
+                                int k, int channels, int dtype,
+                                const void* assignment, const void* values,
+                                const int64_t* receiver_indices,
+                                const uint8_t* receiver_valid,
+                                const void* grad_out, void* grad_assignment,
+                                void* grad_values, void* stream);
+
+/* ThreTopK, opentome/utils/thetopk.py:4-43: x f32 [rows, n] -> y f32.
+ * One global max-min range over all rows, per-row threshold.
+ * workspace: mn_thre_topk_workspace_bytes(rows, n) bytes. */
+size_t mn_thre_topk_workspace_bytes(int rows, int n);
+int mn_thre_topk(int rows, int n, const float* x, int k, float temperature,
+                 float* y, void* workspace, size_t workspace_bytes,
+                 int* status, void* stream);
+
+/* Soft-k-max block of DTEMBlock._select with the sparse spatial mask,
+ * opentome/timm/dtem.py:1551-1580: scores f32 [B,Na,K] + allowed uint8 ->
+ * assignment f32 [B,Na,K].  Returns MN_INFEASIBLE_BUDGET through the device
+ * status when a batch row has fewer than k valid donor rows. */
+size_t mn_dtem_select_workspace_bytes(int batch, int num_donors);
+int mn_dtem_select(int batch, int num_donors, int k_slots, const float* scores,
+                   const uint8_t* allowed, int k, float tau1, float tau2,
+                   float* assignment, void* workspace, size_t workspace_bytes,
+                   int* status, void* stream);
+
+/* Transpose of the carrier gather: out [B,P,C] (dtype) gets carrier row i+1
+ * of topk_x [B,k+1,C] at patch topk_idx[b,i]; other rows are zero. */
+int mn_carrier_scatter(int batch, int k, int num_patches, int channels,
+                       int dtype, const void* topk_x, const int64_t* topk_idx,
+                       void* out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Attention.
+ * ------------------------------------------------------------------------ */
+
+/* unbiased_local_attention / biased_local_attention,
+ * opentome/timm/bias_local_attn.py:486-625 and :243-483, plus the CLS-global
+ * row of LocalAttention.forward (:704-719).
+ * q/k/v: element (b, n, h, d) at base + b*s_b + n*s_n + h*s_h + d (elements).
+ * out  : [B, N, H, D] contiguous, dtype out_dtype.
+ * bias : optional per-key additive bias [B, N] (NULL for the unbiased op),
+ *        rounded to the q/k/v dtype like the reference's extra column.
+ * window: |i - j| <= window; window < 0 means global attention.
+ * cls_global: 1 = row 0 attends to every key (the LocalAttention CLS row).
+ * scale: softmax scale (1/sqrt(D) in the reference). */
+int mn_local_attention(int batch, int tokens, int heads, int head_dim,
+                       int dtype, const void* q, const void* k, const void* v,
+                       int64_t s_b, int64_t s_n, int64_t s_h,
+                       const void* bias, int bias_dtype, int window,
+                       int cls_global, float scale, void* out, int out_dtype,
+                       void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MERGENET_B200_H */

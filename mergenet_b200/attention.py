@@ -1,0 +1,121 @@
+"""Windowed local attention on the B200 kernels, behind the reference's
+function signatures (opentome/timm/bias_local_attn.py:243-625)."""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+
+
+def _strides_bnhd(t: torch.Tensor):
+    if t.stride(-1) != 1:
+        raise ValueError("the head dimension must be contiguous")
+    return t.stride(0), t.stride(1), t.stride(2)
+
+
+def _launch(q, k, v, bias, window, cls_global, scale, out_dtype):
+    """q/k/v in (B, N, H, D) view form (any strides with a unit last stride)."""
+    dev = L.require_cuda(q, k, v, bias)
+    if q.shape != k.shape or q.shape != v.shape:
+        raise ValueError(f"q/k/v shape mismatch: {q.shape}, {k.shape}, {v.shape}")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("q/k/v must share a dtype")
+    if not (q.stride() == k.stride() == v.stride()):
+        k = k.contiguous() if k.stride() != q.stride() else k
+        v = v.contiguous() if v.stride() != q.stride() else v
+        if not (q.stride() == k.stride() == v.stride()):
+            q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    b, n, h, d = q.shape
+    sb, sn, sh = _strides_bnhd(q)
+    out = torch.empty(b, n, h, d, device=dev, dtype=out_dtype)
+    bias_c = None
+    bias_code = 0
+    if bias is not None:
+        bias_c = bias.contiguous()
+        bias_code = L.dtype_code(bias_c.dtype)
+    L.check(L.lib().mn_local_attention(b, n, h, d, L.dtype_code(q.dtype), L.ptr(q), L.ptr(k), L.ptr(v), sb, sn, sh,
+                                       L.ptr(bias_c), bias_code, int(window), int(bool(cls_global)), float(scale),
+                                       L.ptr(out), L.dtype_code(out_dtype), L.stream_of(q)), "mn_local_attention")
+    return out
+
+
+def unbiased_local_attention(q, k, v, local_window, *, logical_dim: Optional[int] = None, dropout_p=0.0,
+                             training=False, x_dtype: Optional[torch.dtype] = None, cls_global=False):
+    """softmax(q k^T / sqrt(D)) v over keys with |i - j| <= local_window
+    (bias_local_attn.py:486-625).  Layout inferred like the reference
+    (BNHD when dim 1 > dim 2).  ``cls_global`` additionally makes row 0
+    attend to every key (LocalAttention.forward, :704-719)."""
+    if q.ndim != 4:
+        raise AssertionError(f"q must be 4D, got shape {q.shape}")
+    if training and dropout_p > 0.0:
+        raise NotImplementedError("attention dropout is a training feature; the B200 path is inference")
+    bnhd = q.shape[1] > q.shape[2]
+    d = q.shape[-1]
+    scale = 1.0 / math.sqrt(logical_dim if logical_dim is not None else d)
+    out_dtype = x_dtype if x_dtype is not None else q.dtype
+    if bnhd:
+        return _launch(q, k, v, None, local_window, cls_global, scale, out_dtype)
+    o = _launch(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), None, local_window, cls_global, scale,
+                out_dtype)
+    return o.transpose(1, 2).contiguous()
+
+
+def biased_local_attention(q, k, v, bias, local_window, *, logical_dim: Optional[int] = None, dropout_p=0.0,
+                           training=False, x_dtype: Optional[torch.dtype] = None, input_layout: Optional[str] = None):
+    """softmax(q k^T / sqrt(D) + bias_j) v over the window
+    (bias_local_attn.py:243-483).  The bias is rounded to the q/k/v dtype as
+    the reference's extra head column does.  Layout inference and its
+    ambiguity error follow :321-347."""
+    if q.ndim != 4:
+        raise AssertionError(f"q must be 4D, got shape {q.shape}")
+    if not (q.shape == k.shape == v.shape):
+        raise AssertionError(f"q/k/v shape mismatch: {q.shape}, {k.shape}, {v.shape}")
+    if not (bias.ndim == 2 and bias.shape[0] == q.shape[0]):
+        raise AssertionError(f"bias must be 2D with matching batch size, got {bias.shape} for q={q.shape}")
+    if input_layout is not None:
+        input_layout = input_layout.upper()
+        if input_layout not in ("BHND", "BNHD"):
+            raise ValueError(f"input_layout must be BHND or BNHD, got {input_layout!r}")
+    else:
+        axis1_is_n = q.shape[1] == bias.shape[1]
+        axis2_is_n = q.shape[2] == bias.shape[1]
+        if axis1_is_n == axis2_is_n:
+            raise ValueError("Cannot infer q/k/v layout from bias length; pass input_layout='BHND' or 'BNHD' "
+                             "explicitly")
+        input_layout = "BNHD" if axis1_is_n else "BHND"
+    if training and dropout_p > 0.0:
+        raise NotImplementedError("attention dropout is a training feature; the B200 path is inference")
+    d_logic = logical_dim if logical_dim is not None else q.shape[-1]
+    scale = 1.0 / math.sqrt(d_logic)
+    out_dtype = x_dtype if x_dtype is not None else q.dtype
+    if q.dtype not in (torch.float16, torch.bfloat16):  # the reference computes in fp16 then
+        q, k, v = q.half(), k.half(), v.half()
+    if d_logic < q.shape[-1]:
+        # columns past the logical width carry the bias / padding in the
+        # reference's layout (:378-415); only the logical columns take part
+        q, k, v = q[..., :d_logic], k[..., :d_logic], v[..., :d_logic]
+    if input_layout == "BNHD":
+        b, n = q.shape[0], q.shape[1]
+        if bias.shape != (b, n):
+            raise AssertionError(f"bias must be (B, N), got {bias.shape}")
+        return _launch(q, k, v, bias, local_window, False, scale, out_dtype)
+    b, n = q.shape[0], q.shape[2]
+    if bias.shape != (b, n):
+        raise AssertionError(f"bias must be (B, N), got {bias.shape}")
+    o = _launch(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), bias, local_window, False, scale, out_dtype)
+    return o.transpose(1, 2).contiguous()
+
+
+def local_attention_packed(qkv, num_heads, local_window, cls_global=True, out_dtype=None):
+    """LocalAttention's core on the packed qkv projection [B, N, 3*H*D]
+    (bias_local_attn.py:687-721 inference layout): q, k, v are read in place
+    through strides; returns [B, N, H*D]."""
+    b, n, c3 = qkv.shape
+    d = c3 // (3 * num_heads)
+    view = qkv.view(b, n, 3, num_heads, d)
+    q, k, v = view[:, :, 0], view[:, :, 1], view[:, :, 2]
+    o = _launch(q, k, v, None, local_window, cls_global, 1.0 / math.sqrt(d), out_dtype or qkv.dtype)
+    return o.view(b, n, num_heads * d)

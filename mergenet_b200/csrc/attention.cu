@@ -1,0 +1,193 @@
+// Sliding-window attention over the flattened token sequence with an optional
+// per-key bias and a global CLS row, replacing the FlashAttention calls of
+// unbiased_local_attention / biased_local_attention
+// (opentome/timm/bias_local_attn.py:486-625, :243-483) and the CLS-row SDPA
+// of LocalAttention.forward (:704-719).
+//
+// This file holds the CUDA-core path: one warp per query row with an online
+// softmax over 32-key chunks, keys/values of the CTA's band staged in fp32
+// shared memory.  Scores, softmax and the P.V accumulation are fp32.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace mn {
+
+constexpr int kLocalQT = 32;  // queries per CTA
+
+template <typename ET>
+__global__ void __launch_bounds__(256) local_attn_kernel(
+    const ET* __restrict__ q, const ET* __restrict__ k, const ET* __restrict__ v, int64_t sb, int64_t sn,
+    int64_t sh, int N, int H, int D, const void* __restrict__ bias, int bias_dtype, int window, float scale,
+    void* __restrict__ out, int out_dtype, int skip_row0) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int q0 = blockIdx.x * kLocalQT;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int W = window < 0 ? N : window;
+  const int lo = max(0, q0 - W), hi = min(N, q0 + kLocalQT + W);
+  const int nk = hi - lo;
+  const int DS = D + 1;  // padded row stride (floats)
+  float* ks = reinterpret_cast<float*>(smem_raw);  // [nk][DS]
+  float* vs = ks + (size_t)nk * DS;                // [nk][DS]
+  float* bs = vs + (size_t)nk * DS;                // [nk]
+  float* qs = bs + nk;                             // [8 warps][D]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int64_t base = (int64_t)b * sb + (int64_t)h * sh;
+  for (int i = threadIdx.x; i < nk * D; i += blockDim.x) {
+    const int r = i / D, c = i % D;
+    const int64_t off = base + (int64_t)(lo + r) * sn + c;
+    ks[r * DS + c] = to_f32(k[off]);
+    vs[r * DS + c] = to_f32(v[off]);
+  }
+  for (int r = threadIdx.x; r < nk; r += blockDim.x) {
+    // the reference rounds the bias to the q/k/v dtype before use
+    float bv = 0.f;
+    if (bias) bv = to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)b * N + lo + r)));
+    bs[r] = bv;
+  }
+  __syncthreads();
+  float* qw = qs + warp * D;
+  for (int qi = q0 + warp; qi < min(N, q0 + kLocalQT); qi += nw) {
+    if (skip_row0 && qi == 0) continue;
+    const int64_t qoff = base + (int64_t)qi * sn;
+    for (int c = lane; c < D; c += 32) qw[c] = to_f32(q[qoff + c]);
+    __syncwarp();
+    const int j0 = max(0, qi - W), j1 = min(N - 1, qi + W);
+    float m = -INFINITY, l = 0.f;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};  // channels lane, lane+32, lane+64, lane+96
+    for (int jc = j0; jc <= j1; jc += 32) {
+      const int j = jc + lane;
+      float s = -INFINITY;
+      if (j <= j1) {
+        const float* kr = ks + (j - lo) * DS;
+        float acc = 0.f;
+        for (int c = 0; c < D; ++c) acc = fmaf(qw[c], kr[c], acc);
+        s = acc * scale + bs[j - lo];
+      }
+      const float mc = warp_max(s);
+      const float mn = fmaxf(m, mc);
+      const float p = (j <= j1) ? expf(s - mn) : 0.f;
+      const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
+      l = l * corr + warp_sum(p);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) o[t] *= corr;
+      const int cnt = min(32, j1 - jc + 1);
+      for (int u = 0; u < cnt; ++u) {
+        const float pu = __shfl_sync(MN_FULL_MASK, p, u);
+        const float* vr = vs + (jc + u - lo) * DS;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int c = lane + 32 * t;
+          if (c < D) o[t] = fmaf(pu, vr[c], o[t]);
+        }
+      }
+      m = mn;
+    }
+    const float inv = 1.0f / l;
+    const int64_t ooff = (((int64_t)b * N + qi) * H + h) * D;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int c = lane + 32 * t;
+      if (c < D) store_any(out, out_dtype, ooff + c, o[t] * inv);
+    }
+    __syncwarp();
+  }
+}
+
+// Row 0 (CLS) attends to every key: one CTA per (head, image).
+template <typename ET>
+__global__ void __launch_bounds__(256) cls_row_kernel(const ET* __restrict__ q, const ET* __restrict__ k,
+                                                      const ET* __restrict__ v, int64_t sb, int64_t sn,
+                                                      int64_t sh, int N, int H, int D,
+                                                      const void* __restrict__ bias, int bias_dtype, float scale,
+                                                      void* __restrict__ out, int out_dtype) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* p = reinterpret_cast<float*>(smem_raw);  // [N]
+  float* qv = p + N;                              // [D]
+  float* part = qv + D;                           // [256]
+  __shared__ float red[64];
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int64_t base = (int64_t)b * sb + (int64_t)h * sh;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) qv[c] = to_f32(q[base + c]);
+  __syncthreads();
+  float mx = -INFINITY, dummy = INFINITY;
+  for (int j = threadIdx.x; j < N; j += blockDim.x) {
+    const ET* kr = k + base + (int64_t)j * sn;
+    float acc = 0.f;
+    for (int c = 0; c < D; ++c) acc = fmaf(qv[c], to_f32(kr[c]), acc);
+    float s = acc * scale;
+    if (bias) s += to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)b * N + j)));
+    p[j] = s;
+    mx = fmaxf(mx, s);
+  }
+  block_minmax(dummy, mx, red);
+  float sum = 0.f;
+  for (int j = threadIdx.x; j < N; j += blockDim.x) {
+    const float e = expf(p[j] - mx);
+    p[j] = e;
+    sum += e;
+  }
+  // block sum through the same scratch
+  sum = warp_sum(sum);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+  __syncthreads();
+  const int groups = blockDim.x / D > 0 ? blockDim.x / D : 1;
+  const int c = threadIdx.x % D, g = threadIdx.x / D;
+  float acc = 0.f;
+  if (g < groups)
+    for (int j = g; j < N; j += groups) acc = fmaf(p[j], to_f32(v[base + (int64_t)j * sn + c]), acc);
+  part[threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.x < D) {
+    float o = 0.f;
+    for (int gg = 0; gg < groups; ++gg) o += part[gg * D + threadIdx.x];
+    store_any(out, out_dtype, (((int64_t)b * N) * H + h) * D + threadIdx.x, o / tot);
+  }
+}
+
+}  // namespace mn
+
+using namespace mn;
+
+extern "C" int mn_local_attention(int batch, int tokens, int heads, int head_dim, int dtype, const void* q,
+                                  const void* k, const void* v, int64_t s_b, int64_t s_n, int64_t s_h,
+                                  const void* bias, int bias_dtype, int window, int cls_global, float scale,
+                                  void* out, int out_dtype, void* stream) {
+  if (batch < 0 || tokens < 0 || heads <= 0 || head_dim <= 0 || head_dim > 128 || !out) return MN_ERR_ARG;
+  if ((int64_t)batch * tokens == 0) return MN_OK;
+  if (!q || !k || !v) return MN_ERR_ARG;
+  if (dtype < 0 || dtype > 2 || out_dtype < 0 || out_dtype > 2 || (bias && (bias_dtype < 0 || bias_dtype > 2)))
+    return MN_ERR_ARG;
+  const int W = window < 0 ? tokens : window;
+  const int nk = std::min(tokens, kLocalQT + 2 * W);
+  const size_t smem = ((size_t)2 * nk * (head_dim + 1) + nk + 8 * head_dim) * sizeof(float);
+  if (smem > 200 * 1024) return MN_ERR_UNSUPPORTED;
+  const bool cls_row = cls_global && window >= 0 && tokens > 1;
+  const size_t smem_cls = ((size_t)tokens + head_dim + 256) * sizeof(float);
+  if (cls_row && (smem_cls > 200 * 1024 || head_dim > 256)) return MN_ERR_UNSUPPORTED;
+  cudaGetLastError();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid((tokens + kLocalQT - 1) / kLocalQT, heads, batch);
+  auto run = [&](auto tag) {
+    using ET = decltype(tag);
+    cudaFuncSetAttribute(local_attn_kernel<ET>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    local_attn_kernel<ET><<<grid, 256, smem, st>>>(static_cast<const ET*>(q), static_cast<const ET*>(k),
+                                                   static_cast<const ET*>(v), s_b, s_n, s_h, tokens, heads,
+                                                   head_dim, bias, bias_dtype, window, scale, out, out_dtype,
+                                                   cls_row ? 1 : 0);
+    if (cls_row) {
+      cudaFuncSetAttribute(cls_row_kernel<ET>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_cls);
+      cls_row_kernel<ET><<<dim3(heads, batch), 256, smem_cls, st>>>(
+          static_cast<const ET*>(q), static_cast<const ET*>(k), static_cast<const ET*>(v), s_b, s_n, s_h, tokens,
+          heads, head_dim, bias, bias_dtype, scale, out, out_dtype);
+    }
+  };
+  if (dtype == MN_F32) run(float{});
+  else if (dtype == MN_F16) run(__half{});
+  else run(__nv_bfloat16{});
+  return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
+}

@@ -1,0 +1,164 @@
+// Shared device helpers for the MergeNet B200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mergenet_b200.h"
+
+#define MN_FULL_MASK 0xffffffffu
+
+namespace mn {
+
+// ---------------------------------------------------------------- dtype I/O
+template <int DT> struct Elem;
+template <> struct Elem<MN_F32> { using T = float; };
+template <> struct Elem<MN_F16> { using T = __half; };
+template <> struct Elem<MN_BF16> { using T = __nv_bfloat16; };
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// Load element i of a buffer whose dtype is only known at run time.
+__device__ __forceinline__ float load_any(const void* p, int dtype, int64_t i) {
+  if (dtype == MN_F32) return static_cast<const float*>(p)[i];
+  if (dtype == MN_F16) return __half2float(static_cast<const __half*>(p)[i]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+__device__ __forceinline__ void store_any(void* p, int dtype, int64_t i, float v) {
+  if (dtype == MN_F32) static_cast<float*>(p)[i] = v;
+  else if (dtype == MN_F16) static_cast<__half*>(p)[i] = __float2half_rn(v);
+  else static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+
+// ---------------------------------------------------------- warp reductions
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(MN_FULL_MASK, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(MN_FULL_MASK, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(MN_FULL_MASK, v, o));
+  return v;
+}
+__device__ __forceinline__ int warp_min_int(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(MN_FULL_MASK, v, o));
+  return v;
+}
+
+// Block-wide min/max of one float per thread (blockDim.x multiple of 32,
+// <= 1024).  scratch: >= 64 floats of shared memory.  Result in every thread.
+__device__ __forceinline__ void block_minmax(float& vmin, float& vmax, float* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  vmin = warp_min(vmin);
+  vmax = warp_max(vmax);
+  __syncthreads();
+  if (lane == 0) { scratch[warp] = vmin; scratch[32 + warp] = vmax; }
+  __syncthreads();
+  float a = (lane < nw) ? scratch[lane] : INFINITY;
+  float b = (lane < nw) ? scratch[32 + lane] : -INFINITY;
+  vmin = warp_min(a);
+  vmax = warp_max(b);
+  __syncthreads();
+}
+
+__device__ __forceinline__ int block_min_int(int v, int* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_min_int(v);
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  int a = (lane < nw) ? scratch[lane] : 0x7fffffff;
+  v = warp_min_int(a);
+  __syncthreads();
+  return v;
+}
+
+// Inclusive block scan of doubles; each thread owns `per` consecutive
+// elements of buf[0 .. blockDim.x*per).  scratch: >= 32 doubles.
+__device__ __forceinline__ void block_scan_inclusive(double* buf, int per, double* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  double* mine = buf + threadIdx.x * per;
+  double run = 0.0;
+  for (int i = 0; i < per; ++i) { run += mine[i]; mine[i] = run; }
+  double incl = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    double t = __shfl_up_sync(MN_FULL_MASK, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) scratch[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    double w = (lane < nw) ? scratch[lane] : 0.0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      double t = __shfl_up_sync(MN_FULL_MASK, w, o);
+      if (lane >= o) w += t;
+    }
+    if (lane < nw) scratch[lane] = w;
+  }
+  __syncthreads();
+  double offset = (incl - run) + (warp > 0 ? scratch[warp - 1] : 0.0);
+  for (int i = 0; i < per; ++i) mine[i] += offset;
+  __syncthreads();
+}
+
+// Ascending bitonic sort of n (power of two) floats in shared memory.
+__device__ __forceinline__ void bitonic_sort_f32(float* s, int n) {
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        int ixj = i ^ j;
+        if (ixj > i) {
+          float a = s[i], b = s[ixj];
+          bool up = (i & k) == 0;
+          if ((a > b) == up) { s[i] = b; s[ixj] = a; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Ascending bitonic sort of n (power of two) 64-bit keys in shared memory.
+__device__ __forceinline__ void bitonic_sort_u64(unsigned long long* s, int n) {
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        int ixj = i ^ j;
+        if (ixj > i) {
+          unsigned long long a = s[i], b = s[ixj];
+          bool up = (i & k) == 0;
+          if ((a > b) == up) { s[i] = b; s[ixj] = a; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+__host__ __device__ inline int next_pow2(int v) {
+  int p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+}  // namespace mn

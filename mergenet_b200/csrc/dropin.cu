@@ -1,0 +1,514 @@
+// Function-level drop-ins for the reference's routing primitives, for
+// arbitrary donor/receiver partitions (training grouping, seeded grouping,
+// odd grids): the fused path in route.cu covers only the canonical eval
+// grouping.
+#include <algorithm>
+
+#include "common.cuh"
+#include "thretopk.cuh"
+
+namespace mn {
+
+// --------------------------------------------------------------------------
+// sparse_spatial_score (dtem.py:361-433 / :554-594): per (batch, donor) one
+// warp.  Lanes resolve the static neighbour -> receiver slot by a left
+// binary search in the sorted receiver list (static-invalid slots map to 0),
+// then the warp computes each valid slot's fp32 dot product.
+// --------------------------------------------------------------------------
+template <typename ET>
+__global__ void __launch_bounds__(256) sparse_score_kernel(
+    const ET* __restrict__ a, const ET* __restrict__ b, const int64_t* __restrict__ nbr,
+    const uint8_t* __restrict__ nbr_valid, const int64_t* __restrict__ donor_patch,
+    const int64_t* __restrict__ recv_patch, int B, int Na, int Nb, int P, int K, int C,
+    ET* __restrict__ scores, int64_t* __restrict__ ridx_out, uint8_t* __restrict__ rvalid_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= (int64_t)B * Na) return;
+  const int bb = (int)(row / Na);
+  const int64_t pd = donor_patch[row];
+  const int64_t* rp = recv_patch + (int64_t)bb * Nb;
+  const ET* arow = a + row * C;
+  for (int k0 = 0; k0 < K; k0 += 32) {
+    const int k = k0 + lane;
+    int64_t slot = 0;
+    bool ok = false;
+    if (k < K && pd >= 0 && pd < P) {
+      const int64_t t = pd * K + k;
+      if (nbr_valid[t]) {
+        const int64_t n = nbr[t];
+        int lo = 0, hi = Nb;
+        while (lo < hi) {
+          int mid = (lo + hi) >> 1;
+          if (rp[mid] < n) lo = mid + 1; else hi = mid;
+        }
+        slot = lo < Nb ? lo : Nb - 1;
+        ok = lo < Nb && rp[slot] == n;
+      }
+    }
+    const int kmax = min(32, K - k0);
+    for (int j = 0; j < kmax; ++j) {
+      const int64_t s = __shfl_sync(MN_FULL_MASK, slot, j);
+      const bool v = __shfl_sync(MN_FULL_MASK, ok, j);
+      float acc = 0.f;
+      if (v) {
+        const ET* brow = b + ((int64_t)bb * Nb + s) * C;
+        for (int c = lane; c < C; c += 32) acc = fmaf(to_f32(arow[c]), to_f32(brow[c]), acc);
+        acc = warp_sum(acc);
+      }
+      if (lane == 0) {
+        const int64_t o = row * K + k0 + j;
+        scores[o] = from_f32<ET>(acc);
+        ridx_out[o] = s;
+        rvalid_out[o] = v ? 1 : 0;
+      }
+    }
+  }
+}
+
+// sparse_neighbor_dot (dtem.py:286-315): same dot with precomputed slots.
+template <typename ET>
+__global__ void __launch_bounds__(256) neighbor_dot_kernel(
+    const ET* __restrict__ a, const ET* __restrict__ b, const int64_t* __restrict__ ridx,
+    const uint8_t* __restrict__ rvalid, int B, int Na, int Nb, int K, int C, ET* __restrict__ scores) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= (int64_t)B * Na) return;
+  const int bb = (int)(row / Na);
+  const ET* arow = a + row * C;
+  for (int k = 0; k < K; ++k) {
+    const int64_t o = row * K + k;
+    const bool v = rvalid[o] != 0;
+    const int64_t s = ridx[o];
+    float acc = 0.f;
+    if (v && s >= 0 && s < Nb) {
+      const ET* brow = b + ((int64_t)bb * Nb + s) * C;
+      for (int c = lane; c < C; c += 32) acc = fmaf(to_f32(arow[c]), to_f32(brow[c]), acc);
+      acc = warp_sum(acc);
+    }
+    if (lane == 0) scores[o] = from_f32<ET>(acc);
+  }
+}
+
+// --------------------------------------------------------------------------
+// sparse_weighted_transport without atomics (dtem.py:436-468, CPU order
+// :911-926): each CTA (batch, channel chunk) builds receiver-centric edge
+// lists in shared memory with a stable counting sort (ascending edge id, the
+// reference's sequential scatter order), then gathers.
+// --------------------------------------------------------------------------
+template <typename ET>
+__global__ void __launch_bounds__(512) transport_kernel(
+    const ET* __restrict__ w, const ET* __restrict__ v, const int64_t* __restrict__ ridx,
+    const uint8_t* __restrict__ rvalid, int Na, int Nb, int K, int C, int CC,
+    ET* __restrict__ out, int* status) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int* start = reinterpret_cast<int*>(smem_raw);  // [Nb + 1]
+  int* cursor = start + Nb + 1;                   // [Nb]
+  int* list = cursor + Nb;                        // [Na*K]
+  const int bb = blockIdx.x;
+  const int c0 = blockIdx.y * CC;
+  const int E = Na * K;
+  const int64_t eb = (int64_t)bb * E;
+  for (int i = threadIdx.x; i < Nb + 1; i += blockDim.x) start[i] = 0;
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int64_t r = ridx[eb + e];
+    if (rvalid[eb + e] && r >= 0 && r < Nb) atomicAdd(&start[r + 1], 1);
+    else if (rvalid[eb + e] && status) atomicOr(status, MN_STATUS_TOO_MANY_EDGES);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < Nb; ++i) start[i + 1] += start[i];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < Nb; i += blockDim.x) cursor[i] = start[i];
+  __syncthreads();
+  if (threadIdx.x < 32) {  // stable fill by one warp, 32 edges at a time
+    const int lane = threadIdx.x;
+    for (int base = 0; base < E; base += 32) {
+      const int e = base + lane;
+      int key = -1;
+      if (e < E) {
+        const int64_t r = ridx[eb + e];
+        if (rvalid[eb + e] && r >= 0 && r < Nb) key = (int)r;
+      }
+      const unsigned peers = __match_any_sync(MN_FULL_MASK, key);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      int pos = 0;
+      if (key >= 0) pos = cursor[key] + rank;
+      __syncwarp();
+      if (key >= 0) {
+        list[pos] = e;
+        if (rank == 0) cursor[key] += __popc(peers);
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const ET* wb = w + eb;
+  const ET* vb = v + (int64_t)bb * Na * C;
+  for (int r = warp; r < Nb; r += nw) {
+    for (int c = c0 + lane; c < min(C, c0 + CC); c += 32) {
+      float acc = 0.f;
+      for (int j = start[r]; j < start[r + 1]; ++j) {
+        const int e = list[j];
+        const int d = e / K;
+        acc = __fadd_rn(acc, __fmul_rn(to_f32(wb[e]), to_f32(vb[(int64_t)d * C + c])));
+      }
+      out[((int64_t)bb * Nb + r) * C + c] = from_f32<ET>(acc);
+    }
+  }
+}
+
+// Adjoint of the transport (dtem.py:962-973): a gather per donor.
+template <typename ET>
+__global__ void __launch_bounds__(256) transport_adjoint_kernel(
+    const ET* __restrict__ w, const ET* __restrict__ v, const int64_t* __restrict__ ridx,
+    const uint8_t* __restrict__ rvalid, const ET* __restrict__ g, int B, int Na, int Nb, int K, int C,
+    ET* __restrict__ grad_w, ET* __restrict__ grad_v) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= (int64_t)B * Na) return;
+  const int bb = (int)(row / Na);
+  const ET* vrow = v + row * C;
+  for (int k = 0; k < K; ++k) {
+    const int64_t o = row * K + k;
+    const int64_t s = ridx[o];
+    float acc = 0.f;
+    if (rvalid[o] && s >= 0 && s < Nb) {
+      const ET* grow = g + ((int64_t)bb * Nb + s) * C;
+      for (int c = lane; c < C; c += 32) acc = fmaf(to_f32(grow[c]), to_f32(vrow[c]), acc);
+      acc = warp_sum(acc);
+    }
+    if (lane == 0) grad_w[o] = from_f32<ET>(acc);
+  }
+  for (int c = lane; c < C; c += 32) {
+    float acc = 0.f;
+    for (int k = 0; k < K; ++k) {
+      const int64_t o = row * K + k;
+      const int64_t s = ridx[o];
+      if (rvalid[o] && s >= 0 && s < Nb)
+        acc = fmaf(to_f32(w[o]), to_f32(g[((int64_t)bb * Nb + s) * C + c]), acc);
+    }
+    grad_v[row * C + c] = from_f32<ET>(acc);
+  }
+}
+
+// --------------------------------------------------------------------------
+// ThreTopK and the soft-k-max select
+// --------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) minmax_partials_kernel(const float* __restrict__ x, int64_t n,
+                                                              float* __restrict__ partials) {
+  __shared__ float red[64];
+  float lo = INFINITY, hi = -INFINITY;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    lo = fminf(lo, v);
+    hi = fmaxf(hi, v);
+  }
+  block_minmax(lo, hi, red);
+  if (threadIdx.x == 0) {
+    partials[2 * blockIdx.x] = lo;
+    partials[2 * blockIdx.x + 1] = hi;
+  }
+}
+
+__device__ __forceinline__ float reduce_range(const float* partials, int nparts, float* red, int* status) {
+  float lo = INFINITY, hi = -INFINITY;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+    lo = fminf(lo, partials[2 * i]);
+    hi = fmaxf(hi, partials[2 * i + 1]);
+  }
+  block_minmax(lo, hi, red);
+  const float range = hi - lo;
+  if (threadIdx.x == 0 && blockIdx.x == 0 && status && !(range > 0.f && range < INFINITY))
+    atomicOr(status, MN_STATUS_DEGENERATE_RANGE);
+  return range;
+}
+
+__global__ void __launch_bounds__(512) thre_topk_rows_kernel(const float* __restrict__ x, int n, int k,
+                                                             float temperature, const float* partials,
+                                                             int nparts, float* __restrict__ y, int* status) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red[64];
+  const int np = next_pow2(n);
+  RowScratch rs = carve_row_scratch(smem_raw, np);
+  float* xrow = reinterpret_cast<float*>(smem_raw + row_scratch_bytes(np));
+  const float range = reduce_range(partials, nparts, red, status);
+  const float* xr = x + (int64_t)blockIdx.x * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) xrow[i] = xr[i] / range * temperature;
+  __syncthreads();
+  const float lam = thre_topk_lambda(xrow, n, np, k, rs);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) y[(int64_t)blockIdx.x * n + i] = thre_topk_map(xrow[i], lam);
+}
+
+// Row energies of the masked scores (dtem.py:1557-1567): one warp per row.
+__global__ void __launch_bounds__(256) select_energy_kernel(const float* __restrict__ scores,
+                                                            const uint8_t* __restrict__ allowed, int rows,
+                                                            int K, float tau1, float* __restrict__ energy,
+                                                            int* __restrict__ valid_count, int Na) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* s = scores + row * K;
+  const uint8_t* al = allowed + row * K;
+  float m = -INFINITY;
+  for (int k = lane; k < K; k += 32)
+    if (al[k]) m = fmaxf(m, s[k] / tau1);
+  m = warp_max(m);
+  float e = 0.f;
+  if (m != -INFINITY) {
+    float sum = 0.f;
+    for (int k = lane; k < K; k += 32)
+      if (al[k]) sum += expf(s[k] / tau1 - m);
+    sum = warp_sum(sum);
+    e = expf(logf(sum) + m);
+  }
+  if (lane == 0) {
+    energy[row] = e;
+    if (m != -INFINITY) atomicAdd(&valid_count[row / Na], 1);
+  }
+}
+
+__global__ void __launch_bounds__(512) select_rows_kernel(const float* __restrict__ scores,
+                                                          const uint8_t* __restrict__ allowed, int Na, int K,
+                                                          int k, float tau1, float tau2,
+                                                          const float* __restrict__ energy,
+                                                          const int* __restrict__ valid_count,
+                                                          const float* partials, int nparts,
+                                                          float* __restrict__ assign, int* status) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red[64];
+  const int np = next_pow2(Na);
+  RowScratch rs = carve_row_scratch(smem_raw, np);
+  float* xrow = reinterpret_cast<float*>(smem_raw + row_scratch_bytes(np));
+  const int bb = blockIdx.x;
+  if (threadIdx.x == 0 && valid_count[bb] < k && status) atomicOr(status, MN_STATUS_INFEASIBLE_BUDGET);
+  const float range = reduce_range(partials, nparts, red, status);
+  const float* e = energy + (int64_t)bb * Na;
+  for (int i = threadIdx.x; i < Na; i += blockDim.x) xrow[i] = e[i] / range * tau2;
+  __syncthreads();
+  const float lam = thre_topk_lambda(xrow, Na, np, k, rs);
+  for (int d = threadIdx.x; d < Na; d += blockDim.x) {
+    const int64_t row = (int64_t)bb * Na + d;
+    const float* s = scores + row * K;
+    const uint8_t* al = allowed + row * K;
+    float* out = assign + row * K;
+    float m = -INFINITY;
+    for (int c = 0; c < K; ++c)
+      if (al[c]) m = fmaxf(m, s[c] / tau1);
+    if (m == -INFINITY) {
+      for (int c = 0; c < K; ++c) out[c] = 0.f;
+      continue;
+    }
+    const float y = thre_topk_map(xrow[d], lam);
+    float sum = 0.f;
+    for (int c = 0; c < K; ++c)
+      if (al[c]) sum += expf(s[c] / tau1 - m);
+    const float inv = 1.0f / sum;
+    float ks = 0.f;
+    for (int c = 0; c < K; ++c) {
+      const float kh = al[c] ? (expf(s[c] / tau1 - m) * inv) * y : 0.f;
+      out[c] = kh;
+      ks += kh;
+    }
+    const float tmp = fmaxf(ks - 1.0f, 0.0f) + 1.0f;
+    for (int c = 0; c < K; ++c) out[c] = out[c] / tmp;
+  }
+}
+
+template <typename ET>
+__global__ void __launch_bounds__(256) carrier_scatter_kernel(const ET* __restrict__ topk_x,
+                                                              const int64_t* __restrict__ idx, int k, int P,
+                                                              int C, ET* __restrict__ out) {
+  const int64_t row = blockIdx.x;  // b * k + i
+  const int bb = (int)(row / k), i = (int)(row % k);
+  const int64_t p = idx[row];
+  if (p < 0 || p >= P) return;
+  const ET* src = topk_x + ((int64_t)bb * (k + 1) + 1 + i) * C;
+  ET* dst = out + ((int64_t)bb * P + p) * C;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) dst[c] = src[c];
+}
+
+template <typename F>
+static int dispatch_dtype(int dtype, F&& f) {
+  if (dtype == MN_F32) { f(float{}); return MN_OK; }
+  if (dtype == MN_F16) { f(__half{}); return MN_OK; }
+  if (dtype == MN_BF16) { f(__nv_bfloat16{}); return MN_OK; }
+  return MN_ERR_ARG;
+}
+
+static int launch_status() { return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH; }
+
+}  // namespace mn
+
+using namespace mn;
+
+extern "C" int mn_sparse_spatial_score(int batch, int num_donors, int num_receivers, int num_patches, int k,
+                                       int channels, int dtype, const void* a, const void* b,
+                                       const int64_t* neighbor_indices, const uint8_t* neighbor_valid,
+                                       const int64_t* donor_patch, const int64_t* receiver_patch, void* scores,
+                                       int64_t* receiver_indices, uint8_t* receiver_valid, void* stream) {
+  if (batch < 0 || num_donors < 0 || num_receivers <= 0 || num_patches <= 0 || k <= 0 || channels <= 0)
+    return MN_ERR_ARG;
+  if ((int64_t)batch * num_donors == 0) return MN_OK;
+  if (!a || !b || !neighbor_indices || !neighbor_valid || !donor_patch || !receiver_patch || !scores ||
+      !receiver_indices || !receiver_valid)
+    return MN_ERR_ARG;
+  cudaGetLastError();
+  const int64_t rows = (int64_t)batch * num_donors;
+  const dim3 grid((unsigned)((rows + 7) / 8));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = dispatch_dtype(dtype, [&](auto tag) {
+    using ET = decltype(tag);
+    sparse_score_kernel<ET><<<grid, 256, 0, st>>>(
+        static_cast<const ET*>(a), static_cast<const ET*>(b), neighbor_indices, neighbor_valid, donor_patch,
+        receiver_patch, batch, num_donors, num_receivers, num_patches, k, channels, static_cast<ET*>(scores),
+        receiver_indices, receiver_valid);
+  });
+  return rc != MN_OK ? rc : launch_status();
+}
+
+extern "C" int mn_sparse_neighbor_dot(int batch, int num_donors, int num_receivers, int k, int channels,
+                                      int dtype, const void* a, const void* b, const int64_t* receiver_indices,
+                                      const uint8_t* receiver_valid, void* scores, void* stream) {
+  if (batch < 0 || num_donors < 0 || num_receivers <= 0 || k <= 0 || channels <= 0) return MN_ERR_ARG;
+  if ((int64_t)batch * num_donors == 0) return MN_OK;
+  if (!a || !b || !receiver_indices || !receiver_valid || !scores) return MN_ERR_ARG;
+  cudaGetLastError();
+  const int64_t rows = (int64_t)batch * num_donors;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = dispatch_dtype(dtype, [&](auto tag) {
+    using ET = decltype(tag);
+    neighbor_dot_kernel<ET><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+        static_cast<const ET*>(a), static_cast<const ET*>(b), receiver_indices, receiver_valid, batch,
+        num_donors, num_receivers, k, channels, static_cast<ET*>(scores));
+  });
+  return rc != MN_OK ? rc : launch_status();
+}
+
+extern "C" int mn_sparse_weighted_transport(int batch, int num_donors, int num_receivers, int k, int channels,
+                                            int dtype, const void* assignment, const void* values,
+                                            const int64_t* receiver_indices, const uint8_t* receiver_valid,
+                                            void* out, int* status, void* stream) {
+  if (batch < 0 || num_donors < 0 || num_receivers <= 0 || k <= 0 || channels <= 0) return MN_ERR_ARG;
+  if (!out) return MN_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t elem = dtype == MN_F32 ? 4 : 2;
+  if (batch == 0) return MN_OK;
+  cudaGetLastError();
+  if (num_donors == 0) {
+    cudaMemsetAsync(out, 0, (size_t)batch * num_receivers * channels * elem, st);
+    return launch_status();
+  }
+  if (!assignment || !values || !receiver_indices || !receiver_valid) return MN_ERR_ARG;
+  const size_t smem = ((size_t)2 * num_receivers + 1 + (size_t)num_donors * k) * sizeof(int);
+  if (smem > 200 * 1024) return MN_ERR_UNSUPPORTED;
+  const int CC = 128;
+  const dim3 grid(batch, (channels + CC - 1) / CC);
+  int rc = dispatch_dtype(dtype, [&](auto tag) {
+    using ET = decltype(tag);
+    cudaFuncSetAttribute(transport_kernel<ET>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    transport_kernel<ET><<<grid, 512, smem, st>>>(static_cast<const ET*>(assignment), static_cast<const ET*>(values),
+                                                  receiver_indices, receiver_valid, num_donors, num_receivers, k,
+                                                  channels, CC, static_cast<ET*>(out), status);
+  });
+  return rc != MN_OK ? rc : launch_status();
+}
+
+extern "C" int mn_sparse_transport_adjoint(int batch, int num_donors, int num_receivers, int k, int channels,
+                                           int dtype, const void* assignment, const void* values,
+                                           const int64_t* receiver_indices, const uint8_t* receiver_valid,
+                                           const void* grad_out, void* grad_assignment, void* grad_values,
+                                           void* stream) {
+  if (batch < 0 || num_donors < 0 || num_receivers <= 0 || k <= 0 || channels <= 0) return MN_ERR_ARG;
+  if ((int64_t)batch * num_donors == 0) return MN_OK;
+  if (!assignment || !values || !receiver_indices || !receiver_valid || !grad_out || !grad_assignment ||
+      !grad_values)
+    return MN_ERR_ARG;
+  cudaGetLastError();
+  const int64_t rows = (int64_t)batch * num_donors;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = dispatch_dtype(dtype, [&](auto tag) {
+    using ET = decltype(tag);
+    transport_adjoint_kernel<ET><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+        static_cast<const ET*>(assignment), static_cast<const ET*>(values), receiver_indices, receiver_valid,
+        static_cast<const ET*>(grad_out), batch, num_donors, num_receivers, k, channels,
+        static_cast<ET*>(grad_assignment), static_cast<ET*>(grad_values));
+  });
+  return rc != MN_OK ? rc : launch_status();
+}
+
+static int thre_topk_parts(int64_t n) { return (int)std::min<int64_t>(1024, std::max<int64_t>(1, (n + 2047) / 2048)); }
+
+extern "C" size_t mn_thre_topk_workspace_bytes(int rows, int n) {
+  if (rows <= 0 || n <= 0) return 0;
+  return (size_t)thre_topk_parts((int64_t)rows * n) * 2 * sizeof(float);
+}
+
+extern "C" int mn_thre_topk(int rows, int n, const float* x, int k, float temperature, float* y,
+                            void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  if (rows <= 0 || n <= 0 || !x || !y || !workspace) return MN_ERR_ARG;
+  if (n > 4096) return MN_ERR_UNSUPPORTED;
+  if (workspace_bytes < mn_thre_topk_workspace_bytes(rows, n)) return MN_ERR_WORKSPACE;
+  cudaGetLastError();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int parts = thre_topk_parts((int64_t)rows * n);
+  float* partials = static_cast<float*>(workspace);
+  minmax_partials_kernel<<<parts, 256, 0, st>>>(x, (int64_t)rows * n, partials);
+  const int np = next_pow2(n);
+  const size_t smem = row_scratch_bytes(np) + (size_t)n * sizeof(float);
+  cudaFuncSetAttribute(thre_topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  thre_topk_rows_kernel<<<rows, 512, smem, st>>>(x, n, k, temperature, partials, parts, y, status);
+  return launch_status();
+}
+
+extern "C" size_t mn_dtem_select_workspace_bytes(int batch, int num_donors) {
+  if (batch <= 0 || num_donors <= 0) return 0;
+  const int64_t rows = (int64_t)batch * num_donors;
+  return (size_t)rows * sizeof(float) + (size_t)batch * sizeof(int) +
+         (size_t)thre_topk_parts(rows) * 2 * sizeof(float) + 64;
+}
+
+extern "C" int mn_dtem_select(int batch, int num_donors, int k_slots, const float* scores, const uint8_t* allowed,
+                              int k, float tau1, float tau2, float* assignment, void* workspace,
+                              size_t workspace_bytes, int* status, void* stream) {
+  if (batch <= 0 || num_donors <= 0 || k_slots <= 0 || !scores || !allowed || !assignment || !workspace)
+    return MN_ERR_ARG;
+  if (num_donors > 4096) return MN_ERR_UNSUPPORTED;
+  if (workspace_bytes < mn_dtem_select_workspace_bytes(batch, num_donors)) return MN_ERR_WORKSPACE;
+  cudaGetLastError();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t rows = (int64_t)batch * num_donors;
+  float* energy = static_cast<float*>(workspace);
+  int* counts = reinterpret_cast<int*>(energy + rows);
+  float* partials = reinterpret_cast<float*>(counts + batch);
+  const int parts = thre_topk_parts(rows);
+  cudaMemsetAsync(counts, 0, (size_t)batch * sizeof(int), st);
+  select_energy_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(scores, allowed, (int)rows, k_slots, tau1,
+                                                                   energy, counts, num_donors);
+  minmax_partials_kernel<<<parts, 256, 0, st>>>(energy, rows, partials);
+  const int np = next_pow2(num_donors);
+  const size_t smem = row_scratch_bytes(np) + (size_t)num_donors * sizeof(float);
+  cudaFuncSetAttribute(select_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  select_rows_kernel<<<batch, 512, smem, st>>>(scores, allowed, num_donors, k_slots, k, tau1, tau2, energy, counts,
+                                               partials, parts, assignment, status);
+  return launch_status();
+}
+
+extern "C" int mn_carrier_scatter(int batch, int k, int num_patches, int channels, int dtype, const void* topk_x,
+                                  const int64_t* topk_idx, void* out, void* stream) {
+  if (batch < 0 || k < 0 || num_patches <= 0 || channels <= 0 || !out) return MN_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t elem = dtype == MN_F32 ? 4 : 2;
+  cudaGetLastError();
+  cudaMemsetAsync(out, 0, (size_t)batch * num_patches * channels * elem, st);
+  if ((int64_t)batch * k == 0) return launch_status();
+  if (!topk_x || !topk_idx) return MN_ERR_ARG;
+  int rc = dispatch_dtype(dtype, [&](auto tag) {
+    using ET = decltype(tag);
+    carrier_scatter_kernel<ET><<<(unsigned)((int64_t)batch * k), 128, 0, st>>>(
+        static_cast<const ET*>(topk_x), topk_idx, k, num_patches, channels, static_cast<ET*>(out));
+  });
+  return rc != MN_OK ? rc : launch_status();
+}

@@ -1,0 +1,567 @@
+// Fused DTEM spatial routing for the canonical eval grouping
+// (alternating_per_layer_fast) on sm_100a.
+//
+// The reference (opentome/timm/dtem.py:1687-2223, driven six times by
+// LocalEncoder.forward, opentome/models/mergenet/model.py:574-590, then the
+// carrier block model.py:1157-1183) runs ~60 ATen/Triton launches per layer
+// and rewrites the full [B,T,C] token tensor six times.  Here the work is
+// split by what it depends on:
+//
+//   route_score    (layer, image, band)  metrics -> compact scores + row energy
+//   route_select   (layer, image)        global ThreTopK range -> assignment
+//   route_mass     (image)               6-layer mass / centre chain + carriers
+//   route_transport(image, channel tile) 6-layer feature transport in shared
+//                                        memory + carrier gather
+//
+// Assignments depend only on metrics (never on tokens or masses), so all
+// layers are scored and selected in parallel; only masses, centres and
+// features chain through the layers, and features are read once from HBM and
+// written once (the carriers).
+#include <algorithm>
+#include <cstdio>
+
+#include "common.cuh"
+#include "thretopk.cuh"
+
+namespace mn {
+
+struct RouteWs {
+  float* assign;     // [L][B][half][kc]   scores, then assignment
+  float* energy;     // [L][B][half]
+  float* asum;       // [L][B][half]       row sums of the assignment
+  float* partials;   // [L][B][bands][2]   per-CTA min / max of the energy
+  float* wa_old;     // [L][B][half]
+  float* wb_old;     // [L][B][half]
+  float* wb_safe;    // [L][B][half]
+  int32_t* carrier_tok;  // [B][k]      token index of each carrier, in order
+};
+
+__host__ inline size_t route_ws_floats(int L, int B, int half, int kc, int bands) {
+  return (size_t)L * B * half * kc + (size_t)L * B * half * 5 + (size_t)L * B * bands * 2;
+}
+
+// Table views for layer parity q.
+struct ParityTables {
+  const int32_t* slot_k;
+  const int32_t* slot_rx;
+  const int32_t* rx_in;
+};
+__host__ __device__ inline ParityTables parity_tables(const int32_t* t, int half, int kc, int kin, int q) {
+  const int32_t* base = t + (int64_t)q * ((int64_t)half * kc * 2 + (int64_t)half * kin);
+  ParityTables p;
+  p.slot_k = base;
+  p.slot_rx = base + (int64_t)half * kc;
+  p.rx_in = base + (int64_t)half * kc * 2;
+  return p;
+}
+
+struct KBudget {
+  int v[64];  // per-layer merge budget r (passed by value)
+};
+
+struct Banding {
+  int bands;     // CTAs per (image, layer)
+  int rows;      // grid rows per band
+  int radius_rows;
+  int cap;       // receivers the shared-memory tile holds
+};
+
+// ---------------------------------------------------------------------------
+// route_score: one CTA per (band, image, layer).  Receivers the band's donors
+// can reach are normalised into shared memory (fp32, metric / max(|m|,1e-6)
+// as dtem.py:1689-1691); each warp then scores one donor at a time against
+// its legal receivers (dtem.py:361-433 restricted to the compact slots) and
+// folds the masked logsumexp energy (dtem.py:1557-1567).
+// ---------------------------------------------------------------------------
+template <int MDT>
+__global__ void __launch_bounds__(512) route_score_kernel(
+    const typename Elem<MDT>::T* __restrict__ metrics, const int32_t* __restrict__ table,
+    int B, int T, int Cm, int grid_w, int half, int kc, int kin, Banding band, float tau1,
+    RouteWs ws, int* status) {
+  using ET = typename Elem<MDT>::T;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* recv = reinterpret_cast<float*>(smem_raw);  // [cap][Cm]
+  __shared__ float red[64];
+
+  const int l = blockIdx.y;
+  const int b = blockIdx.x / band.bands;
+  const int bi = blockIdx.x % band.bands;
+  const int q = l & 1;
+  const int dp = q ? 0 : 1, rp = 1 - dp;
+  const ParityTables pt = parity_tables(table, half, kc, kin, q);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int grid_h = (2 * half) / grid_w;
+
+  // donor / receiver local ranges of this band
+  const int r0 = bi * band.rows, r1 = min(grid_h, r0 + band.rows);
+  const int p_lo = r0 * grid_w, p_hi = r1 * grid_w;                  // donor patches
+  const int d_lo = (p_lo - dp + 1) >> 1, d_hi = (p_hi - dp + 1) >> 1;  // ceil((p - dp)/2)
+  const int rr0 = max(0, r0 - band.radius_rows), rr1 = min(grid_h, r1 + band.radius_rows);
+  const int s_lo = (rr0 * grid_w - rp + 1) >> 1, s_hi = (rr1 * grid_w - rp + 1) >> 1;
+
+  const ET* mbase = metrics + ((int64_t)l * B + b) * (int64_t)T * Cm;
+  const int per = (Cm + 31) >> 5;  // <= 4
+
+  // normalised receivers -> shared memory
+  for (int s = s_lo + warp; s < s_hi; s += nwarps) {
+    const ET* row = mbase + (int64_t)(1 + 2 * s + rp) * Cm;
+    float v[4];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int c = lane + 32 * j;
+      v[j] = (j < per && c < Cm) ? to_f32(row[c]) : 0.f;
+      ss = fmaf(v[j], v[j], ss);
+    }
+    ss = warp_sum(ss);
+    float nrm = fmaxf(sqrtf(ss), 1e-6f);
+    float* dst = recv + (int64_t)(s - s_lo) * Cm;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int c = lane + 32 * j;
+      if (j < per && c < Cm) dst[c] = v[j] / nrm;
+    }
+  }
+  __syncthreads();
+
+  float emin = INFINITY, emax = -INFINITY;
+  const int64_t lb = (int64_t)l * B + b;
+  float* sc_out = ws.assign + lb * half * kc;
+  float* e_out = ws.energy + lb * half;
+  for (int d = d_lo + warp; d < d_hi; d += nwarps) {
+    const ET* row = mbase + (int64_t)(1 + 2 * d + dp) * Cm;
+    float a[4];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int c = lane + 32 * j;
+      a[j] = (j < per && c < Cm) ? to_f32(row[c]) : 0.f;
+      ss = fmaf(a[j], a[j], ss);
+    }
+    ss = warp_sum(ss);
+    float nrm = fmaxf(sqrtf(ss), 1e-6f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) a[j] = a[j] / nrm;
+    float mine = -INFINITY;
+    const int32_t* srx = pt.slot_rx + (int64_t)d * kc;
+    for (int c = 0; c < kc; ++c) {
+      int s = srx[c];
+      if (s < 0) break;
+      if (s < s_lo || s >= s_hi) {  // outside the staged band: a table/banding bug
+        if (lane == 0 && status) atomicOr(status, MN_STATUS_TOO_MANY_EDGES);
+        continue;
+      }
+      const float* rv = recv + (int64_t)(s - s_lo) * Cm;
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        int cc = lane + 32 * j;
+        if (j < per && cc < Cm) acc = fmaf(a[j], rv[cc], acc);
+      }
+      acc = warp_sum(acc);
+      if (lane == c) mine = acc / tau1;
+    }
+    float m = warp_max(mine);
+    float e = 0.f;
+    if (m != -INFINITY) {
+      float ex = (mine != -INFINITY) ? expf(mine - m) : 0.f;
+      float sum = warp_sum(ex);
+      e = expf(logf(sum) + m);
+    }
+    if (lane < kc) sc_out[(int64_t)d * kc + lane] = mine;
+    if (lane == 0) e_out[d] = e;
+    emin = fminf(emin, e);
+    emax = fmaxf(emax, e);
+  }
+  block_minmax(emin, emax, red);
+  if (threadIdx.x == 0) {
+    float* p = ws.partials + (lb * band.bands + bi) * 2;
+    p[0] = emin;
+    p[1] = emax;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// route_select: one CTA per (image, layer).  Global ThreTopK range over the
+// whole batch for this layer (thetopk.py:12-13), per-row threshold, then the
+// masked softmax x row k-hot and the clamp-normalise (dtem.py:1568-1579).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) route_select_kernel(
+    const int32_t* __restrict__ table, int B, int half, int kc, int kin, int bands,
+    KBudget kb, float tau2, RouteWs ws, int* status) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int np = next_pow2(half);
+  RowScratch rs = carve_row_scratch(smem_raw, np);
+  float* xrow = reinterpret_cast<float*>(smem_raw + row_scratch_bytes(np));  // [half] scaled energies
+  __shared__ float red[64];
+
+  const int b = blockIdx.x, l = blockIdx.y, q = l & 1;
+  const int64_t lb = (int64_t)l * B + b;
+  const ParityTables pt = parity_tables(table, half, kc, kin, q);
+
+  // batch-global range of this layer's energies
+  float gmin = INFINITY, gmax = -INFINITY;
+  const float* part = ws.partials + (int64_t)l * B * bands * 2;
+  for (int i = threadIdx.x; i < B * bands; i += blockDim.x) {
+    gmin = fminf(gmin, part[2 * i]);
+    gmax = fmaxf(gmax, part[2 * i + 1]);
+  }
+  block_minmax(gmin, gmax, red);
+  const float range = gmax - gmin;
+  if (threadIdx.x == 0 && b == 0 && !(range > 0.f && range < INFINITY) && status)
+    atomicOr(status, MN_STATUS_DEGENERATE_RANGE);
+
+  const float* e = ws.energy + lb * half;
+  for (int d = threadIdx.x; d < half; d += blockDim.x) xrow[d] = e[d] / range * tau2;
+  __syncthreads();
+  const int k = kb.v[l];
+  const float lam = thre_topk_lambda(xrow, half, np, k, rs);
+
+  float* asg = ws.assign + lb * half * kc;
+  float* asum = ws.asum + lb * half;
+  for (int d = threadIdx.x; d < half; d += blockDim.x) {
+    float* row = asg + (int64_t)d * kc;
+    const int32_t* srx = pt.slot_rx + (int64_t)d * kc;
+    int cnt = 0;
+    float m = -INFINITY;
+    for (int c = 0; c < kc; ++c) {
+      if (srx[c] < 0) break;
+      ++cnt;
+      m = fmaxf(m, row[c]);
+    }
+    if (cnt == 0) { asum[d] = 0.f; continue; }
+    const float y = thre_topk_map(xrow[d], lam);  // row k-hot (valid row)
+    float sum = 0.f;
+    for (int c = 0; c < cnt; ++c) sum += expf(row[c] - m);
+    const float inv = 1.0f / sum;
+    float khot[32];
+    float ks = 0.f;
+    for (int c = 0; c < cnt; ++c) {
+      float p = expf(row[c] - m) * inv;
+      khot[c] = p * y;
+      ks += khot[c];
+    }
+    const float tmp = fmaxf(ks - 1.0f, 0.0f) + 1.0f;
+    float as = 0.f;
+    for (int c = 0; c < cnt; ++c) {
+      float v = khot[c] / tmp;
+      row[c] = v;
+      as += v;
+    }
+    for (int c = cnt; c < kc; ++c) row[c] = 0.f;
+    asum[d] = as;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// route_mass: one CTA per image.  Mass and centre-of-mass chain over the
+// layers (dtem.py:1978-1983, :2016-2025, :2027-2044, interleave :2196-2222),
+// then the exact top-k by mass and the centre-of-mass ordering
+// (model.py:1167-1171).  Also records the per-layer scalars the feature
+// transport needs.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) route_mass_kernel(
+    const int32_t* __restrict__ table, int B, int T, int half, int kc, int kin, int L, int k,
+    RouteWs ws, float* __restrict__ size_out, float* __restrict__ center_out,
+    float* __restrict__ topk_size, int64_t* __restrict__ topk_idx) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* size = reinterpret_cast<float*>(smem_raw);  // [T]
+  float* center = size + T;                          // [T]
+  const int P = T - 1;
+  const int np = next_pow2(P);
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(center + T);  // 8T bytes above base
+  const int b = blockIdx.x;
+  const float eps = 1.1920928955078125e-07f;  // torch.finfo(float32).eps
+
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    size[t] = 1.0f;
+    center[t] = (float)t;
+  }
+  __syncthreads();
+  for (int l = 0; l < L; ++l) {
+    const int q = l & 1, dp = q ? 0 : 1, rp = 1 - dp;
+    const ParityTables pt = parity_tables(table, half, kc, kin, q);
+    const int64_t lb = (int64_t)l * B + b;
+    const float* asg = ws.assign + lb * half * kc;
+    const float* asum = ws.asum + lb * half;
+    float* wa_rec = ws.wa_old + lb * half;
+    float* wb_rec = ws.wb_old + lb * half;
+    float* ws_rec = ws.wb_safe + lb * half;
+    // new values computed from the old state, written after a barrier
+    float nv_b[4], nc_b[4], nv_a[4];
+    int cnt = 0;
+    for (int i = threadIdx.x; i < half; i += blockDim.x, ++cnt) {
+      const int tb = 1 + 2 * i + rp;
+      const float wb = size[tb], cb = center[tb];
+      float contrib = 0.f, ccontrib = 0.f;
+      const int32_t* in = pt.rx_in + (int64_t)i * kin;
+      for (int j = 0; j < kin; ++j) {
+        int e = in[j];
+        if (e < 0) break;
+        int d = e / kc;
+        float w = asg[e];
+        int ta = 1 + 2 * d + dp;
+        float wa = size[ta];
+        contrib = __fadd_rn(contrib, __fmul_rn(w, wa));
+        ccontrib = __fadd_rn(ccontrib, __fmul_rn(w, __fmul_rn(wa, center[ta])));
+      }
+      const float wbn = __fadd_rn(wb, contrib);
+      const float wsafe = fmaxf(wbn, eps);
+      nv_b[cnt] = wbn;
+      nc_b[cnt] = __fdiv_rn(__fadd_rn(__fmul_rn(wb, cb), ccontrib), wsafe);
+      wb_rec[i] = wb;
+      ws_rec[i] = wsafe;
+      // donor i of this layer
+      const int ta = 1 + 2 * i + dp;
+      const float wa = size[ta];
+      wa_rec[i] = wa;
+      const float tmp = __fsub_rn(1.0f, asum[i]);
+      nv_a[cnt] = __fmul_rn(wa, fminf(fmaxf(tmp, 0.f), 1.f));
+    }
+    __syncthreads();
+    cnt = 0;
+    for (int i = threadIdx.x; i < half; i += blockDim.x, ++cnt) {
+      size[1 + 2 * i + rp] = nv_b[cnt];
+      center[1 + 2 * i + rp] = nc_b[cnt];
+      size[1 + 2 * i + dp] = nv_a[cnt];
+    }
+    if (threadIdx.x == 0) center[0] = 0.f;  // CLS centre after the first layer
+    __syncthreads();
+  }
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    size_out[(int64_t)b * T + t] = size[t];
+    center_out[(int64_t)b * T + t] = center[t];
+  }
+  // exact top-k by (mass desc, patch asc): key = (~bits(mass) << 32) | patch
+  for (int i = threadIdx.x; i < np; i += blockDim.x) {
+    unsigned long long key = ~0ull;
+    if (i < P) {
+      unsigned int bits = __float_as_uint(size[1 + i]);
+      key = ((unsigned long long)(~bits) << 32) | (unsigned int)i;
+    }
+    keys[i] = key;
+  }
+  __syncthreads();
+  bitonic_sort_u64(keys, np);
+  // re-key the k winners by (centre asc, patch asc); centres are >= 0
+  const int nk = next_pow2(k);
+  unsigned long long* keys2 = keys + np;
+  for (int i = threadIdx.x; i < nk; i += blockDim.x) {
+    unsigned long long key = ~0ull;
+    if (i < k) {
+      unsigned int p = (unsigned int)(keys[i] & 0xffffffffu);
+      key = ((unsigned long long)__float_as_uint(center[1 + p]) << 32) | p;
+    }
+    keys2[i] = key;
+  }
+  __syncthreads();
+  bitonic_sort_u64(keys2, nk);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    unsigned int p = (unsigned int)(keys2[i] & 0xffffffffu);
+    topk_idx[(int64_t)b * k + i] = p;
+    ws.carrier_tok[(int64_t)b * k + i] = (int)p + 1;
+    topk_size[(int64_t)b * (k + 1) + 1 + i] = size[1 + p];
+  }
+  if (threadIdx.x == 0) topk_size[(int64_t)b * (k + 1)] = size[0];
+}
+
+// ---------------------------------------------------------------------------
+// route_transport: one CTA per (image, CT-channel tile).  The token tile
+// [T][CT] lives in shared memory in fp32; each layer updates the receivers in
+// place (donor features are unchanged by a layer, dtem.py:1973-2025):
+//   x_s <- (wb_old[s] * x_s + sum_edges assign * (wa_old[d] * x_d)) / wb_safe[s]
+// accumulated in the reference's edge order, then the carriers are gathered.
+// ---------------------------------------------------------------------------
+template <typename XT, int CT>
+__global__ void __launch_bounds__(256) route_transport_kernel(
+    const XT* __restrict__ x, const int32_t* __restrict__ table, int B, int T, int C, int half,
+    int kc, int kin, int L, int k, RouteWs ws, XT* __restrict__ topk_x) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* tile = reinterpret_cast<float*>(smem_raw);  // [T][CT]
+  const int b = blockIdx.x;
+  const int c0 = blockIdx.y * CT;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  constexpr int RPW = 32 / CT;  // receivers per warp pass
+  const int sub = lane / CT, ch = lane % CT;
+  const bool ch_ok = (c0 + ch) < C;
+
+  const XT* xb = x + (int64_t)b * T * C;
+  for (int i = threadIdx.x; i < T * CT; i += blockDim.x) {
+    int t = i / CT, c = i % CT;
+    tile[i] = (c0 + c < C) ? to_f32(xb[(int64_t)t * C + c0 + c]) : 0.f;
+  }
+  __syncthreads();
+  for (int l = 0; l < L; ++l) {
+    const int q = l & 1, dp = q ? 0 : 1, rp = 1 - dp;
+    const ParityTables pt = parity_tables(table, half, kc, kin, q);
+    const int64_t lb = (int64_t)l * B + b;
+    const float* asg = ws.assign + lb * half * kc;
+    const float* wa_old = ws.wa_old + lb * half;
+    const float* wb_old = ws.wb_old + lb * half;
+    const float* wb_safe = ws.wb_safe + lb * half;
+    for (int s0 = warp * RPW; s0 < half; s0 += nwarps * RPW) {
+      const int s = s0 + sub;
+      if (s < half) {
+        const int32_t* in = pt.rx_in + (int64_t)s * kin;
+        float acc = 0.f;
+        for (int j = 0; j < kin; ++j) {
+          int e = in[j];
+          if (e < 0) break;
+          int d = e / kc;
+          float t = __fmul_rn(wa_old[d], tile[(1 + 2 * d + dp) * CT + ch]);
+          acc = __fadd_rn(acc, __fmul_rn(asg[e], t));
+        }
+        float* xs = tile + (1 + 2 * s + rp) * CT + ch;
+        *xs = __fdiv_rn(__fadd_rn(__fmul_rn(wb_old[s], *xs), acc), wb_safe[s]);
+      }
+    }
+    __syncthreads();
+  }
+  XT* out = topk_x + (int64_t)b * (k + 1) * C;
+  const int32_t* ctok = ws.carrier_tok + (int64_t)b * k;
+  for (int i = threadIdx.x; i < (k + 1) * CT; i += blockDim.x) {
+    int r = i / CT, c = i % CT;
+    if (c0 + c >= C) continue;
+    int t = (r == 0) ? 0 : ctok[r - 1];
+    out[(int64_t)r * C + c0 + c] = from_f32<XT>(tile[t * CT + c]);
+  }
+  (void)ch_ok;
+}
+
+
+static Banding make_banding(int grid_h, int grid_w, int radius_rows, int Cm) {
+  Banding bd;
+  bd.radius_rows = radius_rows;
+  const int max_smem = 110 * 1024;
+  bd.cap = max_smem / (Cm * 4);
+  for (int nb = 1; nb <= grid_h; ++nb) {
+    const int rows = (grid_h + nb - 1) / nb;
+    const int need_rows = (nb == 1) ? grid_h : std::min(grid_h, rows + 2 * radius_rows);
+    const int need = (need_rows * grid_w + 1) / 2 + 1;
+    if (need <= bd.cap) {
+      bd.bands = (grid_h + rows - 1) / rows;
+      bd.rows = rows;
+      return bd;
+    }
+  }
+  bd.bands = -1;
+  bd.rows = 0;
+  return bd;
+}
+
+}  // namespace mn
+
+using namespace mn;
+
+extern "C" size_t mn_route_workspace_bytes(const mn_route_dims* dims, int batch, int num_layers) {
+  if (!dims || batch <= 0 || num_layers <= 0) return 0;
+  size_t floats = route_ws_floats(num_layers, batch, dims->half, dims->kc, dims->grid_h);
+  return floats * sizeof(float) + (size_t)batch * dims->num_patches * sizeof(int32_t);
+}
+
+template <typename XT>
+static void launch_transport(const void* x, const int32_t* table, int B, int T, int C, int half, int kc,
+                             int kin, int L, int k, const RouteWs& ws, void* topk_x, int ct,
+                             cudaStream_t st) {
+  size_t smem = (size_t)T * ct * sizeof(float);
+  dim3 grid(B, (C + ct - 1) / ct);
+  const XT* xp = static_cast<const XT*>(x);
+  XT* op = static_cast<XT*>(topk_x);
+  if (ct == 32) {
+    cudaFuncSetAttribute(route_transport_kernel<XT, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    route_transport_kernel<XT, 32><<<grid, 256, smem, st>>>(xp, table, B, T, C, half, kc, kin, L, k, ws, op);
+  } else if (ct == 16) {
+    cudaFuncSetAttribute(route_transport_kernel<XT, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    route_transport_kernel<XT, 16><<<grid, 256, smem, st>>>(xp, table, B, T, C, half, kc, kin, L, k, ws, op);
+  } else {
+    cudaFuncSetAttribute(route_transport_kernel<XT, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    route_transport_kernel<XT, 8><<<grid, 256, smem, st>>>(xp, table, B, T, C, half, kc, kin, L, k, ws, op);
+  }
+}
+
+template <int MDT>
+static void launch_score(const void* metrics, const int32_t* table, int B, int T, int Cm, int grid_w,
+                         int half, int kc, int kin, const Banding& bd, float tau1, const RouteWs& ws,
+                         int L, int* status, cudaStream_t st) {
+  using ET = typename Elem<MDT>::T;
+  size_t smem = (size_t)bd.cap * Cm * sizeof(float);
+  dim3 grid(B * bd.bands, L);
+  cudaFuncSetAttribute(route_score_kernel<MDT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  route_score_kernel<MDT><<<grid, 512, smem, st>>>(static_cast<const ET*>(metrics), table, B, T, Cm,
+                                                    grid_w, half, kc, kin, bd, tau1, ws, status);
+}
+
+extern "C" int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev_table, int batch,
+                                   int channels, int metric_dim, int num_layers, const int* r_list,
+                                   int k, float tau1, float tau2, const void* x, int x_dtype,
+                                   const void* metrics, int metric_dtype, void* workspace,
+                                   size_t workspace_bytes, void* topk_x, float* topk_size,
+                                   int64_t* topk_idx, float* size_out, float* center_out,
+                                   int* status, void* stream) {
+  if (!dims || !dev_table || !x || !metrics || !workspace || !topk_x || !topk_size || !topk_idx ||
+      !size_out || !center_out || !r_list)
+    return MN_ERR_ARG;
+  if (batch <= 0 || channels <= 0 || metric_dim <= 0 || num_layers <= 0 || num_layers > 64)
+    return MN_ERR_ARG;
+  if (x_dtype < 0 || x_dtype > 2 || metric_dtype < 0 || metric_dtype > 2) return MN_ERR_ARG;
+  const int half = dims->half, kc = dims->kc, kin = dims->kin;
+  const int P = dims->num_patches, T = P + 1;
+  if (P <= 0 || P % 2 != 0 || half * 2 != P || dims->grid_h * dims->grid_w != P) return MN_ERR_ARG;
+  if (metric_dim > 128 || kc <= 0 || kc > 32 || kin <= 0 || k <= 0 || k > P) return MN_ERR_UNSUPPORTED;
+  if (half > 4 * 1024 || next_pow2(half) > 2048 * 4) return MN_ERR_UNSUPPORTED;
+  if (mn_route_workspace_bytes(dims, batch, num_layers) > workspace_bytes) return MN_ERR_WORKSPACE;
+  KBudget kb;
+  for (int l = 0; l < num_layers; ++l) {
+    int r = std::min(r_list[l], (T - 1) / 2);
+    if (r <= 0) return MN_ERR_UNSUPPORTED;  // a no-op layer is not on the canonical path
+    if (dims->valid_rows[l & 1] < r) return MN_INFEASIBLE_BUDGET;
+    kb.v[l] = r;
+  }
+  const Banding bd = make_banding(dims->grid_h, dims->grid_w, dims->radius_rows, metric_dim);
+  if (bd.bands <= 0) return MN_ERR_UNSUPPORTED;
+  int ct = 32;
+  while (ct > 8 && (size_t)T * ct * sizeof(float) > 200 * 1024) ct >>= 1;
+  if ((size_t)T * ct * sizeof(float) > 220 * 1024) return MN_ERR_UNSUPPORTED;
+  const int np_sel = next_pow2(half);
+  const size_t smem_sel = row_scratch_bytes(np_sel) + (size_t)half * sizeof(float);
+  const int np_mass = next_pow2(P), nk = next_pow2(k);
+  const size_t smem_mass = (size_t)2 * T * sizeof(float) + (size_t)(np_mass + nk) * 8;
+  if (smem_sel > 220 * 1024 || smem_mass > 220 * 1024) return MN_ERR_UNSUPPORTED;
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* f = static_cast<float*>(workspace);
+  RouteWs ws;
+  const size_t LBh = (size_t)num_layers * batch * half;
+  ws.assign = f;   f += LBh * kc;
+  ws.energy = f;   f += LBh;
+  ws.asum = f;     f += LBh;
+  ws.wa_old = f;   f += LBh;
+  ws.wb_old = f;   f += LBh;
+  ws.wb_safe = f;  f += LBh;
+  ws.partials = f; f += (size_t)num_layers * batch * dims->grid_h * 2;
+  ws.carrier_tok = reinterpret_cast<int32_t*>(f);
+
+  cudaGetLastError();  // clear any stale error so the check below is ours
+  if (metric_dtype == MN_F16)
+    launch_score<MN_F16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, bd, tau1, ws, num_layers, status, st);
+  else if (metric_dtype == MN_BF16)
+    launch_score<MN_BF16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, bd, tau1, ws, num_layers, status, st);
+  else
+    launch_score<MN_F32>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, bd, tau1, ws, num_layers, status, st);
+
+  cudaFuncSetAttribute(route_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_sel);
+  route_select_kernel<<<dim3(batch, num_layers), 512, smem_sel, st>>>(dev_table, batch, half, kc, kin,
+                                                                       bd.bands, kb, tau2, ws, status);
+
+  cudaFuncSetAttribute(route_mass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_mass);
+  route_mass_kernel<<<batch, 1024, smem_mass, st>>>(dev_table, batch, T, half, kc, kin, num_layers, k, ws,
+                                                    size_out, center_out, topk_size, topk_idx);
+
+  if (x_dtype == MN_F16)
+    launch_transport<__half>(x, dev_table, batch, T, channels, half, kc, kin, num_layers, k, ws, topk_x, ct, st);
+  else if (x_dtype == MN_BF16)
+    launch_transport<__nv_bfloat16>(x, dev_table, batch, T, channels, half, kc, kin, num_layers, k, ws, topk_x, ct, st);
+  else
+    launch_transport<float>(x, dev_table, batch, T, channels, half, kc, kin, num_layers, k, ws, topk_x, ct, st);
+  return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
+}

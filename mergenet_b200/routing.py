@@ -1,0 +1,327 @@
+"""DTEM spatial routing on the B200 kernels: drop-ins for the reference's
+routing functions plus the fused six-layer route-and-gather.
+
+Function names, argument order and meaning follow opentome/timm/dtem.py and
+opentome/utils/thetopk.py; every function takes and returns torch tensors on a
+CUDA device and launches on the current stream.  There is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import operator
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib as L
+
+EPS32 = torch.finfo(torch.float32).eps
+
+
+# --------------------------------------------------------------------------
+# Geometry (dtem.py:50-143)
+# --------------------------------------------------------------------------
+def _check_grid(grid_size, radius):
+    if not isinstance(grid_size, (tuple, list, torch.Size)) or len(grid_size) != 2:
+        raise ValueError(f"grid_size must be a (height, width) pair, got {grid_size!r}")
+    if any(isinstance(v, bool) for v in grid_size):
+        raise ValueError(f"grid_size values must be integers, got {grid_size!r}")
+    try:
+        h, w = operator.index(grid_size[0]), operator.index(grid_size[1])
+    except TypeError as exc:
+        raise ValueError(f"grid_size values must be integers, got {grid_size!r}") from exc
+    if h <= 0 or w <= 0:
+        raise ValueError(f"grid_size values must be positive, got {(h, w)!r}")
+    if isinstance(radius, bool):
+        raise ValueError("radius must be a positive finite number, not bool")
+    radius = float(radius)
+    if not math.isfinite(radius) or radius <= 0:
+        raise ValueError(f"radius must be a positive finite number, got {radius!r}")
+    return h, w, radius
+
+
+def build_patch_spatial_neighbors(grid_size, radius, metric="euclidean", device=None):
+    """Padded [P, K] neighbour table (indices int64, valid bool), ascending
+    patch order, built by the library's host geometry (dtem.py:130-143)."""
+    if metric != "euclidean":
+        raise ValueError(f"Unsupported DTEM spatial metric {metric!r}; expected one of ('euclidean',)")
+    h, w, radius = _check_grid(grid_size, radius)
+    lib = L.lib()
+    k = ctypes.c_int()
+    L.check(lib.mn_neighbor_table_width(h, w, radius, ctypes.byref(k)), "mn_neighbor_table_width")
+    idx = np.zeros((h * w, k.value), np.int64)
+    val = np.zeros((h * w, k.value), np.uint8)
+    L.check(lib.mn_neighbor_table_fill(h, w, radius, k.value, idx.ctypes.data_as(ctypes.c_void_p),
+                                       val.ctypes.data_as(ctypes.c_void_p)), "mn_neighbor_table_fill")
+    return (torch.from_numpy(idx).to(device), torch.from_numpy(val.astype(bool)).to(device))
+
+
+def build_patch_spatial_adjacency(grid_size, radius, metric="euclidean", device=None):
+    """Dense [P, P] bool adjacency (dtem.py:50-92), from the neighbour table."""
+    idx, val = build_patch_spatial_neighbors(grid_size, radius, metric, device="cpu")
+    p = idx.shape[0]
+    adj = torch.zeros(p, p, dtype=torch.bool)
+    rows = torch.arange(p)[:, None].expand_as(idx)
+    adj[rows[val], idx[val]] = True
+    return adj.to(device)
+
+
+# --------------------------------------------------------------------------
+# Function-level drop-ins
+# --------------------------------------------------------------------------
+def _contig(*ts):
+    for t in ts:
+        if t is not None and not t.is_contiguous():
+            raise ValueError("mergenet_b200 kernels take contiguous tensors")
+
+
+def _as_u8(t):
+    return t.view(torch.uint8) if t.dtype == torch.bool else t
+
+
+def sparse_spatial_score(a, b, neighbor_patch_indices, neighbor_patch_valid, donor_patch_indices,
+                         receiver_patch_indices):
+    """(scores [B,Na,K], receiver_indices int64 [B,Na,K], receiver_valid bool
+    [B,Na,K]) exactly as dtem.py:813-848; receivers must be sorted per row."""
+    dev = L.require_cuda(a, b, neighbor_patch_indices, neighbor_patch_valid, donor_patch_indices,
+                         receiver_patch_indices)
+    if a.ndim != 3 or b.ndim != 3 or a.shape[0] != b.shape[0] or a.shape[-1] != b.shape[-1]:
+        raise ValueError("a and b must have shape [B, N, C] with matching batch/channels")
+    if a.dtype != b.dtype:
+        raise ValueError("a and b must share a dtype")
+    nbr = neighbor_patch_indices.long().contiguous()
+    nval = neighbor_patch_valid.bool().contiguous()
+    dpat = donor_patch_indices.long().contiguous()
+    rpat = receiver_patch_indices.long().contiguous()
+    a, b = a.contiguous(), b.contiguous()
+    bsz, na, c = a.shape
+    nb = b.shape[1]
+    p, k = nbr.shape
+    scores = torch.empty(bsz, na, k, device=dev, dtype=a.dtype)
+    ridx = torch.empty(bsz, na, k, device=dev, dtype=torch.long)
+    rval = torch.empty(bsz, na, k, device=dev, dtype=torch.bool)
+    L.check(L.lib().mn_sparse_spatial_score(bsz, na, nb, p, k, c, L.dtype_code(a.dtype), L.ptr(a), L.ptr(b),
+                                            L.ptr(nbr), L.ptr(_as_u8(nval)), L.ptr(dpat), L.ptr(rpat),
+                                            L.ptr(scores), L.ptr(ridx), L.ptr(_as_u8(rval)), L.stream_of(a)),
+            "sparse_spatial_score")
+    return scores, ridx, rval
+
+
+def sparse_neighbor_dot(a, b, receiver_indices, receiver_valid):
+    """Indexed donor/receiver dot products (dtem.py:680-687)."""
+    dev = L.require_cuda(a, b, receiver_indices, receiver_valid)
+    if a.dtype != b.dtype:
+        raise ValueError("a and b must share a dtype")
+    a, b = a.contiguous(), b.contiguous()
+    ridx = receiver_indices.long().contiguous()
+    rval = receiver_valid.bool().contiguous()
+    bsz, na, c = a.shape
+    k = ridx.shape[-1]
+    out = torch.empty(bsz, na, k, device=dev, dtype=a.dtype)
+    L.check(L.lib().mn_sparse_neighbor_dot(bsz, na, b.shape[1], k, c, L.dtype_code(a.dtype), L.ptr(a), L.ptr(b),
+                                           L.ptr(ridx), L.ptr(_as_u8(rval)), L.ptr(out), L.stream_of(a)),
+            "sparse_neighbor_dot")
+    return out
+
+
+def sparse_weighted_transport(assignment, values, receiver_indices, receiver_valid, num_receivers):
+    """out[b, s] = sum of assignment * values over edges into receiver s
+    (dtem.py:1035-1067), accumulated in edge order without atomics."""
+    dev = L.require_cuda(assignment, values, receiver_indices, receiver_valid)
+    num_receivers = int(num_receivers)
+    if assignment.dtype != values.dtype:
+        values = values.to(assignment.dtype)
+    assignment, values = assignment.contiguous(), values.contiguous()
+    ridx = receiver_indices.long().contiguous()
+    rval = receiver_valid.bool().contiguous()
+    bsz, na, k = assignment.shape
+    c = values.shape[-1]
+    out = torch.empty(bsz, num_receivers, c, device=dev, dtype=values.dtype)
+    L.check(L.lib().mn_sparse_weighted_transport(bsz, na, num_receivers, k, c, L.dtype_code(values.dtype),
+                                                 L.ptr(assignment), L.ptr(values), L.ptr(ridx),
+                                                 L.ptr(_as_u8(rval)), L.ptr(out), None, L.stream_of(values)),
+            "sparse_weighted_transport")
+    return out
+
+
+def sparse_weighted_transport_pair(assignment, weighted_features, donor_mass, receiver_indices, receiver_valid,
+                                   num_receivers):
+    """Features and mass with one shared assignment (dtem.py:1006-1032)."""
+    features = sparse_weighted_transport(assignment, weighted_features, receiver_indices, receiver_valid,
+                                         num_receivers)
+    mass = sparse_weighted_transport(assignment, donor_mass.unsqueeze(-1), receiver_indices, receiver_valid,
+                                     num_receivers).squeeze(-1)
+    return features, mass
+
+
+def sparse_transport_adjoint(assignment, values, receiver_indices, receiver_valid, grad_output):
+    """(grad_assignment, grad_values) of the transport (dtem.py:962-973)."""
+    dev = L.require_cuda(assignment, values, receiver_indices, receiver_valid, grad_output)
+    assignment, values, grad_output = assignment.contiguous(), values.contiguous(), grad_output.contiguous()
+    ridx = receiver_indices.long().contiguous()
+    rval = receiver_valid.bool().contiguous()
+    bsz, na, k = assignment.shape
+    c = values.shape[-1]
+    gw = torch.empty_like(assignment)
+    gv = torch.empty_like(values)
+    L.check(L.lib().mn_sparse_transport_adjoint(bsz, na, grad_output.shape[1], k, c, L.dtype_code(values.dtype),
+                                                L.ptr(assignment), L.ptr(values), L.ptr(ridx), L.ptr(_as_u8(rval)),
+                                                L.ptr(grad_output), L.ptr(gw), L.ptr(gv), L.stream_of(values)),
+            "sparse_transport_adjoint")
+    del dev
+    return gw, gv
+
+
+def _status(dev):
+    return torch.zeros(1, dtype=torch.int32, device=dev)
+
+
+def _raise_status(status, what):
+    s = int(status.item())
+    if s & L.MN_STATUS_INFEASIBLE_BUDGET:
+        raise RuntimeError(f"{what}: DTEM spatial radius leaves fewer eligible donor rows than the required "
+                           "merge budget")
+    if s & L.MN_STATUS_TOO_MANY_EDGES:
+        raise ValueError(f"{what}: receiver index out of range")
+
+
+def ThreTopK(x, k, temperature=30.0):  # noqa: N802 - reference name
+    """Threshold soft top-k (opentome/utils/thetopk.py:4-43): one global
+    max - min range over the whole input, per-row threshold."""
+    dev = L.require_cuda(x)
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    x32 = x.float().contiguous()
+    rows, n = x32.shape
+    y = torch.empty_like(x32)
+    wsb = L.lib().mn_thre_topk_workspace_bytes(rows, n)
+    ws = torch.empty(max(int(wsb), 16), dtype=torch.uint8, device=dev)
+    L.check(L.lib().mn_thre_topk(rows, n, L.ptr(x32), int(k), float(temperature), L.ptr(y), L.ptr(ws), wsb, None,
+                                 L.stream_of(x32)), "ThreTopK")
+    return y if x.dtype == torch.float32 else y.to(x.dtype)
+
+
+def dtem_select(k, scores, allowed, tau1=1.0, tau2=30.0, check=True):
+    """Soft-k-max block of DTEMBlock._select with the sparse mask
+    (dtem.py:1536-1580): scores/allowed [B,Na,K] -> assignment [B,Na,K]."""
+    dev = L.require_cuda(scores, allowed)
+    s = scores.float().contiguous()
+    al = allowed.bool().contiguous()
+    bsz, na, kk = s.shape
+    out = torch.empty_like(s)
+    wsb = L.lib().mn_dtem_select_workspace_bytes(bsz, na)
+    ws = torch.empty(int(wsb), dtype=torch.uint8, device=dev)
+    status = _status(dev)
+    L.check(L.lib().mn_dtem_select(bsz, na, kk, L.ptr(s), L.ptr(_as_u8(al)), int(k), float(tau1), float(tau2),
+                                   L.ptr(out), L.ptr(ws), wsb, L.ptr(status), L.stream_of(s)), "dtem_select")
+    if check:
+        _raise_status(status, "dtem_select")
+    return out.to(scores.dtype)
+
+
+# --------------------------------------------------------------------------
+# Fused route + gather (canonical eval grouping)
+# --------------------------------------------------------------------------
+@dataclass
+class RouteResult:
+    topk_x: torch.Tensor      # [B, k+1, C]  CLS + carriers (centre-of-mass order)
+    topk_size: torch.Tensor   # [B, k+1]
+    topk_idx: torch.Tensor    # [B, k] int64 patch indices
+    size: torch.Tensor        # [B, T]  mass after the last layer
+    center: torch.Tensor      # [B, T]  token_center after the last layer
+    status: torch.Tensor      # [1] int32 device status word
+
+
+class RoutePlan:
+    """Geometry tables of one (grid, radius, layer budgets), resident on one
+    device.  Mirrors the state LocalEncoder keeps in its non-persistent
+    buffers and ``_tome_info`` (model.py:336-407)."""
+
+    def __init__(self, grid_size, radius=3.0, r_list=None, device=None, tau1=1.0, tau2=30.0):
+        h, w, radius = _check_grid(grid_size, radius)
+        lib = L.lib()
+        dims = L.RouteDims()
+        rc = lib.mn_route_dims_query(h, w, radius, ctypes.byref(dims))
+        L.check(rc, "mn_route_dims_query (the fused path needs an even patch count)")
+        table = np.zeros(int(dims.table_ints), np.int32)
+        L.check(lib.mn_route_tables_fill(h, w, radius, ctypes.byref(dims), table.ctypes.data_as(ctypes.c_void_p)),
+                "mn_route_tables_fill")
+        self.grid_size = (h, w)
+        self.radius = radius
+        self.dims = dims
+        self.num_patches = h * w
+        if r_list is None:
+            total = self.num_patches // 2
+            r_list = [total // 6] * 6
+            r_list[-1] += total - sum(r_list)
+        self.r_list = [int(r) for r in r_list]
+        for i, r in enumerate(self.r_list):
+            r_eff = min(r, self.num_patches // 2)
+            if r_eff > dims.valid_rows[i % 2]:
+                raise RuntimeError(
+                    "DTEM spatial radius leaves fewer eligible donor rows than the required merge budget "
+                    f"k={r_eff}; radius={radius}, grid={self.grid_size}")
+        self.k = self.num_patches - sum(self.r_list)
+        if self.k <= 0 or self.k > self.num_patches:
+            self.k = self.num_patches
+        self.tau1, self.tau2 = float(tau1), float(tau2)
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.table = torch.from_numpy(table).to(self.device)
+        self._r_arr = (ctypes.c_int * len(self.r_list))(*self.r_list)
+
+    def workspace_bytes(self, batch):
+        return int(L.lib().mn_route_workspace_bytes(ctypes.byref(self.dims), batch, len(self.r_list)))
+
+    def __call__(self, x, metrics, out=None, workspace=None, status=None):
+        """x [B, T, C] (fp32/fp16/bf16), metrics [L, B, T, Cm] -> RouteResult."""
+        L.require_cuda(x, metrics)
+        if x.device != self.device:
+            raise ValueError(f"plan lives on {self.device}, inputs on {x.device}")
+        _contig(x, metrics)
+        bsz, t, c = x.shape
+        nl, mb, mt, cm = metrics.shape
+        if t != self.num_patches + 1 or mt != t or mb != bsz or nl != len(self.r_list):
+            raise ValueError(f"expected x [B,{self.num_patches + 1},C] and metrics [{len(self.r_list)},B,T,Cm], "
+                             f"got {tuple(x.shape)} and {tuple(metrics.shape)}")
+        k = self.k
+        dev = self.device
+        if out is None:
+            out = (torch.empty(bsz, k + 1, c, device=dev, dtype=x.dtype),
+                   torch.empty(bsz, k + 1, device=dev, dtype=torch.float32),
+                   torch.empty(bsz, k, device=dev, dtype=torch.long),
+                   torch.empty(bsz, t, device=dev, dtype=torch.float32),
+                   torch.empty(bsz, t, device=dev, dtype=torch.float32))
+        topk_x, topk_size, topk_idx, size, center = out
+        wsb = self.workspace_bytes(bsz)
+        if workspace is None:
+            workspace = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        if status is None:
+            status = _status(dev)
+        rc = L.lib().mn_route_and_gather(ctypes.byref(self.dims), L.ptr(self.table), bsz, c, cm, nl, self._r_arr, k,
+                                         self.tau1, self.tau2, L.ptr(x), L.dtype_code(x.dtype), L.ptr(metrics),
+                                         L.dtype_code(metrics.dtype), L.ptr(workspace), wsb, L.ptr(topk_x),
+                                         L.ptr(topk_size), L.ptr(topk_idx), L.ptr(size), L.ptr(center),
+                                         L.ptr(status), L.stream_of(x))
+        L.check(rc, "mn_route_and_gather")
+        return RouteResult(topk_x, topk_size, topk_idx, size, center, status)
+
+
+def route_and_gather(x_embed, metrics, grid_size, radius=3.0, r_list=None):
+    """One-shot convenience: build a plan and run it."""
+    plan = RoutePlan(grid_size, radius, r_list, device=x_embed.device)
+    return plan(x_embed, metrics)
+
+
+def carrier_scatter(topk_x, topk_idx, num_patches):
+    """Transpose of the carrier gather: [B, k+1, C] -> [B, P, C], carrier i at
+    patch topk_idx[b, i], zeros elsewhere."""
+    dev = L.require_cuda(topk_x, topk_idx)
+    topk_x = topk_x.contiguous()
+    idx = topk_idx.long().contiguous()
+    bsz, k1, c = topk_x.shape
+    out = torch.empty(bsz, num_patches, c, device=dev, dtype=topk_x.dtype)
+    L.check(L.lib().mn_carrier_scatter(bsz, k1 - 1, num_patches, c, L.dtype_code(topk_x.dtype), L.ptr(topk_x),
+                                       L.ptr(idx), L.ptr(out), L.stream_of(topk_x)), "carrier_scatter")
+    return out

@@ -1,0 +1,247 @@
+#!/usr/bin/env python3
+"""Generate golden fixtures by running the MergeNet reference itself.
+
+Run in a container that has the reference checkout (read-only) at
+$MERGENET_REFERENCE (default /root/reference):
+
+    python tests/golden/make_golden.py
+
+The reference's routing modules import timm at module level; timm is not
+installed, so ``timm_shim/`` (inert placeholders written for this repository)
+satisfies those imports.  Everything computed here runs the reference's own
+code: ``DTEMBlock._merge_train`` / ``_select`` (opentome/timm/dtem.py),
+``sparse_spatial_score`` / ``sparse_weighted_transport`` and ``ThreTopK``
+(opentome/utils/thetopk.py).  The carrier block of
+``CLSHybridToMeModel.forward`` (opentome/models/mergenet/model.py:1157-1183)
+needs the full timm model, so its five tensor ops (topk, gather, argsort,
+gather, gather) are executed here in the same order on the reference's
+outputs.  Inputs come from ``inputs.py`` and are regenerated from their seed
+by the tests; only outputs are stored.
+"""
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("MERGENET_REFERENCE", "/root/reference"))
+sys.path.insert(0, str(HERE))
+sys.path.insert(0, str(HERE / "timm_shim"))
+sys.path.insert(0, str(REF))
+
+import torch  # noqa: E402
+
+from inputs import canonical_r_list, routing_inputs  # noqa: E402
+from opentome.timm.dtem import (  # noqa: E402
+    DTEMBlock,
+    adjacency_to_padded_neighbors,
+    build_patch_spatial_adjacency,
+    sparse_spatial_score,
+    sparse_weighted_transport,
+)
+from opentome.utils.thetopk import ThreTopK  # noqa: E402
+from opentome.timm.bias_local_attn import (  # noqa: E402
+    naive_biased_local_attention,
+    naive_unbiased_local_attention,
+)
+
+torch.set_num_threads(max(1, os.cpu_count() or 1))
+
+
+def make_block(grid, radius, backend):
+    """Bare DTEMBlock with a hand-filled _tome_info, as the reference's own
+    tests build it (tests/test_dtem_spatial_sparse.py:27-47, :281-304)."""
+    adjacency = build_patch_spatial_adjacency(grid, radius)
+    nbr, valid = adjacency_to_padded_neighbors(adjacency)
+    block = DTEMBlock.__new__(DTEMBlock)
+    torch.nn.Module.__init__(block)
+    block._tome_info = {
+        "window_size": 0,
+        "dtem_spatial_radius": radius,
+        "dtem_spatial_metric": "euclidean",
+        "dtem_spatial_backend": backend,
+        "patch_grid_size": grid,
+        "num_prefix_tokens": 1,
+        "spatial_adjacency": adjacency,
+        "spatial_neighbor_indices": nbr,
+        "spatial_neighbor_valid": valid,
+        "tau1": 1.0,
+        "tau2": 30.0,
+        "use_softkmax": True,
+        "collect_merge_stats": False,
+        "class_token": True,
+        "distill_token": False,
+        "source_trace_mode": "center",
+        "trace_source": False,
+        "source_tracking_mode": "none",
+        "local_depth": 6,
+        "eval_grouping": "alternating_per_layer_fast",
+        "eval_grouping_seed": 0,
+        "merge_layer_index": 0,
+        "t": 1,
+        "token_center": None,
+    }
+    block.eval()
+    return block
+
+
+def run_routing(x, metrics, r_list, grid, radius, backend="sparse", capture=False):
+    """Reference merge loop (model.py:574-590) + carrier block (:1157-1183)."""
+    block = make_block(grid, radius, backend)
+    layers = []
+    if capture:
+        original = DTEMBlock._select
+
+        def recording_select(k, a, b, a_orig_idx=None, b_orig_idx=None):
+            assign, out = original(block, k, a, b, a_orig_idx, b_orig_idx)
+            layers.append(dict(
+                assign=assign.detach().numpy().copy(),
+                receiver_indices=block._tome_info["assign_b_indices"].numpy().copy(),
+                receiver_valid=block._tome_info["assign_valid_mask"].numpy().copy()))
+            return assign, out
+
+        block._select = recording_select
+    bsz, t, _ = x.shape
+    xt = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32))
+    size = torch.ones(bsz, t, 1)
+    n = t
+    with torch.no_grad():
+        for i, r in enumerate(r_list):
+            block._tome_info["merge_layer_index"] = i
+            # fp16 autocast computes the metric norm in fp32 and promotes the
+            # division to fp32; on the CPU reproduce that by upcasting first.
+            m = torch.from_numpy(np.ascontiguousarray(metrics[i]).astype(np.float32))
+            xt, size, n, _, _ = block._merge_train(xt, size, r, n, {"metric": m})
+        center = block._tome_info["token_center"].float()
+        k = t - sum(r_list) - 1
+        strength = size[..., 0][:, 1:]
+        _, topk_indices = torch.topk(strength, k, dim=1, largest=True, sorted=False)
+        topk_com = torch.gather(center[:, 1:], 1, topk_indices)
+        sorted_order = torch.argsort(topk_com, dim=1)
+        sorted_topk = torch.gather(topk_indices, 1, sorted_order)
+        full = sorted_topk + 1
+        topk_x = torch.cat([xt[:, :1], torch.gather(xt, 1, full.unsqueeze(-1).expand(-1, -1, xt.shape[-1]))], 1)
+        topk_size = torch.cat([size[:, :1, 0], torch.gather(size[..., 0], 1, full)], 1)
+    s = np.sort(size[:, 1:, 0].numpy().astype(np.float64), axis=1)[:, ::-1]
+    margin = (s[:, k - 1] - s[:, k]) / np.abs(s[:, k - 1])
+    out = dict(topk_idx=sorted_topk.numpy().astype(np.int32), size=size[..., 0].numpy(),
+               center=center.numpy(), topk_size=topk_size.numpy(), margin=margin)
+    return out, topk_x.numpy(), layers
+
+
+def route_case(name, seed, batch, grid, radius, channels, metric_dim, r_list,
+               keep_features=True, capture=False, dense_check=False):
+    x, metrics = routing_inputs(seed, batch, grid, channels, metric_dim, layers=len(r_list))
+    out, topk_x, layers = run_routing(x, metrics, r_list, grid, radius, capture=capture)
+    payload = dict(seed=seed, batch=batch, grid=np.array(grid), radius=radius,
+                   channels=channels, metric_dim=metric_dim, r_list=np.array(r_list), **out)
+    if keep_features:
+        payload["topk_x"] = topk_x
+    for i, layer in enumerate(layers):
+        payload[f"assign_{i}"] = layer["assign"]
+        payload[f"receiver_indices_{i}"] = layer["receiver_indices"].astype(np.int32)
+        payload[f"receiver_valid_{i}"] = layer["receiver_valid"]
+    if dense_check:
+        dense, _, _ = run_routing(x, metrics, r_list, grid, radius, backend="dense")
+        payload["dense_topk_idx"] = dense["topk_idx"]
+        payload["dense_size"] = dense["size"]
+    np.savez_compressed(HERE / f"{name}.npz", **payload)
+    print(name, "min margin", float(out["margin"].min()))
+
+
+def thre_topk_case():
+    rng = np.random.default_rng(7)
+    cases = {}
+    x = (rng.random((4, 37), dtype=np.float32) * 20 + 1).astype(np.float32)
+    cases["x0"], cases["k0"] = x, 9
+    cases["y0"] = ThreTopK(torch.from_numpy(x), 9, 30.0).numpy()
+    x1 = x.copy()
+    x1[1, ::3] = 0.0  # invalid rows contribute zero energy to the global range
+    cases["x1"], cases["k1"] = x1, 5
+    cases["y1"] = ThreTopK(torch.from_numpy(x1), 5, 30.0).numpy()
+    x2 = (rng.random(50, dtype=np.float32) * 3).astype(np.float32)
+    cases["x2"], cases["k2"] = x2, 20
+    cases["y2"] = ThreTopK(torch.from_numpy(x2), 20, 30.0).numpy()
+    x3 = (rng.standard_normal((2, 392), dtype=np.float32) * 2 + 12).astype(np.float32)
+    cases["x3"], cases["k3"] = x3, 65
+    cases["y3"] = ThreTopK(torch.from_numpy(x3), 65, 30.0).numpy()
+    np.savez_compressed(HERE / "thre_topk.npz", **cases)
+
+
+def select_case():
+    """The reference test's (3,5) R=2 geometry with per-sample partitions
+    (tests/test_dtem_spatial_sparse.py:179-227)."""
+    grid, radius = (3, 5), 2
+    a_idx = torch.tensor([[1, 3, 5, 7, 9, 11, 13], [2, 4, 6, 8, 10, 12, 14]])
+    b_idx = torch.tensor([[2, 4, 6, 8, 10, 12, 14, 15], [1, 3, 5, 7, 9, 11, 13, 15]])
+    rng = np.random.default_rng(20260820)
+    a = rng.standard_normal((2, 7, 9), dtype=np.float32)
+    b = rng.standard_normal((2, 8, 9), dtype=np.float32)
+    block = make_block(grid, radius, "sparse")
+    with torch.no_grad():
+        scores, ridx, rvalid = sparse_spatial_score(
+            torch.from_numpy(a), torch.from_numpy(b),
+            block._tome_info["spatial_neighbor_indices"],
+            block._tome_info["spatial_neighbor_valid"], a_idx - 1, b_idx - 1)
+        assign, _ = block._select(3, torch.from_numpy(a), torch.from_numpy(b), a_idx, b_idx)
+        dense = make_block(grid, radius, "dense")
+        dense_assign, _ = dense._select(3, torch.from_numpy(a), torch.from_numpy(b), a_idx, b_idx)
+    np.savez_compressed(
+        HERE / "select_g3x5.npz", a=a, b=b, a_idx=a_idx.numpy(), b_idx=b_idx.numpy(),
+        scores=scores.numpy(), receiver_indices=ridx.numpy().astype(np.int32),
+        receiver_valid=rvalid.numpy(), assign=assign.numpy(), dense_assign=dense_assign.numpy())
+
+
+def transport_case():
+    """Random edge lists as in tests/test_dtem_spatial_sparse.py:127-159."""
+    rng = np.random.default_rng(20260820)
+    batch, donors, receivers, neighbors, channels = 2, 7, 8, 6, 11
+    assignment = rng.random((batch, donors, neighbors), dtype=np.float32)
+    values = rng.standard_normal((batch, donors, channels), dtype=np.float32)
+    ridx = rng.integers(0, receivers, (batch, donors, neighbors))
+    rvalid = rng.random((batch, donors, neighbors)) > 0.25
+    with torch.no_grad():
+        out = sparse_weighted_transport(torch.from_numpy(assignment), torch.from_numpy(values),
+                                        torch.from_numpy(ridx), torch.from_numpy(rvalid), receivers)
+    np.savez_compressed(HERE / "transport.npz", assignment=assignment, values=values,
+                        receiver_indices=ridx.astype(np.int32), receiver_valid=rvalid,
+                        receivers=receivers, out=out.numpy())
+
+
+def attention_case():
+    """The reference's own CPU unfold implementations of the windowed
+    attention (opentome/timm/bias_local_attn.py:46-240), BNHD layout."""
+    rng = np.random.default_rng(20260809)
+    cases = {}
+    for i, (b, n, h, d, w) in enumerate([(2, 11, 3, 16, 2), (2, 40, 4, 64, 16), (1, 37, 2, 32, 5)]):
+        q = (rng.standard_normal((b, n, h, d), dtype=np.float32) * 0.5).astype(np.float32)
+        k = (rng.standard_normal((b, n, h, d), dtype=np.float32) * 0.5).astype(np.float32)
+        v = rng.standard_normal((b, n, h, d), dtype=np.float32)
+        bias = (rng.standard_normal((b, n), dtype=np.float32) * 0.5).astype(np.float32)
+        tq, tk, tv, tb = (torch.from_numpy(t) for t in (q, k, v, bias))
+        cases[f"q{i}"], cases[f"k{i}"], cases[f"v{i}"], cases[f"bias{i}"] = q, k, v, bias
+        cases[f"window{i}"] = w
+        cases[f"unbiased{i}"] = naive_unbiased_local_attention(tq, tk, tv, w).numpy()
+        cases[f"biased{i}"] = naive_biased_local_attention(tq, tk, tv, tb, w).numpy()
+    np.savez_compressed(HERE / "attention.npz", **cases)
+
+
+def main():
+    attention_case()
+    thre_topk_case()
+    select_case()
+    transport_case()
+    route_case("route_g3x6", 101, 2, (3, 6), 2.0, 7, 5, [3, 3], capture=True)
+    route_case("route_g4x4", 102, 3, (4, 4), 1.5, 16, 8, [2, 2, 2], capture=True)
+    route_case("route_c1", 0, 2, (28, 28), 3.0, 384, 64, canonical_r_list((28, 28)),
+               capture=True, dense_check=True)
+    route_case("route_c2_b128", 1, 128, (28, 28), 3.0, 8, 64, canonical_r_list((28, 28)),
+               keep_features=False, dense_check=True)
+    route_case("route_g48", 5, 2, (48, 48), 3.0, 16, 64, canonical_r_list((48, 48)))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,143 @@
+"""Parity of the CUDA windowed attention with the reference semantics."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.attention import local_attention as oracle_attention
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import mergenet_b200  # noqa: F401
+    return torch.device("cuda", 0)
+
+
+def reference_bhnd(q, k, v, bias, window):
+    """The reference test's fp32 restatement (tests/test_biased_local_attention.py:17-29)."""
+    q32, k32, v32 = q.float(), k.float(), v.float()
+    scores = q32 @ k32.transpose(-1, -2) / math.sqrt(q.shape[-1])
+    if bias is not None:
+        scores = scores + bias.float()[:, None, None, :]
+    if window >= 0:
+        tokens = q.shape[-2]
+        pos = torch.arange(tokens, device=q.device)
+        allowed = (pos[:, None] - pos[None, :]).abs() <= window
+        scores = scores.masked_fill(~allowed.view(1, 1, tokens, tokens), float("-inf"))
+    return torch.softmax(scores, dim=-1) @ v32
+
+
+def test_attention_matches_reference_naive(dev, golden_dir):
+    """Against the reference's own unfold implementations (which take a
+    pre-scaled q, so the softmax scale is 1 here)."""
+    from mergenet_b200.attention import _launch
+    g = np.load(golden_dir / "attention.npz")
+    for i in range(3):
+        q, k, v, bias = (torch.from_numpy(g[f"{n}{i}"]).to(dev) for n in ("q", "k", "v", "bias"))
+        w = int(g[f"window{i}"])
+        u = _launch(q, k, v, None, w, False, 1.0, torch.float32)
+        b = _launch(q, k, v, bias, w, False, 1.0, torch.float32)
+        np.testing.assert_allclose(u.cpu().numpy(), g[f"unbiased{i}"], rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(b.cpu().numpy(), g[f"biased{i}"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("layout", ["BHND", "BNHD"])
+@pytest.mark.parametrize("tokens,heads,window", [(11, 3, 2), (3, 5, 1), (11, 3, -1)])
+def test_biased_parity(dev, layout, tokens, heads, window):
+    """tests/test_biased_local_attention.py:32-63 (forward, fp16)."""
+    import mergenet_b200 as mn
+    torch.manual_seed(20260809)
+    batch, dim = 2, 16
+    q = torch.randn(batch, heads, tokens, dim, device=dev, dtype=torch.float16) * 0.25
+    k = torch.randn_like(q) * 0.25
+    v = torch.randn_like(q)
+    bias = torch.randn(batch, tokens, device=dev, dtype=torch.float16) * 0.25
+    if layout == "BHND":
+        args = (q, k, v)
+    else:
+        args = tuple(t.transpose(1, 2).contiguous() for t in (q, k, v))
+    out = mn.biased_local_attention(*args, bias, local_window=window, x_dtype=torch.float16, input_layout=layout)
+    out_bhnd = out if layout == "BHND" else out.transpose(1, 2)
+    expected = reference_bhnd(q, k, v, bias, window)
+    # the reference gate allows 1.5e-2; fp32 softmax and P.V keep us well inside it
+    torch.testing.assert_close(out_bhnd.float(), expected, atol=2e-3, rtol=2e-3)
+
+
+def test_unbiased_parity_layouts(dev):
+    import mergenet_b200 as mn
+    torch.manual_seed(3)
+    q = torch.randn(2, 40, 4, 64, device=dev, dtype=torch.float16) * 0.3
+    k = torch.randn_like(q) * 0.3
+    v = torch.randn_like(q)
+    out = mn.unbiased_local_attention(q, k, v, 16)
+    exp = reference_bhnd(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), None, 16).transpose(1, 2)
+    torch.testing.assert_close(out.float(), exp, atol=2e-3, rtol=2e-3)
+    out2 = mn.unbiased_local_attention(q.transpose(1, 2).contiguous(), k.transpose(1, 2).contiguous(),
+                                       v.transpose(1, 2).contiguous(), 16)
+    torch.testing.assert_close(out2.transpose(1, 2).float(), exp, atol=2e-3, rtol=2e-3)
+
+
+def test_locality(dev):
+    """tests/test_biased_local_attention.py:87-113."""
+    import mergenet_b200 as mn
+    batch, heads, tokens, dim = 1, 3, 11, 16
+    window, target = 2, 5
+    q = torch.randn(batch, heads, tokens, dim, device=dev, dtype=torch.float16)
+    k = torch.randn_like(q)
+    v = torch.randn_like(q)
+    bias = torch.randn(batch, tokens, device=dev, dtype=torch.float16)
+
+    def run(value):
+        return mn.biased_local_attention(q, k, value, bias, window, input_layout="BHND")
+
+    base = run(v)
+    inside = v.clone()
+    inside[:, :, target + 1] += 1
+    outside = v.clone()
+    outside[:, :, target + window + 2] += 1
+    assert (run(inside)[:, :, target] - base[:, :, target]).abs().max().item() > 1e-4
+    assert (run(outside)[:, :, target] - base[:, :, target]).abs().max().item() <= 1e-6
+
+
+def test_ambiguous_layout_rejected(dev):
+    import mergenet_b200 as mn
+    amb = torch.randn(1, 4, 4, 16, device=dev, dtype=torch.float16)
+    with pytest.raises(ValueError):
+        mn.biased_local_attention(amb, amb, amb, torch.zeros(1, 4, device=dev, dtype=torch.float16), 1)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_local_block_attention_cls_global(dev, dtype):
+    """LocalAttention core at the canonical shape: packed qkv [B, 785, 3*384],
+    window 16, CLS row global (bias_local_attn.py:687-721)."""
+    import mergenet_b200 as mn
+    torch.manual_seed(7)
+    b, n, h, d = 4, 785, 6, 64
+    qkv = (torch.randn(b, n, 3 * h * d, device=dev) * 0.5).to(dtype)
+    out = mn.local_attention_packed(qkv, h, 16, cls_global=True)
+    view = qkv.view(b, n, 3, h, d)
+    q, k, v = (view[:, :, i].transpose(1, 2) for i in range(3))
+    exp = reference_bhnd(q, k, v, None, 16)
+    cls = torch.softmax(q[:, :, :1].float() @ k.float().transpose(-1, -2) / 8.0, -1) @ v.float()
+    exp[:, :, :1] = cls
+    exp = exp.transpose(1, 2).reshape(b, n, h * d)
+    tol = 1e-2 if dtype == torch.bfloat16 else 3e-3
+    torch.testing.assert_close(out.float(), exp, atol=tol, rtol=tol)
+
+
+def test_config3_biased_block_against_oracle(dev):
+    """Config 3 shape family (785 tokens, 6x64, window 16, per-key bias) at a
+    batch the float64 oracle finishes quickly."""
+    import mergenet_b200 as mn
+    from inputs import attention_inputs
+    q, k, v, bias = attention_inputs(0, 2, 785, 6, 64)
+    tq, tk, tv, tb = (torch.from_numpy(t).to(dev) for t in (q, k, v, bias))
+    out = mn.biased_local_attention(tq, tk, tv, tb, 16, input_layout="BNHD")
+    exp = oracle_attention(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), 16,
+                           bias=bias.astype(np.float32))
+    err = np.abs(out.float().cpu().numpy() - exp).max() / np.abs(exp).max()
+    assert err <= 1e-2

@@ -1,0 +1,125 @@
+"""Host-side checks of libmergenet_b200.so that need no GPU: it loads, it
+exports every entry point the header declares, and its host geometry matches
+the oracle (and through it the reference's own tests)."""
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import routing as O
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def test_library_exports_every_header_symbol():
+    from mergenet_b200 import _lib
+    lib = _lib.lib()
+    header = (ROOT / "include" / "mergenet_b200.h").read_text()
+    declared = set(re.findall(r"^(?:int|size_t)\s+(mn_\w+)\s*\(", header, flags=re.M))
+    assert declared, "no declarations parsed"
+    assert declared == set(_lib.EXPORTED), declared ^ set(_lib.EXPORTED)
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert lib.mn_version() == 1
+
+
+@pytest.mark.parametrize("grid,radius", [((28, 28), 3.0), ((48, 48), 3.0), ((3, 5), 1.5), ((2, 3), 1.0),
+                                         ((3, 6), 2.0), ((4, 4), 1.5), ((1, 4), 0.5), ((3, 5), 4.47213595499958)])
+def test_neighbor_table_matches_oracle(grid, radius):
+    import mergenet_b200 as mn
+    idx, val = mn.build_patch_spatial_neighbors(grid, radius)
+    geom = O.Geometry(grid, radius)
+    np.testing.assert_array_equal(idx.numpy(), geom.nbr_idx)
+    np.testing.assert_array_equal(val.numpy(), geom.nbr_valid)
+    adj = mn.build_patch_spatial_adjacency(grid, radius)
+    np.testing.assert_array_equal(adj.numpy(), geom.adjacency)
+
+
+def test_reference_geometry_facts():
+    """tests/test_dtem_spatial_sparse.py:50-65 and test_dtem_spatial_mask.py:32-63."""
+    import mergenet_b200 as mn
+    idx, val = mn.build_patch_spatial_neighbors((3, 5), 1.5)
+    assert idx.shape == val.shape == (15, 9)
+    assert int(val[0].sum()) == 4
+    adj = mn.build_patch_spatial_adjacency((3, 5), 1.5)
+    assert not bool(adj[4, 5]) and bool(adj[4, 9])
+    adj = mn.build_patch_spatial_adjacency((2, 3), 1)
+    assert not bool(adj[2, 3]) and bool(adj[0, 3]) and bool(torch.diagonal(adj).all())
+    assert bool(mn.build_patch_spatial_adjacency((3, 5), float(np.hypot(2, 4))).all())
+    idx, val = mn.build_patch_spatial_neighbors((28, 28), 3.0)
+    assert idx.shape == (784, 29) and int(val.sum()) == 20756
+    counts = val.sum(1)
+    assert int(counts.min()) == 11 and int(counts.max()) == 29
+    _, val = mn.build_patch_spatial_neighbors((48, 48), 3.0)
+    assert int(val.sum()) == 63396
+
+
+@pytest.mark.parametrize("grid", [0, -1, (0, 3), (2, 0), (2.0, 3), (2,), (2, 3, 4)])
+def test_invalid_grid_fails_closed(grid):
+    import mergenet_b200 as mn
+    with pytest.raises(ValueError):
+        mn.build_patch_spatial_neighbors(grid, 1.0)
+
+
+@pytest.mark.parametrize("radius", [-1, float("nan"), 0.0, True])
+def test_invalid_radius_fails_closed(radius):
+    import mergenet_b200 as mn
+    with pytest.raises(ValueError):
+        mn.build_patch_spatial_neighbors((2, 3), radius)
+
+
+def _route_tables(grid, radius):
+    from mergenet_b200 import _lib
+    lib = _lib.lib()
+    dims = _lib.RouteDims()
+    assert lib.mn_route_dims_query(grid[0], grid[1], radius, ctypes.byref(dims)) == 0
+    table = np.zeros(dims.table_ints, np.int32)
+    assert lib.mn_route_tables_fill(grid[0], grid[1], radius, ctypes.byref(dims),
+                                    table.ctypes.data_as(ctypes.c_void_p)) == 0
+    return dims, table
+
+
+@pytest.mark.parametrize("grid,radius", [((28, 28), 3.0), ((48, 48), 3.0), ((3, 6), 2.0), ((4, 4), 1.5)])
+def test_route_tables_match_sparse_mapping(grid, radius):
+    """Compact donor slots and receiver in-lists agree with the reference's
+    sorted-receiver mapping (dtem.py:219-234) for both layer parities."""
+    dims, table = _route_tables(grid, radius)
+    geom = O.Geometry(grid, radius)
+    half, kc, kin = dims.half, dims.kc, dims.kin
+    p = grid[0] * grid[1]
+    per = half * kc * 2 + half * kin
+    for q in (0, 1):
+        dp = 0 if q else 1
+        t = table[q * per:(q + 1) * per]
+        slot_k = t[:half * kc].reshape(half, kc)
+        slot_rx = t[half * kc:2 * half * kc].reshape(half, kc)
+        rx_in = t[2 * half * kc:].reshape(half, kin)
+        donors = np.arange(dp, p, 2)[None]
+        recv = np.arange(1 - dp, p, 2)[None]
+        ridx, rvalid = O.map_sorted_receivers(geom.nbr_idx, geom.nbr_valid, donors, recv)
+        edges = []
+        for d in range(half):
+            ks = np.nonzero(rvalid[0, d])[0]
+            got = slot_k[d][slot_k[d] >= 0]
+            np.testing.assert_array_equal(got, ks)
+            np.testing.assert_array_equal(slot_rx[d][: len(ks)], ridx[0, d, ks])
+            edges += [(int(ridx[0, d, k]), d * kc + c) for c, k in enumerate(ks)]
+        for s in range(half):
+            want = [e for r, e in edges if r == s]  # donor-major order = sequential scatter order
+            got = rx_in[s][rx_in[s] >= 0].tolist()
+            assert got == want
+        assert dims.valid_rows[q] == int(rvalid[0].any(-1).sum())
+    if grid == (28, 28):
+        assert (dims.kc, dims.kin, dims.k_static) == (12, 12, 29)
+
+
+def test_cpu_tensors_are_rejected():
+    """No CPU fallback: the product path refuses host tensors loudly."""
+    import mergenet_b200 as mn
+    with pytest.raises(RuntimeError):
+        mn.ThreTopK(torch.rand(2, 5), 2)
+    with pytest.raises(RuntimeError):
+        mn.unbiased_local_attention(torch.rand(1, 5, 2, 8), torch.rand(1, 5, 2, 8), torch.rand(1, 5, 2, 8), 1)

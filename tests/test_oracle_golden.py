@@ -1,0 +1,90 @@
+"""The numpy oracle against fixtures produced by the reference itself."""
+import numpy as np
+import pytest
+
+from inputs import canonical_r_list, routing_inputs
+from oracle import routing as O
+
+ROUTE_CASES = ["route_g3x6", "route_g4x4", "route_c1", "route_g48", "route_c2_b128"]
+
+
+def load(golden_dir, name):
+    return np.load(golden_dir / f"{name}.npz")
+
+
+def run_case(g):
+    grid = tuple(int(v) for v in g["grid"])
+    r_list = [int(v) for v in g["r_list"]]
+    x, metrics = routing_inputs(int(g["seed"]), int(g["batch"]), grid, int(g["channels"]),
+                                int(g["metric_dim"]), layers=len(r_list))
+    geom = O.Geometry(grid, float(g["radius"]))
+    return O.route_and_gather(x, metrics, r_list, geom, keep_info=True), r_list
+
+
+@pytest.mark.parametrize("name", ROUTE_CASES)
+def test_oracle_route_matches_reference(golden_dir, name):
+    g = load(golden_dir, name)
+    out, r_list = run_case(g)
+    np.testing.assert_array_equal(out["topk_idx"], g["topk_idx"])
+    # the reference's own dense and sparse CPU backends differ by up to 1.4e-5
+    np.testing.assert_allclose(out["size"], g["size"], rtol=3e-5, atol=3e-5)
+    np.testing.assert_allclose(out["center"], g["center"], rtol=0, atol=2e-3)
+    np.testing.assert_allclose(out["topk_size"], g["topk_size"], rtol=3e-5, atol=3e-5)
+    if "topk_x" in g:
+        np.testing.assert_allclose(out["topk_x"], g["topk_x"], rtol=1e-4, atol=1e-4)
+    for i in range(len(r_list)):
+        if f"assign_{i}" in g:
+            np.testing.assert_allclose(out["layers"][i]["assign"], g[f"assign_{i}"], rtol=0, atol=5e-6)
+            np.testing.assert_array_equal(out["layers"][i]["receiver_indices"], g[f"receiver_indices_{i}"])
+            np.testing.assert_array_equal(out["layers"][i]["receiver_valid"], g[f"receiver_valid_{i}"])
+
+
+def test_reference_dense_and_sparse_agree(golden_dir):
+    for name in ("route_c1", "route_c2_b128"):
+        g = load(golden_dir, name)
+        np.testing.assert_array_equal(g["dense_topk_idx"], g["topk_idx"])
+
+
+def test_oracle_thre_topk(golden_dir):
+    g = load(golden_dir, "thre_topk")
+    for i in range(4):
+        y = O.thre_topk(g[f"x{i}"], int(g[f"k{i}"]))
+        np.testing.assert_allclose(y, g[f"y{i}"].reshape(y.shape), rtol=0, atol=2e-6)
+
+
+def test_oracle_select_and_score(golden_dir):
+    g = load(golden_dir, "select_g3x5")
+    geom = O.Geometry((3, 5), 2.0)
+    scores, ridx, rvalid = O.sparse_spatial_score(g["a"], g["b"], geom.nbr_idx, geom.nbr_valid,
+                                                  g["a_idx"] - 1, g["b_idx"] - 1)
+    np.testing.assert_allclose(scores, g["scores"], rtol=0, atol=1e-5)
+    np.testing.assert_array_equal(ridx, g["receiver_indices"])
+    np.testing.assert_array_equal(rvalid, g["receiver_valid"])
+    an = O.normalize_metric(g["a"]) * 0 + g["a"]  # _select receives already-normalised a/b in the merge
+    assign, _, _ = O.select(3, scores, rvalid)
+    np.testing.assert_allclose(assign, g["assign"], rtol=0, atol=2e-6)
+    del an
+
+
+def test_oracle_transport(golden_dir):
+    g = load(golden_dir, "transport")
+    out = O.sparse_weighted_transport(g["assignment"], g["values"], g["receiver_indices"], g["receiver_valid"],
+                                      int(g["receivers"]))
+    np.testing.assert_allclose(out, g["out"], rtol=1e-6, atol=1e-6)
+
+
+def test_oracle_budget_fails_closed():
+    geom = O.Geometry((1, 4), 0.5)
+    a = np.random.default_rng(0).standard_normal((1, 2, 4)).astype(np.float32)
+    scores, ridx, rvalid = O.sparse_spatial_score(a, a, geom.nbr_idx, geom.nbr_valid,
+                                                  np.array([[0, 2]]), np.array([[1, 3]]))
+    assert not rvalid.any()
+    with pytest.raises(RuntimeError):
+        O.select(1, scores, rvalid)
+
+
+def test_parse_r_schedule():
+    assert O.parse_r(6, 65, 392) == [65, 65, 65, 65, 65, 67]
+    assert canonical_r_list((28, 28)) == [65, 65, 65, 65, 65, 67]
+    assert canonical_r_list((48, 48)) == [192] * 6
+    assert O.parse_r(3, [1, 2]) == [1, 2, 0]
