@@ -75,6 +75,8 @@ typedef struct mn_route_dims {
   int kin;           /* max donors of one receiver                          */
   int radius_rows;   /* largest row offset between two neighbours           */
   int valid_rows[2]; /* donors with >= 1 legal receiver, per layer parity   */
+  int stencil_dy1;   /* even-width stencil: max |dy| of donors at |dx| = 1,  */
+  int stencil_dy3;   /* and at |dx| = 3 (-1 none); both -2: no stencil form  */
   int64_t table_ints;/* int32 entries of the routing table buffer           */
 } mn_route_dims;
 
@@ -86,7 +88,8 @@ int mn_route_dims_query(int grid_h, int grid_w, double radius, mn_route_dims* di
  *   slot_k  [half][kc]  static slot of each compact donor slot (or -1)
  *   slot_rx [half][kc]  receiver local index of that slot (or -1)
  *   rx_in   [half][kin] edge ids d*kc+c feeding each receiver, ascending
- *                       (the reference's sequential scatter order), or -1 */
+ *                       (the reference's sequential scatter order), or -1
+ *   rx_off  [half][kin] stencil offset index of that edge (or -1) */
 int mn_route_tables_fill(int grid_h, int grid_w, double radius,
                          const mn_route_dims* dims, int32_t* host_table);
 
@@ -210,6 +213,17 @@ int mn_local_attention(int batch, int tokens, int heads, int head_dim,
                        const void* bias, int bias_dtype, int window,
                        int cls_global, float scale, void* out, int out_dtype,
                        void* stream);
+
+/* Attention of nq query rows over nk key rows, optionally windowed
+ * (|i - j| <= window, window < 0 = every key): the recovery cross-attention
+ * core of MyCrossAttention.forward (opentome/models/mergenet/model.py:173-188,
+ * 393 carrier queries over the 785 pre-merge tokens).  Strides in elements;
+ * out [B, nq, H, D] contiguous. */
+int mn_attention(int batch, int nq, int nk, int heads, int head_dim, int dtype,
+                 const void* q, int64_t q_sb, int64_t q_sn, int64_t q_sh,
+                 const void* k, const void* v, int64_t kv_sb, int64_t kv_sn,
+                 int64_t kv_sh, int window, float scale, void* out,
+                 int out_dtype, void* stream);
 
 #ifdef __cplusplus
 }

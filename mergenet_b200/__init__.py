@@ -22,6 +22,7 @@ from .routing import (  # noqa: F401
 )
 from .attention import (  # noqa: F401
     biased_local_attention,
+    cross_attention,
     local_attention_packed,
     unbiased_local_attention,
 )

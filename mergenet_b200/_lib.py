@@ -34,7 +34,7 @@ class RouteDims(ctypes.Structure):
     _fields_ = [
         ("grid_h", c_int), ("grid_w", c_int), ("num_patches", c_int), ("half", c_int),
         ("k_static", c_int), ("kc", c_int), ("kin", c_int), ("radius_rows", c_int),
-        ("valid_rows", c_int * 2), ("table_ints", c_int64),
+        ("valid_rows", c_int * 2), ("stencil_dy1", c_int), ("stencil_dy3", c_int), ("table_ints", c_int64),
     ]
 
 
@@ -63,6 +63,8 @@ _SIGNATURES = {
     "mn_carrier_scatter": (c_int, [c_int, c_int, c_int, c_int, c_int, _P, _P, _P, _P]),
     "mn_local_attention": (c_int, [c_int, c_int, c_int, c_int, c_int, _P, _P, _P, c_int64, c_int64, c_int64, _P,
                                    c_int, c_int, c_int, c_float, _P, c_int, _P]),
+    "mn_attention": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, _P, c_int64, c_int64, c_int64, _P, _P,
+                             c_int64, c_int64, c_int64, c_int, c_float, _P, c_int, _P]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

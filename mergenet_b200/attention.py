@@ -119,3 +119,27 @@ def local_attention_packed(qkv, num_heads, local_window, cls_global=True, out_dt
     q, k, v = view[:, :, 0], view[:, :, 1], view[:, :, 2]
     o = _launch(q, k, v, None, local_window, cls_global, 1.0 / math.sqrt(d), out_dtype or qkv.dtype)
     return o.view(b, n, num_heads * d)
+
+
+def cross_attention(q, k, v, scale=None, out_dtype=None, window=-1):
+    """softmax(q k^T * scale) v with q [B, Nq, H, D] and k/v [B, Nk, H, D]
+    (any strides with a unit last stride): the SDPA core of the recovery
+    cross-attention (opentome/models/mergenet/model.py:173-188)."""
+    dev = L.require_cuda(q, k, v)
+    if k.shape != v.shape or q.shape[0] != k.shape[0] or q.shape[2:] != k.shape[2:]:
+        raise ValueError(f"shape mismatch: q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)}")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q/k/v must share a dtype")
+    if k.stride() != v.stride():
+        k, v = k.contiguous(), v.contiguous()
+    b, nq, h, d = q.shape
+    nk = k.shape[1]
+    qsb, qsn, qsh = _strides_bnhd(q)
+    ksb, ksn, ksh = _strides_bnhd(k)
+    out_dtype = out_dtype or q.dtype
+    scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
+    out = torch.empty(b, nq, h, d, device=dev, dtype=out_dtype)
+    L.check(L.lib().mn_attention(b, nq, nk, h, d, L.dtype_code(q.dtype), L.ptr(q), qsb, qsn, qsh, L.ptr(k), L.ptr(v),
+                                 ksb, ksn, ksh, int(window), scale, L.ptr(out), L.dtype_code(out_dtype),
+                                 L.stream_of(q)), "mn_attention")
+    return out

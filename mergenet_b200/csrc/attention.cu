@@ -149,9 +149,137 @@ __global__ void __launch_bounds__(256) cls_row_kernel(const ET* __restrict__ q, 
   }
 }
 
+// General attention with separate query / key sequences (the recovery
+// cross-attention, model.py:173-188: 393 carrier queries over 785 tokens) or
+// a window.  Keys are streamed through shared memory in chunks of 64 with an
+// online softmax; one warp owns 4 query rows.
+constexpr int kXQ = 32;     // queries per CTA
+constexpr int kXK = 64;     // keys per chunk
+template <typename ET>
+__global__ void __launch_bounds__(256) attn_chunked_kernel(
+    const ET* __restrict__ q, int64_t qb, int64_t qn, int64_t qh, const ET* __restrict__ k,
+    const ET* __restrict__ v, int64_t kb, int64_t kn, int64_t kh, int Nq, int Nk, int H, int D, int window,
+    float scale, void* __restrict__ out, int out_dtype) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int DS = D + 1;
+  float* qs = reinterpret_cast<float*>(smem_raw);  // [kXQ][D]
+  float* ks = qs + kXQ * D;                        // [kXK][DS]
+  float* vs = ks + kXK * DS;                       // [kXK][DS]
+  const int q0 = blockIdx.x * kXQ, h = blockIdx.y, b = blockIdx.z;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t qbase = (int64_t)b * qb + (int64_t)h * qh;
+  const int64_t kbase = (int64_t)b * kb + (int64_t)h * kh;
+  for (int i = threadIdx.x; i < kXQ * D; i += blockDim.x) {
+    const int r = i / D, c = i % D;
+    qs[i] = (q0 + r < Nq) ? to_f32(q[qbase + (int64_t)(q0 + r) * qn + c]) : 0.f;
+  }
+  int lo = 0, hi = Nk;
+  if (window >= 0) {
+    lo = max(0, q0 - window);
+    hi = min(Nk, q0 + kXQ + window);
+  }
+  float m[4], l[4], o[4][4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    m[u] = -INFINITY;
+    l[u] = 0.f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) o[u][t] = 0.f;
+  }
+  for (int j0 = lo; j0 < hi; j0 += kXK) {
+    const int nk = min(kXK, hi - j0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nk * D; i += blockDim.x) {
+      const int r = i / D, c = i % D;
+      const int64_t off = kbase + (int64_t)(j0 + r) * kn + c;
+      ks[r * DS + c] = to_f32(k[off]);
+      vs[r * DS + c] = to_f32(v[off]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int qr = warp * 4 + u, qi = q0 + qr;
+      if (qi >= Nq) continue;
+      const float* qv = qs + qr * D;
+      float sc[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int jj = lane + 32 * t, j = j0 + jj;
+        bool ok = jj < nk;
+        if (ok && window >= 0) ok = (j - qi <= window) && (qi - j <= window);
+        float acc = -INFINITY;
+        if (ok) {
+          const float* kr = ks + jj * DS;
+          acc = 0.f;
+          for (int c = 0; c < D; ++c) acc = fmaf(qv[c], kr[c], acc);
+          acc *= scale;
+        }
+        sc[t] = acc;
+      }
+      const float mc = warp_max(fmaxf(sc[0], sc[1]));
+      if (mc == -INFINITY) continue;
+      const float mn = fmaxf(m[u], mc);
+      const float corr = (m[u] == -INFINITY) ? 0.f : expf(m[u] - mn);
+      const float p0 = (sc[0] == -INFINITY) ? 0.f : expf(sc[0] - mn);
+      const float p1 = (sc[1] == -INFINITY) ? 0.f : expf(sc[1] - mn);
+      l[u] = l[u] * corr + warp_sum(p0 + p1);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) o[u][t] *= corr;
+      for (int jj = 0; jj < nk; ++jj) {
+        const float pj = __shfl_sync(MN_FULL_MASK, jj < 32 ? p0 : p1, jj & 31);
+        if (pj == 0.f) continue;
+        const float* vr = vs + jj * DS;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int c = lane + 32 * t;
+          if (c < D) o[u][t] = fmaf(pj, vr[c], o[u][t]);
+        }
+      }
+      m[u] = mn;
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int qi = q0 + warp * 4 + u;
+    if (qi >= Nq) continue;
+    const float inv = 1.0f / l[u];
+    const int64_t ooff = (((int64_t)b * Nq + qi) * H + h) * D;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int c = lane + 32 * t;
+      if (c < D) store_any(out, out_dtype, ooff + c, o[u][t] * inv);
+    }
+  }
+}
+
 }  // namespace mn
 
 using namespace mn;
+
+extern "C" int mn_attention(int batch, int nq, int nk, int heads, int head_dim, int dtype, const void* q,
+                            int64_t q_sb, int64_t q_sn, int64_t q_sh, const void* k, const void* v, int64_t kv_sb,
+                            int64_t kv_sn, int64_t kv_sh, int window, float scale, void* out, int out_dtype,
+                            void* stream) {
+  if (batch < 0 || nq < 0 || nk <= 0 || heads <= 0 || head_dim <= 0 || head_dim > 128 || !out) return MN_ERR_ARG;
+  if ((int64_t)batch * nq == 0) return MN_OK;
+  if (!q || !k || !v || dtype < 0 || dtype > 2 || out_dtype < 0 || out_dtype > 2) return MN_ERR_ARG;
+  cudaGetLastError();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t smem = ((size_t)kXQ * head_dim + 2 * (size_t)kXK * (head_dim + 1)) * sizeof(float);
+  const dim3 grid((nq + kXQ - 1) / kXQ, heads, batch);
+  auto run = [&](auto tag) {
+    using ET = decltype(tag);
+    cudaFuncSetAttribute(attn_chunked_kernel<ET>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attn_chunked_kernel<ET><<<grid, 256, smem, st>>>(static_cast<const ET*>(q), q_sb, q_sn, q_sh,
+                                                     static_cast<const ET*>(k), static_cast<const ET*>(v), kv_sb,
+                                                     kv_sn, kv_sh, nq, nk, heads, head_dim, window, scale, out,
+                                                     out_dtype);
+  };
+  if (dtype == MN_F32) run(float{});
+  else if (dtype == MN_F16) run(__half{});
+  else run(__nv_bfloat16{});
+  return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
+}
 
 extern "C" int mn_local_attention(int batch, int tokens, int heads, int head_dim, int dtype, const void* q,
                                   const void* k, const void* v, int64_t s_b, int64_t s_n, int64_t s_h,

@@ -33,11 +33,15 @@ struct RouteWs {
   float* wa_old;     // [L][B][half]
   float* wb_old;     // [L][B][half]
   float* wb_safe;    // [L][B][half]
+  float* cf;         // [L][B][half][16]  stencil form: [alpha, c_0 .. c_11, 0 ..]
   int32_t* carrier_tok;  // [B][k]      token index of each carrier, in order
 };
 
+constexpr int kStencilSlots = 16;
+
 __host__ inline size_t route_ws_floats(int L, int B, int half, int kc, int bands) {
-  return (size_t)L * B * half * kc + (size_t)L * B * half * 5 + (size_t)L * B * bands * 2;
+  return (size_t)L * B * half * kc + (size_t)L * B * half * 5 + (size_t)L * B * bands * 2 +
+         (size_t)L * B * half * kStencilSlots;
 }
 
 // Table views for layer parity q.
@@ -45,13 +49,15 @@ struct ParityTables {
   const int32_t* slot_k;
   const int32_t* slot_rx;
   const int32_t* rx_in;
+  const int32_t* rx_off;
 };
 __host__ __device__ inline ParityTables parity_tables(const int32_t* t, int half, int kc, int kin, int q) {
-  const int32_t* base = t + (int64_t)q * ((int64_t)half * kc * 2 + (int64_t)half * kin);
+  const int32_t* base = t + (int64_t)q * ((int64_t)half * kc * 2 + (int64_t)half * kin * 2);
   ParityTables p;
   p.slot_k = base;
   p.slot_rx = base + (int64_t)half * kc;
   p.rx_in = base + (int64_t)half * kc * 2;
+  p.rx_off = p.rx_in + (int64_t)half * kin;
   return p;
 }
 
@@ -262,7 +268,7 @@ __global__ void __launch_bounds__(512) route_select_kernel(
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) route_mass_kernel(
     const int32_t* __restrict__ table, int B, int T, int half, int kc, int kin, int L, int k,
-    RouteWs ws, float* __restrict__ size_out, float* __restrict__ center_out,
+    int write_stencil, RouteWs ws, float* __restrict__ size_out, float* __restrict__ center_out,
     float* __restrict__ topk_size, int64_t* __restrict__ topk_idx) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* size = reinterpret_cast<float*>(smem_raw);  // [T]
@@ -307,6 +313,28 @@ __global__ void __launch_bounds__(1024) route_mass_kernel(
       }
       const float wbn = __fadd_rn(wb, contrib);
       const float wsafe = fmaxf(wbn, eps);
+      if (write_stencil) {
+        // x_s <- alpha * x_s + sum_j c_j * x_dj, the same update scaled by
+        // 1 / wb_safe once per coefficient instead of once per channel
+        float* cf = ws.cf + (lb * half + i) * kStencilSlots;
+        float slots[kStencilSlots];
+#pragma unroll
+        for (int u = 0; u < kStencilSlots; ++u) slots[u] = 0.f;
+        slots[0] = wb / wsafe;
+        const int32_t* off = pt.rx_off + (int64_t)i * kin;
+        for (int j = 0; j < kin; ++j) {
+          int e = in[j];
+          if (e < 0) break;
+          const int o = off[j];
+          const float v = (asg[e] * size[1 + 2 * (e / kc) + dp]) / wsafe;
+#pragma unroll
+          for (int u = 1; u < kStencilSlots; ++u)
+            if (o == u - 1) slots[u] = v;
+        }
+#pragma unroll
+        for (int u = 0; u < kStencilSlots; u += 4)
+          *reinterpret_cast<float4*>(cf + u) = make_float4(slots[u], slots[u + 1], slots[u + 2], slots[u + 3]);
+      }
       nv_b[cnt] = wbn;
       nc_b[cnt] = __fdiv_rn(__fadd_rn(__fmul_rn(wb, cb), ccontrib), wsafe);
       wb_rec[i] = wb;
@@ -429,6 +457,100 @@ __global__ void __launch_bounds__(256) route_transport_kernel(
 }
 
 
+// ---------------------------------------------------------------------------
+// route_transport_stencil: the same per-layer update for even-width grids,
+// where receivers fill whole grid columns and a receiver's donors sit at odd
+// column offsets dx in {-3,-1,1,3} and |dy| <= DY1 (|dx| = 1) or DY3
+// (|dx| = 3).  A thread owns 4 channels of one receiver column and walks its
+// rows with a sliding window of the two neighbouring donor columns, so every
+// donor value it loads serves 2*DY1+1 receivers.  The coefficients
+// (alpha = wb_old / wb_safe, c = assign * wa_old / wb_safe) come from
+// route_mass in stencil order.
+// ---------------------------------------------------------------------------
+template <typename XT, int CT, int DY1, int DY3>
+__global__ void __launch_bounds__(512) route_transport_stencil_kernel(
+    const XT* __restrict__ x, int B, int T, int C, int grid_h, int grid_w, int half, int L, int k,
+    int row_splits, RouteWs ws, XT* __restrict__ topk_x) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* tile = reinterpret_cast<float*>(smem_raw);  // [T][CT]
+  constexpr int G = CT / 4;                           // float4 channel groups
+  constexpr int NW = 2 * DY1 + 1;                     // window rows
+  const int b = blockIdx.x;
+  const int c0 = blockIdx.y * CT;
+  const XT* xb = x + (int64_t)b * T * C;
+  for (int i = threadIdx.x; i < T * CT; i += blockDim.x) {
+    const int t = i / CT, c = i % CT;
+    tile[i] = (c0 + c < C) ? to_f32(xb[(int64_t)t * C + c0 + c]) : 0.f;
+  }
+  __syncthreads();
+  const int half_w = grid_w >> 1;
+  const int g = threadIdx.x % G;
+  const int cr = (threadIdx.x / G) % half_w;
+  const int rs = threadIdx.x / (G * half_w);
+  const bool active = rs < row_splits;
+  const int rows_per = (grid_h + row_splits - 1) / row_splits;
+  const int r_begin = rs * rows_per, r_end = min(grid_h, r_begin + rows_per);
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto ld = [&](int r, int c) -> float4 {
+    if (r < 0 || r >= grid_h || c < 0 || c >= grid_w) return zero;
+    return *reinterpret_cast<const float4*>(tile + (1 + r * grid_w + c) * CT + 4 * g);
+  };
+  auto fma4 = [](float w, float4 v, float4 a) {
+    a.x = fmaf(w, v.x, a.x); a.y = fmaf(w, v.y, a.y); a.z = fmaf(w, v.z, a.z); a.w = fmaf(w, v.w, a.w);
+    return a;
+  };
+  for (int l = 0; l < L; ++l) {
+    const int rp = (l & 1) ? 1 : 0;  // receiver patch parity = column parity
+    const int c = 2 * cr + rp;
+    const float* cfl = ws.cf + ((int64_t)l * B + b) * half * kStencilSlots;
+    if (active && r_begin < r_end) {
+      float4 wl[NW], wr[NW];
+#pragma unroll
+      for (int u = 0; u < NW - 1; ++u) {
+        wl[u + 1] = ld(r_begin - DY1 + u, c - 1);
+        wr[u + 1] = ld(r_begin - DY1 + u, c + 1);
+      }
+      for (int r = r_begin; r < r_end; ++r) {
+#pragma unroll
+        for (int u = 0; u < NW - 1; ++u) { wl[u] = wl[u + 1]; wr[u] = wr[u + 1]; }
+        wl[NW - 1] = ld(r + DY1, c - 1);
+        wr[NW - 1] = ld(r + DY1, c + 1);
+        const int s = (r * grid_w + c) >> 1;
+        const float4* cfp = reinterpret_cast<const float4*>(cfl + (int64_t)s * kStencilSlots);
+        const float4 q0 = __ldg(cfp), q1 = __ldg(cfp + 1), q2 = __ldg(cfp + 2), q3 = __ldg(cfp + 3);
+        const float cw[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
+                              q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
+        float4* own = reinterpret_cast<float4*>(tile + (1 + r * grid_w + c) * CT + 4 * g);
+        const float4 xo = *own;
+        float4 acc = make_float4(cw[0] * xo.x, cw[0] * xo.y, cw[0] * xo.z, cw[0] * xo.w);
+        int j = 1;
+        if (DY3 >= 0) {
+#pragma unroll
+          for (int dy = -DY3; dy <= DY3; ++dy) acc = fma4(cw[j++], ld(r + dy, c - 3), acc);
+        }
+#pragma unroll
+        for (int u = 0; u < NW; ++u) acc = fma4(cw[j++], wl[u], acc);
+#pragma unroll
+        for (int u = 0; u < NW; ++u) acc = fma4(cw[j++], wr[u], acc);
+        if (DY3 >= 0) {
+#pragma unroll
+          for (int dy = -DY3; dy <= DY3; ++dy) acc = fma4(cw[j++], ld(r + dy, c + 3), acc);
+        }
+        *own = acc;
+      }
+    }
+    __syncthreads();
+  }
+  XT* out = topk_x + (int64_t)b * (k + 1) * C;
+  const int32_t* ctok = ws.carrier_tok + (int64_t)b * k;
+  for (int i = threadIdx.x; i < (k + 1) * CT; i += blockDim.x) {
+    const int r = i / CT, cc = i % CT;
+    if (c0 + cc >= C) continue;
+    const int t = (r == 0) ? 0 : ctok[r - 1];
+    out[(int64_t)r * C + c0 + cc] = from_f32<XT>(tile[t * CT + cc]);
+  }
+}
+
 static Banding make_banding(int grid_h, int grid_w, int radius_rows, int Cm) {
   Banding bd;
   bd.radius_rows = radius_rows;
@@ -476,6 +598,48 @@ static void launch_transport(const void* x, const int32_t* table, int B, int T, 
   } else {
     cudaFuncSetAttribute(route_transport_kernel<XT, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     route_transport_kernel<XT, 8><<<grid, 256, smem, st>>>(xp, table, B, T, C, half, kc, kin, L, k, ws, op);
+  }
+}
+
+// Which compiled stencil fits the geometry: 1 = (DY1 2, DY3 0) radius 3,
+// 2 = (1, none) radius in [sqrt 2, sqrt 5), 3 = (0, none); 0 = generic path.
+static int stencil_variant(const mn_route_dims* d) {
+  if (d->grid_w % 2 != 0 || d->grid_w / 2 > 64) return 0;
+  if (d->stencil_dy1 == 2 && d->stencil_dy3 == 0) return 1;
+  if (d->stencil_dy1 == 1 && d->stencil_dy3 == -1) return 2;
+  if (d->stencil_dy1 == 0 && d->stencil_dy3 == -1) return 3;
+  return 0;
+}
+
+template <typename XT, int CT, int DY1, int DY3>
+static void launch_stencil_ct(const void* x, int B, int T, int C, const mn_route_dims* d, int L, int k,
+                              const RouteWs& ws, void* topk_x, cudaStream_t st) {
+  const int half_w = d->grid_w / 2;
+  const int per_split = (CT / 4) * half_w;
+  int splits = std::max(1, std::min(d->grid_h, 512 / per_split));
+  splits = std::min(splits, 4);
+  const int threads = ((per_split * splits + 31) / 32) * 32;
+  const size_t smem = (size_t)T * CT * sizeof(float);
+  auto kern = route_transport_stencil_kernel<XT, CT, DY1, DY3>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<dim3(B, (C + CT - 1) / CT), threads, smem, st>>>(static_cast<const XT*>(x), B, T, C, d->grid_h,
+                                                            d->grid_w, d->half, L, k, splits, ws,
+                                                            static_cast<XT*>(topk_x));
+}
+
+template <typename XT>
+static void launch_stencil(int variant, const void* x, int B, int T, int C, const mn_route_dims* d, int L, int k,
+                           const RouteWs& ws, void* topk_x, cudaStream_t st) {
+  const bool wide = (size_t)T * 32 * sizeof(float) <= 200 * 1024;
+  if (variant == 1) {
+    if (wide) launch_stencil_ct<XT, 32, 2, 0>(x, B, T, C, d, L, k, ws, topk_x, st);
+    else launch_stencil_ct<XT, 16, 2, 0>(x, B, T, C, d, L, k, ws, topk_x, st);
+  } else if (variant == 2) {
+    if (wide) launch_stencil_ct<XT, 32, 1, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
+    else launch_stencil_ct<XT, 16, 1, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
+  } else {
+    if (wide) launch_stencil_ct<XT, 32, 0, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
+    else launch_stencil_ct<XT, 16, 0, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
   }
 }
 
@@ -539,6 +703,7 @@ extern "C" int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev
   ws.wb_old = f;   f += LBh;
   ws.wb_safe = f;  f += LBh;
   ws.partials = f; f += (size_t)num_layers * batch * dims->grid_h * 2;
+  ws.cf = f;       f += LBh * kStencilSlots;
   ws.carrier_tok = reinterpret_cast<int32_t*>(f);
 
   cudaGetLastError();  // clear any stale error so the check below is ours
@@ -553,15 +718,25 @@ extern "C" int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev
   route_select_kernel<<<dim3(batch, num_layers), 512, smem_sel, st>>>(dev_table, batch, half, kc, kin,
                                                                        bd.bands, kb, tau2, ws, status);
 
+  const int stencil = stencil_variant(dims);
   cudaFuncSetAttribute(route_mass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_mass);
-  route_mass_kernel<<<batch, 1024, smem_mass, st>>>(dev_table, batch, T, half, kc, kin, num_layers, k, ws,
-                                                    size_out, center_out, topk_size, topk_idx);
+  route_mass_kernel<<<batch, 1024, smem_mass, st>>>(dev_table, batch, T, half, kc, kin, num_layers, k,
+                                                    stencil > 0 ? 1 : 0, ws, size_out, center_out, topk_size,
+                                                    topk_idx);
 
-  if (x_dtype == MN_F16)
+  if (stencil > 0) {
+    if (x_dtype == MN_F16)
+      launch_stencil<__half>(stencil, x, batch, T, channels, dims, num_layers, k, ws, topk_x, st);
+    else if (x_dtype == MN_BF16)
+      launch_stencil<__nv_bfloat16>(stencil, x, batch, T, channels, dims, num_layers, k, ws, topk_x, st);
+    else
+      launch_stencil<float>(stencil, x, batch, T, channels, dims, num_layers, k, ws, topk_x, st);
+  } else if (x_dtype == MN_F16) {
     launch_transport<__half>(x, dev_table, batch, T, channels, half, kc, kin, num_layers, k, ws, topk_x, ct, st);
-  else if (x_dtype == MN_BF16)
+  } else if (x_dtype == MN_BF16) {
     launch_transport<__nv_bfloat16>(x, dev_table, batch, T, channels, half, kc, kin, num_layers, k, ws, topk_x, ct, st);
-  else
+  } else {
     launch_transport<float>(x, dev_table, batch, T, channels, half, kc, kin, num_layers, k, ws, topk_x, ct, st);
+  }
   return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
 }

@@ -46,7 +46,25 @@ void neighbor_lists(int h, int w, double radius, std::vector<std::vector<int>>& 
 struct Parity {
   std::vector<std::vector<int>> slot_k, slot_rx;  // per donor: compact slots
   std::vector<std::vector<int>> rx_in;             // per receiver: edge ids
+  std::vector<std::vector<int>> rx_off;            // per receiver: stencil offset index
 };
+
+// Stencil offsets of a receiver's donors for an even-width grid: donor
+// columns differ by an odd dx.  Order: dx ascending over odd values, then dy
+// ascending.  Returns -1 when (dy, dx) is outside the stencil.
+int stencil_index(int dy, int dx, int dy1, int dy3) {
+  int idx = 0;
+  const int dxs[4] = {-3, -1, 1, 3};
+  for (int i = 0; i < 4; ++i) {
+    const int lim = (dxs[i] == -3 || dxs[i] == 3) ? dy3 : dy1;
+    if (lim < 0) continue;
+    for (int y = -lim; y <= lim; ++y) {
+      if (dxs[i] == dx && y == dy) return idx;
+      ++idx;
+    }
+  }
+  return -1;
+}
 
 void build_parity(int h, int w, double radius, int q, const std::vector<std::vector<int>>& nbr,
                   int kc_stride, Parity& out, int* kc_max, int* kin_max, int* valid_rows) {
@@ -55,6 +73,7 @@ void build_parity(int h, int w, double radius, int q, const std::vector<std::vec
   out.slot_k.assign(half, {});
   out.slot_rx.assign(half, {});
   out.rx_in.assign(half, {});
+  out.rx_off.assign(half, {});
   int kc = 0, rows = 0;
   for (int d = 0; d < half; ++d) {
     const int pd = 2 * d + dp;
@@ -71,7 +90,13 @@ void build_parity(int h, int w, double radius, int q, const std::vector<std::vec
   }
   const int stride = kc_stride > 0 ? kc_stride : kc;
   for (int d = 0; d < half; ++d)
-    for (int c = 0; c < (int)out.slot_rx[d].size(); ++c) out.rx_in[out.slot_rx[d][c]].push_back(d * stride + c);
+    for (int c = 0; c < (int)out.slot_rx[d].size(); ++c) {
+      const int s = out.slot_rx[d][c];
+      out.rx_in[s].push_back(d * stride + c);
+      const int pd = 2 * d + dp, ps = 2 * s + rp;
+      out.rx_off[s].push_back(pd / w - ps / w);      // dy, resolved to an index below
+      out.rx_off[s].push_back(pd % w - ps % w);      // dx
+    }
   int kin = 0;
   for (int s = 0; s < half; ++s) kin = std::max(kin, (int)out.rx_in[s].size());
   *kc_max = kc;
@@ -136,7 +161,25 @@ extern "C" int mn_route_dims_query(int grid_h, int grid_w, double radius, mn_rou
   }
   dims->kc = std::max(kc, 1);
   dims->kin = std::max(kin, 1);
-  dims->table_ints = (int64_t)2 * ((int64_t)dims->half * dims->kc * 2 + (int64_t)dims->half * dims->kin);
+  // Stencil form of the feature transport: even width (patch parity =
+  // column parity), donors at odd dx in {-3,-1,1,3}; dy limits per |dx|.
+  int dy1 = -1, dy3 = -1;
+  bool ok = (grid_w % 2) == 0;
+  for (int q = 0; q < 2 && ok; ++q) {
+    Parity par;
+    int a, b, rows;
+    build_parity(grid_h, grid_w, radius, q, nbr, 0, par, &a, &b, &rows);
+    for (int s = 0; s < dims->half && ok; ++s)
+      for (size_t j = 0; j + 1 < par.rx_off[s].size(); j += 2) {
+        const int dy = std::abs(par.rx_off[s][j]), dx = std::abs(par.rx_off[s][j + 1]);
+        if (dx == 1) dy1 = std::max(dy1, dy);
+        else if (dx == 3) dy3 = std::max(dy3, dy);
+        else ok = false;
+      }
+  }
+  dims->stencil_dy1 = ok ? dy1 : -2;
+  dims->stencil_dy3 = ok ? dy3 : -2;
+  dims->table_ints = (int64_t)2 * ((int64_t)dims->half * dims->kc * 2 + (int64_t)dims->half * dims->kin * 2);
   return MN_OK;
 }
 
@@ -158,6 +201,7 @@ extern "C" int mn_route_tables_fill(int grid_h, int grid_w, double radius, const
     int32_t* sk = t;
     int32_t* sr = t + (int64_t)half * kc;
     int32_t* ri = t + (int64_t)half * kc * 2;
+    int32_t* ro = ri + (int64_t)half * kin;
     for (int d = 0; d < half; ++d)
       for (int c = 0; c < kc; ++c) {
         const bool v = c < (int)par.slot_k[d].size();
@@ -165,8 +209,15 @@ extern "C" int mn_route_tables_fill(int grid_h, int grid_w, double radius, const
         sr[(int64_t)d * kc + c] = v ? par.slot_rx[d][c] : -1;
       }
     for (int s = 0; s < half; ++s)
-      for (int j = 0; j < kin; ++j) ri[(int64_t)s * kin + j] = j < (int)par.rx_in[s].size() ? par.rx_in[s][j] : -1;
-    t += (int64_t)half * kc * 2 + (int64_t)half * kin;
+      for (int j = 0; j < kin; ++j) {
+        const bool v = j < (int)par.rx_in[s].size();
+        ri[(int64_t)s * kin + j] = v ? par.rx_in[s][j] : -1;
+        ro[(int64_t)s * kin + j] =
+            (v && dims->stencil_dy1 >= -1)
+                ? stencil_index(par.rx_off[s][2 * j], par.rx_off[s][2 * j + 1], dims->stencil_dy1, dims->stencil_dy3)
+                : -1;
+      }
+    t += (int64_t)half * kc * 2 + (int64_t)half * kin * 2;
   }
   return MN_OK;
 }

@@ -1,0 +1,265 @@
+"""mergenet_small_cls inference on the B200 kernels.
+
+Module tree and parameter names follow the reference's
+CLSHybridToMeModel built by ``mergenet_small_cls`` (opentome/models/mergenet/
+model.py:1602-1607 with the canonical kwargs :24-53): ``local.vit.*`` (patch
+embed, CLS, position embedding, six LocalBlocks), ``local.metric_layers.*``,
+``encode_cross_attention.*``, ``latent.vit.*`` (six global blocks + norm) and
+``head``, so a reference state dict maps onto it key for key.
+
+The forward is the reference's inference path under fp16 autocast
+(model.py:1141-1222): fp16 GEMMs and attention inside fp32 residual
+streams, fp32 LayerNorms, fp32 routing, fp32 cross-attention projections.
+The hot path runs on the library: windowed local attention with the CLS row
+(bias_local_attn.py:679-724), the fused six-layer routing + carrier gather
+(model.py:574-590, :1157-1183) and the cross-attention core (model.py:173-188).
+GEMMs, LayerNorm and GELU are cuBLAS / ATen.  The latent blocks' biased
+global attention (opentome/timm/tome.py:50-54) runs on PyTorch SDPA.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .attention import cross_attention, local_attention_packed
+from .routing import RoutePlan
+
+
+class _PatchEmbed(nn.Module):
+    def __init__(self, patch, dim):
+        super().__init__()
+        self.proj = nn.Conv2d(3, dim, patch, patch)
+
+
+class _Attention(nn.Module):
+    def __init__(self, dim):
+        super().__init__()
+        self.qkv = nn.Linear(dim, dim * 3)
+        self.proj = nn.Linear(dim, dim)
+
+
+class _Mlp(nn.Module):
+    def __init__(self, dim, hidden):
+        super().__init__()
+        self.fc1 = nn.Linear(dim, hidden)
+        self.fc2 = nn.Linear(hidden, dim)
+
+
+class _Block(nn.Module):
+    def __init__(self, dim, mlp_ratio):
+        super().__init__()
+        self.norm1 = nn.LayerNorm(dim)
+        self.attn = _Attention(dim)
+        self.norm2 = nn.LayerNorm(dim)
+        self.mlp = _Mlp(dim, int(dim * mlp_ratio))
+
+
+class _LocalVit(nn.Module):
+    def __init__(self, img, patch, dim, depth, mlp_ratio):
+        super().__init__()
+        self.patch_embed = _PatchEmbed(patch, dim)
+        n = (img // patch) ** 2
+        self.cls_token = nn.Parameter(torch.zeros(1, 1, dim))
+        self.pos_embed = nn.Parameter(torch.zeros(1, n + 1, dim))
+        self.blocks = nn.ModuleList([_Block(dim, mlp_ratio) for _ in range(depth)])
+
+
+class _Local(nn.Module):
+    def __init__(self, img, patch, dim, depth, mlp_ratio, metric_dim):
+        super().__init__()
+        self.vit = _LocalVit(img, patch, dim, depth, mlp_ratio)
+        self.metric_layers = nn.ModuleList([nn.Linear(dim, metric_dim) for _ in range(depth)])
+
+
+class _LatentVit(nn.Module):
+    def __init__(self, img, patch, dim, depth, mlp_ratio):
+        super().__init__()
+        self.pos_embed = nn.Parameter(torch.zeros(1, (img // patch) ** 2, dim), requires_grad=False)
+        self.blocks = nn.ModuleList([_Block(dim, mlp_ratio) for _ in range(depth)])
+        self.norm = nn.LayerNorm(dim)
+
+
+class _Latent(nn.Module):
+    def __init__(self, img, patch, dim, depth, mlp_ratio):
+        super().__init__()
+        self.vit = _LatentVit(img, patch, dim, depth, mlp_ratio)
+
+
+class CrossAttention(nn.Module):
+    """MyCrossAttention (model.py:90-221) parameters."""
+
+    def __init__(self, dim, heads):
+        super().__init__()
+        self.num_heads = heads
+        self.q_norm = nn.LayerNorm(dim)
+        self.kv_norm = nn.LayerNorm(dim)
+        self.q_proj = nn.Linear(dim, dim)
+        self.k_proj = nn.Linear(dim, dim)
+        self.v_proj = nn.Linear(dim, dim)
+        self.out_proj = nn.Linear(dim, dim)
+
+
+class MergeNetSmall(nn.Module):
+    """Canonical MN-L2-R3 classifier (dim 384, 6 heads, 6 local + 6 latent)."""
+
+    def __init__(self, img_size=224, patch_size=8, embed_dim=384, num_heads=6, mlp_ratio=4.0, local_depth=6,
+                 latent_depth=6, num_classes=1000, metric_dim=64, spatial_radius=3.0, local_window=16,
+                 lambda_local=2.0):
+        super().__init__()
+        self.img_size, self.patch_size = img_size, patch_size
+        self.embed_dim, self.num_heads = embed_dim, num_heads
+        self.local_window = local_window
+        self.spatial_radius = spatial_radius
+        self.grid = (img_size // patch_size, img_size // patch_size)
+        num_patches = self.grid[0] * self.grid[1]
+        self.total_merge_local = int(num_patches * (lambda_local - 1) / lambda_local)
+        default_r = self.total_merge_local // max(local_depth, 1)
+        r_list = [default_r] * local_depth  # parse_r(local_depth, default_r, total) (tome.py:12-53)
+        r_list[-1] += self.total_merge_local - sum(r_list)
+        self.r_list = r_list
+        self.local = _Local(img_size, patch_size, embed_dim, local_depth, mlp_ratio, metric_dim)
+        self.latent = _Latent(img_size, patch_size, embed_dim, latent_depth, mlp_ratio)
+        self.head = nn.Linear(embed_dim, num_classes)
+        self.encode_cross_attention = CrossAttention(embed_dim, num_heads)
+        self._plans = {}
+        self._half = None
+
+    # ------------------------------------------------------------------ init
+    @torch.no_grad()
+    def init_weights(self, seed=0):
+        """Random init in the reference's style: timm ViT init for the ViT
+        parts (trunc-normal 0.02 linears, zero biases, CLS ~ N(0, 1e-6)),
+        PyTorch defaults for the metric heads and cross-attention, zero
+        cross-attention output projection (model.py:822-829)."""
+        g = torch.Generator().manual_seed(seed)
+
+        def tn(t, std=0.02):
+            t.copy_(torch.nn.init.trunc_normal_(torch.empty_like(t), std=std, generator=g))
+
+        for vit in (self.local.vit, self.latent.vit):
+            tn(vit.pos_embed)
+            for blk in vit.blocks:
+                for lin in (blk.attn.qkv, blk.attn.proj, blk.mlp.fc1, blk.mlp.fc2):
+                    tn(lin.weight)
+                    lin.bias.zero_()
+        self.local.vit.cls_token.normal_(0, 1e-6, generator=g)
+        pe = self.local.vit.patch_embed.proj
+        bound = 1 / math.sqrt(pe.weight[0].numel())
+        pe.weight.uniform_(-bound, bound, generator=g)
+        pe.bias.uniform_(-bound, bound, generator=g)
+        for lin in list(self.local.metric_layers) + [self.encode_cross_attention.q_proj,
+                                                      self.encode_cross_attention.k_proj,
+                                                      self.encode_cross_attention.v_proj]:
+            bound = 1 / math.sqrt(lin.in_features)
+            lin.weight.uniform_(-bound, bound, generator=g)
+            lin.bias.uniform_(-bound, bound, generator=g)
+        self.encode_cross_attention.out_proj.weight.zero_()
+        self.encode_cross_attention.out_proj.bias.zero_()
+        tn(self.head.weight)
+        self.head.bias.zero_()
+        self._half = None
+        return self
+
+    # ------------------------------------------------------------- execution
+    def _plan(self, device):
+        key = (device.type, device.index)
+        if key not in self._plans:
+            self._plans[key] = RoutePlan(self.grid, self.spatial_radius, self.r_list, device=device)
+        return self._plans[key]
+
+    def _weights16(self):
+        """fp16 copies of the GEMM weights autocast would cast on every call."""
+        if self._half is None:
+            self._half = {n: p.detach().half() for n, p in self.named_parameters()
+                          if p.ndim >= 2 and "encode_cross_attention" not in n and "pos_embed" not in n
+                          and "cls_token" not in n}
+        return self._half
+
+    def _linear16(self, x, name, lin):
+        w = self._weights16()[name + ".weight"]
+        return F.linear(x.half(), w, lin.bias.half())
+
+    def _block_local(self, x, i, blk, metrics, w16):
+        b, n, c = x.shape
+        h = F.layer_norm(x, (c,), blk.norm1.weight, blk.norm1.bias)
+        qkv = self._linear16(h, f"local.vit.blocks.{i}.attn.qkv", blk.attn.qkv)
+        a = local_attention_packed(qkv, self.num_heads, self.local_window, cls_global=True)
+        x = x + self._linear16(a, f"local.vit.blocks.{i}.attn.proj", blk.attn.proj)
+        h = F.layer_norm(x, (c,), blk.norm2.weight, blk.norm2.bias)
+        h = F.gelu(self._linear16(h, f"local.vit.blocks.{i}.mlp.fc1", blk.mlp.fc1))
+        x = x + self._linear16(h, f"local.vit.blocks.{i}.mlp.fc2", blk.mlp.fc2)
+        lin = self.local.metric_layers[i]
+        torch.addmm(lin.bias.half(), x.view(-1, c).half(), w16[f"local.metric_layers.{i}.weight"].t(),
+                    out=metrics[i].view(-1, metrics.shape[-1]))
+        return x
+
+    def _block_latent(self, x, i, blk, log_size):
+        b, n, c = x.shape
+        hd = c // self.num_heads
+        h = F.layer_norm(x, (c,), blk.norm1.weight, blk.norm1.bias)
+        qkv = self._linear16(h, f"latent.vit.blocks.{i}.attn.qkv", blk.attn.qkv)
+        q, k, v = qkv.view(b, n, 3, self.num_heads, hd).permute(2, 0, 3, 1, 4).unbind(0)
+        a = F.scaled_dot_product_attention(q, k, v, attn_mask=log_size)
+        a = a.transpose(1, 2).reshape(b, n, c)
+        x = x + self._linear16(a, f"latent.vit.blocks.{i}.attn.proj", blk.attn.proj)
+        h = F.layer_norm(x, (c,), blk.norm2.weight, blk.norm2.bias)
+        h = F.gelu(self._linear16(h, f"latent.vit.blocks.{i}.mlp.fc1", blk.mlp.fc1))
+        return x + self._linear16(h, f"latent.vit.blocks.{i}.mlp.fc2", blk.mlp.fc2)
+
+    def _cross(self, topk_x, x_embed):
+        ca = self.encode_cross_attention
+        b, nq, c = topk_x.shape
+        nk = x_embed.shape[1]
+        hd = c // self.num_heads
+        q = F.linear(F.layer_norm(topk_x, (c,), ca.q_norm.weight, ca.q_norm.bias), ca.q_proj.weight, ca.q_proj.bias)
+        kv_in = F.layer_norm(x_embed, (c,), ca.kv_norm.weight, ca.kv_norm.bias)
+        k = F.linear(kv_in, ca.k_proj.weight, ca.k_proj.bias)
+        v = F.linear(kv_in, ca.v_proj.weight, ca.v_proj.bias)
+        # SDPA runs on fp16 operands under autocast; the context comes back fp32
+        ctx = cross_attention(q.half().view(b, nq, self.num_heads, hd), k.half().view(b, nk, self.num_heads, hd),
+                              v.half().view(b, nk, self.num_heads, hd), out_dtype=torch.float32)
+        return F.linear(ctx.view(b, nq, c), ca.out_proj.weight, ca.out_proj.bias)
+
+    @torch.no_grad()
+    def forward(self, images):
+        """images [B, 3, H, W] -> (logits [B, classes] fp16, aux dict)."""
+        if not images.is_cuda:
+            raise RuntimeError("MergeNetSmall runs on CUDA (there is no CPU path)")
+        w16 = self._weights16()
+        vit = self.local.vit
+        b = images.shape[0]
+        pe = vit.patch_embed.proj
+        x = F.conv2d(images.half(), w16["local.vit.patch_embed.proj.weight"], pe.bias.half(), stride=self.patch_size)
+        x = x.flatten(2).transpose(1, 2)
+        x = torch.cat([vit.cls_token.expand(b, -1, -1), x.float()], dim=1) + vit.pos_embed
+        n, c = x.shape[1], x.shape[2]
+        depth = len(vit.blocks)
+        metrics = torch.empty(depth, b, n, self.local.metric_layers[0].out_features, device=x.device,
+                              dtype=torch.float16)
+        for i, blk in enumerate(vit.blocks):
+            x = self._block_local(x, i, blk, metrics, w16)
+        x_embed = x
+        route = self._plan(x.device)(x_embed, metrics)
+        topk_x = route.topk_x
+        x_trace = self._cross(topk_x, x_embed) + topk_x
+        log_size = route.topk_size.log().half()[:, None, None, :]
+        for i, blk in enumerate(self.latent.vit.blocks):
+            x_trace = self._block_latent(x_trace, i, blk, log_size)
+        lv = self.latent.vit
+        cls = F.layer_norm(x_trace[:, 0], (c,), lv.norm.weight, lv.norm.bias)
+        logits = self._linear16(cls, "head", self.head)
+        aux = {
+            "token_strength_no_cls": route.size[:, 1:],
+            "topk_patch_indices": route.topk_idx,
+            "retained_tokens": int(route.topk_idx.shape[1]),
+            "cls_feature": cls,
+        }
+        return logits, aux
+
+
+def mergenet_small_cls(**kwargs):
+    """Factory with the reference's canonical single-branch defaults."""
+    return MergeNetSmall(**kwargs)

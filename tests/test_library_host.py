@@ -90,13 +90,24 @@ def test_route_tables_match_sparse_mapping(grid, radius):
     geom = O.Geometry(grid, radius)
     half, kc, kin = dims.half, dims.kc, dims.kin
     p = grid[0] * grid[1]
-    per = half * kc * 2 + half * kin
+    per = half * kc * 2 + half * kin * 2
+    w = grid[1]
+    # stencil order: odd dx ascending, then dy ascending within each |dx| limit
+    offsets = [(dy, dx) for dx in (-3, -1, 1, 3)
+               for dy in range(-(dims.stencil_dy3 if abs(dx) == 3 else dims.stencil_dy1),
+                               (dims.stencil_dy3 if abs(dx) == 3 else dims.stencil_dy1) + 1)]
     for q in (0, 1):
         dp = 0 if q else 1
         t = table[q * per:(q + 1) * per]
         slot_k = t[:half * kc].reshape(half, kc)
         slot_rx = t[half * kc:2 * half * kc].reshape(half, kc)
-        rx_in = t[2 * half * kc:].reshape(half, kin)
+        rx_in = t[2 * half * kc:2 * half * kc + half * kin].reshape(half, kin)
+        rx_off = t[2 * half * kc + half * kin:].reshape(half, kin)
+        for s_ in range(half):
+            for j in np.nonzero(rx_in[s_] >= 0)[0]:
+                d = rx_in[s_, j] // kc
+                pd, ps = 2 * d + dp, 2 * s_ + (1 - dp)
+                assert offsets[rx_off[s_, j]] == (pd // w - ps // w, pd % w - ps % w)
         donors = np.arange(dp, p, 2)[None]
         recv = np.arange(1 - dp, p, 2)[None]
         ridx, rvalid = O.map_sorted_receivers(geom.nbr_idx, geom.nbr_valid, donors, recv)
@@ -114,6 +125,7 @@ def test_route_tables_match_sparse_mapping(grid, radius):
         assert dims.valid_rows[q] == int(rvalid[0].any(-1).sum())
     if grid == (28, 28):
         assert (dims.kc, dims.kin, dims.k_static) == (12, 12, 29)
+        assert (dims.stencil_dy1, dims.stencil_dy3) == (2, 0)
 
 
 def test_cpu_tensors_are_rejected():

@@ -1,0 +1,109 @@
+"""End-to-end mergenet_small_cls forward on the B200 kernels."""
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import carrier_mismatches
+from oracle import routing as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch.device("cuda", 0)
+
+
+def torch_forward(model, images):
+    """The same inference forward restated with PyTorch ops (band-masked SDPA
+    for the local attention + CLS row, SDPA for the cross attention) and the
+    numpy routing oracle, with the model's fp16 / fp32 rounding points."""
+    w16 = model._weights16()
+    vit = model.local.vit
+    b = images.shape[0]
+    heads = model.num_heads
+    x = F.conv2d(images.half(), w16["local.vit.patch_embed.proj.weight"], vit.patch_embed.proj.bias.half(),
+                 stride=model.patch_size).flatten(2).transpose(1, 2)
+    x = torch.cat([vit.cls_token.expand(b, -1, -1), x.float()], 1) + vit.pos_embed
+    n, c = x.shape[1], x.shape[2]
+    hd = c // heads
+    pos = torch.arange(n, device=x.device)
+    band = (pos[:, None] - pos[None, :]).abs() <= model.local_window
+    band[0] = True
+    metrics = []
+    for i, blk in enumerate(vit.blocks):
+        h = F.layer_norm(x, (c,), blk.norm1.weight, blk.norm1.bias)
+        qkv = model._linear16(h, f"local.vit.blocks.{i}.attn.qkv", blk.attn.qkv)
+        q, k, v = qkv.view(b, n, 3, heads, hd).permute(2, 0, 3, 1, 4).unbind(0)
+        s = (q.float() @ k.float().transpose(-1, -2)) / math.sqrt(hd)
+        a = torch.softmax(s.masked_fill(~band, float("-inf")), -1) @ v.float()
+        a = a.half().transpose(1, 2).reshape(b, n, c)
+        x = x + model._linear16(a, f"local.vit.blocks.{i}.attn.proj", blk.attn.proj)
+        h = F.layer_norm(x, (c,), blk.norm2.weight, blk.norm2.bias)
+        h = F.gelu(model._linear16(h, f"local.vit.blocks.{i}.mlp.fc1", blk.mlp.fc1))
+        x = x + model._linear16(h, f"local.vit.blocks.{i}.mlp.fc2", blk.mlp.fc2)
+        lin = model.local.metric_layers[i]
+        m = torch.empty(b, n, lin.out_features, device=x.device, dtype=torch.float16)
+        torch.addmm(lin.bias.half(), x.view(-1, c).half(), w16[f"local.metric_layers.{i}.weight"].t(),
+                    out=m.view(-1, lin.out_features))
+        metrics.append(m)
+    route = O.route_and_gather(x.cpu().numpy(), [m.cpu().numpy() for m in metrics], model.r_list,
+                               O.Geometry(model.grid, model.spatial_radius))
+    topk_x = torch.from_numpy(route["topk_x"]).to(x.device)
+    ca = model.encode_cross_attention
+    q = F.linear(F.layer_norm(topk_x, (c,), ca.q_norm.weight, ca.q_norm.bias), ca.q_proj.weight, ca.q_proj.bias)
+    kv = F.layer_norm(x, (c,), ca.kv_norm.weight, ca.kv_norm.bias)
+    k = F.linear(kv, ca.k_proj.weight, ca.k_proj.bias)
+    v = F.linear(kv, ca.v_proj.weight, ca.v_proj.bias)
+    split = lambda t: t.half().view(b, -1, heads, hd).transpose(1, 2).float()  # noqa: E731
+    ctx = torch.softmax(split(q) @ split(k).transpose(-1, -2) / math.sqrt(hd), -1) @ split(v)
+    xt = F.linear(ctx.transpose(1, 2).reshape(b, -1, c), ca.out_proj.weight, ca.out_proj.bias) + topk_x
+    log_size = torch.from_numpy(route["topk_size"]).to(x.device).log().half()[:, None, None, :]
+    for i, blk in enumerate(model.latent.vit.blocks):
+        xt = model._block_latent(xt, i, blk, log_size)
+    lv = model.latent.vit
+    cls = F.layer_norm(xt[:, 0], (c,), lv.norm.weight, lv.norm.bias)
+    return model._linear16(cls, "head", model.head), route
+
+
+def test_reference_smoke_config(dev):
+    """tests/test_model_smoke.py:27-134: a 32x32 model keeps 8 carriers and
+    repeated eval forwards agree (here bit-exactly: no atomics anywhere)."""
+    from mergenet_b200.model import MergeNetSmall
+    torch.manual_seed(20260809)
+    model = MergeNetSmall(img_size=32, patch_size=8, num_classes=10, metric_dim=16, local_depth=2,
+                          latent_depth=2, local_window=2).init_weights(0).to(dev).eval()
+    images = torch.randn(2, 3, 32, 32, device=dev)
+    first, aux1 = model(images)
+    second, aux2 = model(images)
+    assert first.shape == (2, 10)
+    assert aux1["retained_tokens"] == 8 == aux2["retained_tokens"]
+    assert bool(torch.isfinite(first).all())
+    assert torch.equal(first, second)
+    exp, route = torch_forward(model, images)
+    assert not carrier_mismatches(aux1["topk_patch_indices"].cpu().numpy(), route["topk_idx"], route["center"])
+    torch.testing.assert_close(first.float(), exp.float(), rtol=1e-2, atol=1e-2)
+
+
+def test_canonical_forward_matches_restatement(dev):
+    """Canonical 224x224 model: logits within the fp16 tolerance (1e-2
+    relative) of the PyTorch/oracle restatement, exact carrier sets."""
+    from mergenet_b200.model import MergeNetSmall
+    model = MergeNetSmall().init_weights(0).to(dev).eval()
+    g = torch.Generator(device=dev).manual_seed(3)
+    images = torch.randn(4, 3, 224, 224, device=dev, generator=g)
+    logits, aux = model(images)
+    exp, route = torch_forward(model, images)
+    mism = carrier_mismatches(aux["topk_patch_indices"].cpu().numpy(), route["topk_idx"], route["center"])
+    assert not mism, mism
+    err = (logits.float() - exp.float()).abs().max() / exp.float().abs().max()
+    assert float(err) <= 1e-2
+    assert aux["retained_tokens"] == 392
+    size = aux["token_strength_no_cls"].double().sum(1)
+    torch.testing.assert_close(size, torch.full_like(size, 784.0), rtol=1e-5, atol=1e-3)
+    np.testing.assert_allclose(aux["token_strength_no_cls"].cpu().numpy(), route["size"][:, 1:], rtol=1e-3,
+                               atol=1e-3)

@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import rel_err
+from conftest import carrier_mismatches, rel_err
 from inputs import canonical_r_list, routing_inputs
 from oracle import routing as O
 
@@ -27,9 +27,8 @@ def _case_inputs(g, x_dtype=np.float32, metric_dtype=np.float16):
     return grid, float(g["radius"]), r_list, x.astype(x_dtype), metrics
 
 
-def _report_mismatch(got, want, margin):
-    bad = np.nonzero((got != want).any(axis=1))[0]
-    return [(int(b), float(margin[b])) for b in bad]
+def _report_mismatch(got, want, center, margin):
+    return [(b, kind, float(margin[b])) for b, kind in carrier_mismatches(got, want, center)]
 
 
 @pytest.mark.parametrize("name", ROUTE_CASES)
@@ -42,8 +41,8 @@ def test_fused_route_matches_reference(dev, golden_dir, name):
     torch.cuda.synchronize()
     assert int(res.status.item()) == 0
     idx = res.topk_idx.cpu().numpy()
-    mism = _report_mismatch(idx, g["topk_idx"], g["margin"])
-    assert not mism, f"carrier index mismatch (image, reference rank-k margin): {mism}"
+    mism = _report_mismatch(idx, g["topk_idx"], g["center"], g["margin"])
+    assert not mism, f"carrier mismatch (image, kind, reference rank-k margin): {mism}"
     np.testing.assert_allclose(res.size.cpu().numpy(), g["size"], rtol=3e-5, atol=3e-5)
     np.testing.assert_allclose(res.center.cpu().numpy(), g["center"], rtol=0, atol=2e-3)
     np.testing.assert_allclose(res.topk_size.cpu().numpy(), g["topk_size"], rtol=3e-5, atol=3e-5)
@@ -59,7 +58,7 @@ def test_fused_route_fp16_tokens(dev, golden_dir):
     x16 = x.astype(np.float16)
     plan = mn.RoutePlan(grid, radius, r_list, device=dev)
     res = plan(torch.from_numpy(x16).to(dev), torch.from_numpy(metrics).to(dev))
-    np.testing.assert_array_equal(res.topk_idx.cpu().numpy(), g["topk_idx"])
+    assert not carrier_mismatches(res.topk_idx.cpu().numpy(), g["topk_idx"], g["center"])
     ref = O.route_and_gather(x16.astype(np.float32), metrics, r_list, O.Geometry(grid, radius))
     assert res.topk_x.dtype == torch.float16
     assert rel_err(res.topk_x.float().cpu().numpy(), ref["topk_x"]) <= 1e-2
@@ -76,7 +75,7 @@ def test_fused_route_bf16_grid48(dev):
     plan = mn.RoutePlan(grid, 3.0, r_list, device=dev)
     res = plan(x_bf.to(dev), m_bf.to(dev))
     ref = O.route_and_gather(x_bf.float().numpy(), m_bf.float().numpy(), r_list, O.Geometry(grid, 3.0))
-    mism = _report_mismatch(res.topk_idx.cpu().numpy(), ref["topk_idx"],
+    mism = _report_mismatch(res.topk_idx.cpu().numpy(), ref["topk_idx"], ref["center"],
                             O.carrier_margin(ref["size"], plan.k))
     assert not mism, mism
     assert rel_err(res.topk_x.float().cpu().numpy(), ref["topk_x"]) <= 1e-2
@@ -111,11 +110,15 @@ def test_fused_route_full_batch_properties(dev):
     cen = torch.gather(res.center[:, 1:], 1, res.topk_idx)
     assert bool((cen[:, 1:] >= cen[:, :-1]).all())
     assert torch.equal(res.topk_x[:, 0], xt[:, 0])
-    # every carrier row is a gathered token row of the routed sequence: spot
-    # check three images against the oracle on the same shard
+    # the whole shard against the oracle: exact carrier sets, order up to
+    # float32-tied centres, features within 2e-3
     ref = O.route_and_gather(x, metrics, canonical_r_list(grid), O.Geometry(grid, 3.0))
-    np.testing.assert_array_equal(res.topk_idx.cpu().numpy(), ref["topk_idx"])
-    assert rel_err(res.topk_x.cpu().numpy(), ref["topk_x"]) <= 2e-3
+    mism = _report_mismatch(res.topk_idx.cpu().numpy(), ref["topk_idx"], ref["center"],
+                            O.carrier_margin(ref["size"], plan.k))
+    assert not mism, mism
+    np.testing.assert_allclose(res.size.cpu().numpy(), ref["size"], rtol=3e-5, atol=3e-5)
+    same = (res.topk_idx.cpu().numpy() == ref["topk_idx"]).all(1)
+    assert rel_err(res.topk_x.cpu().numpy()[same], ref["topk_x"][same]) <= 2e-3
 
 
 def test_route_budget_fails_closed(dev):
@@ -264,6 +267,6 @@ def test_empty_batches(dev):
     b = torch.empty(0, 8, 9, device=dev)
     e = torch.empty(0, 7, dtype=torch.long, device=dev)
     s, ri, rv = mn.sparse_spatial_score(a, b, nbr, val, e, torch.empty(0, 8, dtype=torch.long, device=dev))
-    assert s.shape == (0, 7, 9)
-    out = mn.sparse_weighted_transport(torch.empty(0, 7, 9, device=dev), a, ri, rv, 8)
+    assert s.shape == (0, 7, nbr.shape[1])
+    out = mn.sparse_weighted_transport(torch.empty(0, 7, nbr.shape[1], device=dev), a, ri, rv, 8)
     assert out.shape == (0, 8, 9)
