@@ -43,6 +43,7 @@ extern "C" {
 #define MN_STATUS_INFEASIBLE_BUDGET 1
 #define MN_STATUS_DEGENERATE_RANGE 2 /* ThreTopK global max == min */
 #define MN_STATUS_TOO_MANY_EDGES 4
+#define MN_STATUS_TC_TIMEOUT 256     /* a bounded tensor-core wait gave up */
 
 /* Library version, for the loader's sanity check. */
 int mn_version(void);
@@ -206,13 +207,17 @@ int mn_carrier_scatter(int batch, int k, int num_patches, int channels,
  *        rounded to the q/k/v dtype like the reference's extra column.
  * window: |i - j| <= window; window < 0 means global attention.
  * cls_global: 1 = row 0 attends to every key (the LocalAttention CLS row).
- * scale: softmax scale (1/sqrt(D) in the reference). */
+ * scale: softmax scale (1/sqrt(D) in the reference).
+ * fp16 / bf16 with head_dim 64 run on the tensor cores (tcgen05, fp32
+ * accumulation, probabilities rounded to the input type for P.V as
+ * FlashAttention does); other shapes on CUDA cores in fp32.
+ * status: optional device int; bit 8 set if a tensor-core wait timed out. */
 int mn_local_attention(int batch, int tokens, int heads, int head_dim,
                        int dtype, const void* q, const void* k, const void* v,
                        int64_t s_b, int64_t s_n, int64_t s_h,
                        const void* bias, int bias_dtype, int window,
                        int cls_global, float scale, void* out, int out_dtype,
-                       void* stream);
+                       int* status, void* stream);
 
 /* Attention of nq query rows over nk key rows, optionally windowed
  * (|i - j| <= window, window < 0 = every key): the recovery cross-attention
@@ -223,7 +228,7 @@ int mn_attention(int batch, int nq, int nk, int heads, int head_dim, int dtype,
                  const void* q, int64_t q_sb, int64_t q_sn, int64_t q_sh,
                  const void* k, const void* v, int64_t kv_sb, int64_t kv_sn,
                  int64_t kv_sh, int window, float scale, void* out,
-                 int out_dtype, void* stream);
+                 int out_dtype, int* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -19,6 +19,7 @@ MN_OK = 0
 MN_ERR_ARG, MN_ERR_UNSUPPORTED, MN_ERR_WORKSPACE, MN_ERR_LAUNCH = -1, -2, -3, -4
 MN_INFEASIBLE_BUDGET = 1
 MN_STATUS_INFEASIBLE_BUDGET, MN_STATUS_DEGENERATE_RANGE, MN_STATUS_TOO_MANY_EDGES = 1, 2, 4
+MN_STATUS_TC_TIMEOUT = 256
 
 _DTYPES = {torch.float32: MN_F32, torch.float16: MN_F16, torch.bfloat16: MN_BF16}
 
@@ -62,9 +63,9 @@ _SIGNATURES = {
     "mn_dtem_select": (c_int, [c_int, c_int, c_int, _P, _P, c_int, c_float, c_float, _P, _P, c_size_t, _P, _P]),
     "mn_carrier_scatter": (c_int, [c_int, c_int, c_int, c_int, c_int, _P, _P, _P, _P]),
     "mn_local_attention": (c_int, [c_int, c_int, c_int, c_int, c_int, _P, _P, _P, c_int64, c_int64, c_int64, _P,
-                                   c_int, c_int, c_int, c_float, _P, c_int, _P]),
+                                   c_int, c_int, c_int, c_float, _P, c_int, _P, _P]),
     "mn_attention": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, _P, c_int64, c_int64, c_int64, _P, _P,
-                             c_int64, c_int64, c_int64, c_int, c_float, _P, c_int, _P]),
+                             c_int64, c_int64, c_int64, c_int, c_float, _P, c_int, _P, _P]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -10,6 +10,23 @@ import torch
 from . import _lib as L
 
 
+_STATUS = {}
+
+
+def _status(dev):
+    """Per-device status word the attention kernels OR error bits into."""
+    key = (dev.type, dev.index)
+    if key not in _STATUS:
+        _STATUS[key] = torch.zeros(1, dtype=torch.int32, device=dev)
+    return _STATUS[key]
+
+
+def attention_status(device=None):
+    """Error bits recorded by attention kernels on ``device`` (synchronises)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    return int(_status(dev).item())
+
+
 def _strides_bnhd(t: torch.Tensor):
     if t.stride(-1) != 1:
         raise ValueError("the head dimension must be contiguous")
@@ -38,7 +55,8 @@ def _launch(q, k, v, bias, window, cls_global, scale, out_dtype):
         bias_code = L.dtype_code(bias_c.dtype)
     L.check(L.lib().mn_local_attention(b, n, h, d, L.dtype_code(q.dtype), L.ptr(q), L.ptr(k), L.ptr(v), sb, sn, sh,
                                        L.ptr(bias_c), bias_code, int(window), int(bool(cls_global)), float(scale),
-                                       L.ptr(out), L.dtype_code(out_dtype), L.stream_of(q)), "mn_local_attention")
+                                       L.ptr(out), L.dtype_code(out_dtype), L.ptr(_status(dev)), L.stream_of(q)),
+            "mn_local_attention")
     return out
 
 
@@ -141,5 +159,5 @@ def cross_attention(q, k, v, scale=None, out_dtype=None, window=-1):
     out = torch.empty(b, nq, h, d, device=dev, dtype=out_dtype)
     L.check(L.lib().mn_attention(b, nq, nk, h, d, L.dtype_code(q.dtype), L.ptr(q), qsb, qsn, qsh, L.ptr(k), L.ptr(v),
                                  ksb, ksn, ksh, int(window), scale, L.ptr(out), L.dtype_code(out_dtype),
-                                 L.stream_of(q)), "mn_attention")
+                                 L.ptr(_status(dev)), L.stream_of(q)), "mn_attention")
     return out

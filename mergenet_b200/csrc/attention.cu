@@ -13,6 +13,10 @@
 
 namespace mn {
 
+bool attention_tc(int dtype, const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v,
+                  int64_t kb, int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int D, int window, float scale,
+                  const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st);
+
 constexpr int kLocalQT = 32;  // queries per CTA
 
 template <typename ET>
@@ -259,12 +263,15 @@ using namespace mn;
 extern "C" int mn_attention(int batch, int nq, int nk, int heads, int head_dim, int dtype, const void* q,
                             int64_t q_sb, int64_t q_sn, int64_t q_sh, const void* k, const void* v, int64_t kv_sb,
                             int64_t kv_sn, int64_t kv_sh, int window, float scale, void* out, int out_dtype,
-                            void* stream) {
+                            int* status, void* stream) {
   if (batch < 0 || nq < 0 || nk <= 0 || heads <= 0 || head_dim <= 0 || head_dim > 128 || !out) return MN_ERR_ARG;
   if ((int64_t)batch * nq == 0) return MN_OK;
   if (!q || !k || !v || dtype < 0 || dtype > 2 || out_dtype < 0 || out_dtype > 2) return MN_ERR_ARG;
   cudaGetLastError();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (attention_tc(dtype, q, q_sb, q_sn, q_sh, k, v, kv_sb, kv_sn, kv_sh, batch, nq, nk, heads, head_dim, window,
+                   scale, nullptr, 0, out, out_dtype, status, st))
+    return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
   const size_t smem = ((size_t)kXQ * head_dim + 2 * (size_t)kXK * (head_dim + 1)) * sizeof(float);
   const dim3 grid((nq + kXQ - 1) / kXQ, heads, batch);
   auto run = [&](auto tag) {
@@ -284,7 +291,7 @@ extern "C" int mn_attention(int batch, int nq, int nk, int heads, int head_dim, 
 extern "C" int mn_local_attention(int batch, int tokens, int heads, int head_dim, int dtype, const void* q,
                                   const void* k, const void* v, int64_t s_b, int64_t s_n, int64_t s_h,
                                   const void* bias, int bias_dtype, int window, int cls_global, float scale,
-                                  void* out, int out_dtype, void* stream) {
+                                  void* out, int out_dtype, int* status, void* stream) {
   if (batch < 0 || tokens < 0 || heads <= 0 || head_dim <= 0 || head_dim > 128 || !out) return MN_ERR_ARG;
   if ((int64_t)batch * tokens == 0) return MN_OK;
   if (!q || !k || !v) return MN_ERR_ARG;
@@ -300,13 +307,18 @@ extern "C" int mn_local_attention(int batch, int tokens, int heads, int head_dim
   cudaGetLastError();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid((tokens + kLocalQT - 1) / kLocalQT, heads, batch);
+  const bool tensor_core = window >= 0 && attention_tc(dtype, q, s_b, s_n, s_h, k, v, s_b, s_n, s_h, batch, tokens,
+                                                       tokens, heads, head_dim, window, scale, bias, bias_dtype, out,
+                                                       out_dtype, status, st);
   auto run = [&](auto tag) {
     using ET = decltype(tag);
-    cudaFuncSetAttribute(local_attn_kernel<ET>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    local_attn_kernel<ET><<<grid, 256, smem, st>>>(static_cast<const ET*>(q), static_cast<const ET*>(k),
-                                                   static_cast<const ET*>(v), s_b, s_n, s_h, tokens, heads,
-                                                   head_dim, bias, bias_dtype, window, scale, out, out_dtype,
-                                                   cls_row ? 1 : 0);
+    if (!tensor_core) {
+      cudaFuncSetAttribute(local_attn_kernel<ET>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      local_attn_kernel<ET><<<grid, 256, smem, st>>>(static_cast<const ET*>(q), static_cast<const ET*>(k),
+                                                     static_cast<const ET*>(v), s_b, s_n, s_h, tokens, heads,
+                                                     head_dim, bias, bias_dtype, window, scale, out, out_dtype,
+                                                     cls_row ? 1 : 0);
+    }
     if (cls_row) {
       cudaFuncSetAttribute(cls_row_kernel<ET>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_cls);
       cls_row_kernel<ET><<<dim3(heads, batch), 256, smem_cls, st>>>(

@@ -1,0 +1,311 @@
+// Tensor-core (tcgen05 + TMEM) attention for head_dim 64, fp16 / bf16.
+//
+// One CTA of 128 threads owns 128 query rows of one (image, head); thread t
+// owns row t, which is TMEM lane t of the accumulators.  Keys and values are
+// staged in 128B-swizzled shared memory, S = Q K^T is accumulated in TMEM by
+// tcgen05.mma issued from one thread, each thread turns its S row into fp16 /
+// bf16 probabilities in shared memory, and O = P V accumulates in TMEM.
+//
+//   window >= 0: sliding window |i - j| <= window over one sequence (the
+//     LocalAttention path, opentome/timm/bias_local_attn.py:486-625 / :243-483):
+//     the 128 + 2*window keys of the tile form a single block, no rescaling.
+//   window <  0: every key (the recovery cross-attention core,
+//     opentome/models/mergenet/model.py:173-188): 128-key blocks with an
+//     online softmax; O is rescaled in TMEM when a row maximum grows.
+//
+// Every wait on the tensor core is bounded; on timeout the CTA records an
+// error bit and stops issuing work.
+#include <algorithm>
+
+#include "common.cuh"
+#include "tc_common.cuh"
+
+namespace mn {
+
+constexpr int kTcD = 64;
+constexpr int kTcM = 128;
+
+template <int NB>
+struct TcSmem {
+  static constexpr int kPAtoms = (NB + 63) / 64;
+  static constexpr uint32_t q_off = 0;
+  static constexpr uint32_t k_off = q_off + kTcM * 128;
+  static constexpr uint32_t v_off = k_off + NB * 128;
+  static constexpr uint32_t p_off = (v_off + NB * 128 + 1023) & ~1023u;
+  static constexpr uint32_t bias_off = p_off + kPAtoms * kTcM * 128;
+  static constexpr uint32_t bar_off = bias_off + NB * 4;
+  static constexpr uint32_t tmem_slot_off = bar_off + 8;
+  static constexpr uint32_t bytes = tmem_slot_off + 8 + 1024;  // + alignment slack
+};
+
+template <typename ET>
+__device__ __forceinline__ uint4 pack8(const float* p) {
+  uint4 r;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    ET lo = from_f32<ET>(p[2 * i]), hi = from_f32<ET>(p[2 * i + 1]);
+    w[i] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+  }
+  return r;
+}
+
+// Stage `rows` rows of 64 elements (16B chunks) into a 128B-swizzled tile;
+// rows outside [0, valid) are zero.
+template <typename ET>
+__device__ __forceinline__ void stage_rows(uint8_t* tile, const ET* src, int64_t row_stride, int first, int rows,
+                                           int valid) {
+  for (int idx = threadIdx.x; idx < rows * 8; idx += blockDim.x) {
+    const int r = idx >> 3, c = idx & 7;
+    const int gr = first + r;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (gr >= 0 && gr < valid) val = *reinterpret_cast<const uint4*>(src + (int64_t)gr * row_stride + c * 8);
+    *reinterpret_cast<uint4*>(tile + tc::sw128_off(r, c)) = val;
+  }
+}
+
+template <typename ET, int NB>
+__global__ void __launch_bounds__(128) attn_tc_kernel(
+    const ET* __restrict__ q, int64_t qb, int64_t qn, int64_t qh, const ET* __restrict__ k,
+    const ET* __restrict__ v, int64_t kb, int64_t kn, int64_t kh, int Nq, int Nk, int H, int window, float scale,
+    const void* __restrict__ bias, int bias_dtype, void* __restrict__ out, int out_dtype, int* __restrict__ err) {
+  using S = TcSmem<NB>;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = base + S::q_off;
+  uint8_t* sk = base + S::k_off;
+  uint8_t* sv = base + S::v_off;
+  uint8_t* sp = base + S::p_off;
+  float* sbias = reinterpret_cast<float*>(base + S::bias_off);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(base + S::bar_off);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + S::tmem_slot_off);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int q0 = blockIdx.x * kTcM, h = blockIdx.y, b = blockIdx.z;
+  const ET* qbase = q + (int64_t)b * qb + (int64_t)h * qh;
+  const ET* kbase = k + (int64_t)b * kb + (int64_t)h * kh;
+  const ET* vbase = v + (int64_t)b * kb + (int64_t)h * kh;
+  constexpr int ab_bf16 = std::is_same<ET, __nv_bfloat16>::value ? 1 : 0;
+  constexpr uint32_t idesc_s = tc::idesc_f16(ab_bf16, 0, kTcM, NB);
+  constexpr uint32_t idesc_o = tc::idesc_f16(ab_bf16, 1, kTcM, kTcD);
+
+  if (warp == 0) tc::tmem_alloc(tmem_slot, 256);
+  if (tid == 0) tc::mbar_init(bar, 1);
+  stage_rows<ET>(sq, qbase, qn, q0, kTcM, Nq);
+  tc::fence_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem, t_o = tmem + NB;
+  const uint32_t lane_sel = (uint32_t)(warp * 32) << 16;
+
+  const int qi = q0 + tid;  // this thread's query row
+  int klo = 0, khi = Nk;
+  if (window >= 0) {
+    klo = max(0, q0 - window);
+    khi = min(Nk, q0 + kTcM + window);
+  }
+  const int nblocks = (khi - klo + NB - 1) / NB;
+  float m_run = -INFINITY, l_run = 0.f;
+  uint32_t phase = 0;
+  bool ok = true;
+  const float kLog2e = 1.4426950408889634f;
+
+  for (int blk = 0; blk < nblocks && ok; ++blk) {
+    const int kstart = klo + blk * NB;
+    if (blk > 0) {  // the previous P.V must finish reading K/V/P before they are overwritten
+      ok = tc::mbar_wait(bar, phase);
+      phase ^= 1;
+      if (!ok) break;
+    }
+    stage_rows<ET>(sk, kbase, kn, kstart, NB, khi);
+    stage_rows<ET>(sv, vbase, kn, kstart, NB, khi);
+    for (int j = tid; j < NB; j += blockDim.x) {
+      float bv = 0.f;
+      if (bias && kstart + j < khi) bv = to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)b * Nk + kstart + j)));
+      sbias[j] = bv;
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t aq = tc::smem_u32(sq), ak = tc::smem_u32(sk);
+#pragma unroll
+      for (int kk = 0; kk < kTcD / 16; ++kk)
+        tc::mma_f16_ss(t_s, tc::sw128_desc(aq + kk * 32, 16), tc::sw128_desc(ak + kk * 32, 16), idesc_s, kk > 0);
+      tc::mma_commit(bar);
+    }
+    ok = tc::mbar_wait(bar, phase);
+    phase ^= 1;
+    if (!ok) break;
+    tc::fence_after_sync();
+
+    // this row's legal keys, relative to the block
+    int jlo = 0, jhi = min(NB, khi - kstart);  // [jlo, jhi)
+    if (window >= 0) {
+      jlo = max(jlo, qi - window - kstart);
+      jhi = min(jhi, qi + window + 1 - kstart);
+    }
+    if (qi >= Nq) jhi = jlo;  // padding rows: no keys
+    // the warp's column chunks that can hold a legal key
+    const int wlo = __reduce_min_sync(0xffffffffu, (unsigned)max(0, min(jlo, NB)));
+    const int whi = __reduce_max_sync(0xffffffffu, (unsigned)max(0, jhi));
+    const int c_lo = wlo >> 5, c_hi = (whi + 31) >> 5;  // [c_lo, c_hi)
+    float mx = -INFINITY;
+    float sc[32];
+    for (int c = c_lo; c < c_hi; ++c) {
+      tc::tmem_ld32(t_s + lane_sel + c * 32, sc);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int j = c * 32 + i;
+        if (j >= jlo && j < jhi) mx = fmaxf(mx, sc[i] * scale + sbias[j]);
+      }
+    }
+    const float m_new = fmaxf(m_run, mx);
+    const float corr = (m_run == -INFINITY) ? 0.f : exp2f((m_run - m_new) * kLog2e);
+    float lsum = 0.f;
+    // probabilities -> P (all NB columns; zero outside this row's keys)
+    for (int c = 0; c < NB / 32; ++c) {
+      float p[32];
+      if (c >= c_lo && c < c_hi) {
+        tc::tmem_ld32(t_s + lane_sel + c * 32, sc);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int j = c * 32 + i;
+          const bool legal = j >= jlo && j < jhi;
+          p[i] = legal ? exp2f((sc[i] * scale + sbias[j] - m_new) * kLog2e) : 0.f;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) p[i] = 0.f;
+      }
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const uint4 pk = pack8<ET>(p + 8 * g);
+        // round-tripped values enter the sum, as the tensor core sees them
+        const ET* pe = reinterpret_cast<const ET*>(&pk);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) lsum += to_f32(pe[i]);
+        const int key8 = c * 4 + g;  // 8-key chunk index
+        const int atom = key8 >> 3, chunk = key8 & 7;
+        *reinterpret_cast<uint4*>(sp + atom * (kTcM * 128) + tc::sw128_off(tid, chunk)) = pk;
+      }
+    }
+    if (NB % 32 != 0) {  // the tail columns (NB not a multiple of 32)
+      for (int key8 = (NB / 32) * 4; key8 < NB / 8; ++key8) {
+        float p[8];
+        for (int i = 0; i < 8; ++i) p[i] = 0.f;
+        const uint4 pk = pack8<ET>(p);
+        *reinterpret_cast<uint4*>(sp + (key8 >> 3) * (kTcM * 128) + tc::sw128_off(tid, key8 & 7)) = pk;
+      }
+    }
+    // rescale the running output rows (warp-collective TMEM access: the
+    // whole warp takes part when any of its rows needs it)
+    if (blk > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+      float o[32];
+#pragma unroll
+      for (int c = 0; c < kTcD / 32; ++c) {
+        tc::tmem_ld32(t_o + lane_sel + c * 32, o);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] *= corr;
+        tc::tmem_st32(t_o + lane_sel + c * 32, o);
+      }
+    }
+    l_run = l_run * corr + lsum;
+    m_run = m_new;
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t ap = tc::smem_u32(sp), av = tc::smem_u32(sv);
+#pragma unroll
+      for (int kk = 0; kk < NB / 16; ++kk)
+        tc::mma_f16_ss(t_o, tc::sw128_desc(ap + (kk >> 2) * (kTcM * 128) + (kk & 3) * 32, 16),
+                       tc::sw128_desc(av + kk * 2048, 16384), idesc_o, (blk > 0 || kk > 0) ? 1u : 0u);
+      tc::mma_commit(bar);
+    }
+  }
+  if (ok && nblocks > 0) {
+    ok = tc::mbar_wait(bar, phase);
+    tc::fence_after_sync();
+  }
+  if (ok && nblocks > 0) {
+    const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+    const int64_t obase = (((int64_t)b * Nq + qi) * H + h) * kTcD;
+#pragma unroll
+    for (int c = 0; c < kTcD / 32; ++c) {
+      float o[32];
+      tc::tmem_ld32(t_o + lane_sel + c * 32, o);  // warp-collective: every row loads
+      if (qi >= Nq) continue;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] *= inv;
+      if (out_dtype == MN_F32) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + obase + c * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+      } else if (out_dtype == MN_F16) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(out) + obase + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = pack8<__half>(o + 8 * i);
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + obase + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = pack8<__nv_bfloat16>(o + 8 * i);
+      }
+    }
+  }
+  if (!ok && tid == 0 && err) atomicOr(err, MN_STATUS_TC_TIMEOUT);
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, 256);
+}
+
+template <typename ET, int NB>
+static void launch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v, int64_t kb,
+                      int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int window, float scale,
+                      const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st) {
+  const size_t smem = TcSmem<NB>::bytes;
+  auto kern = attn_tc_kernel<ET, NB>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid((Nq + kTcM - 1) / kTcM, H, B);
+  kern<<<grid, 128, smem, st>>>(static_cast<const ET*>(q), qb, qn, qh, static_cast<const ET*>(k),
+                                static_cast<const ET*>(v), kb, kn, kh, Nq, Nk, H, window, scale, bias, bias_dtype,
+                                out, out_dtype, err);
+}
+
+// Host-side dispatch used by mn_local_attention / mn_attention.  Returns
+// false when the shape is not one the tensor-core kernel covers.
+bool attention_tc(int dtype, const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v,
+                  int64_t kb, int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int D, int window, float scale,
+                  const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st) {
+  if (D != kTcD || (dtype != MN_F16 && dtype != MN_BF16)) return false;
+  // 16-byte aligned rows for the vector loads
+  auto aligned = [](const void* p, int64_t s1, int64_t s2, int64_t s3) {
+    return (reinterpret_cast<uintptr_t>(p) % 16 == 0) && s1 % 8 == 0 && s2 % 8 == 0 && s3 % 8 == 0;
+  };
+  if (!aligned(q, qb, qn, qh) || !aligned(k, kb, kn, kh) || !aligned(v, kb, kn, kh)) return false;
+  if (window >= 0) {
+    const int need = kTcM + 2 * window;
+    if (need <= 160) {
+      if (dtype == MN_F16)
+        launch_tc<__half, 160>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
+                               out_dtype, err, st);
+      else
+        launch_tc<__nv_bfloat16, 160>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
+                                      out, out_dtype, err, st);
+      return true;
+    }
+  }
+  if (dtype == MN_F16)
+    launch_tc<__half, 128>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
+                           out_dtype, err, st);
+  else
+    launch_tc<__nv_bfloat16, 128>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
+                                  out, out_dtype, err, st);
+  return true;
+}
+
+}  // namespace mn

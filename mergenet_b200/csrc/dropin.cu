@@ -392,10 +392,10 @@ extern "C" int mn_sparse_weighted_transport(int batch, int num_donors, int num_r
                                             const int64_t* receiver_indices, const uint8_t* receiver_valid,
                                             void* out, int* status, void* stream) {
   if (batch < 0 || num_donors < 0 || num_receivers <= 0 || k <= 0 || channels <= 0) return MN_ERR_ARG;
+  if (batch == 0) return MN_OK;
   if (!out) return MN_ERR_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t elem = dtype == MN_F32 ? 4 : 2;
-  if (batch == 0) return MN_OK;
   cudaGetLastError();
   if (num_donors == 0) {
     cudaMemsetAsync(out, 0, (size_t)batch * num_receivers * channels * elem, st);

@@ -75,10 +75,12 @@ def test_unbiased_parity_layouts(dev):
     v = torch.randn_like(q)
     out = mn.unbiased_local_attention(q, k, v, 16)
     exp = reference_bhnd(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), None, 16).transpose(1, 2)
-    torch.testing.assert_close(out.float(), exp, atol=2e-3, rtol=2e-3)
+    # head_dim 64 runs on the tensor cores with P rounded to fp16 (as FlashAttention does)
+    torch.testing.assert_close(out.float(), exp, atol=5e-3, rtol=5e-3)
     out2 = mn.unbiased_local_attention(q.transpose(1, 2).contiguous(), k.transpose(1, 2).contiguous(),
                                        v.transpose(1, 2).contiguous(), 16)
-    torch.testing.assert_close(out2.transpose(1, 2).float(), exp, atol=2e-3, rtol=2e-3)
+    torch.testing.assert_close(out2.transpose(1, 2).float(), exp, atol=5e-3, rtol=5e-3)
+    assert mn.attention.attention_status(dev) == 0
 
 
 def test_locality(dev):
@@ -125,7 +127,7 @@ def test_local_block_attention_cls_global(dev, dtype):
     cls = torch.softmax(q[:, :, :1].float() @ k.float().transpose(-1, -2) / 8.0, -1) @ v.float()
     exp[:, :, :1] = cls
     exp = exp.transpose(1, 2).reshape(b, n, h * d)
-    tol = 1e-2 if dtype == torch.bfloat16 else 3e-3
+    tol = 2e-2 if dtype == torch.bfloat16 else 5e-3
     torch.testing.assert_close(out.float(), exp, atol=tol, rtol=tol)
 
 
@@ -141,3 +143,38 @@ def test_config3_biased_block_against_oracle(dev):
                            bias=bias.astype(np.float32))
     err = np.abs(out.float().cpu().numpy() - exp).max() / np.abs(exp).max()
     assert err <= 1e-2
+
+
+@pytest.mark.parametrize("dtype,out_dtype", [(torch.float16, torch.float32), (torch.bfloat16, torch.bfloat16),
+                                             (torch.float16, torch.float16)])
+@pytest.mark.parametrize("nq,nk", [(393, 785), (128, 128), (9, 200), (300, 17)])
+def test_cross_attention(dev, dtype, out_dtype, nq, nk):
+    """Recovery cross-attention core (model.py:173-188): 393 carriers over 785
+    tokens, plus ragged query / key counts (partial tiles, one short block)."""
+    import mergenet_b200 as mn
+    torch.manual_seed(nq * 7 + nk)
+    b, h, d = 3, 6, 64
+    q = (torch.randn(b, nq, h, d, device=dev) * 0.5).to(dtype)
+    k = (torch.randn(b, nk, h, d, device=dev) * 0.5).to(dtype)
+    v = torch.randn(b, nk, h, d, device=dev).to(dtype)
+    out = mn.cross_attention(q, k, v, out_dtype=out_dtype)
+    exp = torch.softmax(q.float().transpose(1, 2) @ k.float().transpose(1, 2).transpose(-1, -2) / 8.0, -1) \
+        @ v.float().transpose(1, 2)
+    exp = exp.transpose(1, 2)
+    tol = 2e-2 if torch.bfloat16 in (dtype, out_dtype) else 5e-3
+    torch.testing.assert_close(out.float(), exp, atol=tol, rtol=tol)
+    assert mn.attention.attention_status(dev) == 0
+
+
+def test_cross_attention_strided_projection_views(dev):
+    """q/k/v as head views of [B, N, 384] projections, fp32 context out."""
+    import mergenet_b200 as mn
+    torch.manual_seed(5)
+    b = 2
+    qp = torch.randn(b, 393, 384, device=dev).half()
+    kvp = torch.randn(b, 785, 768, device=dev).half()
+    k, v = kvp[..., :384].view(b, 785, 6, 64), kvp[..., 384:].view(b, 785, 6, 64)
+    out = mn.cross_attention(qp.view(b, 393, 6, 64), k, v, out_dtype=torch.float32)
+    exp = torch.nn.functional.scaled_dot_product_attention(
+        qp.view(b, 393, 6, 64).transpose(1, 2).float(), k.transpose(1, 2).float(), v.transpose(1, 2).float())
+    torch.testing.assert_close(out, exp.transpose(1, 2), atol=5e-3, rtol=5e-3)
