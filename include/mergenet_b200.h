@@ -230,6 +230,16 @@ int mn_attention(int batch, int nq, int nk, int heads, int head_dim, int dtype,
                  int64_t kv_sh, int window, float scale, void* out,
                  int out_dtype, int* status, void* stream);
 
+/* Residual add + LayerNorm + fp16 cast over rows of a fp32 residual stream
+ * (the norm1/norm2 inputs of the LocalBlock / latent Block forward under fp16
+ * autocast, opentome/timm/bias_local_attn.py:867-868): s = x + y (y fp16,
+ * optional); x_out = s (fp32, optional, may alias x); h_ln = LayerNorm(s)
+ * (fp16, optional; gamma/beta fp32); h_raw = fp16(s) (optional).
+ * channels in {256, 384, 512, 768}. */
+int mn_add_layernorm(int64_t rows, int channels, const float* x, const void* y,
+                     const float* gamma, const float* beta, float eps,
+                     float* x_out, void* h_ln, void* h_raw, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

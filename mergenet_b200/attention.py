@@ -127,15 +127,17 @@ def biased_local_attention(q, k, v, bias, local_window, *, logical_dim: Optional
     return o.transpose(1, 2).contiguous()
 
 
-def local_attention_packed(qkv, num_heads, local_window, cls_global=True, out_dtype=None):
+def local_attention_packed(qkv, num_heads, local_window, cls_global=True, out_dtype=None, bias=None):
     """LocalAttention's core on the packed qkv projection [B, N, 3*H*D]
     (bias_local_attn.py:687-721 inference layout): q, k, v are read in place
-    through strides; returns [B, N, H*D]."""
+    through strides; returns [B, N, H*D].  ``local_window < 0`` attends to
+    every key; ``bias`` [B, N] adds a per-key bias (rounded to the qkv dtype,
+    as SDPA's autocast rounds the float mask)."""
     b, n, c3 = qkv.shape
     d = c3 // (3 * num_heads)
     view = qkv.view(b, n, 3, num_heads, d)
     q, k, v = view[:, :, 0], view[:, :, 1], view[:, :, 2]
-    o = _launch(q, k, v, None, local_window, cls_global, 1.0 / math.sqrt(d), out_dtype or qkv.dtype)
+    o = _launch(q, k, v, bias, local_window, cls_global, 1.0 / math.sqrt(d), out_dtype or qkv.dtype)
     return o.view(b, n, num_heads * d)
 
 

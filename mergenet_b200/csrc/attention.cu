@@ -115,10 +115,20 @@ __global__ void __launch_bounds__(256) cls_row_kernel(const ET* __restrict__ q, 
   for (int c = threadIdx.x; c < D; c += blockDim.x) qv[c] = to_f32(q[base + c]);
   __syncthreads();
   float mx = -INFINITY, dummy = INFINITY;
+  const bool vec = (D % 8 == 0) && (sn % 8 == 0) && ((reinterpret_cast<uintptr_t>(k + base) & 15) == 0);
   for (int j = threadIdx.x; j < N; j += blockDim.x) {
     const ET* kr = k + base + (int64_t)j * sn;
     float acc = 0.f;
-    for (int c = 0; c < D; ++c) acc = fmaf(qv[c], to_f32(kr[c]), acc);
+    if (vec) {
+      for (int c = 0; c < D; c += 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(kr + c);
+        const ET* e = reinterpret_cast<const ET*>(&u);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc = fmaf(qv[c + i], to_f32(e[i]), acc);
+      }
+    } else {
+      for (int c = 0; c < D; ++c) acc = fmaf(qv[c], to_f32(kr[c]), acc);
+    }
     float s = acc * scale;
     if (bias) s += to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)b * N + j)));
     p[j] = s;
@@ -300,16 +310,16 @@ extern "C" int mn_local_attention(int batch, int tokens, int heads, int head_dim
   const int W = window < 0 ? tokens : window;
   const int nk = std::min(tokens, kLocalQT + 2 * W);
   const size_t smem = ((size_t)2 * nk * (head_dim + 1) + nk + 8 * head_dim) * sizeof(float);
-  if (smem > 200 * 1024) return MN_ERR_UNSUPPORTED;
+  const bool tc_shape = head_dim == 64 && (dtype == MN_F16 || dtype == MN_BF16);
+  if (smem > 200 * 1024 && !tc_shape) return MN_ERR_UNSUPPORTED;
   const bool cls_row = cls_global && window >= 0 && tokens > 1;
   const size_t smem_cls = ((size_t)tokens + head_dim + 256) * sizeof(float);
   if (cls_row && (smem_cls > 200 * 1024 || head_dim > 256)) return MN_ERR_UNSUPPORTED;
   cudaGetLastError();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid((tokens + kLocalQT - 1) / kLocalQT, heads, batch);
-  const bool tensor_core = window >= 0 && attention_tc(dtype, q, s_b, s_n, s_h, k, v, s_b, s_n, s_h, batch, tokens,
-                                                       tokens, heads, head_dim, window, scale, bias, bias_dtype, out,
-                                                       out_dtype, status, st);
+  const bool tensor_core = attention_tc(dtype, q, s_b, s_n, s_h, k, v, s_b, s_n, s_h, batch, tokens, tokens, heads,
+                                        head_dim, window, scale, bias, bias_dtype, out, out_dtype, status, st);
   auto run = [&](auto tag) {
     using ET = decltype(tag);
     if (!tensor_core) {

@@ -27,16 +27,22 @@ constexpr int kTcM = 128;
 
 template <int NB>
 struct TcSmem {
+  // K is dead once S = Q K^T has completed, so one K buffer suffices; V is
+  // read by P.V while the next block streams in, so the multi-block path
+  // (NB = 128) keeps two V stages.  ~97 KB: two CTAs per SM.
+  static constexpr int kStages = NB == 128 ? 2 : 1;
   static constexpr int kPAtoms = (NB + 63) / 64;
   static constexpr uint32_t q_off = 0;
   static constexpr uint32_t k_off = q_off + kTcM * 128;
-  static constexpr uint32_t v_off = k_off + NB * 128;
-  static constexpr uint32_t p_off = (v_off + NB * 128 + 1023) & ~1023u;
+  static constexpr uint32_t kv_stage = NB * 128;
+  static constexpr uint32_t v_off = k_off + kv_stage;
+  static constexpr uint32_t p_off = (v_off + kStages * kv_stage + 1023) & ~1023u;
   static constexpr uint32_t bias_off = p_off + kPAtoms * kTcM * 128;
   static constexpr uint32_t bar_off = bias_off + NB * 4;
   static constexpr uint32_t tmem_slot_off = bar_off + 8;
   static constexpr uint32_t bytes = tmem_slot_off + 8 + 1024;  // + alignment slack
 };
+static_assert(TcSmem<160>::bytes <= 113 * 1024 && TcSmem<128>::bytes <= 113 * 1024, "two CTAs per SM");
 
 template <typename ET>
 __device__ __forceinline__ uint4 pack8(const float* p) {
@@ -50,17 +56,18 @@ __device__ __forceinline__ uint4 pack8(const float* p) {
   return r;
 }
 
-// Stage `rows` rows of 64 elements (16B chunks) into a 128B-swizzled tile;
-// rows outside [0, valid) are zero.
+// Issue asynchronous copies of `rows` rows of 64 elements (16B chunks) into a
+// 128B-swizzled tile; rows outside [0, valid) are zero-filled.
 template <typename ET>
 __device__ __forceinline__ void stage_rows(uint8_t* tile, const ET* src, int64_t row_stride, int first, int rows,
                                            int valid) {
+  const uint32_t base = tc::smem_u32(tile);
   for (int idx = threadIdx.x; idx < rows * 8; idx += blockDim.x) {
     const int r = idx >> 3, c = idx & 7;
     const int gr = first + r;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (gr >= 0 && gr < valid) val = *reinterpret_cast<const uint4*>(src + (int64_t)gr * row_stride + c * 8);
-    *reinterpret_cast<uint4*>(tile + tc::sw128_off(r, c)) = val;
+    const bool in = gr >= 0 && gr < valid;
+    const ET* g = in ? src + (int64_t)gr * row_stride + c * 8 : src;
+    tc::cp_async16(base + tc::sw128_off(r, c), g, in ? 16u : 0u);
   }
 }
 
@@ -91,8 +98,17 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
 
   if (warp == 0) tc::tmem_alloc(tmem_slot, 256);
   if (tid == 0) tc::mbar_init(bar, 1);
+  int klo = 0, khi = Nk;
+  if (window >= 0) {
+    klo = max(0, q0 - window);
+    khi = min(Nk, q0 + kTcM + window);
+  }
+  const int nblocks = (khi - klo + NB - 1) / NB;
+  // Q and the first K/V block in flight together
   stage_rows<ET>(sq, qbase, qn, q0, kTcM, Nq);
-  tc::fence_async_smem();
+  stage_rows<ET>(sk, kbase, kn, klo, NB, khi);
+  stage_rows<ET>(sv, vbase, kn, klo, NB, khi);
+  tc::cp_async_commit();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -101,12 +117,6 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
   const uint32_t lane_sel = (uint32_t)(warp * 32) << 16;
 
   const int qi = q0 + tid;  // this thread's query row
-  int klo = 0, khi = Nk;
-  if (window >= 0) {
-    klo = max(0, q0 - window);
-    khi = min(Nk, q0 + kTcM + window);
-  }
-  const int nblocks = (khi - klo + NB - 1) / NB;
   float m_run = -INFINITY, l_run = 0.f;
   uint32_t phase = 0;
   bool ok = true;
@@ -114,24 +124,21 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
 
   for (int blk = 0; blk < nblocks && ok; ++blk) {
     const int kstart = klo + blk * NB;
-    if (blk > 0) {  // the previous P.V must finish reading K/V/P before they are overwritten
-      ok = tc::mbar_wait(bar, phase);
-      phase ^= 1;
-      if (!ok) break;
-    }
-    stage_rows<ET>(sk, kbase, kn, kstart, NB, khi);
-    stage_rows<ET>(sv, vbase, kn, kstart, NB, khi);
+    const int stage = blk % S::kStages;
+    uint8_t* skb = sk;
+    uint8_t* svb = sv + stage * S::kv_stage;
     for (int j = tid; j < NB; j += blockDim.x) {
       float bv = 0.f;
       if (bias && kstart + j < khi) bv = to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)b * Nk + kstart + j)));
       sbias[j] = bv;
     }
+    tc::cp_async_wait<0>();  // this block's K/V (and Q) have landed
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
     if (tid == 0) {
       tc::fence_after_sync();
-      const uint32_t aq = tc::smem_u32(sq), ak = tc::smem_u32(sk);
+      const uint32_t aq = tc::smem_u32(sq), ak = tc::smem_u32(skb);
 #pragma unroll
       for (int kk = 0; kk < kTcD / 16; ++kk)
         tc::mma_f16_ss(t_s, tc::sw128_desc(aq + kk * 32, 16), tc::sw128_desc(ak + kk * 32, 16), idesc_s, kk > 0);
@@ -141,6 +148,14 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
     phase ^= 1;
     if (!ok) break;
     tc::fence_after_sync();
+    // S done (and with it the previous P.V): prefetch the next K/V block into
+    // the other stage while this block's softmax runs
+    if (blk + 1 < nblocks) {
+      const int ns = (blk + 1) % S::kStages;
+      stage_rows<ET>(sk, kbase, kn, kstart + NB, NB, khi);
+      stage_rows<ET>(sv + ns * S::kv_stage, vbase, kn, kstart + NB, NB, khi);
+      tc::cp_async_commit();
+    }
 
     // this row's legal keys, relative to the block
     int jlo = 0, jhi = min(NB, khi - kstart);  // [jlo, jhi)
@@ -220,7 +235,7 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
     __syncthreads();
     if (tid == 0) {
       tc::fence_after_sync();
-      const uint32_t ap = tc::smem_u32(sp), av = tc::smem_u32(sv);
+      const uint32_t ap = tc::smem_u32(sp), av = tc::smem_u32(svb);
 #pragma unroll
       for (int kk = 0; kk < NB / 16; ++kk)
         tc::mma_f16_ss(t_o, tc::sw128_desc(ap + (kk >> 2) * (kTcM * 128) + (kk & 3) * 32, 16),
@@ -228,6 +243,7 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
       tc::mma_commit(bar);
     }
   }
+  tc::cp_async_wait<0>();
   if (ok && nblocks > 0) {
     ok = tc::mbar_wait(bar, phase);
     tc::fence_after_sync();

@@ -1,0 +1,108 @@
+// Fused residual add + LayerNorm + fp16 cast for the fp32 residual streams of
+// the local and latent blocks.  Under fp16 autocast the reference computes
+// x = x + f(...) in fp32, LayerNorm in fp32 and casts the result to fp16 for
+// the next Linear (timm Block / LocalBlock forward,
+// opentome/timm/bias_local_attn.py:867-868); here one pass reads x (and the
+// fp16 branch output) once and writes the fp32 sum and the fp16 LayerNorm.
+#include "common.cuh"
+
+namespace mn {
+
+// One warp per row; C must be a multiple of 128 (four floats per lane-step).
+template <int C>
+__global__ void __launch_bounds__(256) add_layernorm_kernel(const float* __restrict__ x, const __half* __restrict__ y,
+                                                            const float* __restrict__ gamma,
+                                                            const float* __restrict__ beta, float eps, int64_t rows,
+                                                            float* __restrict__ x_out, __half* __restrict__ h_ln,
+                                                            __half* __restrict__ h_raw) {
+  constexpr int V = C / 128;  // float4 groups per lane
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * C);
+  float v[V][4];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const float4 a = xr[lane + 32 * i];
+    v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+  }
+  if (y) {
+    const uint2* yr = reinterpret_cast<const uint2*>(y + row * C);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const uint2 u = yr[lane + 32 * i];
+      const __half2 lo = *reinterpret_cast<const __half2*>(&u.x), hi = *reinterpret_cast<const __half2*>(&u.y);
+      v[i][0] += __low2float(lo); v[i][1] += __high2float(lo);
+      v[i][2] += __low2float(hi); v[i][3] += __high2float(hi);
+    }
+  }
+  if (x_out) {
+    float4* xo = reinterpret_cast<float4*>(x_out + row * C);
+#pragma unroll
+    for (int i = 0; i < V; ++i) xo[lane + 32 * i] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+  }
+  if (h_raw) {
+    uint2* hr = reinterpret_cast<uint2*>(h_raw + row * C);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      __half2 lo = __floats2half2_rn(v[i][0], v[i][1]), hi = __floats2half2_rn(v[i][2], v[i][3]);
+      uint2 u;
+      u.x = *reinterpret_cast<uint32_t*>(&lo);
+      u.y = *reinterpret_cast<uint32_t*>(&hi);
+      hr[lane + 32 * i] = u;
+    }
+  }
+  if (!h_ln) return;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) s += (v[i][0] + v[i][1]) + (v[i][2] + v[i][3]);
+  const float mean = warp_sum(s) * (1.0f / C);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d = v[i][j] - mean;
+      q = fmaf(d, d, q);
+    }
+  const float rstd = rsqrtf(warp_sum(q) * (1.0f / C) + eps);
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
+  uint2* hl = reinterpret_cast<uint2*>(h_ln + row * C);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const float4 g = g4[lane + 32 * i], bb = b4[lane + 32 * i];
+    const float o0 = (v[i][0] - mean) * rstd * g.x + bb.x, o1 = (v[i][1] - mean) * rstd * g.y + bb.y;
+    const float o2 = (v[i][2] - mean) * rstd * g.z + bb.z, o3 = (v[i][3] - mean) * rstd * g.w + bb.w;
+    __half2 lo = __floats2half2_rn(o0, o1), hi = __floats2half2_rn(o2, o3);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&lo);
+    u.y = *reinterpret_cast<uint32_t*>(&hi);
+    hl[lane + 32 * i] = u;
+  }
+}
+
+}  // namespace mn
+
+using namespace mn;
+
+extern "C" int mn_add_layernorm(int64_t rows, int channels, const float* x, const void* y, const float* gamma,
+                                const float* beta, float eps, float* x_out, void* h_ln, void* h_raw, void* stream) {
+  if (rows < 0 || channels <= 0) return MN_ERR_ARG;
+  if (rows == 0) return MN_OK;
+  if (!x || (h_ln && (!gamma || !beta))) return MN_ERR_ARG;
+  cudaGetLastError();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  const __half* yh = static_cast<const __half*>(y);
+  __half* hl = static_cast<__half*>(h_ln);
+  __half* hr = static_cast<__half*>(h_raw);
+  switch (channels) {
+    case 384: add_layernorm_kernel<384><<<grid, 256, 0, st>>>(x, yh, gamma, beta, eps, rows, x_out, hl, hr); break;
+    case 256: add_layernorm_kernel<256><<<grid, 256, 0, st>>>(x, yh, gamma, beta, eps, rows, x_out, hl, hr); break;
+    case 512: add_layernorm_kernel<512><<<grid, 256, 0, st>>>(x, yh, gamma, beta, eps, rows, x_out, hl, hr); break;
+    case 768: add_layernorm_kernel<768><<<grid, 256, 0, st>>>(x, yh, gamma, beta, eps, rows, x_out, hl, hr); break;
+    default: return MN_ERR_UNSUPPORTED;
+  }
+  return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
+}

@@ -9,12 +9,13 @@ embed, CLS, position embedding, six LocalBlocks), ``local.metric_layers.*``,
 
 The forward is the reference's inference path under fp16 autocast
 (model.py:1141-1222): fp16 GEMMs and attention inside fp32 residual
-streams, fp32 LayerNorms, fp32 routing, fp32 cross-attention projections.
-The hot path runs on the library: windowed local attention with the CLS row
-(bias_local_attn.py:679-724), the fused six-layer routing + carrier gather
-(model.py:574-590, :1157-1183) and the cross-attention core (model.py:173-188).
-GEMMs, LayerNorm and GELU are cuBLAS / ATen.  The latent blocks' biased
-global attention (opentome/timm/tome.py:50-54) runs on PyTorch SDPA.
+streams, fp32 LayerNorm statistics, fp32 routing.  The hot path runs on the
+library: windowed local attention with the CLS row (bias_local_attn.py:
+679-724), the fused six-layer routing + carrier gather (model.py:574-590,
+:1157-1183), the cross-attention core (model.py:173-188), the latent blocks'
+proportional attention (opentome/timm/tome.py:44-58) and the fused residual
+add + LayerNorm + fp16 cast around every block.  GEMMs and GELU are cuBLAS /
+ATen.
 """
 from __future__ import annotations
 
@@ -49,11 +50,11 @@ class _Mlp(nn.Module):
 
 
 class _Block(nn.Module):
-    def __init__(self, dim, mlp_ratio):
+    def __init__(self, dim, mlp_ratio, eps=1e-5):
         super().__init__()
-        self.norm1 = nn.LayerNorm(dim)
+        self.norm1 = nn.LayerNorm(dim, eps=eps)
         self.attn = _Attention(dim)
-        self.norm2 = nn.LayerNorm(dim)
+        self.norm2 = nn.LayerNorm(dim, eps=eps)
         self.mlp = _Mlp(dim, int(dim * mlp_ratio))
 
 
@@ -78,8 +79,9 @@ class _LatentVit(nn.Module):
     def __init__(self, img, patch, dim, depth, mlp_ratio):
         super().__init__()
         self.pos_embed = nn.Parameter(torch.zeros(1, (img // patch) ** 2, dim), requires_grad=False)
-        self.blocks = nn.ModuleList([_Block(dim, mlp_ratio) for _ in range(depth)])
-        self.norm = nn.LayerNorm(dim)
+        # timm VisionTransformer blocks and final norm use LayerNorm(eps=1e-6)
+        self.blocks = nn.ModuleList([_Block(dim, mlp_ratio, eps=1e-6) for _ in range(depth)])
+        self.norm = nn.LayerNorm(dim, eps=1e-6)
 
 
 class _Latent(nn.Module):
@@ -126,6 +128,7 @@ class MergeNetSmall(nn.Module):
         self.encode_cross_attention = CrossAttention(embed_dim, num_heads)
         self._plans = {}
         self._half = None
+        self._kv16 = None
 
     # ------------------------------------------------------------------ init
     @torch.no_grad()
@@ -161,6 +164,7 @@ class MergeNetSmall(nn.Module):
         tn(self.head.weight)
         self.head.bias.zero_()
         self._half = None
+        self._kv16 = None
         return self
 
     # ------------------------------------------------------------- execution
@@ -174,54 +178,59 @@ class MergeNetSmall(nn.Module):
         """fp16 copies of the GEMM weights autocast would cast on every call."""
         if self._half is None:
             self._half = {n: p.detach().half() for n, p in self.named_parameters()
-                          if p.ndim >= 2 and "encode_cross_attention" not in n and "pos_embed" not in n
-                          and "cls_token" not in n}
+                          if p.ndim >= 2 and "pos_embed" not in n and "cls_token" not in n}
         return self._half
 
     def _linear16(self, x, name, lin):
         w = self._weights16()[name + ".weight"]
         return F.linear(x.half(), w, lin.bias.half())
 
-    def _block_local(self, x, i, blk, metrics, w16):
-        b, n, c = x.shape
-        h = F.layer_norm(x, (c,), blk.norm1.weight, blk.norm1.bias)
+    def _metric(self, h_raw, i, metrics, w16):
+        lin = self.local.metric_layers[i]
+        torch.addmm(lin.bias.half(), h_raw.view(-1, h_raw.shape[-1]), w16[f"local.metric_layers.{i}.weight"].t(),
+                    out=metrics[i].view(-1, metrics.shape[-1]))
+
+    def _attn_local(self, h, i, blk):
         qkv = self._linear16(h, f"local.vit.blocks.{i}.attn.qkv", blk.attn.qkv)
         a = local_attention_packed(qkv, self.num_heads, self.local_window, cls_global=True)
-        x = x + self._linear16(a, f"local.vit.blocks.{i}.attn.proj", blk.attn.proj)
-        h = F.layer_norm(x, (c,), blk.norm2.weight, blk.norm2.bias)
-        h = F.gelu(self._linear16(h, f"local.vit.blocks.{i}.mlp.fc1", blk.mlp.fc1))
-        x = x + self._linear16(h, f"local.vit.blocks.{i}.mlp.fc2", blk.mlp.fc2)
-        lin = self.local.metric_layers[i]
-        torch.addmm(lin.bias.half(), x.view(-1, c).half(), w16[f"local.metric_layers.{i}.weight"].t(),
-                    out=metrics[i].view(-1, metrics.shape[-1]))
-        return x
+        return self._linear16(a, f"local.vit.blocks.{i}.attn.proj", blk.attn.proj)
 
-    def _block_latent(self, x, i, blk, log_size):
-        b, n, c = x.shape
-        hd = c // self.num_heads
-        h = F.layer_norm(x, (c,), blk.norm1.weight, blk.norm1.bias)
+    def _attn_latent(self, h, i, blk, log_size):
+        # ToMeAttention with proportional attention (opentome/timm/tome.py:44-58):
+        # softmax(q k^T / sqrt(d) + log size_j) v over all carriers
         qkv = self._linear16(h, f"latent.vit.blocks.{i}.attn.qkv", blk.attn.qkv)
-        q, k, v = qkv.view(b, n, 3, self.num_heads, hd).permute(2, 0, 3, 1, 4).unbind(0)
-        a = F.scaled_dot_product_attention(q, k, v, attn_mask=log_size)
-        a = a.transpose(1, 2).reshape(b, n, c)
-        x = x + self._linear16(a, f"latent.vit.blocks.{i}.attn.proj", blk.attn.proj)
-        h = F.layer_norm(x, (c,), blk.norm2.weight, blk.norm2.bias)
-        h = F.gelu(self._linear16(h, f"latent.vit.blocks.{i}.mlp.fc1", blk.mlp.fc1))
-        return x + self._linear16(h, f"latent.vit.blocks.{i}.mlp.fc2", blk.mlp.fc2)
+        a = local_attention_packed(qkv, self.num_heads, -1, cls_global=False, bias=log_size)
+        return self._linear16(a, f"latent.vit.blocks.{i}.attn.proj", blk.attn.proj)
+
+    def _mlp(self, h, prefix, blk):
+        f = F.gelu(self._linear16(h, prefix + ".mlp.fc1", blk.mlp.fc1))
+        return self._linear16(f, prefix + ".mlp.fc2", blk.mlp.fc2)
 
     def _cross(self, topk_x, x_embed):
+        """MyCrossAttention (model.py:122-221).  The q/k/v projections feed an
+        fp16 attention (SDPA autocasts its inputs), so they run as fp16 GEMMs
+        with fp32 accumulation on LayerNorm outputs rounded to fp16; the
+        out-projection keeps an fp32 result (TF32 tensor cores)."""
         ca = self.encode_cross_attention
         b, nq, c = topk_x.shape
         nk = x_embed.shape[1]
         hd = c // self.num_heads
-        q = F.linear(F.layer_norm(topk_x, (c,), ca.q_norm.weight, ca.q_norm.bias), ca.q_proj.weight, ca.q_proj.bias)
-        kv_in = F.layer_norm(x_embed, (c,), ca.kv_norm.weight, ca.kv_norm.bias)
-        k = F.linear(kv_in, ca.k_proj.weight, ca.k_proj.bias)
-        v = F.linear(kv_in, ca.v_proj.weight, ca.v_proj.bias)
-        # SDPA runs on fp16 operands under autocast; the context comes back fp32
-        ctx = cross_attention(q.half().view(b, nq, self.num_heads, hd), k.half().view(b, nk, self.num_heads, hd),
-                              v.half().view(b, nk, self.num_heads, hd), out_dtype=torch.float32)
-        return F.linear(ctx.view(b, nq, c), ca.out_proj.weight, ca.out_proj.bias)
+        w16 = self._weights16()
+        qn = add_layernorm(topk_x, None, ca.q_norm)[1]
+        kvn = add_layernorm(x_embed, None, ca.kv_norm)[1]
+        q = F.linear(qn, w16["encode_cross_attention.q_proj.weight"], ca.q_proj.bias.half())
+        if self._kv16 is None:
+            self._kv16 = (torch.cat([ca.k_proj.weight, ca.v_proj.weight]).half(),
+                          torch.cat([ca.k_proj.bias, ca.v_proj.bias]).half())
+        kv = F.linear(kvn, *self._kv16).view(b, nk, 2, self.num_heads, hd)
+        ctx = cross_attention(q.view(b, nq, self.num_heads, hd), kv[:, :, 0], kv[:, :, 1], out_dtype=torch.float32)
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = True
+        try:
+            out = F.linear(ctx.view(b, nq, c), ca.out_proj.weight, ca.out_proj.bias)
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev
+        return out
 
     @torch.no_grad()
     def forward(self, images):
@@ -239,17 +248,31 @@ class MergeNetSmall(nn.Module):
         depth = len(vit.blocks)
         metrics = torch.empty(depth, b, n, self.local.metric_layers[0].out_features, device=x.device,
                               dtype=torch.float16)
+        y = None
         for i, blk in enumerate(vit.blocks):
-            x = self._block_local(x, i, blk, metrics, w16)
+            # x <- x + y (previous MLP), h = LN1(x); fp16(x) feeds the previous metric head
+            _, h, raw = add_layernorm(x, y, blk.norm1, x_out=x if y is not None else None, want_raw=i > 0)
+            if i > 0:
+                self._metric(raw, i - 1, metrics, w16)
+            p = self._attn_local(h, i, blk)
+            _, h, _ = add_layernorm(x, p, blk.norm2, x_out=x)
+            y = self._mlp(h, f"local.vit.blocks.{i}", blk)
+        _, _, raw = add_layernorm(x, y, None, x_out=x, want_ln=False, want_raw=True)
+        self._metric(raw, depth - 1, metrics, w16)
         x_embed = x
         route = self._plan(x.device)(x_embed, metrics)
         topk_x = route.topk_x
         x_trace = self._cross(topk_x, x_embed) + topk_x
-        log_size = route.topk_size.log().half()[:, None, None, :]
+        log_size = route.topk_size.log()
+        y = None
         for i, blk in enumerate(self.latent.vit.blocks):
-            x_trace = self._block_latent(x_trace, i, blk, log_size)
+            _, h, _ = add_layernorm(x_trace, y, blk.norm1, x_out=x_trace if y is not None else None)
+            p = self._attn_latent(h, i, blk, log_size)
+            _, h, _ = add_layernorm(x_trace, p, blk.norm2, x_out=x_trace)
+            y = self._mlp(h, f"latent.vit.blocks.{i}", blk)
         lv = self.latent.vit
-        cls = F.layer_norm(x_trace[:, 0], (c,), lv.norm.weight, lv.norm.bias)
+        cls = x_trace[:, 0] + y[:, 0].float()
+        cls = F.layer_norm(cls, (c,), lv.norm.weight, lv.norm.bias, lv.norm.eps)
         logits = self._linear16(cls, "head", self.head)
         aux = {
             "token_strength_no_cls": route.size[:, 1:],
@@ -258,6 +281,22 @@ class MergeNetSmall(nn.Module):
             "cls_feature": cls,
         }
         return logits, aux
+
+
+def add_layernorm(x, y, ln, x_out=None, want_ln=True, want_raw=False):
+    """(x + y [fp32], LayerNorm(x + y) [fp16], fp16(x + y)) in one pass of the
+    library's fused kernel; y (fp16) may be None, outputs not wanted are None."""
+    from . import _lib as L
+    c = x.shape[-1]
+    rows = x.numel() // c
+    h_ln = torch.empty(x.shape, device=x.device, dtype=torch.float16) if want_ln else None
+    h_raw = torch.empty(x.shape, device=x.device, dtype=torch.float16) if want_raw else None
+    if y is not None and y.dtype != torch.float16:
+        y = y.half()
+    L.check(L.lib().mn_add_layernorm(rows, c, L.ptr(x), L.ptr(y), L.ptr(ln.weight) if want_ln else None,
+                                     L.ptr(ln.bias) if want_ln else None, float(ln.eps) if want_ln else 0.0,
+                                     L.ptr(x_out), L.ptr(h_ln), L.ptr(h_raw), L.stream_of(x)), "mn_add_layernorm")
+    return x_out, h_ln, h_raw
 
 
 def mergenet_small_cls(**kwargs):

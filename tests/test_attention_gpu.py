@@ -178,3 +178,37 @@ def test_cross_attention_strided_projection_views(dev):
     exp = torch.nn.functional.scaled_dot_product_attention(
         qp.view(b, 393, 6, 64).transpose(1, 2).float(), k.transpose(1, 2).float(), v.transpose(1, 2).float())
     torch.testing.assert_close(out, exp.transpose(1, 2), atol=5e-3, rtol=5e-3)
+
+
+@pytest.mark.parametrize("n", [393, 130, 17])
+def test_latent_proportional_attention(dev, n):
+    """The latent blocks' ToMe attention (opentome/timm/tome.py:44-58):
+    every key, plus log(size) per key, against SDPA with the float mask."""
+    import mergenet_b200 as mn
+    torch.manual_seed(n)
+    b, h, d = 3, 6, 64
+    qkv = (torch.randn(b, n, 3 * h * d, device=dev) * 0.5).half()
+    size = torch.rand(b, n, device=dev) * 3 + 0.05
+    out = mn.local_attention_packed(qkv, h, -1, cls_global=False, bias=size.log())
+    q, k, v = qkv.view(b, n, 3, h, d).permute(2, 0, 3, 1, 4).unbind(0)
+    exp = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(),
+                                                           attn_mask=size.log().half().float()[:, None, None, :])
+    torch.testing.assert_close(out.float(), exp.transpose(1, 2).reshape(b, n, h * d), atol=5e-3, rtol=5e-3)
+    assert mn.attention.attention_status(dev) == 0
+
+
+@pytest.mark.parametrize("rows,y", [(785 * 3, True), (393 * 2, False), (7, True)])
+def test_add_layernorm(dev, rows, y):
+    from mergenet_b200.model import add_layernorm
+    torch.manual_seed(rows)
+    x = torch.randn(rows, 384, device=dev) * 3
+    yy = torch.randn(rows, 384, device=dev).half() if y else None
+    ln = torch.nn.LayerNorm(384, eps=1e-6).to(dev)
+    torch.nn.init.normal_(ln.weight)
+    torch.nn.init.normal_(ln.bias)
+    s = x + (yy.float() if y else 0)
+    xo = torch.empty_like(x)
+    _, h, raw = add_layernorm(x, yy, ln, x_out=xo, want_raw=True)
+    assert torch.equal(xo, s)
+    assert torch.equal(raw, s.half())
+    torch.testing.assert_close(h.float(), ln(s).half().float(), atol=2e-3, rtol=2e-3)

@@ -64,10 +64,19 @@ def torch_forward(model, images):
     ctx = torch.softmax(split(q) @ split(k).transpose(-1, -2) / math.sqrt(hd), -1) @ split(v)
     xt = F.linear(ctx.transpose(1, 2).reshape(b, -1, c), ca.out_proj.weight, ca.out_proj.bias) + topk_x
     log_size = torch.from_numpy(route["topk_size"]).to(x.device).log().half()[:, None, None, :]
+    nt = xt.shape[1]
     for i, blk in enumerate(model.latent.vit.blocks):
-        xt = model._block_latent(xt, i, blk, log_size)
+        # ToMeBlock with proportional attention (opentome/timm/tome.py:89-143)
+        h = F.layer_norm(xt, (c,), blk.norm1.weight, blk.norm1.bias, blk.norm1.eps)
+        qkv = model._linear16(h, f"latent.vit.blocks.{i}.attn.qkv", blk.attn.qkv)
+        q, k, v = qkv.view(b, nt, 3, heads, hd).permute(2, 0, 3, 1, 4).unbind(0)
+        a = F.scaled_dot_product_attention(q, k, v, attn_mask=log_size).transpose(1, 2).reshape(b, nt, c)
+        xt = xt + model._linear16(a, f"latent.vit.blocks.{i}.attn.proj", blk.attn.proj)
+        h = F.layer_norm(xt, (c,), blk.norm2.weight, blk.norm2.bias, blk.norm2.eps)
+        h = F.gelu(model._linear16(h, f"latent.vit.blocks.{i}.mlp.fc1", blk.mlp.fc1))
+        xt = xt + model._linear16(h, f"latent.vit.blocks.{i}.mlp.fc2", blk.mlp.fc2)
     lv = model.latent.vit
-    cls = F.layer_norm(xt[:, 0], (c,), lv.norm.weight, lv.norm.bias)
+    cls = F.layer_norm(xt[:, 0], (c,), lv.norm.weight, lv.norm.bias, lv.norm.eps)
     return model._linear16(cls, "head", model.head), route
 
 
