@@ -21,10 +21,15 @@ def _status(dev):
     return _STATUS[key]
 
 
-def attention_status(device=None):
-    """Error bits recorded by attention kernels on ``device`` (synchronises)."""
+def attention_status(device=None, reset=False):
+    """Error bits recorded by attention kernels on ``device`` (sticky until
+    reset; reading synchronises)."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    return int(_status(dev).item())
+    st = _status(dev)
+    val = int(st.item())
+    if reset:
+        st.zero_()
+    return val
 
 
 def _strides_bnhd(t: torch.Tensor):

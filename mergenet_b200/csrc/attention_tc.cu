@@ -38,8 +38,8 @@ struct TcSmem {
   static constexpr uint32_t v_off = k_off + kv_stage;
   static constexpr uint32_t p_off = (v_off + kStages * kv_stage + 1023) & ~1023u;
   static constexpr uint32_t bias_off = p_off + kPAtoms * kTcM * 128;
-  static constexpr uint32_t bar_off = bias_off + NB * 4;
-  static constexpr uint32_t tmem_slot_off = bar_off + 8;
+  static constexpr uint32_t bar_off = bias_off + NB * 4;  // [0]: S done, [1]: P.V done
+  static constexpr uint32_t tmem_slot_off = bar_off + 16;
   static constexpr uint32_t bytes = tmem_slot_off + 8 + 1024;  // + alignment slack
 };
 static_assert(TcSmem<160>::bytes <= 113 * 1024 && TcSmem<128>::bytes <= 113 * 1024, "two CTAs per SM");
@@ -96,8 +96,14 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
   constexpr uint32_t idesc_s = tc::idesc_f16(ab_bf16, 0, kTcM, NB);
   constexpr uint32_t idesc_o = tc::idesc_f16(ab_bf16, 1, kTcM, kTcD);
 
+  uint64_t* bar_s = bar;      // arrives when S = Q K^T (and all earlier MMAs) completed
+  uint64_t* bar_o = bar + 1;  // arrives when P.V (and all earlier MMAs) completed
   if (warp == 0) tc::tmem_alloc(tmem_slot, 256);
-  if (tid == 0) tc::mbar_init(bar, 1);
+  if (tid == 0) {
+    tc::mbar_init(bar_s, 1);
+    tc::mbar_init(bar_o, 1);
+    tc::fence_mbar_init();
+  }
   int klo = 0, khi = Nk;
   if (window >= 0) {
     klo = max(0, q0 - window);
@@ -118,7 +124,6 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
 
   const int qi = q0 + tid;  // this thread's query row
   float m_run = -INFINITY, l_run = 0.f;
-  uint32_t phase = 0;
   bool ok = true;
   const float kLog2e = 1.4426950408889634f;
 
@@ -142,14 +147,15 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
 #pragma unroll
       for (int kk = 0; kk < kTcD / 16; ++kk)
         tc::mma_f16_ss(t_s, tc::sw128_desc(aq + kk * 32, 16), tc::sw128_desc(ak + kk * 32, 16), idesc_s, kk > 0);
-      tc::mma_commit(bar);
+      tc::mma_commit(bar_s);
     }
-    ok = tc::mbar_wait(bar, phase);
-    phase ^= 1;
+    // every S commit is waited for, in order: phase blk of bar_s
+    ok = tc::mbar_wait(bar_s, blk & 1, err);
     if (!ok) break;
     tc::fence_after_sync();
-    // S done (and with it the previous P.V): prefetch the next K/V block into
-    // the other stage while this block's softmax runs
+    // S done -- and with it every earlier MMA, including the previous P.V --
+    // so K and the other V stage are free: prefetch the next block while
+    // this block's softmax runs
     if (blk + 1 < nblocks) {
       const int ns = (blk + 1) % S::kStages;
       stage_rows<ET>(sk, kbase, kn, kstart + NB, NB, khi);
@@ -240,12 +246,14 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
       for (int kk = 0; kk < NB / 16; ++kk)
         tc::mma_f16_ss(t_o, tc::sw128_desc(ap + (kk >> 2) * (kTcM * 128) + (kk & 3) * 32, 16),
                        tc::sw128_desc(av + kk * 2048, 16384), idesc_o, (blk > 0 || kk > 0) ? 1u : 0u);
-      tc::mma_commit(bar);
+      tc::mma_commit(bar_o);
     }
   }
   tc::cp_async_wait<0>();
   if (ok && nblocks > 0) {
-    ok = tc::mbar_wait(bar, phase);
+    // bar_o is only waited for here, after its last arrival: the phase of the
+    // final P.V has parity (nblocks - 1) & 1
+    ok = tc::mbar_wait(bar_o, (nblocks - 1) & 1, err);
     tc::fence_after_sync();
   }
   if (ok && nblocks > 0) {

@@ -18,12 +18,24 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
+// Make mbarrier initialisation visible to the async proxy (tcgen05.commit).
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
-// Wait for the phase with the given parity to complete.  Bounded: after
-// `limit` polls it gives up and returns false (the caller records an error).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = (1u << 26)) {
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the phase with the given parity to complete.  Bounded in time:
+// gives up (returns false) after `limit_ns`, or early once another CTA has
+// recorded an error in *err, so a stuck wait costs each CTA at most the
+// bound and the grid drains quickly.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const int* err = nullptr,
+                                          uint64_t limit_ns = 100000000ull) {
   const uint32_t addr = smem_u32(bar);
-  for (uint32_t i = 0; i < limit; ++i) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -33,8 +45,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
         : "r"(addr), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((i & 255) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (i == 0) t0 = now;
+      else if (now - t0 > limit_ns) return false;
+      if (err && *reinterpret_cast<const volatile int*>(err) != 0) return false;
+    }
   }
-  return false;
 }
 
 // Make generic-proxy shared-memory writes visible to the tensor core.

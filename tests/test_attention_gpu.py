@@ -17,6 +17,15 @@ def dev():
     return torch.device("cuda", 0)
 
 
+@pytest.fixture(autouse=True)
+def _clean_status():
+    """Each case starts with a clear (sticky) attention status word."""
+    if torch.cuda.is_available():
+        import mergenet_b200
+        mergenet_b200.attention.attention_status(torch.device("cuda", 0), reset=True)
+    yield
+
+
 def reference_bhnd(q, k, v, bias, window):
     """The reference test's fp32 restatement (tests/test_biased_local_attention.py:17-29)."""
     q32, k32, v32 = q.float(), k.float(), v.float()
