@@ -187,6 +187,144 @@ __global__ void __launch_bounds__(512) route_score_kernel(
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// route_score_fast: same contract as route_score for Cm a multiple of 8.  The
+// band's raw metric rows (both parities) arrive in shared memory through
+// cp.async in one shot; receivers are normalised from there into fp32 rows,
+// and each warp scores four donors at a time with eight lanes per donor
+// (Cm / 8 channels per lane, three-step shuffle reductions).
+// ---------------------------------------------------------------------------
+constexpr int kMaxKc = 16;
+
+template <int MDT, int CPL>
+__global__ void __launch_bounds__(512) route_score_fast_kernel(
+    const typename Elem<MDT>::T* __restrict__ metrics, const int32_t* __restrict__ table, int B, int T, int grid_w,
+    int half, int kc, int kin, Banding band, float tau1, RouteWs ws, int* status) {
+  using ET = typename Elem<MDT>::T;
+  constexpr int Cm = 8 * CPL;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red[64];
+  const int l = blockIdx.y;
+  const int b = blockIdx.x / band.bands;
+  const int bi = blockIdx.x % band.bands;
+  const int q = l & 1;
+  const int dp = q ? 0 : 1, rp = 1 - dp;
+  const ParityTables pt = parity_tables(table, half, kc, kin, q);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int grp = lane >> 3, sl = lane & 7;
+  const int grid_h = (2 * half) / grid_w;
+  const int r0 = bi * band.rows, r1 = min(grid_h, r0 + band.rows);
+  const int p_lo = r0 * grid_w, p_hi = r1 * grid_w;
+  const int d_lo = (p_lo - dp + 1) >> 1, d_hi = (p_hi - dp + 1) >> 1;
+  const int rr0 = max(0, r0 - band.radius_rows), rr1 = min(grid_h, r1 + band.radius_rows);
+  const int s_lo = (rr0 * grid_w - rp + 1) >> 1, s_hi = (rr1 * grid_w - rp + 1) >> 1;
+  const int t_lo = 1 + rr0 * grid_w, t_hi = 1 + rr1 * grid_w;  // raw token rows held
+  ET* raw = reinterpret_cast<ET*>(smem_raw);
+  const size_t raw_bytes = (((size_t)(t_hi - t_lo) * Cm * sizeof(ET)) + 15) & ~size_t(15);
+  float* nrm = reinterpret_cast<float*>(smem_raw + raw_bytes);  // [s_hi - s_lo][Cm]
+
+  const ET* mbase = metrics + ((int64_t)l * B + b) * (int64_t)T * Cm;
+  {
+    const uint32_t sb = static_cast<uint32_t>(__cvta_generic_to_shared(raw));
+    const char* src = reinterpret_cast<const char*>(mbase + (int64_t)t_lo * Cm);
+    const int nvec = (int)(((size_t)(t_hi - t_lo) * Cm * sizeof(ET)) / 16);
+    for (int i = threadIdx.x; i < nvec; i += blockDim.x)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sb + 16u * i), "l"(src + 16 * (int64_t)i)
+                   : "memory");
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  }
+  __syncthreads();
+
+  auto load_norm = [&](int token, float* v) {  // this lane's CPL channels, normalised
+    const ET* row = raw + (int64_t)(token - t_lo) * Cm + sl * CPL;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      v[i] = to_f32(row[i]);
+      ss = fmaf(v[i], v[i], ss);
+    }
+    ss += __shfl_xor_sync(MN_FULL_MASK, ss, 1);
+    ss += __shfl_xor_sync(MN_FULL_MASK, ss, 2);
+    ss += __shfl_xor_sync(MN_FULL_MASK, ss, 4);
+    const float nr = fmaxf(sqrtf(ss), 1e-6f);
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) v[i] = v[i] / nr;
+  };
+
+  // receivers -> normalised fp32 rows
+  for (int s0 = s_lo + warp * 4; s0 < s_hi; s0 += nwarps * 4) {
+    const int s = s0 + grp;
+    const bool live = s < s_hi;
+    float v[CPL];
+    load_norm(live ? 1 + 2 * s + rp : t_lo, v);
+    if (live) {
+      float* dst = nrm + (int64_t)(s - s_lo) * Cm + sl * CPL;
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) dst[i] = v[i];
+    }
+  }
+  __syncthreads();
+
+  float emin = INFINITY, emax = -INFINITY;
+  const int64_t lb = (int64_t)l * B + b;
+  float* sc_out = ws.assign + lb * half * kc;
+  float* e_out = ws.energy + lb * half;
+  for (int d0 = d_lo + warp * 4; d0 < d_hi; d0 += nwarps * 4) {
+    const int d = d0 + grp;
+    const bool live = d < d_hi;
+    float a[CPL];
+    load_norm(live ? 1 + 2 * d + dp : t_lo, a);
+    const int32_t* srx = pt.slot_rx + (int64_t)(live ? d : d_lo) * kc;
+    float sc[kMaxKc];
+#pragma unroll
+    for (int c = 0; c < kMaxKc; ++c) {
+      int s = -1;
+      if (c < kc) s = srx[c];
+      const bool valid = live && s >= 0;
+      if (__any_sync(MN_FULL_MASK, valid)) {
+        const bool inside = valid && s >= s_lo && s < s_hi;
+        if (valid && !inside && status) atomicOr(status, MN_STATUS_TOO_MANY_EDGES);
+        const float* rv = nrm + (int64_t)((inside ? s : s_lo) - s_lo) * Cm + sl * CPL;
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) acc = fmaf(a[i], rv[i], acc);
+        acc += __shfl_xor_sync(MN_FULL_MASK, acc, 1);
+        acc += __shfl_xor_sync(MN_FULL_MASK, acc, 2);
+        acc += __shfl_xor_sync(MN_FULL_MASK, acc, 4);
+        sc[c] = inside ? acc / tau1 : -INFINITY;
+      } else {
+        sc[c] = -INFINITY;
+      }
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kMaxKc; ++c) m = fmaxf(m, sc[c]);
+    float e = 0.f;
+    if (m != -INFINITY) {
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < kMaxKc; ++c) sum += (sc[c] != -INFINITY) ? expf(sc[c] - m) : 0.f;
+      e = expf(logf(sum) + m);
+    }
+    if (live) {
+      float* dst = sc_out + (int64_t)d * kc;
+#pragma unroll
+      for (int c = 0; c < kMaxKc; ++c)  // lane sl writes the slots c == sl (mod 8)
+        if ((c & 7) == sl && c < kc) dst[c] = sc[c];
+      if (sl == 0) e_out[d] = e;
+      emin = fminf(emin, e);
+      emax = fmaxf(emax, e);
+    }
+  }
+  block_minmax(emin, emax, red);
+  if (threadIdx.x == 0) {
+    float* p = ws.partials + (lb * band.bands + bi) * 2;
+    p[0] = emin;
+    p[1] = emax;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // route_select: one CTA per (image, layer).  Global ThreTopK range over the
 // whole batch for this layer (thetopk.py:12-13), per-row threshold, then the
@@ -393,6 +531,80 @@ __global__ void __launch_bounds__(1024) route_mass_kernel(
   if (threadIdx.x == 0) topk_size[(int64_t)b * (k + 1)] = size[0];
 }
 
+// Stage x[b][0..T)[c0 .. c0+CT) into the fp32 shared tile [T][CT].  Full,
+// aligned tiles issue every load before the first use: cp.async for fp32,
+// 16-byte vector loads batched 8 deep for fp16 / bf16.
+template <typename XT, int CT>
+__device__ __forceinline__ void load_token_tile(float* tile, const XT* __restrict__ xb, int T, int C, int c0) {
+  const bool vec = (c0 + CT <= C) && (C % 8 == 0) && ((reinterpret_cast<uintptr_t>(xb) & 15) == 0);
+  if (!vec) {
+    for (int i = threadIdx.x; i < T * CT; i += blockDim.x) {
+      const int t = i / CT, c = i % CT;
+      tile[i] = (c0 + c < C) ? to_f32(xb[(int64_t)t * C + c0 + c]) : 0.f;
+    }
+    return;
+  }
+  if (sizeof(XT) == 4) {
+    constexpr int VPR = CT / 4;  // 16-byte vectors per row
+    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(tile));
+    for (int i = threadIdx.x; i < T * VPR; i += blockDim.x) {
+      const int t = i / VPR, v = i % VPR;
+      const void* src = xb + (int64_t)t * C + c0 + 4 * v;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sbase + (uint32_t)(t * CT + 4 * v) * 4u),
+                   "l"(src) : "memory");
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    return;
+  }
+  constexpr int VPR = CT / 8;  // 16-byte vectors (8 halves) per row
+  const int nvec = T * VPR;
+  for (int i0 = threadIdx.x; i0 < nvec; i0 += 8 * blockDim.x) {
+    uint4 buf[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < nvec) buf[u] = *reinterpret_cast<const uint4*>(xb + (int64_t)(i / VPR) * C + c0 + 8 * (i % VPR));
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i >= nvec) break;
+      const XT* e = reinterpret_cast<const XT*>(&buf[u]);
+      float* dst = tile + (i / VPR) * CT + 8 * (i % VPR);
+      *reinterpret_cast<float4*>(dst) = make_float4(to_f32(e[0]), to_f32(e[1]), to_f32(e[2]), to_f32(e[3]));
+      *reinterpret_cast<float4*>(dst + 4) = make_float4(to_f32(e[4]), to_f32(e[5]), to_f32(e[6]), to_f32(e[7]));
+    }
+  }
+}
+
+// Gather the CLS row and the k carriers out of the shared tile.
+template <typename XT, int CT>
+__device__ __forceinline__ void store_carriers(XT* __restrict__ out, const float* tile, const int32_t* ctok, int k,
+                                               int C, int c0) {
+  if (c0 + CT <= C && C % 4 == 0 && ((reinterpret_cast<uintptr_t>(out) & 15) == 0)) {
+    constexpr int VPR = CT / 4;
+    for (int i = threadIdx.x; i < (k + 1) * VPR; i += blockDim.x) {
+      const int r = i / VPR, v = i % VPR;
+      const int t = (r == 0) ? 0 : ctok[r - 1];
+      const float4 val = *reinterpret_cast<const float4*>(tile + t * CT + 4 * v);
+      XT* dst = out + (int64_t)r * C + c0 + 4 * v;
+      if (sizeof(XT) == 4) {
+        *reinterpret_cast<float4*>(dst) = val;
+      } else {
+        XT h[4] = {from_f32<XT>(val.x), from_f32<XT>(val.y), from_f32<XT>(val.z), from_f32<XT>(val.w)};
+        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(h);
+      }
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < (k + 1) * CT; i += blockDim.x) {
+    const int r = i / CT, cc = i % CT;
+    if (c0 + cc >= C) continue;
+    const int t = (r == 0) ? 0 : ctok[r - 1];
+    out[(int64_t)r * C + c0 + cc] = from_f32<XT>(tile[t * CT + cc]);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // route_transport: one CTA per (image, CT-channel tile).  The token tile
 // [T][CT] lives in shared memory in fp32; each layer updates the receivers in
@@ -414,10 +626,7 @@ __global__ void __launch_bounds__(256) route_transport_kernel(
   const bool ch_ok = (c0 + ch) < C;
 
   const XT* xb = x + (int64_t)b * T * C;
-  for (int i = threadIdx.x; i < T * CT; i += blockDim.x) {
-    int t = i / CT, c = i % CT;
-    tile[i] = (c0 + c < C) ? to_f32(xb[(int64_t)t * C + c0 + c]) : 0.f;
-  }
+  load_token_tile<XT, CT>(tile, xb, T, C, c0);
   __syncthreads();
   for (int l = 0; l < L; ++l) {
     const int q = l & 1, dp = q ? 0 : 1, rp = 1 - dp;
@@ -445,14 +654,7 @@ __global__ void __launch_bounds__(256) route_transport_kernel(
     }
     __syncthreads();
   }
-  XT* out = topk_x + (int64_t)b * (k + 1) * C;
-  const int32_t* ctok = ws.carrier_tok + (int64_t)b * k;
-  for (int i = threadIdx.x; i < (k + 1) * CT; i += blockDim.x) {
-    int r = i / CT, c = i % CT;
-    if (c0 + c >= C) continue;
-    int t = (r == 0) ? 0 : ctok[r - 1];
-    out[(int64_t)r * C + c0 + c] = from_f32<XT>(tile[t * CT + c]);
-  }
+  store_carriers<XT, CT>(topk_x + (int64_t)b * (k + 1) * C, tile, ws.carrier_tok + (int64_t)b * k, k, C, c0);
   (void)ch_ok;
 }
 
@@ -478,10 +680,7 @@ __global__ void __launch_bounds__(512) route_transport_stencil_kernel(
   const int b = blockIdx.x;
   const int c0 = blockIdx.y * CT;
   const XT* xb = x + (int64_t)b * T * C;
-  for (int i = threadIdx.x; i < T * CT; i += blockDim.x) {
-    const int t = i / CT, c = i % CT;
-    tile[i] = (c0 + c < C) ? to_f32(xb[(int64_t)t * C + c0 + c]) : 0.f;
-  }
+  load_token_tile<XT, CT>(tile, xb, T, C, c0);
   __syncthreads();
   const int half_w = grid_w >> 1;
   const int g = threadIdx.x % G;
@@ -541,14 +740,7 @@ __global__ void __launch_bounds__(512) route_transport_stencil_kernel(
     }
     __syncthreads();
   }
-  XT* out = topk_x + (int64_t)b * (k + 1) * C;
-  const int32_t* ctok = ws.carrier_tok + (int64_t)b * k;
-  for (int i = threadIdx.x; i < (k + 1) * CT; i += blockDim.x) {
-    const int r = i / CT, cc = i % CT;
-    if (c0 + cc >= C) continue;
-    const int t = (r == 0) ? 0 : ctok[r - 1];
-    out[(int64_t)r * C + c0 + cc] = from_f32<XT>(tile[t * CT + cc]);
-  }
+  store_carriers<XT, CT>(topk_x + (int64_t)b * (k + 1) * C, tile, ws.carrier_tok + (int64_t)b * k, k, C, c0);
 }
 
 static Banding make_banding(int grid_h, int grid_w, int radius_rows, int Cm) {
@@ -643,6 +835,66 @@ static void launch_stencil(int variant, const void* x, int B, int T, int C, cons
   }
 }
 
+// Banding for route_score_fast: the fewest bands whose raw rows + normalised
+// receivers fit the shared-memory budget.
+static Banding make_fast_banding(int grid_h, int grid_w, int radius_rows, int Cm, int esize, size_t* smem_out) {
+  Banding bd;
+  bd.radius_rows = radius_rows;
+  bd.cap = 0;
+  const size_t budget = 200 * 1024;
+  for (int nb = 1; nb <= grid_h; ++nb) {
+    const int rows = (grid_h + nb - 1) / nb;
+    const int need_rows = (nb == 1) ? grid_h : std::min(grid_h, rows + 2 * radius_rows);
+    const size_t raw = (((size_t)need_rows * grid_w * Cm * esize) + 15) & ~size_t(15);
+    const size_t nrm = ((size_t)(need_rows * grid_w + 1) / 2 + 1) * Cm * 4;
+    if (raw + nrm <= budget) {
+      bd.bands = (grid_h + rows - 1) / rows;
+      bd.rows = rows;
+      *smem_out = raw + nrm;
+      return bd;
+    }
+  }
+  bd.bands = -1;
+  bd.rows = 0;
+  *smem_out = 0;
+  return bd;
+}
+
+template <int MDT, int CPL>
+static void launch_score_fast_cpl(const void* metrics, const int32_t* table, int B, int T, int grid_w, int half,
+                                  int kc, int kin, const Banding& bd, size_t smem, float tau1, const RouteWs& ws, int L,
+                                  int* status, cudaStream_t st) {
+  using ET = typename Elem<MDT>::T;
+  auto kern = route_score_fast_kernel<MDT, CPL>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<dim3(B * bd.bands, L), 512, smem, st>>>(static_cast<const ET*>(metrics), table, B, T, grid_w, half, kc, kin,
+                                                 bd, tau1, ws, status);
+}
+
+// Whether route_score_fast covers the shape (and its banding).
+static bool fast_score_plan(int Cm, int kc, int grid_h, int grid_w, int radius_rows, int esize, Banding* bd,
+                            size_t* smem) {
+  if (Cm % 8 != 0 || kc > kMaxKc) return false;
+  const int cpl = Cm / 8;
+  if (cpl != 1 && cpl != 2 && cpl != 4 && cpl != 8 && cpl != 16) return false;
+  *bd = make_fast_banding(grid_h, grid_w, radius_rows, Cm, esize, smem);
+  return bd->bands > 0;
+}
+
+template <int MDT>
+static void launch_score_fast(const void* metrics, const int32_t* table, int B, int T, int Cm, int grid_w, int half,
+                              int kc, int kin, const Banding& bd, size_t smem, float tau1, const RouteWs& ws, int L,
+                              int* status, cudaStream_t st) {
+  const int cpl = Cm / 8;
+  switch (cpl) {
+    case 1: launch_score_fast_cpl<MDT, 1>(metrics, table, B, T, grid_w, half, kc, kin, bd, smem, tau1, ws, L, status, st); break;
+    case 2: launch_score_fast_cpl<MDT, 2>(metrics, table, B, T, grid_w, half, kc, kin, bd, smem, tau1, ws, L, status, st); break;
+    case 4: launch_score_fast_cpl<MDT, 4>(metrics, table, B, T, grid_w, half, kc, kin, bd, smem, tau1, ws, L, status, st); break;
+    case 8: launch_score_fast_cpl<MDT, 8>(metrics, table, B, T, grid_w, half, kc, kin, bd, smem, tau1, ws, L, status, st); break;
+    default: launch_score_fast_cpl<MDT, 16>(metrics, table, B, T, grid_w, half, kc, kin, bd, smem, tau1, ws, L, status, st); break;
+  }
+}
+
 template <int MDT>
 static void launch_score(const void* metrics, const int32_t* table, int B, int T, int Cm, int grid_w,
                          int half, int kc, int kin, const Banding& bd, float tau1, const RouteWs& ws,
@@ -707,16 +959,29 @@ extern "C" int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev
   ws.carrier_tok = reinterpret_cast<int32_t*>(f);
 
   cudaGetLastError();  // clear any stale error so the check below is ours
-  if (metric_dtype == MN_F16)
+  Banding fbd;
+  size_t fsmem = 0;
+  const int esize = metric_dtype == MN_F32 ? 4 : 2;
+  const bool fast = fast_score_plan(metric_dim, kc, dims->grid_h, dims->grid_w, dims->radius_rows, esize, &fbd, &fsmem);
+  const int bands_used = fast ? fbd.bands : bd.bands;
+  if (fast) {
+    if (metric_dtype == MN_F16)
+      launch_score_fast<MN_F16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, fbd, fsmem, tau1, ws, num_layers, status, st);
+    else if (metric_dtype == MN_BF16)
+      launch_score_fast<MN_BF16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, fbd, fsmem, tau1, ws, num_layers, status, st);
+    else
+      launch_score_fast<MN_F32>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, fbd, fsmem, tau1, ws, num_layers, status, st);
+  } else if (metric_dtype == MN_F16) {
     launch_score<MN_F16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, bd, tau1, ws, num_layers, status, st);
-  else if (metric_dtype == MN_BF16)
+  } else if (metric_dtype == MN_BF16) {
     launch_score<MN_BF16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, bd, tau1, ws, num_layers, status, st);
-  else
+  } else {
     launch_score<MN_F32>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, bd, tau1, ws, num_layers, status, st);
+  }
 
   cudaFuncSetAttribute(route_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_sel);
   route_select_kernel<<<dim3(batch, num_layers), 512, smem_sel, st>>>(dev_table, batch, half, kc, kin,
-                                                                       bd.bands, kb, tau2, ws, status);
+                                                                       bands_used, kb, tau2, ws, status);
 
   const int stencil = stencil_variant(dims);
   cudaFuncSetAttribute(route_mass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_mass);
