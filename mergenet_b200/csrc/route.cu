@@ -238,12 +238,22 @@ __global__ void __launch_bounds__(512) route_score_fast_kernel(
 
   auto load_norm = [&](int token, float* v) {  // this lane's CPL channels, normalised
     const ET* row = raw + (int64_t)(token - t_lo) * Cm + sl * CPL;
+    constexpr int VB = CPL * (int)sizeof(ET);  // bytes of this lane's slice
+    if (VB % 16 == 0) {
+#pragma unroll
+      for (int w = 0; w < VB / 16; ++w) {
+        const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(row) + 16 * w);
+        const ET* e = reinterpret_cast<const ET*>(&u);
+#pragma unroll
+        for (int i = 0; i < 16 / (int)sizeof(ET); ++i) v[w * (16 / (int)sizeof(ET)) + i] = to_f32(e[i]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) v[i] = to_f32(row[i]);
+    }
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < CPL; ++i) {
-      v[i] = to_f32(row[i]);
-      ss = fmaf(v[i], v[i], ss);
-    }
+    for (int i = 0; i < CPL; ++i) ss = fmaf(v[i], v[i], ss);
     ss += __shfl_xor_sync(MN_FULL_MASK, ss, 1);
     ss += __shfl_xor_sync(MN_FULL_MASK, ss, 2);
     ss += __shfl_xor_sync(MN_FULL_MASK, ss, 4);
@@ -270,29 +280,44 @@ __global__ void __launch_bounds__(512) route_score_fast_kernel(
   const int64_t lb = (int64_t)l * B + b;
   float* sc_out = ws.assign + lb * half * kc;
   float* e_out = ws.energy + lb * half;
+  const bool unit_tau = tau1 == 1.0f;
   for (int d0 = d_lo + warp * 4; d0 < d_hi; d0 += nwarps * 4) {
     const int d = d0 + grp;
     const bool live = d < d_hi;
     float a[CPL];
     load_norm(live ? 1 + 2 * d + dp : t_lo, a);
     const int32_t* srx = pt.slot_rx + (int64_t)(live ? d : d_lo) * kc;
+    int slot[kMaxKc];
+#pragma unroll
+    for (int c = 0; c < kMaxKc; ++c) slot[c] = (c < kc) ? __ldg(srx + c) : -1;  // all in flight together
     float sc[kMaxKc];
 #pragma unroll
     for (int c = 0; c < kMaxKc; ++c) {
-      int s = -1;
-      if (c < kc) s = srx[c];
+      const int s = slot[c];
       const bool valid = live && s >= 0;
       if (__any_sync(MN_FULL_MASK, valid)) {
         const bool inside = valid && s >= s_lo && s < s_hi;
         if (valid && !inside && status) atomicOr(status, MN_STATUS_TOO_MANY_EDGES);
         const float* rv = nrm + (int64_t)((inside ? s : s_lo) - s_lo) * Cm + sl * CPL;
         float acc = 0.f;
+        if (CPL % 4 == 0) {
 #pragma unroll
-        for (int i = 0; i < CPL; ++i) acc = fmaf(a[i], rv[i], acc);
+          for (int w = 0; w < CPL / 4; ++w) {
+            const float4 r4 = *reinterpret_cast<const float4*>(rv + 4 * w);
+            acc = fmaf(a[4 * w], r4.x, acc);
+            acc = fmaf(a[4 * w + 1], r4.y, acc);
+            acc = fmaf(a[4 * w + 2], r4.z, acc);
+            acc = fmaf(a[4 * w + 3], r4.w, acc);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < CPL; ++i) acc = fmaf(a[i], rv[i], acc);
+        }
         acc += __shfl_xor_sync(MN_FULL_MASK, acc, 1);
         acc += __shfl_xor_sync(MN_FULL_MASK, acc, 2);
         acc += __shfl_xor_sync(MN_FULL_MASK, acc, 4);
-        sc[c] = inside ? acc / tau1 : -INFINITY;
+        // logits = scores / tau1 (dtem.py:1557); exact without a division at tau1 == 1
+        sc[c] = inside ? (unit_tau ? acc : acc / tau1) : -INFINITY;
       } else {
         sc[c] = -INFINITY;
       }
@@ -304,7 +329,8 @@ __global__ void __launch_bounds__(512) route_score_fast_kernel(
     if (m != -INFINITY) {
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < kMaxKc; ++c) sum += (sc[c] != -INFINITY) ? expf(sc[c] - m) : 0.f;
+      for (int c = 0; c < kMaxKc; ++c)
+        if (sc[c] != -INFINITY) sum += expf(sc[c] - m);
       e = expf(logf(sum) + m);
     }
     if (live) {
@@ -709,14 +735,22 @@ __global__ void __launch_bounds__(512) route_transport_stencil_kernel(
         wl[u + 1] = ld(r_begin - DY1 + u, c - 1);
         wr[u + 1] = ld(r_begin - DY1 + u, c + 1);
       }
+      // coefficients of row r + 1 load while row r computes
+      auto cf_row = [&](int r) {
+        return reinterpret_cast<const float4*>(cfl + (int64_t)((r * grid_w + c) >> 1) * kStencilSlots);
+      };
+      float4 n0 = __ldg(cf_row(r_begin)), n1 = __ldg(cf_row(r_begin) + 1), n2 = __ldg(cf_row(r_begin) + 2),
+             n3 = __ldg(cf_row(r_begin) + 3);
       for (int r = r_begin; r < r_end; ++r) {
+        const float4 q0 = n0, q1 = n1, q2 = n2, q3 = n3;
+        if (r + 1 < r_end) {
+          const float4* nx = cf_row(r + 1);
+          n0 = __ldg(nx); n1 = __ldg(nx + 1); n2 = __ldg(nx + 2); n3 = __ldg(nx + 3);
+        }
 #pragma unroll
         for (int u = 0; u < NW - 1; ++u) { wl[u] = wl[u + 1]; wr[u] = wr[u + 1]; }
         wl[NW - 1] = ld(r + DY1, c - 1);
         wr[NW - 1] = ld(r + DY1, c + 1);
-        const int s = (r * grid_w + c) >> 1;
-        const float4* cfp = reinterpret_cast<const float4*>(cfl + (int64_t)s * kStencilSlots);
-        const float4 q0 = __ldg(cfp), q1 = __ldg(cfp + 1), q2 = __ldg(cfp + 2), q3 = __ldg(cfp + 3);
         const float cw[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
                               q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
         float4* own = reinterpret_cast<float4*>(tile + (1 + r * grid_w + c) * CT + 4 * g);

@@ -129,6 +129,7 @@ class MergeNetSmall(nn.Module):
         self._plans = {}
         self._half = None
         self._kv16 = None
+        self._patch_w16 = None
 
     # ------------------------------------------------------------------ init
     @torch.no_grad()
@@ -165,6 +166,7 @@ class MergeNetSmall(nn.Module):
         self.head.bias.zero_()
         self._half = None
         self._kv16 = None
+        self._patch_w16 = None
         return self
 
     # ------------------------------------------------------------- execution
@@ -203,8 +205,13 @@ class MergeNetSmall(nn.Module):
         return self._linear16(a, f"latent.vit.blocks.{i}.attn.proj", blk.attn.proj)
 
     def _mlp(self, h, prefix, blk):
-        f = F.gelu(self._linear16(h, prefix + ".mlp.fc1", blk.mlp.fc1))
-        return self._linear16(f, prefix + ".mlp.fc2", blk.mlp.fc2)
+        # fc1 + GELU in one cuBLASLt call (bias + GELU epilogue; its GELU agrees
+        # with the exact erf GELU to within fp16 output rounding)
+        w16 = self._weights16()
+        shp = h.shape
+        f = torch._addmm_activation(blk.mlp.fc1.bias.half(), h.reshape(-1, shp[-1]),
+                                    w16[prefix + ".mlp.fc1.weight"].t(), use_gelu=True)
+        return self._linear16(f, prefix + ".mlp.fc2", blk.mlp.fc2).view(*shp[:-1], -1)
 
     def _cross(self, topk_x, x_embed):
         """MyCrossAttention (model.py:122-221).  The q/k/v projections feed an
@@ -232,6 +239,26 @@ class MergeNetSmall(nn.Module):
             torch.backends.cuda.matmul.allow_tf32 = prev
         return out
 
+    def _embed(self, images, w16):
+        """timm PatchEmbed + _pos_embed: the non-overlapping patch conv as one
+        GEMM over fp16 patch rows, written with the position embedding into
+        the fp32 residual stream (CLS row first)."""
+        vit = self.local.vit
+        b, ch, hh, ww = images.shape
+        p = self.patch_size
+        gh, gw = hh // p, ww // p
+        patches = torch.empty(b, gh, gw, ch, p, p, device=images.device, dtype=torch.float16)
+        patches.copy_(images.view(b, ch, gh, p, gw, p).permute(0, 2, 4, 1, 3, 5))  # cast + unfold, one pass
+        wpe = self._patch_w16
+        if wpe is None:
+            wpe = w16["local.vit.patch_embed.proj.weight"].reshape(self.embed_dim, -1).t().contiguous()
+            self._patch_w16 = wpe
+        emb = torch.addmm(vit.patch_embed.proj.bias.half(), patches.view(b * gh * gw, -1), wpe)
+        x = torch.empty(b, gh * gw + 1, self.embed_dim, device=images.device, dtype=torch.float32)
+        torch.add(emb.view(b, gh * gw, -1), vit.pos_embed[:, 1:], out=x[:, 1:])
+        x[:, 0] = vit.cls_token[:, 0] + vit.pos_embed[:, 0]
+        return x
+
     @torch.no_grad()
     def forward(self, images):
         """images [B, 3, H, W] -> (logits [B, classes] fp16, aux dict)."""
@@ -240,10 +267,7 @@ class MergeNetSmall(nn.Module):
         w16 = self._weights16()
         vit = self.local.vit
         b = images.shape[0]
-        pe = vit.patch_embed.proj
-        x = F.conv2d(images.half(), w16["local.vit.patch_embed.proj.weight"], pe.bias.half(), stride=self.patch_size)
-        x = x.flatten(2).transpose(1, 2)
-        x = torch.cat([vit.cls_token.expand(b, -1, -1), x.float()], dim=1) + vit.pos_embed
+        x = self._embed(images, w16)
         n, c = x.shape[1], x.shape[2]
         depth = len(vit.blocks)
         metrics = torch.empty(depth, b, n, self.local.metric_layers[0].out_features, device=x.device,
