@@ -696,7 +696,7 @@ __global__ void __launch_bounds__(256) route_transport_kernel(
 // route_mass in stencil order.
 // ---------------------------------------------------------------------------
 template <typename XT, int CT, int DY1, int DY3>
-__global__ void __launch_bounds__(512) route_transport_stencil_kernel(
+__global__ void __launch_bounds__(448, 2) route_transport_stencil_kernel(
     const XT* __restrict__ x, int B, int T, int C, int grid_h, int grid_w, int half, int L, int k,
     int row_splits, RouteWs ws, XT* __restrict__ topk_x) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -830,7 +830,8 @@ static void launch_transport(const void* x, const int32_t* table, int B, int T, 
 // Which compiled stencil fits the geometry: 1 = (DY1 2, DY3 0) radius 3,
 // 2 = (1, none) radius in [sqrt 2, sqrt 5), 3 = (0, none); 0 = generic path.
 static int stencil_variant(const mn_route_dims* d) {
-  if (d->grid_w % 2 != 0 || d->grid_w / 2 > 64) return 0;
+  // 8 channel groups per receiver column must fit the 448-thread launch bound
+  if (d->grid_w % 2 != 0 || (d->grid_w / 2) * 8 > 448) return 0;
   if (d->stencil_dy1 == 2 && d->stencil_dy3 == 0) return 1;
   if (d->stencil_dy1 == 1 && d->stencil_dy3 == -1) return 2;
   if (d->stencil_dy1 == 0 && d->stencil_dy3 == -1) return 3;
@@ -842,7 +843,7 @@ static void launch_stencil_ct(const void* x, int B, int T, int C, const mn_route
                               const RouteWs& ws, void* topk_x, cudaStream_t st) {
   const int half_w = d->grid_w / 2;
   const int per_split = (CT / 4) * half_w;
-  int splits = std::max(1, std::min(d->grid_h, 512 / per_split));
+  int splits = std::max(1, std::min(d->grid_h, 448 / per_split));  // <= the kernel's launch bound
   splits = std::min(splits, 4);
   const int threads = ((per_split * splits + 31) / 32) * 32;
   const size_t smem = (size_t)T * CT * sizeof(float);

@@ -260,8 +260,10 @@ class MergeNetSmall(nn.Module):
         return x
 
     @torch.no_grad()
-    def forward(self, images):
-        """images [B, 3, H, W] -> (logits [B, classes] fp16, aux dict)."""
+    def forward(self, images, return_intermediates=False):
+        """images [B, 3, H, W] -> (logits [B, classes] fp16, aux dict).
+        ``return_intermediates`` adds the tensors handed between stages
+        (x_embed, metrics, topk_x, topk_size) to aux, for checking."""
         if not images.is_cuda:
             raise RuntimeError("MergeNetSmall runs on CUDA (there is no CPU path)")
         w16 = self._weights16()
@@ -304,6 +306,9 @@ class MergeNetSmall(nn.Module):
             "retained_tokens": int(route.topk_idx.shape[1]),
             "cls_feature": cls,
         }
+        if return_intermediates:
+            aux.update(x_embed=x_embed, metrics=metrics, topk_x=topk_x, topk_size=route.topk_size,
+                       token_center=route.center)
         return logits, aux
 
 
