@@ -696,7 +696,7 @@ __global__ void __launch_bounds__(256) route_transport_kernel(
 // route_mass in stencil order.
 // ---------------------------------------------------------------------------
 template <typename XT, int CT, int DY1, int DY3>
-__global__ void __launch_bounds__(448, 2) route_transport_stencil_kernel(
+__global__ void __launch_bounds__(448) route_transport_stencil_kernel(
     const XT* __restrict__ x, int B, int T, int C, int grid_h, int grid_w, int half, int L, int k,
     int row_splits, RouteWs ws, XT* __restrict__ topk_x) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -735,18 +735,10 @@ __global__ void __launch_bounds__(448, 2) route_transport_stencil_kernel(
         wl[u + 1] = ld(r_begin - DY1 + u, c - 1);
         wr[u + 1] = ld(r_begin - DY1 + u, c + 1);
       }
-      // coefficients of row r + 1 load while row r computes
-      auto cf_row = [&](int r) {
-        return reinterpret_cast<const float4*>(cfl + (int64_t)((r * grid_w + c) >> 1) * kStencilSlots);
-      };
-      float4 n0 = __ldg(cf_row(r_begin)), n1 = __ldg(cf_row(r_begin) + 1), n2 = __ldg(cf_row(r_begin) + 2),
-             n3 = __ldg(cf_row(r_begin) + 3);
       for (int r = r_begin; r < r_end; ++r) {
-        const float4 q0 = n0, q1 = n1, q2 = n2, q3 = n3;
-        if (r + 1 < r_end) {
-          const float4* nx = cf_row(r + 1);
-          n0 = __ldg(nx); n1 = __ldg(nx + 1); n2 = __ldg(nx + 2); n3 = __ldg(nx + 3);
-        }
+        const int s = (r * grid_w + c) >> 1;
+        const float4* cfp = reinterpret_cast<const float4*>(cfl + (int64_t)s * kStencilSlots);
+        const float4 q0 = __ldg(cfp), q1 = __ldg(cfp + 1), q2 = __ldg(cfp + 2), q3 = __ldg(cfp + 3);
 #pragma unroll
         for (int u = 0; u < NW - 1; ++u) { wl[u] = wl[u + 1]; wr[u] = wr[u + 1]; }
         wl[NW - 1] = ld(r + DY1, c - 1);
