@@ -696,7 +696,7 @@ __global__ void __launch_bounds__(256) route_transport_kernel(
 // route_mass in stencil order.
 // ---------------------------------------------------------------------------
 template <typename XT, int CT, int DY1, int DY3>
-__global__ void __launch_bounds__(448) route_transport_stencil_kernel(
+__global__ void __launch_bounds__(512) route_transport_stencil_kernel(
     const XT* __restrict__ x, int B, int T, int C, int grid_h, int grid_w, int half, int L, int k,
     int row_splits, RouteWs ws, XT* __restrict__ topk_x) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -736,13 +736,13 @@ __global__ void __launch_bounds__(448) route_transport_stencil_kernel(
         wr[u + 1] = ld(r_begin - DY1 + u, c + 1);
       }
       for (int r = r_begin; r < r_end; ++r) {
-        const int s = (r * grid_w + c) >> 1;
-        const float4* cfp = reinterpret_cast<const float4*>(cfl + (int64_t)s * kStencilSlots);
-        const float4 q0 = __ldg(cfp), q1 = __ldg(cfp + 1), q2 = __ldg(cfp + 2), q3 = __ldg(cfp + 3);
 #pragma unroll
         for (int u = 0; u < NW - 1; ++u) { wl[u] = wl[u + 1]; wr[u] = wr[u + 1]; }
         wl[NW - 1] = ld(r + DY1, c - 1);
         wr[NW - 1] = ld(r + DY1, c + 1);
+        const int s = (r * grid_w + c) >> 1;
+        const float4* cfp = reinterpret_cast<const float4*>(cfl + (int64_t)s * kStencilSlots);
+        const float4 q0 = __ldg(cfp), q1 = __ldg(cfp + 1), q2 = __ldg(cfp + 2), q3 = __ldg(cfp + 3);
         const float cw[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
                               q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
         float4* own = reinterpret_cast<float4*>(tile + (1 + r * grid_w + c) * CT + 4 * g);
