@@ -58,8 +58,9 @@ class ClockSampler:
                 ["nvidia-smi", "-i", str(self.index),
                  "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.fh, stderr=subprocess.DEVNULL)
+            time.sleep(1.0)  # let nvidia-smi attach before the timed region starts
         except Exception:
             self.proc = None
         return self
@@ -173,6 +174,7 @@ def run_b200(args):
     import mergenet_b200
     from mergenet_b200 import _lib
     from mergenet_b200.model import MergeNetSmall
+    from mergenet_b200.replicas import gather_logits, max_over_ranks
 
     _lib.lib()
     model = MergeNetSmall().init_weights(0).to(dev).eval()
@@ -197,11 +199,7 @@ def run_b200(args):
             logits, aux = model(images)
         end.record(stream)
         barrier()
-    t_dev = start.elapsed_time(end) / 1e3
-    t = torch.tensor([t_dev], device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    t_max = float(t.item())
+    t_max = max_over_ranks(start.elapsed_time(end) / 1e3, dev)
     value = world * B * args.steps / t_max
 
     # end to end through the public call: pinned host images -> device -> logits -> host
@@ -218,19 +216,11 @@ def run_b200(args):
         host_logits.copy_(lg, non_blocking=True)
     e2.record(stream)
     barrier()
-    te = torch.tensor([s2.elapsed_time(e2) / 1e3], device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
-    e2e_value = world * B * args.steps / float(te.item())
+    e2e_value = world * B * args.steps / max_over_ranks(s2.elapsed_time(e2) / 1e3, dev)
 
     # logits check across ranks (the only data collective): every rank's
-    # logits are finite and gathered to rank 0
-    if world > 1:
-        gathered = [torch.empty_like(logits) for _ in range(world)]
-        torch.distributed.all_gather(gathered, logits)
-        finite = all(bool(torch.isfinite(x).all()) for x in gathered)
-    else:
-        finite = bool(torch.isfinite(logits).all())
+    # logits are finite and gathered
+    finite = bool(torch.isfinite(gather_logits(logits)).all())
 
     # roofline of the dominant library kernel: the windowed local attention
     qkv = torch.randn(B, 785, 3 * 384, device=dev, dtype=torch.float16) * 0.5
