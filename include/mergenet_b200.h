@@ -188,6 +188,21 @@ int mn_dtem_select(int batch, int num_donors, int k_slots, const float* scores,
                    float* assignment, void* workspace, size_t workspace_bytes,
                    int* status, void* stream);
 
+/* Soft-k-max select without any device allocation by the caller.  No
+ * counterpart in the reference: it exists for callers that cannot allocate
+ * device memory (no allocator of their own, or no cudaMalloc allowed on
+ * their path).  Same inputs, outputs and results as mn_dtem_select; its
+ * scratch is a fixed array inside the library (about 1.3 MB per GPU, held
+ * until exit).  Limits: batch * num_donors <= 262144, batch <= 65536,
+ * num_donors <= 4096 (MN_ERR_UNSUPPORTED beyond).  Calls that overlap on one
+ * GPU share the scratch and race; order them on a single stream.  The first
+ * call on a device looks up the scratch address; make it before any stream
+ * capture. */
+int mn_dtem_select_noalloc(int batch, int num_donors, int k_slots,
+                           const float* scores, const uint8_t* allowed, int k,
+                           float tau1, float tau2, float* assignment,
+                           int* status, void* stream);
+
 /* Transpose of the carrier gather: out [B,P,C] (dtype) gets carrier row i+1
  * of topk_x [B,k+1,C] at patch topk_idx[b,i]; other rows are zero. */
 int mn_carrier_scatter(int batch, int k, int num_patches, int channels,

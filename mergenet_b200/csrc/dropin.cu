@@ -3,6 +3,7 @@
 // odd grids): the fused path in route.cu covers only the canonical eval
 // grouping.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "thretopk.cuh"
@@ -511,4 +512,87 @@ extern "C" int mn_carrier_scatter(int batch, int k, int num_patches, int channel
         static_cast<const ET*>(topk_x), topk_idx, k, num_patches, channels, static_cast<ET*>(out));
   });
   return rc != MN_OK ? rc : launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// mn_dtem_select_noalloc: the soft-k-max select for callers that cannot
+// allocate device memory.  Some callers have no device allocator to draw on
+// (a host application or language binding that hands the library raw
+// pointers but owns no CUDA memory pool), and some must not call cudaMalloc
+// at all (a serving loop that cannot afford the implicit device
+// synchronisation and unpredictable latency of an allocation, or a process
+// whose device memory is already carved up by another runtime).  This
+// variant keeps its scratch (row energies, per-batch valid-row counts,
+// energy min/max partials) in a fixed array compiled into the library, so
+// the caller passes only inputs and outputs.
+//
+// The array holds at most kNoAllocMaxRows donor rows (batch * num_donors)
+// and kNoAllocMaxBatch batch rows; larger calls are rejected with
+// MN_ERR_UNSUPPORTED before anything is launched.  Every GPU that loads the
+// library carries the array (about 1.3 MB) until the process exits.  All
+// calls on a device share it: calls whose kernels overlap on that device
+// (different streams without ordering) race and corrupt each other, so
+// order them on one stream.  The valid-row counters start from zero on every
+// call (cleared with cudaMemsetAsync, which allocates nothing); the other
+// scratch is fully rewritten by each call.
+//
+// The first call on each device looks up the array's device address with
+// cudaGetSymbolAddress while that device is current (a host-side lookup,
+// cached per device); make that first call before any stream capture.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int64_t kNoAllocMaxRows = 262144;
+constexpr int kNoAllocMaxBatch = 65536;
+constexpr int kNoAllocMaxParts = 1024;
+constexpr size_t kNoAllocScratchBytes =
+    (size_t)kNoAllocMaxRows * sizeof(float) + (size_t)kNoAllocMaxBatch * sizeof(int) +
+    (size_t)kNoAllocMaxParts * 2 * sizeof(float);
+static __device__ __align__(256) unsigned char g_select_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 128;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_select_scratch on the current device (looked up once).
+int select_scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MN_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_select_scratch) != cudaSuccess || p == nullptr) return MN_ERR_LAUNCH;
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return MN_OK;
+}
+}  // namespace
+
+extern "C" int mn_dtem_select_noalloc(int batch, int num_donors, int k_slots, const float* scores,
+                                      const uint8_t* allowed, int k, float tau1, float tau2, float* assignment,
+                                      int* status, void* stream) {
+  if (batch <= 0 || num_donors <= 0 || k_slots <= 0 || !scores || !allowed || !assignment) return MN_ERR_ARG;
+  if (num_donors > 4096) return MN_ERR_UNSUPPORTED;
+  const int64_t rows = (int64_t)batch * num_donors;
+  if (rows > kNoAllocMaxRows || batch > kNoAllocMaxBatch) return MN_ERR_UNSUPPORTED;
+  const int parts = thre_topk_parts(rows);
+  if (parts > kNoAllocMaxParts) return MN_ERR_UNSUPPORTED;
+  void* scratch = nullptr;
+  const int rc = select_scratch_address(&scratch);
+  if (rc != MN_OK) return rc;
+  cudaGetLastError();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* energy = static_cast<float*>(scratch);
+  int* counts = reinterpret_cast<int*>(energy + rows);
+  float* partials = reinterpret_cast<float*>(counts + batch);
+  cudaMemsetAsync(counts, 0, (size_t)batch * sizeof(int), st);
+  select_energy_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(scores, allowed, (int)rows, k_slots, tau1,
+                                                                   energy, counts, num_donors);
+  minmax_partials_kernel<<<parts, 256, 0, st>>>(energy, rows, partials);
+  const int np = next_pow2(num_donors);
+  const size_t smem = row_scratch_bytes(np) + (size_t)num_donors * sizeof(float);
+  cudaFuncSetAttribute(select_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  select_rows_kernel<<<batch, 512, smem, st>>>(scores, allowed, num_donors, k_slots, k, tau1, tau2, energy, counts,
+                                               partials, parts, assignment, status);
+  return launch_status();
 }
