@@ -71,12 +71,46 @@ __device__ __forceinline__ void stage_rows(uint8_t* tile, const ET* src, int64_t
   }
 }
 
-template <typename ET, int NB>
-__global__ void __launch_bounds__(128) attn_tc_kernel(
+__device__ __forceinline__ float fast_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename ET>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Log2-domain growth of a row maximum that is absorbed without rescaling O:
+// probabilities then reach at most 2^8, well inside fp16 / bf16 range, and O
+// and the row sum share the same stale maximum, so the result is unchanged.
+constexpr float kRescaleLog2 = 8.0f;
+
+// NCH: S chunks (32 columns) a warp can need in one block.  With a window
+// the legal keys of a warp's 32 rows span at most 32 + 2*window columns, so
+// NB = 160 (window <= 16) needs at most three chunks.
+template <int NB>
+struct TcChunks {
+  static constexpr int kAll = NB / 32;
+  static constexpr int kWarp = NB == 160 ? 3 : kAll;
+};
+
+template <typename ET, int NB, bool BIAS>
+__global__ void __launch_bounds__(128, 2) attn_tc_kernel(
     const ET* __restrict__ q, int64_t qb, int64_t qn, int64_t qh, const ET* __restrict__ k,
     const ET* __restrict__ v, int64_t kb, int64_t kn, int64_t kh, int Nq, int Nk, int H, int window, float scale,
     const void* __restrict__ bias, int bias_dtype, void* __restrict__ out, int out_dtype, int* __restrict__ err) {
   using S = TcSmem<NB>;
+  constexpr int NCH = TcChunks<NB>::kWarp;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sq = base + S::q_off;
@@ -93,8 +127,9 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
   const ET* kbase = k + (int64_t)b * kb + (int64_t)h * kh;
   const ET* vbase = v + (int64_t)b * kb + (int64_t)h * kh;
   constexpr int ab_bf16 = std::is_same<ET, __nv_bfloat16>::value ? 1 : 0;
-  constexpr uint32_t idesc_s = tc::idesc_f16(ab_bf16, 0, kTcM, NB);
   constexpr uint32_t idesc_o = tc::idesc_f16(ab_bf16, 1, kTcM, kTcD);
+  const float kLog2e = 1.4426950408889634f;
+  const float sl2 = scale * kLog2e;  // scores enter the softmax in log2 units
 
   uint64_t* bar_s = bar;      // arrives when S = Q K^T (and all earlier MMAs) completed
   uint64_t* bar_o = bar + 1;  // arrives when P.V (and all earlier MMAs) completed
@@ -125,17 +160,19 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
   const int qi = q0 + tid;  // this thread's query row
   float m_run = -INFINITY, l_run = 0.f;
   bool ok = true;
-  const float kLog2e = 1.4426950408889634f;
 
   for (int blk = 0; blk < nblocks && ok; ++blk) {
     const int kstart = klo + blk * NB;
+    const int kvalid = min(NB, khi - kstart);  // keys of this block
+    const int kpad = (kvalid + 15) & ~15;      // MMA extent over them
     const int stage = blk % S::kStages;
-    uint8_t* skb = sk;
     uint8_t* svb = sv + stage * S::kv_stage;
-    for (int j = tid; j < NB; j += blockDim.x) {
-      float bv = 0.f;
-      if (bias && kstart + j < khi) bv = to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)b * Nk + kstart + j)));
-      sbias[j] = bv;
+    if (BIAS) {
+      for (int j = tid; j < NB; j += blockDim.x) {
+        float bv = 0.f;
+        if (j < kvalid) bv = to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)b * Nk + kstart + j)));
+        sbias[j] = bv * kLog2e;
+      }
     }
     tc::cp_async_wait<0>();  // this block's K/V (and Q) have landed
     tc::fence_async_smem();
@@ -143,7 +180,8 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
     __syncthreads();
     if (tid == 0) {
       tc::fence_after_sync();
-      const uint32_t aq = tc::smem_u32(sq), ak = tc::smem_u32(skb);
+      const uint32_t aq = tc::smem_u32(sq), ak = tc::smem_u32(sk);
+      const uint32_t idesc_s = tc::idesc_f16(ab_bf16, 0, kTcM, kpad);
 #pragma unroll
       for (int kk = 0; kk < kTcD / 16; ++kk)
         tc::mma_f16_ss(t_s, tc::sw128_desc(aq + kk * 32, 16), tc::sw128_desc(ak + kk * 32, 16), idesc_s, kk > 0);
@@ -163,63 +201,106 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
       tc::cp_async_commit();
     }
 
-    // this row's legal keys, relative to the block
-    int jlo = 0, jhi = min(NB, khi - kstart);  // [jlo, jhi)
+    // this row's legal keys, relative to the block: [jlo, jhi)
+    int jlo = 0, jhi = kvalid;
     if (window >= 0) {
       jlo = max(jlo, qi - window - kstart);
       jhi = min(jhi, qi + window + 1 - kstart);
     }
     if (qi >= Nq) jhi = jlo;  // padding rows: no keys
-    // the warp's column chunks that can hold a legal key
+    // the warp's column chunks that can hold a legal key: [c_lo, c_lo + nch)
     const int wlo = __reduce_min_sync(0xffffffffu, (unsigned)max(0, min(jlo, NB)));
     const int whi = __reduce_max_sync(0xffffffffu, (unsigned)max(0, jhi));
-    const int c_lo = wlo >> 5, c_hi = (whi + 31) >> 5;  // [c_lo, c_hi)
-    float mx = -INFINITY;
-    float sc[32];
-    for (int c = c_lo; c < c_hi; ++c) {
-      tc::tmem_ld32(t_s + lane_sel + c * 32, sc);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int j = c * 32 + i;
-        if (j >= jlo && j < jhi) mx = fmaxf(mx, sc[i] * scale + sbias[j]);
-      }
+    const int c_lo = wlo >> 5;
+    int nch = ((whi + 31) >> 5) - c_lo;
+    if (whi <= wlo) nch = 0;
+    if (nch > NCH) {  // cannot happen for the shapes the dispatch admits
+      nch = NCH;
+      if (err && (tid & 31) == 0) atomicOr(err, MN_STATUS_TC_TIMEOUT);
     }
-    const float m_new = fmaxf(m_run, mx);
-    const float corr = (m_run == -INFINITY) ? 0.f : exp2f((m_run - m_new) * kLog2e);
-    float lsum = 0.f;
-    // probabilities -> P (all NB columns; zero outside this row's keys)
-    for (int c = 0; c < NB / 32; ++c) {
-      float p[32];
-      if (c >= c_lo && c < c_hi) {
-        tc::tmem_ld32(t_s + lane_sel + c * 32, sc);
+
+    // S rows of the warp's chunks, all loads in flight before one wait
+    float sc[NCH * 32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int j = c * 32 + i;
-          const bool legal = j >= jlo && j < jhi;
-          p[i] = legal ? exp2f((sc[i] * scale + sbias[j] - m_new) * kLog2e) : 0.f;
+    for (int u = 0; u < NCH; ++u)
+      if (u < nch) tc::tmem_ld32_nowait(t_s + lane_sel + (c_lo + u) * 32, sc + u * 32);
+    tc::tmem_ld_wait<NCH * 32>(sc);
+
+    // pass 1: log2-domain logits (illegal keys -inf) and the row maximum
+    float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+      if (u >= nch) continue;
+      const int cb = (c_lo + u) * 32;
+      const bool whole = __all_sync(0xffffffffu, jlo <= cb && jhi >= cb + 32);
+      const float4* b4 = reinterpret_cast<const float4*>(sbias + cb);
+      if (whole) {
+#pragma unroll
+        for (int i4 = 0; i4 < 8; ++i4) {
+          float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (BIAS) bb = b4[i4];
+          const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float& x = sc[u * 32 + i4 * 4 + e];
+            x = fmaf(x, sl2, bv[e]);
+            mx4[e] = fmaxf(mx4[e], x);
+          }
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) p[i] = 0.f;
-      }
+        for (int i4 = 0; i4 < 8; ++i4) {
+          float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (BIAS) bb = b4[i4];
+          const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const uint4 pk = pack8<ET>(p + 8 * g);
-        // round-tripped values enter the sum, as the tensor core sees them
-        const ET* pe = reinterpret_cast<const ET*>(&pk);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) lsum += to_f32(pe[i]);
-        const int key8 = c * 4 + g;  // 8-key chunk index
-        const int atom = key8 >> 3, chunk = key8 & 7;
-        *reinterpret_cast<uint4*>(sp + atom * (kTcM * 128) + tc::sw128_off(tid, chunk)) = pk;
+          for (int e = 0; e < 4; ++e) {
+            const int j = cb + i4 * 4 + e;
+            float& x = sc[u * 32 + i4 * 4 + e];
+            x = (j >= jlo && j < jhi) ? fmaf(x, sl2, bv[e]) : -INFINITY;
+            mx4[e] = fmaxf(mx4[e], x);
+          }
+        }
       }
     }
-    if (NB % 32 != 0) {  // the tail columns (NB not a multiple of 32)
-      for (int key8 = (NB / 32) * 4; key8 < NB / 8; ++key8) {
-        float p[8];
-        for (int i = 0; i < 8; ++i) p[i] = 0.f;
-        const uint4 pk = pack8<ET>(p);
+    const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+    const float m_new = fmaxf(m_run, mx);
+    // keep the running maximum unless it grew by more than 2^8
+    const float m_use = (m_run == -INFINITY || m_new - m_run > kRescaleLog2) ? m_new : m_run;
+    const float corr = (m_run == -INFINITY || m_use == m_run) ? 1.f : fast_ex2(m_run - m_use);
+    const float msub = m_use == -INFINITY ? 0.f : m_use;
+
+    // pass 2: probabilities -> P in shared memory; chunks outside the warp's
+    // range are zero
+    float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+      if (u >= nch) continue;
+      const int c = c_lo + u;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint4 pk;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = fast_ex2(sc[u * 32 + g * 8 + 2 * e] - msub);
+          const float p1 = fast_ex2(sc[u * 32 + g * 8 + 2 * e + 1] - msub);
+          ls4[(2 * e) & 3] += p0;
+          ls4[(2 * e + 1) & 3] += p1;
+          w[e] = pack2<ET>(p0, p1);
+        }
+        const int key8 = c * 4 + g;  // 8-key chunk index
         *reinterpret_cast<uint4*>(sp + (key8 >> 3) * (kTcM * 128) + tc::sw128_off(tid, key8 & 7)) = pk;
+      }
+    }
+    const int c_end = (kpad + 31) >> 5;  // chunks the P.V MMA reads
+    for (int c = 0; c < c_end; ++c) {
+      if (c >= c_lo && c < c_lo + nch) continue;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int key8 = c * 4 + g;
+        *reinterpret_cast<uint4*>(sp + (key8 >> 3) * (kTcM * 128) + tc::sw128_off(tid, key8 & 7)) =
+            make_uint4(0u, 0u, 0u, 0u);
       }
     }
     // rescale the running output rows (warp-collective TMEM access: the
@@ -234,16 +315,15 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(
         tc::tmem_st32(t_o + lane_sel + c * 32, o);
       }
     }
-    l_run = l_run * corr + lsum;
-    m_run = m_new;
+    l_run = l_run * corr + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
+    m_run = m_use;
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
     if (tid == 0) {
       tc::fence_after_sync();
       const uint32_t ap = tc::smem_u32(sp), av = tc::smem_u32(svb);
-#pragma unroll
-      for (int kk = 0; kk < NB / 16; ++kk)
+      for (int kk = 0; kk < kpad / 16; ++kk)
         tc::mma_f16_ss(t_o, tc::sw128_desc(ap + (kk >> 2) * (kTcM * 128) + (kk & 3) * 32, 16),
                        tc::sw128_desc(av + kk * 2048, 16384), idesc_o, (blk > 0 || kk > 0) ? 1u : 0u);
       tc::mma_commit(bar_o);
@@ -292,7 +372,7 @@ static void launch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const v
                       int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int window, float scale,
                       const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st) {
   const size_t smem = TcSmem<NB>::bytes;
-  auto kern = attn_tc_kernel<ET, NB>;
+  auto kern = bias ? attn_tc_kernel<ET, NB, true> : attn_tc_kernel<ET, NB, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((Nq + kTcM - 1) / kTcM, H, B);
   kern<<<grid, 128, smem, st>>>(static_cast<const ET*>(q), qb, qn, qh, static_cast<const ET*>(k),
