@@ -31,6 +31,10 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "images/sec mergenet_small_cls fp16 B=256/GPU"
 IMG = 224
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture
+# of a B=128 launch) of the latent attention kernel, per image; the traffic
+# grows in proportion to the batch
+TRAFFIC_LATENT_ATTN = 137.2e6 / 128
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 
 
@@ -134,7 +138,7 @@ def run_reference(args):
     world, rank, _ = _dist()
     if rank != 0:
         return
-    from mergenet_b200.model import MergeNetSmall
+    from mergenet_b200.model import ForwardGraph, MergeNetSmall
     model = MergeNetSmall().init_weights(0)
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
@@ -173,7 +177,7 @@ def run_b200(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     import mergenet_b200
     from mergenet_b200 import _lib
-    from mergenet_b200.model import MergeNetSmall
+    from mergenet_b200.model import ForwardGraph, MergeNetSmall
     from mergenet_b200.replicas import gather_logits, max_over_ranks
 
     _lib.lib()
@@ -188,15 +192,18 @@ def run_b200(args):
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
+    # the forward is captured once as a CUDA graph (after `warmup` eager
+    # forwards) and replayed: same kernels, no per-kernel host launch cost
+    fwd = ForwardGraph(model, images, warmup=args.warmup)
     for _ in range(args.warmup):
-        model(images)
+        fwd()
     barrier()
     sampler = ClockSampler(local)
     with sampler:
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for _ in range(args.steps):
-            logits, aux = model(images)
+            logits, aux = fwd()
         end.record(stream)
         barrier()
     t_max = max_over_ranks(start.elapsed_time(end) / 1e3, dev)
@@ -206,13 +213,13 @@ def run_b200(args):
     host_images = images.cpu().pin_memory()
     host_logits = torch.empty(B, logits.shape[1], dtype=logits.dtype).pin_memory()
     for _ in range(max(1, args.warmup // 2)):
-        lg, _ = model(host_images.to(dev, non_blocking=True))
+        lg, _ = fwd(host_images)
         host_logits.copy_(lg, non_blocking=True)
     barrier()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s2.record(stream)
     for _ in range(args.steps):
-        lg, _ = model(host_images.to(dev, non_blocking=True))
+        lg, _ = fwd(host_images)  # pinned host batch -> graph input buffer, then replay
         host_logits.copy_(lg, non_blocking=True)
     e2.record(stream)
     barrier()
@@ -222,12 +229,21 @@ def run_b200(args):
     # logits are finite and gathered
     finite = bool(torch.isfinite(gather_logits(logits)).all())
 
-    # roofline of the dominant library kernel: the windowed local attention
-    qkv = torch.randn(B, 785, 3 * 384, device=dev, dtype=torch.float16) * 0.5
-    t_attn = _time_kernel(lambda: mergenet_b200.local_attention_packed(qkv, 6, 16, cls_global=True), stream)
-    attn_bytes = qkv.numel() * 2 + B * 785 * 384 * 2  # q, k, v read + o write (fp16)
+    # roofline of the dominant library kernel: the latent attention over all
+    # 393 carriers with the log-size bias (attn_tc_kernel<half, 128>)
+    nt = 393
+    qkv_l = torch.randn(B, nt, 3 * 384, device=dev, dtype=torch.float16) * 0.5
+    log_size = torch.rand(B, nt, device=dev).mul_(3.0).log1p_()
+    t_attn = _time_kernel(lambda: mergenet_b200.local_attention_packed(qkv_l, 6, -1, cls_global=False,
+                                                                         bias=log_size), stream)
+    attn_bytes = qkv_l.numel() * 2 + log_size.numel() * 4 + B * nt * 384 * 2  # q,k,v,bias read + o write
+    attn_flops = 4 * B * 6 * nt * nt * 64
     peak, peak_kind = _peaks()
     achieved = attn_bytes / t_attn / 1e9
+    # the windowed local attention (attn_tc_kernel<half, 160> + cls_row_kernel)
+    qkv = torch.randn(B, 785, 3 * 384, device=dev, dtype=torch.float16) * 0.5
+    t_local = _time_kernel(lambda: mergenet_b200.local_attention_packed(qkv, 6, 16, cls_global=True), stream)
+    local_bytes = qkv.numel() * 2 + B * 785 * 384 * 2
     # the routing op on the same shard (routing HBM GB/s)
     x_embed = torch.randn(B, 785, 384, device=dev)
     metrics = (torch.randn(6, B, 785, 64, device=dev) * 1.3).half()
@@ -250,11 +266,16 @@ def run_b200(args):
                        "l2": "inputs larger than L2 (154 MB images per step)", "logits_finite": finite},
             "e2e": {"value": e2e_value, "unit": "images/sec", "h2d_bytes_per_step": host_images.numel() * 4,
                     "d2h_bytes_per_step": host_logits.numel() * host_logits.element_size()},
-            "gpu_launches": 17 * args.steps,
-            "roofline": {"kernel": "local_attn_kernel + cls_row_kernel (windowed attention, B=%d)" % B,
+            "gpu_launches": ForwardGraph.library_launches(model) * args.steps,
+            "roofline": {"kernel": "attn_tc_kernel<half,64,full,bias> (latent attention, 393 carriers, 6 heads, B=%d)" % B,
                          "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
-                         "algorithmic_bytes": attn_bytes, "ms_per_launch": t_attn * 1e3},
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": TRAFFIC_LATENT_ATTN * B,
+                         "algorithmic_bytes": attn_bytes, "ms_per_launch": t_attn * 1e3,
+                         "tflops": attn_flops / t_attn / 1e12},
+            "local_attention": {"kernel": "attn_tc_kernel<half,160> + cls_row_kernel (window 16)",
+                                "ms_per_call": t_local * 1e3, "algorithmic_bytes": local_bytes,
+                                "achieved_gbs": local_bytes / t_local / 1e9,
+                                "frac": local_bytes / t_local / 1e9 / peak},
             "routing": {"ms_per_call": t_route * 1e3, "algorithmic_bytes": route_bytes,
                         "achieved_gbs": route_bytes / t_route / 1e9, "frac": route_bytes / t_route / 1e9 / peak},
             "cpu_baseline": ({"value": cpu_v, "unit": "images/sec", "cores": os.cpu_count(), "kind": "port",

@@ -255,6 +255,19 @@ int mn_add_layernorm(int64_t rows, int channels, const float* x, const void* y,
                      const float* gamma, const float* beta, float eps,
                      float* x_out, void* h_ln, void* h_raw, void* stream);
 
+/* Patch embedding finish fused with the first block's LayerNorm (timm
+ * PatchEmbed + VisionTransformer._pos_embed, then blocks[0].norm1, as the
+ * LocalEncoder runs them under fp16 autocast,
+ * opentome/models/mergenet/model.py:517-535): for image b and token t,
+ * x_out[b, t] = cls + pos[0] (t == 0) or float(emb[b, t - 1]) + pos[t]
+ * (fp32), h_ln[b, t] = LayerNorm(x_out[b, t]) (fp16).  emb is the fp16 patch
+ * projection [batch, tokens - 1, channels]; pos fp32 [tokens, channels];
+ * cls fp32 [channels].  channels in {256, 384, 512, 768}. */
+int mn_embed_layernorm(int batch, int tokens, int channels, const void* emb,
+                       const float* pos, const float* cls, const float* gamma,
+                       const float* beta, float eps, float* x_out, void* h_ln,
+                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,9 +28,12 @@ constexpr int kTcM = 128;
 template <int NB>
 struct TcSmem {
   // K is dead once S = Q K^T has completed, so one K buffer suffices; V is
-  // read by P.V while the next block streams in, so the multi-block path
-  // (NB = 128) keeps two V stages.  ~97 KB: two CTAs per SM.
-  static constexpr int kStages = NB == 128 ? 2 : 1;
+  // read by P.V while the next block streams in, so the multi-block paths
+  // (NB <= 128) keep two V stages.  NB = 128 / 160: ~97 KB, two CTAs per SM;
+  // NB = 64: ~57 KB, three CTAs per SM.
+  static constexpr int kStages = NB <= 128 ? 2 : 1;
+  static constexpr int kTmemCols = NB + kTcD <= 128 ? 128 : 256;  // S then O
+  static constexpr int kMinBlocks = NB == 64 ? 3 : 2;
   static constexpr int kPAtoms = (NB + 63) / 64;
   static constexpr uint32_t q_off = 0;
   static constexpr uint32_t k_off = q_off + kTcM * 128;
@@ -43,6 +46,7 @@ struct TcSmem {
   static constexpr uint32_t bytes = tmem_slot_off + 8 + 1024;  // + alignment slack
 };
 static_assert(TcSmem<160>::bytes <= 113 * 1024 && TcSmem<128>::bytes <= 113 * 1024, "two CTAs per SM");
+static_assert(TcSmem<64>::bytes <= 75 * 1024, "three CTAs per SM");
 
 template <typename ET>
 __device__ __forceinline__ uint4 pack8(const float* p) {
@@ -97,15 +101,18 @@ constexpr float kRescaleLog2 = 8.0f;
 
 // NCH: S chunks (32 columns) a warp can need in one block.  With a window
 // the legal keys of a warp's 32 rows span at most 32 + 2*window columns, so
-// NB = 160 (window <= 16) needs at most three chunks.
+// NB = 160 (window <= 16) needs at most three chunks; otherwise all.
 template <int NB>
 struct TcChunks {
   static constexpr int kAll = NB / 32;
   static constexpr int kWarp = NB == 160 ? 3 : kAll;
 };
 
-template <typename ET, int NB, bool BIAS>
-__global__ void __launch_bounds__(128, 2) attn_tc_kernel(
+// WIN: sliding window (per-row key ranges, masked per element).  Without a
+// window every row sees the same keys, so keys past the end get a -inf bias
+// and no element is masked.  BIAS: a per-key bias is given.
+template <typename ET, int NB, bool WIN, bool BIAS>
+__global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
     const ET* __restrict__ q, int64_t qb, int64_t qn, int64_t qh, const ET* __restrict__ k,
     const ET* __restrict__ v, int64_t kb, int64_t kn, int64_t kh, int Nq, int Nk, int H, int window, float scale,
     const void* __restrict__ bias, int bias_dtype, void* __restrict__ out, int out_dtype, int* __restrict__ err) {
@@ -133,14 +140,14 @@ __global__ void __launch_bounds__(128, 2) attn_tc_kernel(
 
   uint64_t* bar_s = bar;      // arrives when S = Q K^T (and all earlier MMAs) completed
   uint64_t* bar_o = bar + 1;  // arrives when P.V (and all earlier MMAs) completed
-  if (warp == 0) tc::tmem_alloc(tmem_slot, 256);
+  if (warp == 0) tc::tmem_alloc(tmem_slot, S::kTmemCols);
   if (tid == 0) {
     tc::mbar_init(bar_s, 1);
     tc::mbar_init(bar_o, 1);
     tc::fence_mbar_init();
   }
   int klo = 0, khi = Nk;
-  if (window >= 0) {
+  if (WIN) {
     klo = max(0, q0 - window);
     khi = min(Nk, q0 + kTcM + window);
   }
@@ -164,14 +171,19 @@ __global__ void __launch_bounds__(128, 2) attn_tc_kernel(
   for (int blk = 0; blk < nblocks && ok; ++blk) {
     const int kstart = klo + blk * NB;
     const int kvalid = min(NB, khi - kstart);  // keys of this block
-    const int kpad = (kvalid + 15) & ~15;      // MMA extent over them
+    // MMA extent: whole 32-column chunks, so every S column the softmax
+    // reads was written by this block's MMA (K rows past the end are zero)
+    const int kpad = (kvalid + 31) & ~31;
     const int stage = blk % S::kStages;
     uint8_t* svb = sv + stage * S::kv_stage;
-    if (BIAS) {
+    if (BIAS || !WIN) {
       for (int j = tid; j < NB; j += blockDim.x) {
-        float bv = 0.f;
-        if (j < kvalid) bv = to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)b * Nk + kstart + j)));
-        sbias[j] = bv * kLog2e;
+        float bv = WIN ? 0.f : -INFINITY;
+        if (j < kvalid) {
+          bv = 0.f;
+          if (BIAS) bv = to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)b * Nk + kstart + j))) * kLog2e;
+        }
+        sbias[j] = bv;
       }
     }
     tc::cp_async_wait<0>();  // this block's K/V (and Q) have landed
@@ -203,19 +215,23 @@ __global__ void __launch_bounds__(128, 2) attn_tc_kernel(
 
     // this row's legal keys, relative to the block: [jlo, jhi)
     int jlo = 0, jhi = kvalid;
-    if (window >= 0) {
+    int c_lo = 0, nch = kpad >> 5;  // without a window: every chunk, every row
+    if (WIN) {
       jlo = max(jlo, qi - window - kstart);
       jhi = min(jhi, qi + window + 1 - kstart);
+      if (qi >= Nq) jhi = jlo;  // padding rows: no keys
+      // the warp's column chunks that can hold a legal key: [c_lo, c_lo + nch).
+      // Rows without a key in this block (jlo >= jhi; jlo may lie past the
+      // block) take no part, so 0 <= wlo and whi <= kvalid <= NB.
+      const bool has = jlo < jhi;
+      const int wlo = (int)__reduce_min_sync(0xffffffffu, (unsigned)(has ? jlo : NB));
+      const int whi = (int)__reduce_max_sync(0xffffffffu, (unsigned)(has ? jhi : 0));
+      c_lo = min(wlo >> 5, TcChunks<NB>::kAll);
+      nch = whi > wlo ? ((whi + 31) >> 5) - c_lo : 0;
     }
-    if (qi >= Nq) jhi = jlo;  // padding rows: no keys
-    // the warp's column chunks that can hold a legal key: [c_lo, c_lo + nch)
-    const int wlo = __reduce_min_sync(0xffffffffu, (unsigned)max(0, min(jlo, NB)));
-    const int whi = __reduce_max_sync(0xffffffffu, (unsigned)max(0, jhi));
-    const int c_lo = wlo >> 5;
-    int nch = ((whi + 31) >> 5) - c_lo;
-    if (whi <= wlo) nch = 0;
-    if (nch > NCH) {  // cannot happen for the shapes the dispatch admits
-      nch = NCH;
+    // never past the S tile: c_lo + nch <= NB / 32 (and at most NCH chunks)
+    if (nch > NCH || c_lo + nch > TcChunks<NB>::kAll) {  // cannot happen, see above
+      nch = max(0, min(NCH, TcChunks<NB>::kAll - c_lo));
       if (err && (tid & 31) == 0) atomicOr(err, MN_STATUS_TC_TIMEOUT);
     }
 
@@ -232,13 +248,13 @@ __global__ void __launch_bounds__(128, 2) attn_tc_kernel(
     for (int u = 0; u < NCH; ++u) {
       if (u >= nch) continue;
       const int cb = (c_lo + u) * 32;
-      const bool whole = __all_sync(0xffffffffu, jlo <= cb && jhi >= cb + 32);
+      const bool whole = !WIN || __all_sync(0xffffffffu, jlo <= cb && jhi >= cb + 32);
       const float4* b4 = reinterpret_cast<const float4*>(sbias + cb);
       if (whole) {
 #pragma unroll
         for (int i4 = 0; i4 < 8; ++i4) {
           float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (BIAS) bb = b4[i4];
+          if (BIAS || !WIN) bb = b4[i4];
           const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -364,20 +380,40 @@ __global__ void __launch_bounds__(128, 2) attn_tc_kernel(
   if (!ok && tid == 0 && err) atomicOr(err, MN_STATUS_TC_TIMEOUT);
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, 256);
+  if (warp == 0) tc::tmem_dealloc(tmem, S::kTmemCols);
 }
 
-template <typename ET, int NB>
+template <typename ET, int NB, bool WIN>
 static void launch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v, int64_t kb,
                       int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int window, float scale,
                       const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st) {
   const size_t smem = TcSmem<NB>::bytes;
-  auto kern = bias ? attn_tc_kernel<ET, NB, true> : attn_tc_kernel<ET, NB, false>;
+  auto kern = bias ? attn_tc_kernel<ET, NB, WIN, true> : attn_tc_kernel<ET, NB, WIN, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((Nq + kTcM - 1) / kTcM, H, B);
   kern<<<grid, 128, smem, st>>>(static_cast<const ET*>(q), qb, qn, qh, static_cast<const ET*>(k),
                                 static_cast<const ET*>(v), kb, kn, kh, Nq, Nk, H, window, scale, bias, bias_dtype,
                                 out, out_dtype, err);
+}
+
+#ifndef MN_TC_BLOCK_KEYS
+#define MN_TC_BLOCK_KEYS 64  // key block of the multi-block paths: 64 or 128
+#endif
+
+template <typename ET>
+static void dispatch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v, int64_t kb,
+                        int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int window, float scale,
+                        const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st) {
+  constexpr int NBM = MN_TC_BLOCK_KEYS;
+  if (window >= 0 && kTcM + 2 * window <= 160)  // the whole band in one block
+    launch_tc<ET, 160, true>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
+                             out_dtype, err, st);
+  else if (window >= 0)
+    launch_tc<ET, NBM, true>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
+                             out_dtype, err, st);
+  else
+    launch_tc<ET, NBM, false>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
+                              out_dtype, err, st);
 }
 
 // Host-side dispatch used by mn_local_attention / mn_attention.  Returns
@@ -391,24 +427,12 @@ bool attention_tc(int dtype, const void* q, int64_t qb, int64_t qn, int64_t qh, 
     return (reinterpret_cast<uintptr_t>(p) % 16 == 0) && s1 % 8 == 0 && s2 % 8 == 0 && s3 % 8 == 0;
   };
   if (!aligned(q, qb, qn, qh) || !aligned(k, kb, kn, kh) || !aligned(v, kb, kn, kh)) return false;
-  if (window >= 0) {
-    const int need = kTcM + 2 * window;
-    if (need <= 160) {
-      if (dtype == MN_F16)
-        launch_tc<__half, 160>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
-                               out_dtype, err, st);
-      else
-        launch_tc<__nv_bfloat16, 160>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
-                                      out, out_dtype, err, st);
-      return true;
-    }
-  }
   if (dtype == MN_F16)
-    launch_tc<__half, 128>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
-                           out_dtype, err, st);
+    dispatch_tc<__half>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
+                        out_dtype, err, st);
   else
-    launch_tc<__nv_bfloat16, 128>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
-                                  out, out_dtype, err, st);
+    dispatch_tc<__nv_bfloat16>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
+                               out_dtype, err, st);
   return true;
 }
 

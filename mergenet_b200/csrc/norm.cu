@@ -8,6 +8,41 @@
 
 namespace mn {
 
+// fp16 LayerNorm of one row held by a warp (four floats per lane-step).
+template <int C>
+__device__ __forceinline__ void layernorm_row_store(const float (&v)[C / 128][4], const float* __restrict__ gamma,
+                                                    const float* __restrict__ beta, float eps, __half* hrow,
+                                                    int lane) {
+  constexpr int V = C / 128;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) s += (v[i][0] + v[i][1]) + (v[i][2] + v[i][3]);
+  const float mean = warp_sum(s) * (1.0f / C);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d = v[i][j] - mean;
+      q = fmaf(d, d, q);
+    }
+  const float rstd = rsqrtf(warp_sum(q) * (1.0f / C) + eps);
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
+  uint2* hl = reinterpret_cast<uint2*>(hrow);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const float4 g = g4[lane + 32 * i], bb = b4[lane + 32 * i];
+    const float o0 = (v[i][0] - mean) * rstd * g.x + bb.x, o1 = (v[i][1] - mean) * rstd * g.y + bb.y;
+    const float o2 = (v[i][2] - mean) * rstd * g.z + bb.z, o3 = (v[i][3] - mean) * rstd * g.w + bb.w;
+    __half2 lo = __floats2half2_rn(o0, o1), hi = __floats2half2_rn(o2, o3);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&lo);
+    u.y = *reinterpret_cast<uint32_t*>(&hi);
+    hl[lane + 32 * i] = u;
+  }
+}
+
 // One warp per row; C must be a multiple of 128 (four floats per lane-step).
 template <int C>
 __global__ void __launch_bounds__(256) add_layernorm_kernel(const float* __restrict__ x, const __half* __restrict__ y,
@@ -52,34 +87,56 @@ __global__ void __launch_bounds__(256) add_layernorm_kernel(const float* __restr
       hr[lane + 32 * i] = u;
     }
   }
-  if (!h_ln) return;
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < V; ++i) s += (v[i][0] + v[i][1]) + (v[i][2] + v[i][3]);
-  const float mean = warp_sum(s) * (1.0f / C);
-  float q = 0.f;
-#pragma unroll
-  for (int i = 0; i < V; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float d = v[i][j] - mean;
-      q = fmaf(d, d, q);
-    }
-  const float rstd = rsqrtf(warp_sum(q) * (1.0f / C) + eps);
-  const float4* g4 = reinterpret_cast<const float4*>(gamma);
-  const float4* b4 = reinterpret_cast<const float4*>(beta);
-  uint2* hl = reinterpret_cast<uint2*>(h_ln + row * C);
+  if (h_ln) layernorm_row_store<C>(v, gamma, beta, eps, h_ln + row * C, lane);
+}
+
+// The embedding step of the local ViT fused with the first block's LayerNorm
+// (timm PatchEmbed + _pos_embed, then norm1): row t of image b is
+// cls + pos[0] for t == 0 and float(emb[b, t - 1]) + pos[t] otherwise, with
+// emb the fp16 patch-projection output.  Writes that fp32 row and its fp16
+// LayerNorm.
+template <int C>
+__global__ void __launch_bounds__(256) embed_layernorm_kernel(const __half* __restrict__ emb,
+                                                              const float* __restrict__ pos,
+                                                              const float* __restrict__ cls, int tokens,
+                                                              const float* __restrict__ gamma,
+                                                              const float* __restrict__ beta, float eps,
+                                                              int64_t rows, float* __restrict__ x_out,
+                                                              __half* __restrict__ h_ln) {
+  constexpr int V = C / 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int t = (int)(row % tokens);
+  const int64_t b = row / tokens;
+  const float4* pr = reinterpret_cast<const float4*>(pos + (int64_t)t * C);
+  float v[V][4];
 #pragma unroll
   for (int i = 0; i < V; ++i) {
-    const float4 g = g4[lane + 32 * i], bb = b4[lane + 32 * i];
-    const float o0 = (v[i][0] - mean) * rstd * g.x + bb.x, o1 = (v[i][1] - mean) * rstd * g.y + bb.y;
-    const float o2 = (v[i][2] - mean) * rstd * g.z + bb.z, o3 = (v[i][3] - mean) * rstd * g.w + bb.w;
-    __half2 lo = __floats2half2_rn(o0, o1), hi = __floats2half2_rn(o2, o3);
-    uint2 u;
-    u.x = *reinterpret_cast<uint32_t*>(&lo);
-    u.y = *reinterpret_cast<uint32_t*>(&hi);
-    hl[lane + 32 * i] = u;
+    const float4 a = pr[lane + 32 * i];
+    v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
   }
+  if (t == 0) {
+    const float4* cr = reinterpret_cast<const float4*>(cls);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float4 a = cr[lane + 32 * i];
+      v[i][0] = a.x + v[i][0]; v[i][1] = a.y + v[i][1]; v[i][2] = a.z + v[i][2]; v[i][3] = a.w + v[i][3];
+    }
+  } else {
+    const uint2* er = reinterpret_cast<const uint2*>(emb + (b * (tokens - 1) + (t - 1)) * C);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const uint2 u = er[lane + 32 * i];
+      const __half2 lo = *reinterpret_cast<const __half2*>(&u.x), hi = *reinterpret_cast<const __half2*>(&u.y);
+      v[i][0] = __low2float(lo) + v[i][0]; v[i][1] = __high2float(lo) + v[i][1];
+      v[i][2] = __low2float(hi) + v[i][2]; v[i][3] = __high2float(hi) + v[i][3];
+    }
+  }
+  float4* xo = reinterpret_cast<float4*>(x_out + row * C);
+#pragma unroll
+  for (int i = 0; i < V; ++i) xo[lane + 32 * i] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+  layernorm_row_store<C>(v, gamma, beta, eps, h_ln + row * C, lane);
 }
 
 }  // namespace mn
@@ -102,6 +159,28 @@ extern "C" int mn_add_layernorm(int64_t rows, int channels, const float* x, cons
     case 256: add_layernorm_kernel<256><<<grid, 256, 0, st>>>(x, yh, gamma, beta, eps, rows, x_out, hl, hr); break;
     case 512: add_layernorm_kernel<512><<<grid, 256, 0, st>>>(x, yh, gamma, beta, eps, rows, x_out, hl, hr); break;
     case 768: add_layernorm_kernel<768><<<grid, 256, 0, st>>>(x, yh, gamma, beta, eps, rows, x_out, hl, hr); break;
+    default: return MN_ERR_UNSUPPORTED;
+  }
+  return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
+}
+
+extern "C" int mn_embed_layernorm(int batch, int tokens, int channels, const void* emb, const float* pos,
+                                  const float* cls, const float* gamma, const float* beta, float eps, float* x_out,
+                                  void* h_ln, void* stream) {
+  if (batch < 0 || tokens < 1 || channels <= 0) return MN_ERR_ARG;
+  if (batch == 0) return MN_OK;
+  if ((tokens > 1 && !emb) || !pos || !cls || !gamma || !beta || !x_out || !h_ln) return MN_ERR_ARG;
+  cudaGetLastError();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t rows = (int64_t)batch * tokens;
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  const __half* e = static_cast<const __half*>(emb);
+  __half* hl = static_cast<__half*>(h_ln);
+  switch (channels) {
+    case 384: embed_layernorm_kernel<384><<<grid, 256, 0, st>>>(e, pos, cls, tokens, gamma, beta, eps, rows, x_out, hl); break;
+    case 256: embed_layernorm_kernel<256><<<grid, 256, 0, st>>>(e, pos, cls, tokens, gamma, beta, eps, rows, x_out, hl); break;
+    case 512: embed_layernorm_kernel<512><<<grid, 256, 0, st>>>(e, pos, cls, tokens, gamma, beta, eps, rows, x_out, hl); break;
+    case 768: embed_layernorm_kernel<768><<<grid, 256, 0, st>>>(e, pos, cls, tokens, gamma, beta, eps, rows, x_out, hl); break;
     default: return MN_ERR_UNSUPPORTED;
   }
   return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;

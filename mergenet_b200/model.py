@@ -180,16 +180,34 @@ class MergeNetSmall(nn.Module):
         """fp16 copies of the GEMM weights autocast would cast on every call."""
         if self._half is None:
             self._half = {n: p.detach().half() for n, p in self.named_parameters()
-                          if p.ndim >= 2 and "pos_embed" not in n and "cls_token" not in n}
+                          if "pos_embed" not in n and "cls_token" not in n and "norm" not in n}
         return self._half
 
+    def _reset_caches(self):
+        self._half = None
+        self._kv16 = None
+        self._patch_w16 = None
+
+    def load_state_dict(self, state_dict, strict=True, assign=False):
+        res = super().load_state_dict(state_dict, strict=strict, assign=assign)
+        self._reset_caches()
+        return res
+
+    def _apply(self, fn, *args, **kwargs):
+        # .to() / .cuda() / .half() move or convert the parameters: the fp16
+        # copies are rebuilt from the new ones on the next forward
+        res = super()._apply(fn, *args, **kwargs)
+        self._reset_caches()
+        return res
+
     def _linear16(self, x, name, lin):
-        w = self._weights16()[name + ".weight"]
-        return F.linear(x.half(), w, lin.bias.half())
+        w16 = self._weights16()
+        return F.linear(x.half(), w16[name + ".weight"], w16[name + ".bias"])
 
     def _metric(self, h_raw, i, metrics, w16):
         lin = self.local.metric_layers[i]
-        torch.addmm(lin.bias.half(), h_raw.view(-1, h_raw.shape[-1]), w16[f"local.metric_layers.{i}.weight"].t(),
+        torch.addmm(w16[f"local.metric_layers.{i}.bias"], h_raw.view(-1, h_raw.shape[-1]),
+                    w16[f"local.metric_layers.{i}.weight"].t(),
                     out=metrics[i].view(-1, metrics.shape[-1]))
 
     def _attn_local(self, h, i, blk):
@@ -209,7 +227,7 @@ class MergeNetSmall(nn.Module):
         # with the exact erf GELU to within fp16 output rounding)
         w16 = self._weights16()
         shp = h.shape
-        f = torch._addmm_activation(blk.mlp.fc1.bias.half(), h.reshape(-1, shp[-1]),
+        f = torch._addmm_activation(w16[prefix + ".mlp.fc1.bias"], h.reshape(-1, shp[-1]),
                                     w16[prefix + ".mlp.fc1.weight"].t(), use_gelu=True)
         return self._linear16(f, prefix + ".mlp.fc2", blk.mlp.fc2).view(*shp[:-1], -1)
 
@@ -225,7 +243,7 @@ class MergeNetSmall(nn.Module):
         w16 = self._weights16()
         qn = add_layernorm(topk_x, None, ca.q_norm)[1]
         kvn = add_layernorm(x_embed, None, ca.kv_norm)[1]
-        q = F.linear(qn, w16["encode_cross_attention.q_proj.weight"], ca.q_proj.bias.half())
+        q = F.linear(qn, w16["encode_cross_attention.q_proj.weight"], w16["encode_cross_attention.q_proj.bias"])
         if self._kv16 is None:
             self._kv16 = (torch.cat([ca.k_proj.weight, ca.v_proj.weight]).half(),
                           torch.cat([ca.k_proj.bias, ca.v_proj.bias]).half())
@@ -239,10 +257,11 @@ class MergeNetSmall(nn.Module):
             torch.backends.cuda.matmul.allow_tf32 = prev
         return out
 
-    def _embed(self, images, w16):
-        """timm PatchEmbed + _pos_embed: the non-overlapping patch conv as one
-        GEMM over fp16 patch rows, written with the position embedding into
-        the fp32 residual stream (CLS row first)."""
+    def _embed(self, images, w16, norm1):
+        """timm PatchEmbed + _pos_embed, then the first block's norm1: the
+        non-overlapping patch conv as one GEMM over fp16 patch rows, then one
+        fused kernel that adds the position embedding (CLS row first) into the
+        fp32 residual stream and writes its fp16 LayerNorm.  Returns (x, h)."""
         vit = self.local.vit
         b, ch, hh, ww = images.shape
         p = self.patch_size
@@ -253,11 +272,8 @@ class MergeNetSmall(nn.Module):
         if wpe is None:
             wpe = w16["local.vit.patch_embed.proj.weight"].reshape(self.embed_dim, -1).t().contiguous()
             self._patch_w16 = wpe
-        emb = torch.addmm(vit.patch_embed.proj.bias.half(), patches.view(b * gh * gw, -1), wpe)
-        x = torch.empty(b, gh * gw + 1, self.embed_dim, device=images.device, dtype=torch.float32)
-        torch.add(emb.view(b, gh * gw, -1), vit.pos_embed[:, 1:], out=x[:, 1:])
-        x[:, 0] = vit.cls_token[:, 0] + vit.pos_embed[:, 0]
-        return x
+        emb = torch.addmm(w16["local.vit.patch_embed.proj.bias"], patches.view(b * gh * gw, -1), wpe)
+        return embed_layernorm(emb.view(b, gh * gw, -1), vit.pos_embed[0], vit.cls_token.view(-1), norm1)
 
     @torch.no_grad()
     def forward(self, images, return_intermediates=False):
@@ -269,7 +285,7 @@ class MergeNetSmall(nn.Module):
         w16 = self._weights16()
         vit = self.local.vit
         b = images.shape[0]
-        x = self._embed(images, w16)
+        x, h0 = self._embed(images, w16, vit.blocks[0].norm1)
         n, c = x.shape[1], x.shape[2]
         depth = len(vit.blocks)
         metrics = torch.empty(depth, b, n, self.local.metric_layers[0].out_features, device=x.device,
@@ -277,8 +293,10 @@ class MergeNetSmall(nn.Module):
         y = None
         for i, blk in enumerate(vit.blocks):
             # x <- x + y (previous MLP), h = LN1(x); fp16(x) feeds the previous metric head
-            _, h, raw = add_layernorm(x, y, blk.norm1, x_out=x if y is not None else None, want_raw=i > 0)
-            if i > 0:
+            if i == 0:
+                h = h0
+            else:
+                _, h, raw = add_layernorm(x, y, blk.norm1, x_out=x, want_raw=True)
                 self._metric(raw, i - 1, metrics, w16)
             p = self._attn_local(h, i, blk)
             _, h, _ = add_layernorm(x, p, blk.norm2, x_out=x)
@@ -310,6 +328,73 @@ class MergeNetSmall(nn.Module):
             aux.update(x_embed=x_embed, metrics=metrics, topk_x=topk_x, topk_size=route.topk_size,
                        token_center=route.center)
         return logits, aux
+
+
+class ForwardGraph:
+    """A forward pass of fixed batch shape captured once as a CUDA graph and
+    replayed: the same kernels as ``model(images)``, launched without the
+    per-kernel host cost (about fifty library kernels and as many cuBLAS and
+    PyTorch kernels per forward).
+
+    ``images`` given at construction becomes the graph's input buffer.  A call
+    with a batch of the same shape copies it into that buffer on the current
+    stream (a pinned host tensor gives an asynchronous host-to-device copy);
+    a call without arguments replays on the buffer's current contents.  The
+    returned logits and aux tensors are the graph's own outputs and are
+    overwritten by the next replay.
+    """
+
+    def __init__(self, model, images, warmup=2):
+        if not images.is_cuda:
+            raise RuntimeError("ForwardGraph needs a CUDA input buffer")
+        self.model = model
+        self.images = images
+        side = torch.cuda.Stream(images.device)
+        side.wait_stream(torch.cuda.current_stream(images.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):  # plans, weight copies and status words exist before capture
+                model(images)
+        torch.cuda.current_stream(images.device).wait_stream(side)
+        torch.cuda.synchronize(images.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits, self.aux = model(images)
+
+    def __call__(self, images=None):
+        if images is not None and images is not self.images:
+            if images.shape != self.images.shape:
+                raise ValueError(f"ForwardGraph was captured for {tuple(self.images.shape)}, "
+                                 f"got {tuple(images.shape)}")
+            self.images.copy_(images, non_blocking=True)
+        self.graph.replay()
+        return self.logits, self.aux
+
+    @staticmethod
+    def library_launches(model):
+        """Library (mn_*) kernels one forward launches: two fused
+        add+LayerNorm per block (the first one fused with the embedding) plus
+        the closing one and the two cross norms; a windowed attention and a CLS row per local block; one
+        attention per latent block and for the recovery cross-attention; and
+        the four routing kernels."""
+        nl, nt = len(model.local.vit.blocks), len(model.latent.vit.blocks)
+        return (2 * nl + 1 + 2 + 2 * nt) + (2 * nl + nt + 1) + 4
+
+
+def embed_layernorm(emb, pos, cls, ln):
+    """x = [cls + pos[0]; float(emb) + pos[1:]] per image (fp32) and its fp16
+    LayerNorm, in one pass of the library's fused kernel.  emb [B, T-1, C]
+    fp16, pos [T, C] fp32, cls [C] fp32.  Returns (x, h_ln)."""
+    from . import _lib as L
+    b, t1, c = emb.shape
+    x = torch.empty(b, t1 + 1, c, device=emb.device, dtype=torch.float32)
+    h = torch.empty(b, t1 + 1, c, device=emb.device, dtype=torch.float16)
+    emb = emb.contiguous()
+    pos = pos.contiguous().float()
+    cls = cls.contiguous().float()
+    L.check(L.lib().mn_embed_layernorm(b, t1 + 1, c, L.ptr(emb), L.ptr(pos), L.ptr(cls), L.ptr(ln.weight),
+                                       L.ptr(ln.bias), float(ln.eps), L.ptr(x), L.ptr(h), L.stream_of(emb)),
+            "mn_embed_layernorm")
+    return x, h
 
 
 def add_layernorm(x, y, ln, x_out=None, want_ln=True, want_raw=False):

@@ -140,6 +140,26 @@ def test_local_block_attention_cls_global(dev, dtype):
     torch.testing.assert_close(out.float(), exp, atol=tol, rtol=tol)
 
 
+@pytest.mark.parametrize("tokens,window,biased", [(785, 17, False), (785, 40, True), (300, 100, False),
+                                                   (131, 70, True)])
+def test_wide_window_multi_block(dev, tokens, window, biased):
+    """Windows wider than one 160-key block run as several key blocks with an
+    online softmax; the last query tile has padding rows whose window starts
+    past the current block."""
+    import mergenet_b200 as mn
+    torch.manual_seed(tokens + window)
+    b, h, d = 2, 6, 64
+    qkv = (torch.randn(b, tokens, 3 * h * d, device=dev) * 0.5).half()
+    bias = (torch.rand(b, tokens, device=dev) * 3 + 0.5).log() if biased else None
+    out = mn.local_attention_packed(qkv, h, window, cls_global=False, bias=bias)
+    view = qkv.view(b, tokens, 3, h, d)
+    q, k, v = (view[:, :, i].transpose(1, 2) for i in range(3))
+    exp = reference_bhnd(q, k, v, bias.half() if biased else None, window)
+    exp = exp.transpose(1, 2).reshape(b, tokens, h * d)
+    torch.testing.assert_close(out.float(), exp, atol=5e-3, rtol=5e-3)
+    assert mn.attention.attention_status(dev) == 0
+
+
 def test_config3_biased_block_against_oracle(dev):
     """Config 3 shape family (785 tokens, 6x64, window 16, per-key bias) at a
     batch the float64 oracle finishes quickly."""
@@ -221,3 +241,22 @@ def test_add_layernorm(dev, rows, y):
     assert torch.equal(xo, s)
     assert torch.equal(raw, s.half())
     torch.testing.assert_close(h.float(), ln(s).half().float(), atol=2e-3, rtol=2e-3)
+
+
+@pytest.mark.parametrize("batch,tokens", [(3, 785), (1, 2), (2, 1)])
+def test_embed_layernorm(dev, batch, tokens):
+    """Position embedding + CLS row into the fp32 stream, fused with norm1:
+    the sum is bit-exact with PyTorch's fp32 add, the LayerNorm within fp16
+    output rounding."""
+    from mergenet_b200.model import embed_layernorm
+    torch.manual_seed(tokens)
+    emb = (torch.randn(batch, tokens - 1, 384, device=dev) * 2).half()
+    pos = torch.randn(tokens, 384, device=dev) * 0.02
+    cls = torch.randn(384, device=dev) * 1e-3
+    ln = torch.nn.LayerNorm(384, eps=1e-6).to(dev)
+    torch.nn.init.normal_(ln.weight)
+    torch.nn.init.normal_(ln.bias)
+    want = torch.cat([cls.expand(batch, 1, -1), emb.float()], 1) + pos
+    x, h = embed_layernorm(emb, pos, cls, ln)
+    assert torch.equal(x, want)
+    torch.testing.assert_close(h.float(), ln(want).half().float(), atol=2e-3, rtol=2e-3)
