@@ -352,6 +352,150 @@ __global__ void __launch_bounds__(512) route_score_fast_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// route_score_lane: the same scores with one thread per donor.  The band's
+// receivers are normalised once into shared memory (fp32 rows of CM + 4
+// floats, so the rows of consecutive receivers start 16 bytes apart modulo
+// 128 and a warp's 16-byte reads spread over all banks); each thread holds
+// its donor's normalised row in registers and walks its compact slots, so a
+// (donor, slot) edge costs CM / 4 vector loads and CM FMAs with no shuffle.
+// ---------------------------------------------------------------------------
+template <int CM>
+__device__ __forceinline__ void load_metric_row_f32(const float* row, float* v) {
+#pragma unroll
+  for (int w = 0; w < CM / 4; ++w) {
+    const float4 u = __ldg(reinterpret_cast<const float4*>(row) + w);
+    v[4 * w] = u.x; v[4 * w + 1] = u.y; v[4 * w + 2] = u.z; v[4 * w + 3] = u.w;
+  }
+}
+template <int CM, typename ET>
+__device__ __forceinline__ void load_metric_row(const ET* row, float* v) {
+  if constexpr (std::is_same<ET, float>::value) {
+    load_metric_row_f32<CM>(row, v);
+  } else {
+#pragma unroll
+    for (int w = 0; w < CM / 8; ++w) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(row) + w);
+      const ET* e = reinterpret_cast<const ET*>(&u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[8 * w + i] = to_f32(e[i]);
+    }
+  }
+}
+// metric / max(|metric|, 1e-6) (dtem.py:1689-1691)
+template <int CM>
+__device__ __forceinline__ void normalise_row(float* v) {
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < CM; ++i) s4[i & 3] = fmaf(v[i], v[i], s4[i & 3]);
+  const float nr = fmaxf(sqrtf((s4[0] + s4[1]) + (s4[2] + s4[3])), 1e-6f);
+#pragma unroll
+  for (int i = 0; i < CM; ++i) v[i] = v[i] / nr;
+}
+
+constexpr int kLaneScoreThreads = 256;
+
+template <int MDT, int CM>
+__global__ void __launch_bounds__(kLaneScoreThreads, 2) route_score_lane_kernel(
+    const typename Elem<MDT>::T* __restrict__ metrics, const int32_t* __restrict__ table, int B, int T, int grid_w,
+    int half, int kc, int kin, Banding band, float tau1, RouteWs ws, int* status) {
+  using ET = typename Elem<MDT>::T;
+  constexpr int RS = CM + 4;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red[64];
+  float* nrm = reinterpret_cast<float*>(smem_raw);  // [s_hi - s_lo][RS]
+  const int l = blockIdx.y;
+  const int b = blockIdx.x / band.bands;
+  const int bi = blockIdx.x % band.bands;
+  const int q = l & 1;
+  const int dp = q ? 0 : 1, rp = 1 - dp;
+  const ParityTables pt = parity_tables(table, half, kc, kin, q);
+  const int grid_h = (2 * half) / grid_w;
+  const int r0 = bi * band.rows, r1 = min(grid_h, r0 + band.rows);
+  const int d_lo = (r0 * grid_w - dp + 1) >> 1, d_hi = (r1 * grid_w - dp + 1) >> 1;
+  const int rr0 = max(0, r0 - band.radius_rows), rr1 = min(grid_h, r1 + band.radius_rows);
+  const int s_lo = (rr0 * grid_w - rp + 1) >> 1, s_hi = (rr1 * grid_w - rp + 1) >> 1;
+  const ET* mbase = metrics + ((int64_t)l * B + b) * (int64_t)T * CM;
+
+  for (int s = s_lo + threadIdx.x; s < s_hi; s += blockDim.x) {
+    float v[CM];
+    load_metric_row<CM>(mbase + (int64_t)(1 + 2 * s + rp) * CM, v);
+    normalise_row<CM>(v);
+    float4* dst = reinterpret_cast<float4*>(nrm + (int64_t)(s - s_lo) * RS);
+#pragma unroll
+    for (int w = 0; w < CM / 4; ++w) dst[w] = make_float4(v[4 * w], v[4 * w + 1], v[4 * w + 2], v[4 * w + 3]);
+  }
+  __syncthreads();
+
+  float emin = INFINITY, emax = -INFINITY;
+  const int64_t lb = (int64_t)l * B + b;
+  float* sc_out = ws.assign + lb * half * kc;
+  float* e_out = ws.energy + lb * half;
+  const bool unit_tau = tau1 == 1.0f;
+  for (int d = d_lo + threadIdx.x; d < d_hi; d += blockDim.x) {
+    float a[CM];
+    load_metric_row<CM>(mbase + (int64_t)(1 + 2 * d + dp) * CM, a);
+    normalise_row<CM>(a);
+    const int32_t* srx = pt.slot_rx + (int64_t)d * kc;
+    float sc[kMaxKc];
+#pragma unroll
+    for (int c = 0; c < kMaxKc; ++c) {
+      sc[c] = -INFINITY;
+      if (c >= kc) continue;
+      const int sidx = __ldg(srx + c);
+      if (sidx < 0) continue;
+      if (sidx < s_lo || sidx >= s_hi) {  // outside the band's receivers: a table error
+        if (status) atomicOr(status, MN_STATUS_TOO_MANY_EDGES);
+        continue;
+      }
+      const float4* rv = reinterpret_cast<const float4*>(nrm + (int64_t)(sidx - s_lo) * RS);
+      float acc4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int w = 0; w < CM / 4; ++w) {
+        const float4 r4 = rv[w];
+        acc4[0] = fmaf(a[4 * w], r4.x, acc4[0]);
+        acc4[1] = fmaf(a[4 * w + 1], r4.y, acc4[1]);
+        acc4[2] = fmaf(a[4 * w + 2], r4.z, acc4[2]);
+        acc4[3] = fmaf(a[4 * w + 3], r4.w, acc4[3]);
+      }
+      const float acc = (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
+      // logits = scores / tau1 (dtem.py:1557); exact without a division at tau1 == 1
+      sc[c] = unit_tau ? acc : acc / tau1;
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kMaxKc; ++c) m = fmaxf(m, sc[c]);
+    float e = 0.f;
+    if (m != -INFINITY) {
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < kMaxKc; ++c)
+        if (sc[c] != -INFINITY) sum += expf(sc[c] - m);
+      e = expf(logf(sum) + m);
+    }
+    float* dst = sc_out + (int64_t)d * kc;
+    if (kc == 12) {  // the radius-3 compact width: three aligned 16-byte stores
+      float4* d4 = reinterpret_cast<float4*>(dst);
+      d4[0] = make_float4(sc[0], sc[1], sc[2], sc[3]);
+      d4[1] = make_float4(sc[4], sc[5], sc[6], sc[7]);
+      d4[2] = make_float4(sc[8], sc[9], sc[10], sc[11]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < kMaxKc; ++c)
+        if (c < kc) dst[c] = sc[c];
+    }
+    e_out[d] = e;
+    emin = fminf(emin, e);
+    emax = fmaxf(emax, e);
+  }
+  block_minmax(emin, emax, red);
+  if (threadIdx.x == 0) {
+    float* p = ws.partials + (lb * band.bands + bi) * 2;
+    p[0] = emin;
+    p[1] = emax;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // route_select: one CTA per (image, layer).  Global ThreTopK range over the
 // whole batch for this layer (thetopk.py:12-13), per-row threshold, then the
 // masked softmax x row k-hot and the clamp-normalise (dtem.py:1568-1579).
@@ -695,8 +839,18 @@ __global__ void __launch_bounds__(256) route_transport_kernel(
 // (alpha = wb_old / wb_safe, c = assign * wa_old / wb_safe) come from
 // route_mass in stencil order.
 // ---------------------------------------------------------------------------
+// fp32x2 fused multiply-add (two independent round-to-nearest FMAs).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)),
+        "l"(*reinterpret_cast<const uint64_t*>(&c)));
+  return *reinterpret_cast<const float2*>(&d);
+}
+
 template <typename XT, int CT, int DY1, int DY3>
-__global__ void __launch_bounds__(512) route_transport_stencil_kernel(
+__global__ void __launch_bounds__(448, 2) route_transport_stencil_kernel(
     const XT* __restrict__ x, int B, int T, int C, int grid_h, int grid_w, int half, int L, int k,
     int row_splits, RouteWs ws, XT* __restrict__ topk_x) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -715,53 +869,68 @@ __global__ void __launch_bounds__(512) route_transport_stencil_kernel(
   const bool active = rs < row_splits;
   const int rows_per = (grid_h + row_splits - 1) / row_splits;
   const int r_begin = rs * rows_per, r_end = min(grid_h, r_begin + rows_per);
+  const int rstride = grid_w * CT;  // floats between grid rows
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  auto ld = [&](int r, int c) -> float4 {
-    if (r < 0 || r >= grid_h || c < 0 || c >= grid_w) return zero;
-    return *reinterpret_cast<const float4*>(tile + (1 + r * grid_w + c) * CT + 4 * g);
-  };
-  auto fma4 = [](float w, float4 v, float4 a) {
-    a.x = fmaf(w, v.x, a.x); a.y = fmaf(w, v.y, a.y); a.z = fmaf(w, v.z, a.z); a.w = fmaf(w, v.w, a.w);
-    return a;
+  // acc (two float2 halves) += w * v, in the order of the scalar form
+  auto fma4 = [](float w, float4 v, float2& lo, float2& hi) {
+    const float2 ww = make_float2(w, w);
+    lo = ffma2(ww, make_float2(v.x, v.y), lo);
+    hi = ffma2(ww, make_float2(v.z, v.w), hi);
   };
   for (int l = 0; l < L; ++l) {
     const int rp = (l & 1) ? 1 : 0;  // receiver patch parity = column parity
     const int c = 2 * cr + rp;
     const float* cfl = ws.cf + ((int64_t)l * B + b) * half * kStencilSlots;
     if (active && r_begin < r_end) {
+      // donor columns c -/+ 1 (window) and c -/+ 3; a column outside the grid
+      // reads as zero (its coefficients are zero too)
+      const bool okl = c >= 1, okr = c + 1 < grid_w, okl3 = c >= 3, okr3 = c + 3 < grid_w;
+      const float* colm1 = tile + (1 + (okl ? c - 1 : c)) * CT + 4 * g;
+      const float* colp1 = tile + (1 + (okr ? c + 1 : c)) * CT + 4 * g;
+      const float* colm3 = tile + (1 + (okl3 ? c - 3 : c)) * CT + 4 * g;
+      const float* colp3 = tile + (1 + (okr3 ? c + 3 : c)) * CT + 4 * g;
+      auto ldc = [&](const float* col, bool ok, int r) -> float4 {
+        return (ok && (unsigned)r < (unsigned)grid_h) ? *reinterpret_cast<const float4*>(col + r * rstride) : zero;
+      };
       float4 wl[NW], wr[NW];
+      // window slot (ph + u) % NW holds grid row r - DY1 + u while row r is
+      // processed at unrolled phase ph; the row loop advances NW rows at a time
 #pragma unroll
       for (int u = 0; u < NW - 1; ++u) {
-        wl[u + 1] = ld(r_begin - DY1 + u, c - 1);
-        wr[u + 1] = ld(r_begin - DY1 + u, c + 1);
+        wl[u] = ldc(colm1, okl, r_begin - DY1 + u);
+        wr[u] = ldc(colp1, okr, r_begin - DY1 + u);
       }
-      for (int r = r_begin; r < r_end; ++r) {
+      for (int rb = r_begin; rb < r_end; rb += NW) {
 #pragma unroll
-        for (int u = 0; u < NW - 1; ++u) { wl[u] = wl[u + 1]; wr[u] = wr[u + 1]; }
-        wl[NW - 1] = ld(r + DY1, c - 1);
-        wr[NW - 1] = ld(r + DY1, c + 1);
-        const int s = (r * grid_w + c) >> 1;
-        const float4* cfp = reinterpret_cast<const float4*>(cfl + (int64_t)s * kStencilSlots);
-        const float4 q0 = __ldg(cfp), q1 = __ldg(cfp + 1), q2 = __ldg(cfp + 2), q3 = __ldg(cfp + 3);
-        const float cw[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
-                              q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
-        float4* own = reinterpret_cast<float4*>(tile + (1 + r * grid_w + c) * CT + 4 * g);
-        const float4 xo = *own;
-        float4 acc = make_float4(cw[0] * xo.x, cw[0] * xo.y, cw[0] * xo.z, cw[0] * xo.w);
-        int j = 1;
-        if (DY3 >= 0) {
+        for (int ph = 0; ph < NW; ++ph) {
+          const int r = rb + ph;
+          if (r < r_end) {
+            wl[(ph + NW - 1) % NW] = ldc(colm1, okl, r + DY1);
+            wr[(ph + NW - 1) % NW] = ldc(colp1, okr, r + DY1);
+            const int s = (r * grid_w + c) >> 1;
+            const float4* cfp = reinterpret_cast<const float4*>(cfl + (int64_t)s * kStencilSlots);
+            const float4 q0 = __ldg(cfp), q1 = __ldg(cfp + 1), q2 = __ldg(cfp + 2), q3 = __ldg(cfp + 3);
+            const float cw[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
+                                  q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
+            float4* own = reinterpret_cast<float4*>(tile + (1 + r * grid_w + c) * CT + 4 * g);
+            const float4 xo = *own;
+            float2 lo = make_float2(cw[0] * xo.x, cw[0] * xo.y), hi = make_float2(cw[0] * xo.z, cw[0] * xo.w);
+            int j = 1;
+            if (DY3 >= 0) {
 #pragma unroll
-          for (int dy = -DY3; dy <= DY3; ++dy) acc = fma4(cw[j++], ld(r + dy, c - 3), acc);
+              for (int dy = -DY3; dy <= DY3; ++dy) fma4(cw[j++], ldc(colm3, okl3, r + dy), lo, hi);
+            }
+#pragma unroll
+            for (int u = 0; u < NW; ++u) fma4(cw[j++], wl[(ph + u) % NW], lo, hi);
+#pragma unroll
+            for (int u = 0; u < NW; ++u) fma4(cw[j++], wr[(ph + u) % NW], lo, hi);
+            if (DY3 >= 0) {
+#pragma unroll
+              for (int dy = -DY3; dy <= DY3; ++dy) fma4(cw[j++], ldc(colp3, okr3, r + dy), lo, hi);
+            }
+            *own = make_float4(lo.x, lo.y, hi.x, hi.y);
+          }
         }
-#pragma unroll
-        for (int u = 0; u < NW; ++u) acc = fma4(cw[j++], wl[u], acc);
-#pragma unroll
-        for (int u = 0; u < NW; ++u) acc = fma4(cw[j++], wr[u], acc);
-        if (DY3 >= 0) {
-#pragma unroll
-          for (int dy = -DY3; dy <= DY3; ++dy) acc = fma4(cw[j++], ld(r + dy, c + 3), acc);
-        }
-        *own = acc;
       }
     }
     __syncthreads();
@@ -922,6 +1091,38 @@ static void launch_score_fast(const void* metrics, const int32_t* table, int B, 
   }
 }
 
+// Banding for route_score_lane: receiver rows of a band in <= 110 KB of
+// shared memory (two CTAs per SM).  Covers Cm in {32, 64} and kc <= 16.
+static bool lane_score_plan(int Cm, int kc, int grid_h, int grid_w, int radius_rows, Banding* bd, size_t* smem) {
+  if ((Cm != 32 && Cm != 64) || kc > kMaxKc) return false;
+  const size_t budget = 110 * 1024;
+  for (int nb = 1; nb <= grid_h; ++nb) {
+    const int rows = (grid_h + nb - 1) / nb;
+    const int need_rows = (nb == 1) ? grid_h : std::min(grid_h, rows + 2 * radius_rows);
+    const size_t bytes = ((size_t)(need_rows * grid_w + 1) / 2 + 1) * (Cm + 4) * sizeof(float);
+    if (bytes <= budget) {
+      bd->bands = (grid_h + rows - 1) / rows;
+      bd->rows = rows;
+      bd->radius_rows = radius_rows;
+      bd->cap = 0;
+      *smem = bytes;
+      return true;
+    }
+  }
+  return false;
+}
+
+template <int MDT>
+static void launch_score_lane(const void* metrics, const int32_t* table, int B, int T, int Cm, int grid_w, int half,
+                              int kc, int kin, const Banding& bd, size_t smem, float tau1, const RouteWs& ws, int L,
+                              int* status, cudaStream_t st) {
+  using ET = typename Elem<MDT>::T;
+  auto kern = Cm == 64 ? route_score_lane_kernel<MDT, 64> : route_score_lane_kernel<MDT, 32>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<dim3(B * bd.bands, L), kLaneScoreThreads, smem, st>>>(static_cast<const ET*>(metrics), table, B, T, grid_w,
+                                                               half, kc, kin, bd, tau1, ws, status);
+}
+
 template <int MDT>
 static void launch_score(const void* metrics, const int32_t* table, int B, int T, int Cm, int grid_w,
                          int half, int kc, int kin, const Banding& bd, float tau1, const RouteWs& ws,
@@ -986,12 +1187,22 @@ extern "C" int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev
   ws.carrier_tok = reinterpret_cast<int32_t*>(f);
 
   cudaGetLastError();  // clear any stale error so the check below is ours
-  Banding fbd;
-  size_t fsmem = 0;
+  Banding fbd, lbd;
+  size_t fsmem = 0, lsmem = 0;
   const int esize = metric_dtype == MN_F32 ? 4 : 2;
-  const bool fast = fast_score_plan(metric_dim, kc, dims->grid_h, dims->grid_w, dims->radius_rows, esize, &fbd, &fsmem);
-  const int bands_used = fast ? fbd.bands : bd.bands;
-  if (fast) {
+  const bool lane = reinterpret_cast<uintptr_t>(metrics) % 16 == 0 &&  // 16-byte row loads
+                    lane_score_plan(metric_dim, kc, dims->grid_h, dims->grid_w, dims->radius_rows, &lbd, &lsmem);
+  const bool fast = !lane &&
+                    fast_score_plan(metric_dim, kc, dims->grid_h, dims->grid_w, dims->radius_rows, esize, &fbd, &fsmem);
+  const int bands_used = lane ? lbd.bands : fast ? fbd.bands : bd.bands;
+  if (lane) {
+    if (metric_dtype == MN_F16)
+      launch_score_lane<MN_F16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, lbd, lsmem, tau1, ws, num_layers, status, st);
+    else if (metric_dtype == MN_BF16)
+      launch_score_lane<MN_BF16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, lbd, lsmem, tau1, ws, num_layers, status, st);
+    else
+      launch_score_lane<MN_F32>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, lbd, lsmem, tau1, ws, num_layers, status, st);
+  } else if (fast) {
     if (metric_dtype == MN_F16)
       launch_score_fast<MN_F16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, fbd, fsmem, tau1, ws, num_layers, status, st);
     else if (metric_dtype == MN_BF16)
