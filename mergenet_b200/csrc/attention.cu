@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(256) cls_row_kernel(const ET* __restrict__ q, 
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* p = reinterpret_cast<float*>(smem_raw);  // [N]
   float* qv = p + N;                              // [D]
-  float* part = qv + D;                           // [256]
+  float* part = qv + D;                           // [256 * 8]
   __shared__ float red[64];
   const int h = blockIdx.x, b = blockIdx.y;
   const int64_t base = (int64_t)b * sb + (int64_t)h * sh;
@@ -149,6 +149,33 @@ __global__ void __launch_bounds__(256) cls_row_kernel(const ET* __restrict__ q, 
   float tot = 0.f;
   for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
   __syncthreads();
+  // o = sum_j p_j v_j: with 16-byte rows, D / 8 threads cover a value row
+  // (8 channels each) and blockDim * 8 / D rows are summed in parallel, each
+  // group keeping its own partial sums, combined at the end
+  const bool vvec = vec && ((reinterpret_cast<uintptr_t>(v + base) & 15) == 0) && D <= 256;
+  if (vvec) {
+    const int per_row = D / 8;
+    const int sub = threadIdx.x % per_row, rg = threadIdx.x / per_row, nrg = blockDim.x / per_row;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (rg < nrg)
+      for (int j = rg; j < N; j += nrg) {
+        const uint4 u = *reinterpret_cast<const uint4*>(v + base + (int64_t)j * sn + sub * 8);
+        const ET* e = reinterpret_cast<const ET*>(&u);
+        const float pj = p[j];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = fmaf(pj, to_f32(e[i]), acc[i]);
+      }
+    if (rg < nrg)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) part[rg * D + sub * 8 + i] = acc[i];
+    __syncthreads();
+    for (int c = threadIdx.x; c < D; c += blockDim.x) {
+      float o = 0.f;
+      for (int gg = 0; gg < nrg; ++gg) o += part[gg * D + c];
+      store_any(out, out_dtype, (((int64_t)b * N) * H + h) * D + c, o / tot);
+    }
+    return;
+  }
   const int groups = blockDim.x / D > 0 ? blockDim.x / D : 1;
   const int c = threadIdx.x % D, g = threadIdx.x / D;
   float acc = 0.f;
@@ -313,7 +340,8 @@ extern "C" int mn_local_attention(int batch, int tokens, int heads, int head_dim
   const bool tc_shape = head_dim == 64 && (dtype == MN_F16 || dtype == MN_BF16);
   if (smem > 200 * 1024 && !tc_shape) return MN_ERR_UNSUPPORTED;
   const bool cls_row = cls_global && window >= 0 && tokens > 1;
-  const size_t smem_cls = ((size_t)tokens + head_dim + 256) * sizeof(float);
+  // p[tokens], q[D] and the partial sums: at most 256 threads x 8 channels
+  const size_t smem_cls = ((size_t)tokens + head_dim + 256 * 8) * sizeof(float);
   if (cls_row && (smem_cls > 200 * 1024 || head_dim > 256)) return MN_ERR_UNSUPPORTED;
   cudaGetLastError();
   cudaStream_t st = static_cast<cudaStream_t>(stream);

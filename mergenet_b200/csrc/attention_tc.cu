@@ -396,6 +396,9 @@ static void launch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const v
                                 out, out_dtype, err);
 }
 
+#ifndef MN_TC_SINGLE_BAND
+#define MN_TC_SINGLE_BAND 1  // windows up to 16: the tile's whole key band as one 160-key block
+#endif
 #ifndef MN_TC_BLOCK_KEYS
 #define MN_TC_BLOCK_KEYS 64  // key block of the multi-block paths: 64 or 128
 #endif
@@ -405,7 +408,7 @@ static void dispatch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const
                         int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int window, float scale,
                         const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st) {
   constexpr int NBM = MN_TC_BLOCK_KEYS;
-  if (window >= 0 && kTcM + 2 * window <= 160)  // the whole band in one block
+  if (MN_TC_SINGLE_BAND && window >= 0 && kTcM + 2 * window <= 160)  // the whole band in one block
     launch_tc<ET, 160, true>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
                              out_dtype, err, st);
   else if (window >= 0)
