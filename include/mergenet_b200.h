@@ -45,6 +45,10 @@ extern "C" {
 #define MN_STATUS_TOO_MANY_EDGES 4
 #define MN_STATUS_TC_TIMEOUT 256     /* a bounded tensor-core wait gave up */
 
+/* GEMM epilogues (mn_gemm_f16) */
+#define MN_EPI_BIAS 0       /* fp16(acc + bias) */
+#define MN_EPI_BIAS_GELU 1  /* fp16(gelu_erf(fp16(acc + bias))) */
+
 /* Library version, for the loader's sanity check. */
 int mn_version(void);
 
@@ -254,6 +258,20 @@ int mn_attention(int batch, int nq, int nk, int heads, int head_dim, int dtype,
 int mn_add_layernorm(int64_t rows, int channels, const float* x, const void* y,
                      const float* gamma, const float* beta, float eps,
                      float* x_out, void* h_ln, void* h_raw, void* stream);
+
+/* out[M, N] = epilogue(A[M, K] . W[N, K]^T + bias[N]) with fp16 A, W, bias
+ * and out, fp32 accumulation in tensor memory (tcgen05).  It replaces the
+ * fp16-autocast nn.Linear calls of the block MLP and projections (timm
+ * Mlp.forward / Attention.forward as used by LocalBlock and the latent
+ * blocks, opentome/timm/bias_local_attn.py:859-869).  With
+ * MN_EPI_BIAS_GELU the output is GELU (exact erf form) of the fp16-rounded
+ * linear output, rounded to fp16 again, as nn.GELU on the fp16 tensor gives.
+ * Rows of A, W and out are K / K / N contiguous with strides lda / ldw / ldo
+ * (elements); K must be a multiple of 64, N of 128, strides of 8, and all
+ * pointers 16-byte aligned (else MN_ERR_UNSUPPORTED).  bias may be NULL. */
+int mn_gemm_f16(int M, int N, int K, const void* a, int64_t lda, const void* w,
+                int64_t ldw, const void* bias, int epilogue, void* out,
+                int64_t ldo, int* status, void* stream);
 
 /* Patch embedding finish fused with the first block's LayerNorm (timm
  * PatchEmbed + VisionTransformer._pos_embed, then blocks[0].norm1, as the

@@ -20,6 +20,8 @@ MN_ERR_ARG, MN_ERR_UNSUPPORTED, MN_ERR_WORKSPACE, MN_ERR_LAUNCH = -1, -2, -3, -4
 MN_INFEASIBLE_BUDGET = 1
 MN_STATUS_INFEASIBLE_BUDGET, MN_STATUS_DEGENERATE_RANGE, MN_STATUS_TOO_MANY_EDGES = 1, 2, 4
 MN_STATUS_TC_TIMEOUT = 256
+MN_EPI_BIAS = 0
+MN_EPI_BIAS_GELU = 1
 
 _DTYPES = {torch.float32: MN_F32, torch.float16: MN_F16, torch.bfloat16: MN_BF16}
 
@@ -69,6 +71,7 @@ _SIGNATURES = {
                              c_int64, c_int64, c_int64, c_int, c_float, _P, c_int, _P, _P]),
     "mn_add_layernorm": (c_int, [c_int64, c_int, _P, _P, _P, _P, c_float, _P, _P, _P, _P]),
     "mn_embed_layernorm": (c_int, [c_int, c_int, c_int, _P, _P, _P, _P, _P, c_float, _P, _P, _P]),
+    "mn_gemm_f16": (c_int, [c_int, c_int, c_int, _P, c_int64, _P, c_int64, _P, c_int, _P, c_int64, _P, _P]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

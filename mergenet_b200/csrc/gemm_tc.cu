@@ -1,0 +1,363 @@
+// Persistent, warp-specialised tcgen05 GEMM for the block MLP:
+//
+//   out[M, N] = epilogue(A[M, K] . W[N, K]^T + bias[N])     (fp16 in, fp32 accumulate)
+//
+// with A the fp16 activations (rows K-contiguous) and W an nn.Linear weight
+// [N, K].  The epilogues reproduce what the reference computes under fp16
+// autocast: F.linear rounds its output to fp16 (bias added in fp32 first),
+// and nn.GELU (exact erf form) then runs on that fp16 tensor and rounds again
+// (timm Mlp.forward; opentome/timm/bias_local_attn.py:859-869).
+//
+// Roles (one CTA per SM, tiles handed out round-robin):
+//   warp 0      TMA producer: A and W k-blocks (128B-swizzled) into a ring of
+//               shared-memory stages, completion counted on mbarriers;
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=BN,
+//               K=16) per 16-wide K step into one of two TMEM accumulators;
+//   warps 2..9  epilogue: two warps per TMEM lane quadrant, each reading half
+//               of the accumulator columns, bias (+ GELU), fp16 stores.
+// The two accumulators let the epilogue of one tile overlap the main loop of
+// the next.  Every wait is bounded; a timeout sets MN_STATUS_TC_TIMEOUT.
+#include <cuda.h>  // CUtensorMap and its enums (the encoder is fetched at run time)
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "tc_common.cuh"
+
+namespace mn {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // one 128-byte swizzle atom of fp16
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = (2 + kEpiWarps) * 32;
+
+// Each epilogue warp stages a 32-row x 32-column fp16 block (2 KB) in shared
+// memory and writes it with one TMA store; two buffers per warp let the next
+// block be staged while the previous store drains.
+constexpr uint32_t kStageOutBytes = 32 * 32 * 2;
+constexpr uint32_t kOutBytes = kEpiWarps * 2 * kStageOutBytes;
+
+template <int BN>
+struct Cfg {
+  static constexpr uint32_t kABytes = BM * BK * 2;
+  static constexpr uint32_t kBBytes = BN * BK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = std::min<int>(8, (227 * 1024 - kOutBytes - 2048) / kStageBytes);
+  static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;  // two accumulators
+  static constexpr uint32_t out_off = kStages * kStageBytes;
+  static constexpr uint32_t bar_off = out_off + kOutBytes;  // full[S], empty[S], acc_full[2], acc_empty[2], done
+  static constexpr uint32_t slot_off = bar_off + (2 * kStages + 5) * 8;
+  static constexpr uint32_t bytes = slot_off + 16 + 1024;  // + alignment slack
+};
+static_assert(Cfg<256>::bytes <= 227 * 1024 && Cfg<192>::bytes <= 227 * 1024 && Cfg<128>::bytes <= 227 * 1024,
+              "shared memory");
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(tc::smem_u32(bar))
+      : "memory");
+}
+// shared -> global tensor store of a staged block (bulk async group)
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N committed store groups may still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
+}
+
+// GELU(x) = 0.5 x (1 + erf(x / sqrt 2)) on a pair, packed fp32x2.  erf(z) is
+// z * P(z^2) with |z| clamped to 2.9: P of degree 9, fitted by
+// mergenet_b200/csrc/gelu_fit.py (weighted least squares on Chebyshev nodes);
+// max |erf error| 4.5e-5 in float32 including the clamp, so
+// |GELU error| <= 2.3e-5 |x|, below half an fp16 ulp of the result for
+// |x| >= 0.2 and below 5e-6 in absolute terms for smaller |x|.
+constexpr float kErfClamp = 2.9f;
+__device__ __forceinline__ float2 splat(float c) { return make_float2(c, c); }
+__device__ __forceinline__ float2 gelu2(float2 x) {
+  float2 z = fmul2(x, splat(0.70710678118654752f));
+  z.x = fminf(fmaxf(z.x, -kErfClamp), kErfClamp);
+  z.y = fminf(fmaxf(z.y, -kErfClamp), kErfClamp);
+  const float2 u = fmul2(z, z);
+  float2 p = splat(-4.687449096e-09f);
+  p = ffma2(p, u, splat(2.359513331e-07f));
+  p = ffma2(p, u, splat(-5.365900961e-06f));
+  p = ffma2(p, u, splat(7.382134936e-05f));
+  p = ffma2(p, u, splat(-6.972589181e-04f));
+  p = ffma2(p, u, splat(4.874169827e-03f));
+  p = ffma2(p, u, splat(-2.638702281e-02f));
+  p = ffma2(p, u, splat(1.124738082e-01f));
+  p = ffma2(p, u, splat(-3.760007918e-01f));
+  p = ffma2(p, u, splat(1.128367066e+00f));
+  const float2 e = fmul2(z, p);
+  const float2 h = fmul2(x, make_float2(0.5f, 0.5f));
+  return ffma2(h, e, h);
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                              const __grid_constant__ CUtensorMap tmap_w,
+                                                              const __grid_constant__ CUtensorMap tmap_o, int M,
+                                                              int N, int K, const __half* __restrict__ bias,
+                                                              int* __restrict__ err) {
+  using C = Cfg<BN>;
+  constexpr int S = C::kStages;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + C::bar_off);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* done = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + C::slot_off);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM, num_n = N / BN, kblocks = K / BK;
+  const int tiles = num_m * num_n;
+
+  if (warp == 1) tc::tmem_alloc(tmem_slot, C::kTmemCols);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      tc::mbar_init(full + s, 1);
+      tc::mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(acc_full + b, 1);
+      tc::mbar_init(acc_empty + b, kEpiWarps);
+    }
+    tc::mbar_init(done, 1);
+    tc::fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_o)) : "memory");
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_phase[8];
+      for (int s = 0; s < 8; ++s) last_phase[s] = -1;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int mb = t / num_n, nb = t % num_n;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!tc::mbar_wait(empty + stage, phase ^ 1u, err)) { ok = false; break; }
+          const uint32_t sa = tc::smem_u32(base + stage * C::kStageBytes);
+          mbar_expect_tx(full + stage, C::kStageBytes);
+          tma_load_2d(sa, &tmap_a, kb * BK, mb * BM, full + stage);
+          tma_load_2d(sa + C::kABytes, &tmap_w, kb * BK, nb * BN, full + stage);
+          last_phase[stage] = (int)phase;
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // every copy this thread issued has landed before the CTA may exit
+      for (int s = 0; s < S; ++s)
+        if (last_phase[s] >= 0) tc::mbar_wait(full + s, (uint32_t)last_phase[s], nullptr);
+      if (!ok && err) atomicOr(err, MN_STATUS_TC_TIMEOUT);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_f16(0, 0, BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        if (!tc::mbar_wait(acc_empty + acc, acc_phase ^ 1u, err)) { ok = false; break; }
+        tc::fence_after_sync();
+        const uint32_t d = tmem + acc * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!tc::mbar_wait(full + stage, phase, err)) { ok = false; break; }
+          tc::fence_after_sync();
+          const uint32_t sa = tc::smem_u32(base + stage * C::kStageBytes);
+          const uint32_t sb = sa + C::kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            tc::mma_f16_ss(d, tc::sw128_desc(sa + k * 32, 16), tc::sw128_desc(sb + k * 32, 16), idesc,
+                           (kb > 0 || k > 0) ? 1u : 0u);
+          tc::mma_commit(empty + stage);  // the stage is free once these MMAs have read it
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        tc::mma_commit(acc_full + acc);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      // all MMAs issued by this thread have completed before TMEM is freed
+      tc::mma_commit(done);
+      tc::mbar_wait(done, 0, nullptr);
+      if (!ok && err) atomicOr(err, MN_STATUS_TC_TIMEOUT);
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int ew = warp - 2;
+    const int quad = warp & 3;  // TMEM lanes this warp may access
+    const int col_half = ew >> 2;
+    const uint32_t lane_sel = (uint32_t)(quad * 32) << 16;
+    uint8_t* stage_out = base + C::out_off + ew * 2 * kStageOutBytes;
+    int acc = 0, buf = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      const int mb = t / num_n, nb = t % num_n;
+      if (!tc::mbar_wait(acc_full + acc, acc_phase, err)) { ok = false; break; }
+      tc::fence_after_sync();
+      const __half* brow = bias ? bias + nb * BN : nullptr;
+#pragma unroll 1
+      for (int c = col_half * (BN / 64); c < (col_half + 1) * (BN / 64); ++c) {
+        float v[32];
+        tc::tmem_ld32(tmem + acc * BN + c * 32 + lane_sel, v);
+        if (c == (col_half + 1) * (BN / 64) - 1) {
+          // the accumulator is fully read: hand it back to the MMA warp
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty + acc);
+        }
+        uint4 bq[4];
+        if (brow) {
+          const uint4* b4 = reinterpret_cast<const uint4*>(brow + c * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) bq[q] = __ldg(b4 + q);
+        }
+        const __half2* bh = reinterpret_cast<const __half2*>(bq);
+        uint4 packed[4];
+        uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float2 p = make_float2(v[2 * i], v[2 * i + 1]);
+          if (brow) p = fadd2(p, __half22float2(bh[i]));
+          if (EPI == 1) p = gelu2(__half22float2(__float22half2_rn(p)));  // GELU of the fp16 linear output
+          __half2 h = __float22half2_rn(p);
+          pw[i] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        // stage this warp's 32 x 32 block (row = lane) and store it with TMA
+        if (lane == 0) bulk_wait_read<1>();  // the buffer's previous store has read it
+        __syncwarp();
+        uint8_t* sb = stage_out + buf * kStageOutBytes;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(sb + lane * 64 + q * 16) = packed[q];
+        tc::fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_o, tc::smem_u32(sb), nb * BN + c * 32, mb * BM + quad * 32);
+          bulk_commit();
+        }
+        buf ^= 1;
+      }
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+    if (lane == 0) bulk_wait_all();  // stores complete before the CTA exits
+    __syncwarp();
+    if (!ok && lane == 0 && err) atomicOr(err, MN_STATUS_TC_TIMEOUT);
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tc::tmem_dealloc(tmem, C::kTmemCols);
+}
+
+// ------------------------------------------------------------------ host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D fp16 tensor map over rows x cols (cols contiguous, row stride ld
+// elements) with a box_rows x box_cols box; operand maps use the 128-byte
+// swizzle the MMA descriptors expect, the output map a plain row-major box.
+static bool make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                     int box_cols, bool swizzle) {
+  EncodeTiledFn enc = encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int EPI>
+static int launch(int M, int N, int K, const void* a, int64_t lda, const void* w, int64_t ldw, const void* bias,
+                  void* out, int64_t ldo, int* status, cudaStream_t st) {
+  CUtensorMap ma, mw, mo;
+  if (!make_map(&ma, a, M, K, lda, BM, BK, true) || !make_map(&mw, w, N, K, ldw, BN, BK, true) ||
+      !make_map(&mo, out, M, N, ldo, 32, 32, false))
+    return MN_ERR_UNSUPPORTED;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int tiles = ((M + BM - 1) / BM) * (N / BN);
+  const int grid = std::max(1, std::min(tiles, sms));
+  auto kern = gemm_tc_kernel<BN, EPI>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<BN>::bytes);
+  kern<<<grid, kThreads, Cfg<BN>::bytes, st>>>(ma, mw, mo, M, N, K, static_cast<const __half*>(bias), status);
+  return MN_OK;
+}
+
+}  // namespace gemm
+}  // namespace mn
+
+using namespace mn;
+
+extern "C" int mn_gemm_f16(int M, int N, int K, const void* a, int64_t lda, const void* w, int64_t ldw,
+                           const void* bias, int epilogue, void* out, int64_t ldo, int* status, void* stream) {
+  if (M < 0 || N <= 0 || K <= 0 || !a || !w || !out) return MN_ERR_ARG;
+  if (M == 0) return MN_OK;
+  if (epilogue != MN_EPI_BIAS && epilogue != MN_EPI_BIAS_GELU) return MN_ERR_ARG;
+  // TMA: 16-byte aligned bases and row strides; whole 64-wide k-blocks
+  auto al16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  if (K % gemm::BK != 0 || lda < K || ldw < K || lda % 8 != 0 || ldw % 8 != 0 || ldo % 8 != 0 || ldo < N ||
+      !al16(a) || !al16(w) || !al16(out) || (bias && !al16(bias)))
+    return MN_ERR_UNSUPPORTED;
+  cudaGetLastError();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = MN_ERR_UNSUPPORTED;
+  const bool gelu = epilogue == MN_EPI_BIAS_GELU;
+  if (N % 256 == 0)
+    rc = gelu ? gemm::launch<256, 1>(M, N, K, a, lda, w, ldw, bias, out, ldo, status, st)
+              : gemm::launch<256, 0>(M, N, K, a, lda, w, ldw, bias, out, ldo, status, st);
+  else if (N % 192 == 0)
+    rc = gelu ? gemm::launch<192, 1>(M, N, K, a, lda, w, ldw, bias, out, ldo, status, st)
+              : gemm::launch<192, 0>(M, N, K, a, lda, w, ldw, bias, out, ldo, status, st);
+  else if (N % 128 == 0)
+    rc = gelu ? gemm::launch<128, 1>(M, N, K, a, lda, w, ldw, bias, out, ldo, status, st)
+              : gemm::launch<128, 0>(M, N, K, a, lda, w, ldw, bias, out, ldo, status, st);
+  if (rc != MN_OK) return rc;
+  return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
+}

@@ -839,16 +839,6 @@ __global__ void __launch_bounds__(256) route_transport_kernel(
 // (alpha = wb_old / wb_safe, c = assign * wa_old / wb_safe) come from
 // route_mass in stencil order.
 // ---------------------------------------------------------------------------
-// fp32x2 fused multiply-add (two independent round-to-nearest FMAs).
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;"
-      : "=l"(d)
-      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)),
-        "l"(*reinterpret_cast<const uint64_t*>(&c)));
-  return *reinterpret_cast<const float2*>(&d);
-}
-
 template <typename XT, int CT, int DY1, int DY3>
 __global__ void __launch_bounds__(448, 2) route_transport_stencil_kernel(
     const XT* __restrict__ x, int B, int T, int C, int grid_h, int grid_w, int half, int L, int k,

@@ -13,6 +13,8 @@ a profiler can skip the first iteration's launches and capture the second's.
   per-key log-size bias, and the 393 x 785 recovery cross-attention.
 * ``routing``: the fused six-layer routing and carrier gather on x_embed
   [B, 785, 384] fp32 and metrics [6, B, 785, 64] fp16.
+* ``gemm``: the MLP GEMMs of one local block on B x 785 token rows: fc1 with
+  the GELU epilogue (384 -> 1536), then fc2 (1536 -> 384).
 """
 from __future__ import annotations
 
@@ -52,13 +54,29 @@ def routing(batch, iters):
     print("routing status", int(res.status.item()))
 
 
+def gemm(batch, iters):
+    from .linear import gemm_status, linear_f16
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    h = torch.randn(batch * 785, 384, device=dev, generator=g).half()
+    w1 = (torch.randn(1536, 384, device=dev, generator=g) * 0.05).half()
+    b1 = torch.zeros(1536, device=dev, dtype=torch.float16)
+    w2 = (torch.randn(384, 1536, device=dev, generator=g) * 0.025).half()
+    b2 = torch.zeros(384, device=dev, dtype=torch.float16)
+    for _ in range(iters):
+        f = linear_f16(h, w1, b1, gelu=True)
+        linear_f16(f, w2, b2)
+    torch.cuda.synchronize()
+    print("gemm status", gemm_status(dev))
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["attention", "routing"])
+    ap.add_argument("case", choices=["attention", "routing", "gemm"])
     ap.add_argument("--batch", type=int, default=128)
     ap.add_argument("--iters", type=int, default=2)
     args = ap.parse_args()
-    {"attention": attention, "routing": routing}[args.case](args.batch, args.iters)
+    {"attention": attention, "routing": routing, "gemm": gemm}[args.case](args.batch, args.iters)
 
 
 if __name__ == "__main__":
