@@ -369,6 +369,45 @@ class ForwardGraph:
         self.graph.replay()
         return self.logits, self.aux
 
+    def run_host_batches(self, host_batches, host_logits):
+        """Forward a sequence of pinned host batches (each of the captured
+        shape) and copy each batch's logits into ``host_logits[i]`` (pinned,
+        [len, B, classes]).  The host-to-device copy of batch i+1 runs on a
+        copy stream into one of two staging buffers while batch i computes,
+        so a step costs about max(copy, forward) rather than their sum.  The
+        work is queued on the current stream; synchronise before reading
+        ``host_logits``."""
+        dev = self.images.device
+        main = torch.cuda.current_stream(dev)
+        if not hasattr(self, "_copy_stream"):
+            self._copy_stream = torch.cuda.Stream(dev)
+            self._staging = [torch.empty_like(self.images) for _ in range(2)]
+            self._ready = [torch.cuda.Event() for _ in range(2)]
+            self._free = [torch.cuda.Event() for _ in range(2)]
+        copy = self._copy_stream
+        copy.wait_stream(main)  # nothing starts before the caller's preceding work
+
+        def issue_copy(i):
+            buf = i % 2
+            copy.wait_event(self._free[buf])  # the staging buffer has been consumed
+            with torch.cuda.stream(copy):
+                self._staging[buf].copy_(host_batches[i], non_blocking=True)
+            self._ready[buf].record(copy)
+
+        n = len(host_batches)
+        if n:
+            issue_copy(0)
+        for i in range(n):
+            if i + 1 < n:
+                issue_copy(i + 1)
+            buf = i % 2
+            main.wait_event(self._ready[buf])
+            self.images.copy_(self._staging[buf], non_blocking=True)
+            self._free[buf].record(main)
+            self.graph.replay()
+            host_logits[i].copy_(self.logits, non_blocking=True)
+        return host_logits
+
     @staticmethod
     def library_launches(model):
         """Library (mn_*) kernels one forward launches: two fused

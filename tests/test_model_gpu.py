@@ -128,3 +128,24 @@ def test_canonical_forward_stages(dev):
     assert aux["retained_tokens"] == 392
     size = aux["token_strength_no_cls"].double().sum(1)
     torch.testing.assert_close(size, torch.full_like(size, 784.0), rtol=1e-5, atol=1e-3)
+
+
+def test_forward_graph_replay_and_host_stream(dev):
+    """The CUDA-graph forward equals the eager forward, and the overlapped
+    host-batch path gives every batch its own logits."""
+    from mergenet_b200.model import ForwardGraph, MergeNetSmall
+    model = MergeNetSmall(img_size=32, patch_size=8, num_classes=10, metric_dim=16, local_depth=2,
+                          latent_depth=2, local_window=2).init_weights(0).to(dev).eval()
+    g = torch.Generator(device=dev).manual_seed(11)
+    batches = [torch.randn(3, 3, 32, 32, device=dev, generator=g) for _ in range(3)]
+    eager = [model(b)[0].clone() for b in batches]
+    fwd = ForwardGraph(model, batches[0].clone(), warmup=1)
+    for b, e in zip(batches, eager):
+        got, _ = fwd(b)
+        assert torch.equal(got, e)
+    host = [b.cpu().pin_memory() for b in batches]
+    out = torch.empty(3, 3, 10, dtype=eager[0].dtype).pin_memory()
+    fwd.run_host_batches(host, out)
+    torch.cuda.synchronize()
+    for i, e in enumerate(eager):
+        assert torch.equal(out[i], e.cpu())
