@@ -1,24 +1,28 @@
 // Tensor-core (tcgen05 + TMEM) attention for head_dim 64, fp16 / bf16.
 //
 // One CTA of 128 threads owns 128 query rows of one (image, head); thread t
-// owns row t, which is TMEM lane t of the accumulators.  Keys and values are
-// staged in 128B-swizzled shared memory, S = Q K^T is accumulated in TMEM by
-// tcgen05.mma issued from one thread, each thread turns its S row into fp16 /
-// bf16 probabilities in shared memory, and O = P V accumulates in TMEM.
+// owns row t, which is TMEM lane t of the accumulators.  Q, K and V tiles are
+// brought into 128B-swizzled shared memory by TMA (one thread issues the
+// bulk tensor copies, completion is counted on mbarriers), S = Q K^T is
+// accumulated in TMEM by tcgen05.mma issued from one thread, each thread
+// turns its S row into fp16 / bf16 probabilities in shared memory, and
+// O = P V accumulates in TMEM.  The next block's S = Q K^T is issued right
+// after this block's P.V, so it runs while the CTA finishes the block.
 //
 //   window >= 0: sliding window |i - j| <= window over one sequence (the
 //     LocalAttention path, opentome/timm/bias_local_attn.py:486-625 / :243-483):
-//     the 128 + 2*window keys of the tile form a single block, no rescaling.
+//     up to window 16 the 128 + 2*window keys of the tile form one block.
 //   window <  0: every key (the recovery cross-attention core,
-//     opentome/models/mergenet/model.py:173-188): 128-key blocks with an
-//     online softmax; O is rescaled in TMEM when a row maximum grows.
+//     opentome/models/mergenet/model.py:173-188, and the latent blocks):
+//     64-key blocks with an online softmax.
 //
-// Every wait on the tensor core is bounded; on timeout the CTA records an
-// error bit and stops issuing work.
+// Every wait is bounded; on timeout the CTA records an error bit and stops
+// issuing work.
 #include <algorithm>
 
 #include "common.cuh"
 #include "tc_common.cuh"
+#include "tma.cuh"
 
 namespace mn {
 
@@ -40,9 +44,10 @@ struct TcSmem {
   static constexpr uint32_t kv_stage = NB * 128;
   static constexpr uint32_t v_off = k_off + kv_stage;
   static constexpr uint32_t p_off = (v_off + kStages * kv_stage + 1023) & ~1023u;
-  static constexpr uint32_t bias_off = p_off + kPAtoms * kTcM * 128;
-  static constexpr uint32_t bar_off = bias_off + NB * 4;  // [0]: S done, [1]: P.V done
-  static constexpr uint32_t tmem_slot_off = bar_off + 16;
+  static constexpr uint32_t bias_off = p_off + kPAtoms * kTcM * 128;  // two blocks' biases
+  // barriers: S done, P.V done, Q landed, K landed, V stage 0 / 1 landed
+  static constexpr uint32_t bar_off = bias_off + 2 * NB * 4;
+  static constexpr uint32_t tmem_slot_off = bar_off + 6 * 8;
   static constexpr uint32_t bytes = tmem_slot_off + 8 + 1024;  // + alignment slack
 };
 static_assert(TcSmem<160>::bytes <= 113 * 1024 && TcSmem<128>::bytes <= 113 * 1024, "two CTAs per SM");
@@ -58,21 +63,6 @@ __device__ __forceinline__ uint4 pack8(const float* p) {
     w[i] = (uint32_t)(*reinterpret_cast<uint16_t*>(&lo)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&hi)) << 16);
   }
   return r;
-}
-
-// Issue asynchronous copies of `rows` rows of 64 elements (16B chunks) into a
-// 128B-swizzled tile; rows outside [0, valid) are zero-filled.
-template <typename ET>
-__device__ __forceinline__ void stage_rows(uint8_t* tile, const ET* src, int64_t row_stride, int first, int rows,
-                                           int valid) {
-  const uint32_t base = tc::smem_u32(tile);
-  for (int idx = threadIdx.x; idx < rows * 8; idx += blockDim.x) {
-    const int r = idx >> 3, c = idx & 7;
-    const int gr = first + r;
-    const bool in = gr >= 0 && gr < valid;
-    const ET* g = in ? src + (int64_t)gr * row_stride + c * 8 : src;
-    tc::cp_async16(base + tc::sw128_off(r, c), g, in ? 16u : 0u);
-  }
 }
 
 __device__ __forceinline__ float fast_ex2(float x) {
@@ -111,11 +101,26 @@ struct TcChunks {
 // WIN: sliding window (per-row key ranges, masked per element).  Without a
 // window every row sees the same keys, so keys past the end get a -inf bias
 // and no element is masked.  BIAS: a per-key bias is given.
+// Tile coordinates of a (d, h, n, b) tensor map: order 0 has heads before
+// tokens in the map's dimension list (packed-qkv / BNHD layouts), order 1
+// tokens before heads (BHND).
+__device__ __forceinline__ void load_rows(uint32_t dst, const CUtensorMap* map, int order, int h, int n, int b,
+                                          uint64_t* bar) {
+  if (order == 0)
+    tma::load_4d(dst, map, 0, h, n, b, bar);
+  else
+    tma::load_4d(dst, map, 0, n, h, b, bar);
+}
+
+// WIN: sliding window (per-row key ranges, masked per element).  Without a
+// window every row sees the same keys, so keys past the end get a -inf bias
+// and no element is masked.  BIAS: a per-key bias is given.
 template <typename ET, int NB, bool WIN, bool BIAS>
 __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
-    const ET* __restrict__ q, int64_t qb, int64_t qn, int64_t qh, const ET* __restrict__ k,
-    const ET* __restrict__ v, int64_t kb, int64_t kn, int64_t kh, int Nq, int Nk, int H, int window, float scale,
-    const void* __restrict__ bias, int bias_dtype, void* __restrict__ out, int out_dtype, int* __restrict__ err) {
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, int q_order, int kv_order, int Nq, int Nk, int H, int window,
+    float scale, const void* __restrict__ bias, int bias_dtype, void* __restrict__ out, int out_dtype,
+    int* __restrict__ err) {
   using S = TcSmem<NB>;
   constexpr int NCH = TcChunks<NB>::kWarp;
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -124,15 +129,12 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
   uint8_t* sk = base + S::k_off;
   uint8_t* sv = base + S::v_off;
   uint8_t* sp = base + S::p_off;
-  float* sbias = reinterpret_cast<float*>(base + S::bias_off);
+  float* sbias2 = reinterpret_cast<float*>(base + S::bias_off);  // [2][NB]
   uint64_t* bar = reinterpret_cast<uint64_t*>(base + S::bar_off);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + S::tmem_slot_off);
 
   const int tid = threadIdx.x, warp = tid >> 5;
   const int q0 = blockIdx.x * kTcM, h = blockIdx.y, b = blockIdx.z;
-  const ET* qbase = q + (int64_t)b * qb + (int64_t)h * qh;
-  const ET* kbase = k + (int64_t)b * kb + (int64_t)h * kh;
-  const ET* vbase = v + (int64_t)b * kb + (int64_t)h * kh;
   constexpr int ab_bf16 = std::is_same<ET, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t idesc_o = tc::idesc_f16(ab_bf16, 1, kTcM, kTcD);
   const float kLog2e = 1.4426950408889634f;
@@ -140,77 +142,109 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
 
   uint64_t* bar_s = bar;      // arrives when S = Q K^T (and all earlier MMAs) completed
   uint64_t* bar_o = bar + 1;  // arrives when P.V (and all earlier MMAs) completed
-  if (warp == 0) tc::tmem_alloc(tmem_slot, S::kTmemCols);
-  if (tid == 0) {
-    tc::mbar_init(bar_s, 1);
-    tc::mbar_init(bar_o, 1);
-    tc::fence_mbar_init();
-  }
+  uint64_t* bar_q = bar + 2;  // Q tile landed
+  uint64_t* bar_k = bar + 3;  // K block landed (one phase per block)
+  uint64_t* bar_v = bar + 4;  // V stage landed: [0], [1]
   int klo = 0, khi = Nk;
   if (WIN) {
     klo = max(0, q0 - window);
     khi = min(Nk, q0 + kTcM + window);
   }
   const int nblocks = (khi - klo + NB - 1) / NB;
-  // Q and the first K/V block in flight together
-  stage_rows<ET>(sq, qbase, qn, q0, kTcM, Nq);
-  stage_rows<ET>(sk, kbase, kn, klo, NB, khi);
-  stage_rows<ET>(sv, vbase, kn, klo, NB, khi);
-  tc::cp_async_commit();
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem, t_o = tmem + NB;
-  const uint32_t lane_sel = (uint32_t)(warp * 32) << 16;
 
-  const int qi = q0 + tid;  // this thread's query row
-  float m_run = -INFINITY, l_run = 0.f;
-  bool ok = true;
-
-  for (int blk = 0; blk < nblocks && ok; ++blk) {
-    const int kstart = klo + blk * NB;
-    const int kvalid = min(NB, khi - kstart);  // keys of this block
-    // MMA extent: whole 32-column chunks, so every S column the softmax
-    // reads was written by this block's MMA (K rows past the end are zero)
-    const int kpad = (kvalid + 31) & ~31;
-    const int stage = blk % S::kStages;
-    uint8_t* svb = sv + stage * S::kv_stage;
+  // the per-key bias (log2 units) of block blk into its buffer; without a
+  // window, keys past the end get -inf
+  auto stage_bias = [&](int blk) {
     if (BIAS || !WIN) {
+      const int kstart = klo + blk * NB;
+      const int kvalid = min(NB, khi - kstart);
+      float* sb = sbias2 + (blk & 1) * NB;
       for (int j = tid; j < NB; j += blockDim.x) {
         float bv = WIN ? 0.f : -INFINITY;
         if (j < kvalid) {
           bv = 0.f;
           if (BIAS) bv = to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)b * Nk + kstart + j))) * kLog2e;
         }
-        sbias[j] = bv;
+        sb[j] = bv;
       }
     }
-    tc::cp_async_wait<0>();  // this block's K/V (and Q) have landed
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t aq = tc::smem_u32(sq), ak = tc::smem_u32(sk);
-      const uint32_t idesc_s = tc::idesc_f16(ab_bf16, 0, kTcM, kpad);
+  };
+  // S = Q K^T for block blk, issued by thread 0 once K has landed
+  auto issue_s = [&](int blk, uint32_t t_s) -> bool {
+    if (!tc::mbar_wait(bar_k, blk & 1, err)) return false;
+    tc::fence_after_sync();
+    const int kvalid = min(NB, khi - (klo + blk * NB));
+    const int kpad = (kvalid + 31) & ~31;
+    const uint32_t aq = tc::smem_u32(sq), ak = tc::smem_u32(sk);
+    const uint32_t idesc_s = tc::idesc_f16(ab_bf16, 0, kTcM, kpad);
 #pragma unroll
-      for (int kk = 0; kk < kTcD / 16; ++kk)
-        tc::mma_f16_ss(t_s, tc::sw128_desc(aq + kk * 32, 16), tc::sw128_desc(ak + kk * 32, 16), idesc_s, kk > 0);
-      tc::mma_commit(bar_s);
+    for (int kk = 0; kk < kTcD / 16; ++kk)
+      tc::mma_f16_ss(t_s, tc::sw128_desc(aq + kk * 32, 16), tc::sw128_desc(ak + kk * 32, 16), idesc_s, kk > 0);
+    tc::mma_commit(bar_s);
+    return true;
+  };
+
+  if (warp == 0) tc::tmem_alloc(tmem_slot, S::kTmemCols);
+  if (tid == 0) {
+    for (int i = 0; i < 6; ++i) tc::mbar_init(bar + i, 1);
+    tc::fence_mbar_init();
+    tma::prefetch_map(&tm_q);
+    tma::prefetch_map(&tm_k);
+    tma::prefetch_map(&tm_v);
+    if (nblocks > 0) {
+      // Q and the first K/V block in flight together
+      tma::expect_tx(bar_q, kTcM * 128);
+      load_rows(tc::smem_u32(sq), &tm_q, q_order, h, q0, b, bar_q);
+      tma::expect_tx(bar_k, NB * 128);
+      load_rows(tc::smem_u32(sk), &tm_k, kv_order, h, klo, b, bar_k);
+      tma::expect_tx(bar_v, NB * 128);
+      load_rows(tc::smem_u32(sv), &tm_v, kv_order, h, klo, b, bar_v);
     }
+  }
+  if (nblocks > 0) stage_bias(0);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem, t_o = tmem + NB;
+  const uint32_t lane_sel = (uint32_t)(warp * 32) << 16;
+  bool ok = true;
+  if (tid == 0 && nblocks > 0) {
+    ok = tc::mbar_wait(bar_q, 0, err) && issue_s(0, t_s);
+    if (!ok && err) atomicOr(err, MN_STATUS_TC_TIMEOUT);
+  }
+
+  const int qi = q0 + tid;  // this thread's query row
+  float m_run = -INFINITY, l_run = 0.f;
+  // the last phase issued on each copy barrier, for the exit drain
+  int k_issued = nblocks > 0 ? 0 : -1, v_issued[2] = {nblocks > 0 ? 0 : -1, -1};
+
+  for (int blk = 0; blk < nblocks && ok; ++blk) {
+    const int kstart = klo + blk * NB;
+    const int kvalid = min(NB, khi - kstart);  // keys of this block
+    // MMA extent: whole 32-column chunks, so every S column the softmax
+    // reads was written by this block's MMA
+    const int kpad = (kvalid + 31) & ~31;
+    const int stage = blk % S::kStages;
+    const float* sbias = sbias2 + (blk & 1) * NB;
     // every S commit is waited for, in order: phase blk of bar_s
     ok = tc::mbar_wait(bar_s, blk & 1, err);
     if (!ok) break;
     tc::fence_after_sync();
     // S done -- and with it every earlier MMA, including the previous P.V --
-    // so K and the other V stage are free: prefetch the next block while
-    // this block's softmax runs
+    // so K and the other V stage are free: fetch the next block while this
+    // block's softmax runs
     if (blk + 1 < nblocks) {
-      const int ns = (blk + 1) % S::kStages;
-      stage_rows<ET>(sk, kbase, kn, kstart + NB, NB, khi);
-      stage_rows<ET>(sv + ns * S::kv_stage, vbase, kn, kstart + NB, NB, khi);
-      tc::cp_async_commit();
+      if (tid == 0) {
+        const int ns = (blk + 1) % S::kStages;
+        tma::expect_tx(bar_k, NB * 128);
+        load_rows(tc::smem_u32(sk), &tm_k, kv_order, h, kstart + NB, b, bar_k);
+        tma::expect_tx(bar_v + ns, NB * 128);
+        load_rows(tc::smem_u32(sv + ns * S::kv_stage), &tm_v, kv_order, h, kstart + NB, b, bar_v + ns);
+        k_issued = blk + 1;
+        v_issued[ns] = blk + 1;
+      }
+      stage_bias(blk + 1);
     }
 
     // this row's legal keys, relative to the block: [jlo, jhi)
@@ -338,14 +372,27 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
     __syncthreads();
     if (tid == 0) {
       tc::fence_after_sync();
-      const uint32_t ap = tc::smem_u32(sp), av = tc::smem_u32(svb);
-      for (int kk = 0; kk < kpad / 16; ++kk)
-        tc::mma_f16_ss(t_o, tc::sw128_desc(ap + (kk >> 2) * (kTcM * 128) + (kk & 3) * 32, 16),
-                       tc::sw128_desc(av + kk * 2048, 16384), idesc_o, (blk > 0 || kk > 0) ? 1u : 0u);
-      tc::mma_commit(bar_o);
+      // P.V once this block's V stage has landed, then the next block's S
+      if (!tc::mbar_wait(bar_v + stage, (blk / S::kStages) & 1, err)) {
+        ok = false;
+      } else {
+        const uint32_t ap = tc::smem_u32(sp), av = tc::smem_u32(sv + stage * S::kv_stage);
+        for (int kk = 0; kk < kpad / 16; ++kk)
+          tc::mma_f16_ss(t_o, tc::sw128_desc(ap + (kk >> 2) * (kTcM * 128) + (kk & 3) * 32, 16),
+                         tc::sw128_desc(av + kk * 2048, 16384), idesc_o, (blk > 0 || kk > 0) ? 1u : 0u);
+        tc::mma_commit(bar_o);
+        if (blk + 1 < nblocks) ok = issue_s(blk + 1, t_s);
+      }
+      if (!ok && err) atomicOr(err, MN_STATUS_TC_TIMEOUT);
     }
   }
-  tc::cp_async_wait<0>();
+  if (tid == 0) {
+    // every bulk copy issued has landed before the CTA may exit
+    if (k_issued >= 0) tc::mbar_wait(bar_k, k_issued & 1, nullptr);
+    for (int st = 0; st < S::kStages; ++st)
+      if (v_issued[st] >= 0) tc::mbar_wait(bar_v + st, (v_issued[st] / S::kStages) & 1, nullptr);
+    if (nblocks > 0) tc::mbar_wait(bar_q, 0, nullptr);
+  }
   if (ok && nblocks > 0) {
     // bar_o is only waited for here, after its last arrival: the phase of the
     // final P.V has parity (nblocks - 1) & 1
@@ -383,17 +430,37 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
   if (warp == 0) tc::tmem_dealloc(tmem, S::kTmemCols);
 }
 
+// 4-D tensor map (d, h, n, b) -- or (d, n, h, b) when heads are strided
+// wider than tokens -- over a [B, N, H, 64] view with element strides sb, sn,
+// sh; box = `rows` tokens of one head.  *order receives the dimension order.
+template <typename ET>
+static bool make_head_map(CUtensorMap* map, int* order, const void* ptr, int B, int N, int H, int64_t sb, int64_t sn,
+                          int64_t sh, int rows) {
+  const bool hn = sh <= sn;
+  *order = hn ? 0 : 1;
+  const cuuint64_t dims[4] = {(cuuint64_t)kTcD, (cuuint64_t)(hn ? H : N), (cuuint64_t)(hn ? N : H), (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)(hn ? sh : sn) * 2, (cuuint64_t)(hn ? sn : sh) * 2, (cuuint64_t)sb * 2};
+  const cuuint32_t box[4] = {(cuuint32_t)kTcD, hn ? 1u : (cuuint32_t)rows, hn ? (cuuint32_t)rows : 1u, 1u};
+  return tma::encode(map, std::is_same<ET, __nv_bfloat16>::value, 4, ptr, dims, strides, box, true);
+}
+
 template <typename ET, int NB, bool WIN>
-static void launch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v, int64_t kb,
+static bool launch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v, int64_t kb,
                       int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int window, float scale,
                       const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st) {
+  CUtensorMap mq, mk, mv;
+  int q_order = 0, kv_order = 0, v_order = 0;
+  if (!make_head_map<ET>(&mq, &q_order, q, B, Nq, H, qb, qn, qh, kTcM) ||
+      !make_head_map<ET>(&mk, &kv_order, k, B, Nk, H, kb, kn, kh, NB) ||
+      !make_head_map<ET>(&mv, &v_order, v, B, Nk, H, kb, kn, kh, NB))
+    return false;
   const size_t smem = TcSmem<NB>::bytes;
   auto kern = bias ? attn_tc_kernel<ET, NB, WIN, true> : attn_tc_kernel<ET, NB, WIN, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((Nq + kTcM - 1) / kTcM, H, B);
-  kern<<<grid, 128, smem, st>>>(static_cast<const ET*>(q), qb, qn, qh, static_cast<const ET*>(k),
-                                static_cast<const ET*>(v), kb, kn, kh, Nq, Nk, H, window, scale, bias, bias_dtype,
-                                out, out_dtype, err);
+  kern<<<grid, 128, smem, st>>>(mq, mk, mv, q_order, kv_order, Nq, Nk, H, window, scale, bias, bias_dtype, out,
+                                out_dtype, err);
+  return true;
 }
 
 #ifndef MN_TC_SINGLE_BAND
@@ -404,19 +471,18 @@ static void launch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const v
 #endif
 
 template <typename ET>
-static void dispatch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v, int64_t kb,
+static bool dispatch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v, int64_t kb,
                         int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int window, float scale,
                         const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st) {
   constexpr int NBM = MN_TC_BLOCK_KEYS;
   if (MN_TC_SINGLE_BAND && window >= 0 && kTcM + 2 * window <= 160)  // the whole band in one block
-    launch_tc<ET, 160, true>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
-                             out_dtype, err, st);
-  else if (window >= 0)
-    launch_tc<ET, NBM, true>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
-                             out_dtype, err, st);
-  else
-    launch_tc<ET, NBM, false>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
-                              out_dtype, err, st);
+    return launch_tc<ET, 160, true>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
+                                    out, out_dtype, err, st);
+  if (window >= 0)
+    return launch_tc<ET, NBM, true>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
+                                    out, out_dtype, err, st);
+  return launch_tc<ET, NBM, false>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
+                                   out, out_dtype, err, st);
 }
 
 // Host-side dispatch used by mn_local_attention / mn_attention.  Returns
@@ -431,12 +497,10 @@ bool attention_tc(int dtype, const void* q, int64_t qb, int64_t qn, int64_t qh, 
   };
   if (!aligned(q, qb, qn, qh) || !aligned(k, kb, kn, kh) || !aligned(v, kb, kn, kh)) return false;
   if (dtype == MN_F16)
-    dispatch_tc<__half>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
-                        out_dtype, err, st);
-  else
-    dispatch_tc<__nv_bfloat16>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
+    return dispatch_tc<__half>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
                                out_dtype, err, st);
-  return true;
+  return dispatch_tc<__nv_bfloat16>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
+                                    out, out_dtype, err, st);
 }
 
 }  // namespace mn

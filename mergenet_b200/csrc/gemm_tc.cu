@@ -17,13 +17,13 @@
 //               of the accumulator columns, bias (+ GELU), fp16 stores.
 // The two accumulators let the epilogue of one tile overlap the main loop of
 // the next.  Every wait is bounded; a timeout sets MN_STATUS_TC_TIMEOUT.
-#include <cuda.h>  // CUtensorMap and its enums (the encoder is fetched at run time)
 
 #include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
 #include "tc_common.cuh"
+#include "tma.cuh"
 
 namespace mn {
 namespace gemm {
@@ -53,36 +53,6 @@ struct Cfg {
 };
 static_assert(Cfg<256>::bytes <= 227 * 1024 && Cfg<192>::bytes <= 227 * 1024 && Cfg<128>::bytes <= 227 * 1024,
               "shared memory");
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(tc::smem_u32(bar))
-      : "memory");
-}
-// shared -> global tensor store of a staged block (bulk async group)
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y), "r"(src)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// wait until at most N committed store groups may still read shared memory
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
-}
 
 // GELU(x) = 0.5 x (1 + erf(x / sqrt 2)) on a pair, packed fp32x2.  erf(z) is
 // z * P(z^2) with |z| clamped to 2.9: P of degree 9, fitted by
@@ -167,9 +137,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!tc::mbar_wait(empty + stage, phase ^ 1u, err)) { ok = false; break; }
           const uint32_t sa = tc::smem_u32(base + stage * C::kStageBytes);
-          mbar_expect_tx(full + stage, C::kStageBytes);
-          tma_load_2d(sa, &tmap_a, kb * BK, mb * BM, full + stage);
-          tma_load_2d(sa + C::kABytes, &tmap_w, kb * BK, nb * BN, full + stage);
+          tma::expect_tx(full + stage, C::kStageBytes);
+          tma::load_2d(sa, &tmap_a, kb * BK, mb * BM, full + stage);
+          tma::load_2d(sa + C::kABytes, &tmap_w, kb * BK, nb * BN, full + stage);
           last_phase[stage] = (int)phase;
           if (++stage == S) { stage = 0; phase ^= 1u; }
         }
@@ -234,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           // the accumulator is fully read: hand it back to the MMA warp
           tc::fence_before_sync();
           __syncwarp();
-          if (lane == 0) mbar_arrive(acc_empty + acc);
+          if (lane == 0) tma::arrive(acc_empty + acc);
         }
         uint4 bq[4];
         if (brow) {
@@ -254,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           pw[i] = *reinterpret_cast<uint32_t*>(&h);
         }
         // stage this warp's 32 x 32 block (row = lane) and store it with TMA
-        if (lane == 0) bulk_wait_read<1>();  // the buffer's previous store has read it
+        if (lane == 0) tma::bulk_wait_read<1>();  // the buffer's previous store has read it
         __syncwarp();
         uint8_t* sb = stage_out + buf * kStageOutBytes;
 #pragma unroll
@@ -262,14 +232,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         tc::fence_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmap_o, tc::smem_u32(sb), nb * BN + c * 32, mb * BM + quad * 32);
-          bulk_commit();
+          tma::store_2d(&tmap_o, tc::smem_u32(sb), nb * BN + c * 32, mb * BM + quad * 32);
+          tma::bulk_commit();
         }
         buf ^= 1;
       }
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
-    if (lane == 0) bulk_wait_all();  // stores complete before the CTA exits
+    if (lane == 0) tma::bulk_wait_all();  // stores complete before the CTA exits
     __syncwarp();
     if (!ok && lane == 0 && err) atomicOr(err, MN_STATUS_TC_TIMEOUT);
   }
@@ -279,37 +249,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 }
 
 // ------------------------------------------------------------------ host
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encoder() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
 // 2-D fp16 tensor map over rows x cols (cols contiguous, row stride ld
 // elements) with a box_rows x box_cols box; operand maps use the 128-byte
 // swizzle the MMA descriptors expect, the output map a plain row-major box.
 static bool make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
                      int box_cols, bool swizzle) {
-  EncodeTiledFn enc = encoder();
-  if (!enc) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
   const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return tma::encode(map, false, 2, ptr, dims, strides, box, swizzle);
 }
 
 template <int BN, int EPI>
