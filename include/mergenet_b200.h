@@ -259,6 +259,14 @@ int mn_add_layernorm(int64_t rows, int channels, const float* x, const void* y,
                      const float* gamma, const float* beta, float eps,
                      float* x_out, void* h_ln, void* h_raw, void* stream);
 
+/* Patch unfold for the patch-embedding GEMM (timm PatchEmbed's stride-p
+ * p x p convolution, opentome/models/mergenet/model.py:517-519):
+ * images fp32 [batch, channels, height, width] ->
+ * out fp16 [batch, height/p, width/p, channels, p, p].  p must be a multiple
+ * of 8 and width of 4, buffers 16-byte aligned (else MN_ERR_UNSUPPORTED). */
+int mn_patch_unfold(int batch, int channels, int height, int width, int patch,
+                    const float* images, void* out, void* stream);
+
 /* out[M, N] = epilogue(A[M, K] . W[N, K]^T + bias[N]) with fp16 A, W, bias
  * and out, fp32 accumulation in tensor memory (tcgen05).  It replaces the
  * fp16-autocast nn.Linear calls of the block MLP and projections (timm

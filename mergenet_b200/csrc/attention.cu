@@ -15,7 +15,8 @@ namespace mn {
 
 bool attention_tc(int dtype, const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v,
                   int64_t kb, int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int D, int window, float scale,
-                  const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st);
+                  const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st,
+                  bool cls_global, bool* cls_done);
 
 constexpr int kLocalQT = 32;  // queries per CTA
 
@@ -306,8 +307,9 @@ extern "C" int mn_attention(int batch, int nq, int nk, int heads, int head_dim, 
   if (!q || !k || !v || dtype < 0 || dtype > 2 || out_dtype < 0 || out_dtype > 2) return MN_ERR_ARG;
   cudaGetLastError();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  bool cls_unused = false;
   if (attention_tc(dtype, q, q_sb, q_sn, q_sh, k, v, kv_sb, kv_sn, kv_sh, batch, nq, nk, heads, head_dim, window,
-                   scale, nullptr, 0, out, out_dtype, status, st))
+                   scale, nullptr, 0, out, out_dtype, status, st, false, &cls_unused))
     return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
   const size_t smem = ((size_t)kXQ * head_dim + 2 * (size_t)kXK * (head_dim + 1)) * sizeof(float);
   const dim3 grid((nq + kXQ - 1) / kXQ, heads, batch);
@@ -346,8 +348,10 @@ extern "C" int mn_local_attention(int batch, int tokens, int heads, int head_dim
   cudaGetLastError();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid((tokens + kLocalQT - 1) / kLocalQT, heads, batch);
+  bool cls_done = false;  // the tensor-core kernel computed the CLS row itself
   const bool tensor_core = attention_tc(dtype, q, s_b, s_n, s_h, k, v, s_b, s_n, s_h, batch, tokens, tokens, heads,
-                                        head_dim, window, scale, bias, bias_dtype, out, out_dtype, status, st);
+                                        head_dim, window, scale, bias, bias_dtype, out, out_dtype, status, st,
+                                        cls_row, &cls_done);
   auto run = [&](auto tag) {
     using ET = decltype(tag);
     if (!tensor_core) {
@@ -357,7 +361,7 @@ extern "C" int mn_local_attention(int batch, int tokens, int heads, int head_dim
                                                      head_dim, bias, bias_dtype, window, scale, out, out_dtype,
                                                      cls_row ? 1 : 0);
     }
-    if (cls_row) {
+    if (cls_row && !cls_done) {
       cudaFuncSetAttribute(cls_row_kernel<ET>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_cls);
       cls_row_kernel<ET><<<dim3(heads, batch), 256, smem_cls, st>>>(
           static_cast<const ET*>(q), static_cast<const ET*>(k), static_cast<const ET*>(v), s_b, s_n, s_h, tokens,

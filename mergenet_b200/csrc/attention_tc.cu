@@ -98,6 +98,83 @@ struct TcChunks {
   static constexpr int kWarp = NB == 160 ? 3 : kAll;
 };
 
+// The CLS row of the LocalAttention block (row 0 attends to every key,
+// opentome/timm/bias_local_attn.py:704-719), computed by the CTA that owns
+// query tile 0 after its windowed rows: scores q0 . k_j * scale (+ bias_j),
+// softmax exp(s - max) / sum, then sum_j p_j v_j with 16-byte value loads
+// (8 threads per value row, 16 rows in flight).  `scratch` holds the scores
+// (Nk floats) and the partial sums; q0 is row 0 of the swizzled Q tile, whose
+// 16-byte chunks are in order.
+template <typename ET>
+__device__ void cls_row_global(const uint8_t* sq, const ET* __restrict__ kg, const ET* __restrict__ vg, int64_t kb,
+                               int64_t kn, int64_t kh, int b, int h, int Nq, int Nk, int H, float scale,
+                               const void* __restrict__ bias, int bias_dtype, float* scratch, void* out,
+                               int out_dtype) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* sp = scratch;                         // [Nk]
+  float* qv = sp + ((Nk + 3) & ~3);            // [64]
+  float* part = qv + kTcD;                     // [16][64]
+  float* red = part + 16 * kTcD;               // [8]
+  if (tid < kTcD) qv[tid] = to_f32(reinterpret_cast<const ET*>(sq)[tid]);
+  __syncthreads();
+  const ET* kbh = kg + (int64_t)b * kb + (int64_t)h * kh;
+  const ET* vbh = vg + (int64_t)b * kb + (int64_t)h * kh;
+  float mx = -INFINITY;
+  for (int j = tid; j < Nk; j += blockDim.x) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kbh + (int64_t)j * kn);
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < kTcD / 8; ++c) {
+      const uint4 u = __ldg(kr + c);
+      const ET* e = reinterpret_cast<const ET*>(&u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = fmaf(qv[c * 8 + i], to_f32(e[i]), acc);
+    }
+    float sc = acc * scale;
+    if (bias) sc += to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)b * Nk + j)));
+    sp[j] = sc;
+    mx = fmaxf(mx, sc);
+  }
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  float sum = 0.f;
+  for (int j = tid; j < Nk; j += blockDim.x) {
+    const float e = expf(sp[j] - mx);
+    sp[j] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  __syncthreads();  // every thread has read red[] and written its p_j
+  if (lane == 0) red[4 + warp] = sum;
+  __syncthreads();
+  const float tot = (red[4] + red[5]) + (red[6] + red[7]);
+  const int sub = tid & 7, rg = tid >> 3;  // 8 threads per value row, 16 rows in flight
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int j = rg; j < Nk; j += 16) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(vbh + (int64_t)j * kn) + sub);
+    const ET* e = reinterpret_cast<const ET*>(&u);
+    const float pj = sp[j];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = fmaf(pj, to_f32(e[i]), acc[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) part[rg * kTcD + sub * 8 + i] = acc[i];
+  __syncthreads();
+  if (tid < kTcD) {
+    float o = 0.f;
+    for (int g = 0; g < 16; ++g) o += part[g * kTcD + tid];
+    store_any(out, out_dtype, ((int64_t)b * Nq * H + h) * kTcD + tid, o / tot);
+  }
+}
+
+// Largest key count whose CLS scratch fits the P tile of the NB-key kernel.
+template <int NB>
+constexpr int cls_max_keys() {
+  return (int)((TcSmem<NB>::kPAtoms * kTcM * 128) / 4) - (kTcD + 16 * kTcD + 8) - 4;
+}
+
 // WIN: sliding window (per-row key ranges, masked per element).  Without a
 // window every row sees the same keys, so keys past the end get a -inf bias
 // and no element is masked.  BIAS: a per-key bias is given.
@@ -120,7 +197,8 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, int q_order, int kv_order, int Nq, int Nk, int H, int window,
     float scale, const void* __restrict__ bias, int bias_dtype, void* __restrict__ out, int out_dtype,
-    int* __restrict__ err) {
+    int* __restrict__ err, int cls_global, const ET* __restrict__ kg, const ET* __restrict__ vg, int64_t kb,
+    int64_t kn, int64_t kh) {
   using S = TcSmem<NB>;
   constexpr int NCH = TcChunks<NB>::kWarp;
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -426,8 +504,14 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
   }
   if (!ok && tid == 0 && err) atomicOr(err, MN_STATUS_TC_TIMEOUT);
   tc::fence_before_sync();
-  __syncthreads();
+  const int all_ok = __syncthreads_and(ok ? 1 : 0);  // a barrier with a CTA-uniform verdict
   if (warp == 0) tc::tmem_dealloc(tmem, S::kTmemCols);
+  // the CLS row over every key, by the CTA of query tile 0 (its windowed row
+  // 0 was written above and is replaced); every MMA has completed, so the P
+  // tile is free scratch
+  if (WIN && cls_global && q0 == 0 && all_ok && nblocks > 0)
+    cls_row_global<ET>(sq, kg, vg, kb, kn, kh, b, h, Nq, Nk, H, scale, bias, bias_dtype,
+                       reinterpret_cast<float*>(sp), out, out_dtype);
 }
 
 // 4-D tensor map (d, h, n, b) -- or (d, n, h, b) when heads are strided
@@ -447,7 +531,8 @@ static bool make_head_map(CUtensorMap* map, int* order, const void* ptr, int B, 
 template <typename ET, int NB, bool WIN>
 static bool launch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v, int64_t kb,
                       int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int window, float scale,
-                      const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st) {
+                      const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st,
+                      bool cls_global, bool* cls_done) {
   CUtensorMap mq, mk, mv;
   int q_order = 0, kv_order = 0, v_order = 0;
   if (!make_head_map<ET>(&mq, &q_order, q, B, Nq, H, qb, qn, qh, kTcM) ||
@@ -458,8 +543,12 @@ static bool launch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const v
   auto kern = bias ? attn_tc_kernel<ET, NB, WIN, true> : attn_tc_kernel<ET, NB, WIN, false>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((Nq + kTcM - 1) / kTcM, H, B);
+  // the CLS row rides along with query tile 0 when its scratch fits the P tile
+  const bool cls = WIN && cls_global && Nq == Nk && Nk <= cls_max_keys<NB>();
   kern<<<grid, 128, smem, st>>>(mq, mk, mv, q_order, kv_order, Nq, Nk, H, window, scale, bias, bias_dtype, out,
-                                out_dtype, err);
+                                out_dtype, err, cls ? 1 : 0, static_cast<const ET*>(k), static_cast<const ET*>(v),
+                                kb, kn, kh);
+  *cls_done = cls;
   return true;
 }
 
@@ -473,23 +562,26 @@ static bool launch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const v
 template <typename ET>
 static bool dispatch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v, int64_t kb,
                         int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int window, float scale,
-                        const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st) {
+                        const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st,
+                        bool cls_global, bool* cls_done) {
   constexpr int NBM = MN_TC_BLOCK_KEYS;
   if (MN_TC_SINGLE_BAND && window >= 0 && kTcM + 2 * window <= 160)  // the whole band in one block
     return launch_tc<ET, 160, true>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
-                                    out, out_dtype, err, st);
+                                    out, out_dtype, err, st, cls_global, cls_done);
   if (window >= 0)
     return launch_tc<ET, NBM, true>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
-                                    out, out_dtype, err, st);
+                                    out, out_dtype, err, st, cls_global, cls_done);
   return launch_tc<ET, NBM, false>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
-                                   out, out_dtype, err, st);
+                                   out, out_dtype, err, st, cls_global, cls_done);
 }
 
 // Host-side dispatch used by mn_local_attention / mn_attention.  Returns
 // false when the shape is not one the tensor-core kernel covers.
 bool attention_tc(int dtype, const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v,
                   int64_t kb, int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int D, int window, float scale,
-                  const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st) {
+                  const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st,
+                  bool cls_global, bool* cls_done) {
+  *cls_done = false;
   if (D != kTcD || (dtype != MN_F16 && dtype != MN_BF16)) return false;
   // 16-byte aligned rows for the vector loads
   auto aligned = [](const void* p, int64_t s1, int64_t s2, int64_t s3) {
@@ -498,9 +590,9 @@ bool attention_tc(int dtype, const void* q, int64_t qb, int64_t qn, int64_t qh, 
   if (!aligned(q, qb, qn, qh) || !aligned(k, kb, kn, kh) || !aligned(v, kb, kn, kh)) return false;
   if (dtype == MN_F16)
     return dispatch_tc<__half>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
-                               out_dtype, err, st);
+                               out_dtype, err, st, cls_global, cls_done);
   return dispatch_tc<__nv_bfloat16>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
-                                    out, out_dtype, err, st);
+                                    out, out_dtype, err, st, cls_global, cls_done);
 }
 
 }  // namespace mn

@@ -185,3 +185,53 @@ extern "C" int mn_embed_layernorm(int batch, int tokens, int channels, const voi
   }
   return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
 }
+
+// Patch unfold of the patch-embedding convolution (timm PatchEmbed, a
+// stride-p p x p conv, computed as one GEMM over unfolded patches): images
+// fp32 [B, C, H, W] -> patches fp16 [B, H/p, W/p, C, p, p] (row = one patch,
+// C*p*p contiguous values, the conv weight's [C, p, p] order).  One thread
+// per 8-value run of a patch row: a 32-byte read of the image row and a
+// 16-byte write; consecutive threads write consecutive output bytes.
+__global__ void __launch_bounds__(256) patch_unfold_kernel(const float* __restrict__ img, int C, int Hh, int Ww,
+                                                           int p, int64_t total, __half* __restrict__ out) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= total) return;
+  const int runs = C * p * p / 8;  // 8-value runs per patch
+  const int64_t patch = t / runs;
+  const int r = (int)(t % runs);
+  const int gw = Ww / p, gh = Hh / p;
+  const int gx = (int)(patch % gw);
+  const int64_t rest = patch / gw;
+  const int gy = (int)(rest % gh);
+  const int64_t b = rest / gh;
+  const int per_c = p * p / 8;
+  const int c = r / per_c, rr = r % per_c;
+  const int py = rr / (p / 8), px0 = (rr % (p / 8)) * 8;
+  const float4* src = reinterpret_cast<const float4*>(img + (((b * C + c) * Hh + gy * p + py) * (int64_t)Ww + gx * p + px0));
+  const float4 a = __ldg(src), d = __ldg(src + 1);
+  __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+  __half2 h2 = __floats2half2_rn(d.x, d.y), h3 = __floats2half2_rn(d.z, d.w);
+  uint4 u;
+  u.x = *reinterpret_cast<uint32_t*>(&h0);
+  u.y = *reinterpret_cast<uint32_t*>(&h1);
+  u.z = *reinterpret_cast<uint32_t*>(&h2);
+  u.w = *reinterpret_cast<uint32_t*>(&h3);
+  reinterpret_cast<uint4*>(out)[t] = u;
+}
+
+extern "C" int mn_patch_unfold(int batch, int channels, int height, int width, int patch, const float* images,
+                               void* out, void* stream) {
+  if (batch < 0 || channels <= 0 || patch <= 0 || height <= 0 || width <= 0) return MN_ERR_ARG;
+  if (height % patch != 0 || width % patch != 0) return MN_ERR_ARG;
+  if (batch == 0) return MN_OK;
+  if (!images || !out) return MN_ERR_ARG;
+  // 16-byte runs: p a multiple of 8, aligned rows and buffers
+  if (patch % 8 != 0 || width % 4 != 0 || reinterpret_cast<uintptr_t>(images) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(out) % 16 != 0)
+    return MN_ERR_UNSUPPORTED;
+  cudaGetLastError();
+  const int64_t total = (int64_t)batch * (height / patch) * (width / patch) * channels * patch * patch / 8;
+  patch_unfold_kernel<<<(unsigned)((total + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      images, channels, height, width, patch, total, static_cast<__half*>(out));
+  return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
+}

@@ -267,7 +267,13 @@ class MergeNetSmall(nn.Module):
         p = self.patch_size
         gh, gw = hh // p, ww // p
         patches = torch.empty(b, gh, gw, ch, p, p, device=images.device, dtype=torch.float16)
-        patches.copy_(images.view(b, ch, gh, p, gw, p).permute(0, 2, 4, 1, 3, 5))  # cast + unfold, one pass
+        from . import _lib as L
+        img = images if images.dtype == torch.float32 and images.is_contiguous() else images.float().contiguous()
+        rc = L.lib().mn_patch_unfold(b, ch, hh, ww, p, L.ptr(img), L.ptr(patches), L.stream_of(img))
+        if rc == L.MN_ERR_UNSUPPORTED:  # patch sizes that are not a multiple of 8
+            patches.copy_(images.view(b, ch, gh, p, gw, p).permute(0, 2, 4, 1, 3, 5))
+        else:
+            L.check(rc, "mn_patch_unfold")
         wpe = self._patch_w16
         if wpe is None:
             wpe = w16["local.vit.patch_embed.proj.weight"].reshape(self.embed_dim, -1).t().contiguous()
@@ -410,13 +416,14 @@ class ForwardGraph:
 
     @staticmethod
     def library_launches(model):
-        """Library (mn_*) kernels one forward launches: two fused
-        add+LayerNorm per block (the first one fused with the embedding) plus
-        the closing one and the two cross norms; a windowed attention and a CLS row per local block; one
-        attention per latent block and for the recovery cross-attention; and
-        the four routing kernels."""
+        """Library (mn_*) kernels one forward launches: the patch unfold; two
+        fused add+LayerNorm per block (the first one fused with the
+        embedding) plus the closing one and the two cross norms; one windowed
+        attention per local block (its CLS row computed by the same kernel);
+        one attention per latent block and for the recovery cross-attention;
+        and the four routing kernels."""
         nl, nt = len(model.local.vit.blocks), len(model.latent.vit.blocks)
-        return (2 * nl + 1 + 2 + 2 * nt) + (2 * nl + nt + 1) + 4
+        return 1 + (2 * nl + 1 + 2 + 2 * nt) + (nl + nt + 1) + 4
 
 
 def embed_layernorm(emb, pos, cls, ln):

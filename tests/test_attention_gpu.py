@@ -260,3 +260,16 @@ def test_embed_layernorm(dev, batch, tokens):
     x, h = embed_layernorm(emb, pos, cls, ln)
     assert torch.equal(x, want)
     torch.testing.assert_close(h.float(), ln(want).half().float(), atol=2e-3, rtol=2e-3)
+
+
+@pytest.mark.parametrize("b,c,hw,p", [(3, 3, 224, 8), (2, 3, 32, 8), (1, 2, 48, 16)])
+def test_patch_unfold_exact(dev, b, c, hw, p):
+    """The patch unfold equals PyTorch's permuted fp16 copy bit for bit."""
+    from mergenet_b200 import _lib as L
+    g = torch.Generator(device=dev).manual_seed(hw + p)
+    img = torch.randn(b, c, hw, hw, device=dev, generator=g)
+    gh = hw // p
+    out = torch.empty(b, gh, gh, c, p, p, device=dev, dtype=torch.float16)
+    L.check(L.lib().mn_patch_unfold(b, c, hw, hw, p, L.ptr(img), L.ptr(out), L.stream_of(img)), "unfold")
+    want = img.view(b, c, gh, p, gh, p).permute(0, 2, 4, 1, 3, 5).half()
+    assert torch.equal(out, want)
