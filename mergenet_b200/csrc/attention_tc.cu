@@ -120,20 +120,39 @@ __device__ void cls_row_global(const uint8_t* sq, const ET* __restrict__ kg, con
   const ET* kbh = kg + (int64_t)b * kb + (int64_t)h * kh;
   const ET* vbh = vg + (int64_t)b * kb + (int64_t)h * kh;
   float mx = -INFINITY;
-  for (int j = tid; j < Nk; j += blockDim.x) {
-    const uint4* kr = reinterpret_cast<const uint4*>(kbh + (int64_t)j * kn);
-    float acc = 0.f;
+  auto score = [&](int j, const uint4* u) {
+    float acc0 = 0.f, acc1 = 0.f;  // even / odd 8-channel groups
 #pragma unroll
     for (int c = 0; c < kTcD / 8; ++c) {
-      const uint4 u = __ldg(kr + c);
-      const ET* e = reinterpret_cast<const ET*>(&u);
+      const ET* e = reinterpret_cast<const ET*>(u + c);
+      float a = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc = fmaf(qv[c * 8 + i], to_f32(e[i]), acc);
+      for (int i = 0; i < 8; ++i) a = fmaf(qv[c * 8 + i], to_f32(e[i]), a);
+      if (c & 1) acc1 += a; else acc0 += a;
     }
-    float sc = acc * scale;
+    float sc = (acc0 + acc1) * scale;
     if (bias) sc += to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)b * Nk + j)));
     sp[j] = sc;
     mx = fmaxf(mx, sc);
+  };
+  int j = tid;
+  for (; j + (int)blockDim.x < Nk; j += 2 * blockDim.x) {  // two keys' rows in flight
+    uint4 u[2][kTcD / 8];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const uint4* kr = reinterpret_cast<const uint4*>(kbh + (int64_t)(j + r * blockDim.x) * kn);
+#pragma unroll
+      for (int c = 0; c < kTcD / 8; ++c) u[r][c] = __ldg(kr + c);
+    }
+    score(j, u[0]);
+    score(j + blockDim.x, u[1]);
+  }
+  if (j < Nk) {
+    uint4 u[kTcD / 8];
+    const uint4* kr = reinterpret_cast<const uint4*>(kbh + (int64_t)j * kn);
+#pragma unroll
+    for (int c = 0; c < kTcD / 8; ++c) u[c] = __ldg(kr + c);
+    score(j, u);
   }
   mx = warp_max(mx);
   if (lane == 0) red[warp] = mx;
@@ -152,13 +171,21 @@ __device__ void cls_row_global(const uint8_t* sq, const ET* __restrict__ kg, con
   const float tot = (red[4] + red[5]) + (red[6] + red[7]);
   const int sub = tid & 7, rg = tid >> 3;  // 8 threads per value row, 16 rows in flight
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int j = rg; j < Nk; j += 16) {
-    const uint4 u = __ldg(reinterpret_cast<const uint4*>(vbh + (int64_t)j * kn) + sub);
+  auto accumulate = [&](int jj, const uint4& u) {
     const ET* e = reinterpret_cast<const ET*>(&u);
-    const float pj = sp[j];
+    const float pj = sp[jj];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = fmaf(pj, to_f32(e[i]), acc[i]);
+  };
+  int jv = rg;
+  for (; jv + 48 < Nk; jv += 64) {  // four value rows in flight per thread
+    uint4 u[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) u[r] = __ldg(reinterpret_cast<const uint4*>(vbh + (int64_t)(jv + 16 * r) * kn) + sub);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) accumulate(jv + 16 * r, u[r]);
   }
+  for (; jv < Nk; jv += 16) accumulate(jv, __ldg(reinterpret_cast<const uint4*>(vbh + (int64_t)jv * kn) + sub));
 #pragma unroll
   for (int i = 0; i < 8; ++i) part[rg * kTcD + sub * 8 + i] = acc[i];
   __syncthreads();
