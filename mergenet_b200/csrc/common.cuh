@@ -146,8 +146,34 @@ __device__ __forceinline__ void block_scan_inclusive(double* buf, int per, doubl
   __syncthreads();
 }
 
-// Ascending bitonic sort of n (power of two) floats in shared memory.
+// Ascending bitonic sort of n (power of two) floats in shared memory.  With
+// one element per thread (n == blockDim.x) each thread keeps its element in a
+// register: exchanges within a warp are shuffles, wider ones go through s
+// (two barriers each) -- 10 barrier pairs instead of 45 barriers at n = 512.
 __device__ __forceinline__ void bitonic_sort_f32(float* s, int n) {
+  if (n == (int)blockDim.x && n >= 32) {
+    const int i = threadIdx.x;
+    float key = s[i];
+    for (int k = 2; k <= n; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        float other;
+        if (j >= 32) {
+          s[i] = key;
+          __syncthreads();
+          other = s[i ^ j];
+          __syncthreads();
+        } else {
+          other = __shfl_xor_sync(MN_FULL_MASK, key, j);
+        }
+        const bool up = (i & k) == 0, lower = (i & j) == 0;
+        const float lo = (key > other) ? other : key, hi = (key > other) ? key : other;
+        key = (lower == up) ? lo : hi;
+      }
+    }
+    s[i] = key;
+    __syncthreads();
+    return;
+  }
   for (int k = 2; k <= n; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
       for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -178,6 +204,37 @@ __device__ __forceinline__ void bitonic_sort_u64(unsigned long long* s, int n) {
       __syncthreads();
     }
   }
+}
+
+// Bitonic sort of n keys (n a power of two, n <= blockDim.x, blockDim.x a
+// power of two), one key per thread: thread i passes key i and receives the
+// i-th smallest.  Exchanges with a partner less than 32 away use warp
+// shuffles; wider ones go through `xbuf` (2 * blockDim.x keys of shared
+// memory, double-buffered so each costs one barrier).  Every thread of the
+// block must call it; threads i >= n sort padding among themselves.
+__device__ __forceinline__ unsigned long long bitonic_sort_u64_reg(unsigned long long key, unsigned long long* xbuf,
+                                                                   int n) {
+  const int i = threadIdx.x;
+  int parity = 0;
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      unsigned long long other;
+      if (j >= 32) {
+        unsigned long long* buf = xbuf + parity * blockDim.x;
+        buf[i] = key;
+        __syncthreads();
+        other = buf[i ^ j];
+        parity ^= 1;
+      } else {
+        other = __shfl_xor_sync(MN_FULL_MASK, key, j);
+      }
+      const bool up = (i & k) == 0;      // ascending run
+      const bool lower = (i & j) == 0;   // lower index of the pair
+      const unsigned long long lo = key < other ? key : other, hi = key < other ? other : key;
+      key = (lower == up) ? lo : hi;
+    }
+  }
+  return key;
 }
 
 __host__ __device__ inline int next_pow2(int v) {

@@ -38,6 +38,7 @@ struct RouteWs {
 };
 
 constexpr int kStencilSlots = 16;
+constexpr int kMaxKin = 12;  // receiver in-degree handled with all loads in flight (radius 3)
 
 __host__ inline size_t route_ws_floats(int L, int B, int half, int kc, int bands) {
   return (size_t)L * B * half * kc + (size_t)L * B * half * 5 + (size_t)L * B * bands * 2 +
@@ -609,15 +610,35 @@ __global__ void __launch_bounds__(1024) route_mass_kernel(
       const float wb = size[tb], cb = center[tb];
       float contrib = 0.f, ccontrib = 0.f;
       const int32_t* in = pt.rx_in + (int64_t)i * kin;
-      for (int j = 0; j < kin; ++j) {
-        int e = in[j];
-        if (e < 0) break;
-        int d = e / kc;
-        float w = asg[e];
-        int ta = 1 + 2 * d + dp;
-        float wa = size[ta];
-        contrib = __fadd_rn(contrib, __fmul_rn(w, wa));
-        ccontrib = __fadd_rn(ccontrib, __fmul_rn(w, __fmul_rn(wa, center[ta])));
+      // the in-edges' assignment weights, all loads in flight before the
+      // sums (which keep the reference's sequential order)
+      int ev[kMaxKin];
+      float wv[kMaxKin];
+      const bool fast_in = kin <= kMaxKin;
+      if (fast_in) {
+#pragma unroll
+        for (int j = 0; j < kMaxKin; ++j) ev[j] = j < kin ? __ldg(in + j) : -1;
+#pragma unroll
+        for (int j = 0; j < kMaxKin; ++j) wv[j] = ev[j] >= 0 ? __ldg(asg + ev[j]) : 0.f;
+#pragma unroll
+        for (int j = 0; j < kMaxKin; ++j) {
+          if (ev[j] < 0) break;
+          const int ta = 1 + 2 * (ev[j] / kc) + dp;
+          const float wa = size[ta];
+          contrib = __fadd_rn(contrib, __fmul_rn(wv[j], wa));
+          ccontrib = __fadd_rn(ccontrib, __fmul_rn(wv[j], __fmul_rn(wa, center[ta])));
+        }
+      } else {
+        for (int j = 0; j < kin; ++j) {
+          int e = in[j];
+          if (e < 0) break;
+          int d = e / kc;
+          float w = asg[e];
+          int ta = 1 + 2 * d + dp;
+          float wa = size[ta];
+          contrib = __fadd_rn(contrib, __fmul_rn(w, wa));
+          ccontrib = __fadd_rn(ccontrib, __fmul_rn(w, __fmul_rn(wa, center[ta])));
+        }
       }
       const float wbn = __fadd_rn(wb, contrib);
       const float wsafe = fmaxf(wbn, eps);
@@ -630,14 +651,26 @@ __global__ void __launch_bounds__(1024) route_mass_kernel(
         for (int u = 0; u < kStencilSlots; ++u) slots[u] = 0.f;
         slots[0] = wb / wsafe;
         const int32_t* off = pt.rx_off + (int64_t)i * kin;
-        for (int j = 0; j < kin; ++j) {
-          int e = in[j];
-          if (e < 0) break;
-          const int o = off[j];
-          const float v = (asg[e] * size[1 + 2 * (e / kc) + dp]) / wsafe;
+        if (fast_in) {
 #pragma unroll
-          for (int u = 1; u < kStencilSlots; ++u)
-            if (o == u - 1) slots[u] = v;
+          for (int j = 0; j < kMaxKin; ++j) {
+            if (ev[j] < 0) break;
+            const int o = __ldg(off + j);
+            const float v = (wv[j] * size[1 + 2 * (ev[j] / kc) + dp]) / wsafe;
+#pragma unroll
+            for (int u = 1; u < kStencilSlots; ++u)
+              if (o == u - 1) slots[u] = v;
+          }
+        } else {
+          for (int j = 0; j < kin; ++j) {
+            int e = in[j];
+            if (e < 0) break;
+            const int o = off[j];
+            const float v = (asg[e] * size[1 + 2 * (e / kc) + dp]) / wsafe;
+#pragma unroll
+            for (int u = 1; u < kStencilSlots; ++u)
+              if (o == u - 1) slots[u] = v;
+          }
         }
 #pragma unroll
         for (int u = 0; u < kStencilSlots; u += 4)
@@ -669,29 +702,36 @@ __global__ void __launch_bounds__(1024) route_mass_kernel(
     center_out[(int64_t)b * T + t] = center[t];
   }
   // exact top-k by (mass desc, patch asc): key = (~bits(mass) << 32) | patch
-  for (int i = threadIdx.x; i < np; i += blockDim.x) {
-    unsigned long long key = ~0ull;
-    if (i < P) {
-      unsigned int bits = __float_as_uint(size[1 + i]);
-      key = ((unsigned long long)(~bits) << 32) | (unsigned int)i;
-    }
-    keys[i] = key;
-  }
-  __syncthreads();
-  bitonic_sort_u64(keys, np);
-  // re-key the k winners by (centre asc, patch asc); centres are >= 0
   const int nk = next_pow2(k);
   unsigned long long* keys2 = keys + np;
-  for (int i = threadIdx.x; i < nk; i += blockDim.x) {
-    unsigned long long key = ~0ull;
-    if (i < k) {
-      unsigned int p = (unsigned int)(keys[i] & 0xffffffffu);
-      key = ((unsigned long long)__float_as_uint(center[1 + p]) << 32) | p;
-    }
-    keys2[i] = key;
+  unsigned long long* xbuf = keys2 + nk;  // [2][blockDim.x] exchange buffers
+  auto mass_key = [&](int i) -> unsigned long long {
+    if (i >= P) return ~0ull;
+    const unsigned int bits = __float_as_uint(size[1 + i]);
+    return ((unsigned long long)(~bits) << 32) | (unsigned int)i;
+  };
+  // re-key the k winners by (centre asc, patch asc); centres are >= 0
+  auto centre_key = [&](unsigned long long mk) -> unsigned long long {
+    const unsigned int p = (unsigned int)(mk & 0xffffffffu);
+    return ((unsigned long long)__float_as_uint(center[1 + p]) << 32) | p;
+  };
+  if (np <= (int)blockDim.x) {
+    // one key per thread: shuffles inside a warp, one barrier per wider step
+    const unsigned long long mk = bitonic_sort_u64_reg(mass_key(threadIdx.x), xbuf, np);
+    if ((int)threadIdx.x < np) keys[threadIdx.x] = mk;
+    __syncthreads();
+    const unsigned long long ck = (int)threadIdx.x < k ? centre_key(keys[threadIdx.x]) : ~0ull;
+    const unsigned long long sk = bitonic_sort_u64_reg(ck, xbuf, nk);
+    if ((int)threadIdx.x < nk) keys2[threadIdx.x] = sk;
+    __syncthreads();
+  } else {
+    for (int i = threadIdx.x; i < np; i += blockDim.x) keys[i] = mass_key(i);
+    __syncthreads();
+    bitonic_sort_u64(keys, np);
+    for (int i = threadIdx.x; i < nk; i += blockDim.x) keys2[i] = i < k ? centre_key(keys[i]) : ~0ull;
+    __syncthreads();
+    bitonic_sort_u64(keys2, nk);
   }
-  __syncthreads();
-  bitonic_sort_u64(keys2, nk);
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
     unsigned int p = (unsigned int)(keys2[i] & 0xffffffffu);
     topk_idx[(int64_t)b * k + i] = p;
@@ -1159,7 +1199,7 @@ extern "C" int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev
   const int np_sel = next_pow2(half);
   const size_t smem_sel = row_scratch_bytes(np_sel) + (size_t)half * sizeof(float);
   const int np_mass = next_pow2(P), nk = next_pow2(k);
-  const size_t smem_mass = (size_t)2 * T * sizeof(float) + (size_t)(np_mass + nk) * 8;
+  const size_t smem_mass = (size_t)2 * T * sizeof(float) + (size_t)(np_mass + nk) * 8 + (size_t)2 * 1024 * 8;
   if (smem_sel > 220 * 1024 || smem_mass > 220 * 1024) return MN_ERR_UNSUPPORTED;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
