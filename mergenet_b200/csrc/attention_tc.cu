@@ -280,11 +280,12 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
     tc::fence_after_sync();
     const int kvalid = min(NB, khi - (klo + blk * NB));
     const int kpad = (kvalid + 31) & ~31;
-    const uint32_t aq = tc::smem_u32(sq), ak = tc::smem_u32(sk);
+    // a 16-wide K step moves the descriptors' start-address field (address
+    // >> 4) by 32 bytes >> 4 = 2
+    const uint64_t dq = tc::sw128_desc(tc::smem_u32(sq), 16), dk = tc::sw128_desc(tc::smem_u32(sk), 16);
     const uint32_t idesc_s = tc::idesc_f16(ab_bf16, 0, kTcM, kpad);
 #pragma unroll
-    for (int kk = 0; kk < kTcD / 16; ++kk)
-      tc::mma_f16_ss(t_s, tc::sw128_desc(aq + kk * 32, 16), tc::sw128_desc(ak + kk * 32, 16), idesc_s, kk > 0);
+    for (int kk = 0; kk < kTcD / 16; ++kk) tc::mma_f16_ss(t_s, dq + 2 * kk, dk + 2 * kk, idesc_s, kk > 0);
     tc::mma_commit(bar_s);
     return true;
   };
@@ -340,15 +341,18 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
     // so K and the other V stage are free: fetch the next block while this
     // block's softmax runs
     if (blk + 1 < nblocks) {
-      if (tid == 0) {
-        const int ns = (blk + 1) % S::kStages;
+      // the K and V copies are issued from warps 1 and 2, so neither issue
+      // latency adds to warp 0's (which issues the MMAs)
+      const int ns = (blk + 1) % S::kStages;
+      if (tid == 32) {
         tma::expect_tx(bar_k, NB * 128);
         load_rows(tc::smem_u32(sk), &tm_k, kv_order, h, kstart + NB, b, bar_k);
+      } else if (tid == 64) {
         tma::expect_tx(bar_v + ns, NB * 128);
         load_rows(tc::smem_u32(sv + ns * S::kv_stage), &tm_v, kv_order, h, kstart + NB, b, bar_v + ns);
-        k_issued = blk + 1;
-        v_issued[ns] = blk + 1;
       }
+      k_issued = blk + 1;  // tracked by every thread: thread 0 drains at exit
+      v_issued[ns] = blk + 1;
       stage_bias(blk + 1);
     }
 
@@ -481,10 +485,13 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
       if (!tc::mbar_wait(bar_v + stage, (blk / S::kStages) & 1, err)) {
         ok = false;
       } else {
-        const uint32_t ap = tc::smem_u32(sp), av = tc::smem_u32(sv + stage * S::kv_stage);
+        // P: 32 bytes per K step inside a 64-key atom, 16 KB between atoms;
+        // V: 16 key rows (2 KB) per K step
+        const uint64_t dp = tc::sw128_desc(tc::smem_u32(sp), 16);
+        const uint64_t dv = tc::sw128_desc(tc::smem_u32(sv + stage * S::kv_stage), 16384);
         for (int kk = 0; kk < kpad / 16; ++kk)
-          tc::mma_f16_ss(t_o, tc::sw128_desc(ap + (kk >> 2) * (kTcM * 128) + (kk & 3) * 32, 16),
-                         tc::sw128_desc(av + kk * 2048, 16384), idesc_o, (blk > 0 || kk > 0) ? 1u : 0u);
+          tc::mma_f16_ss(t_o, dp + (uint64_t)((kk >> 2) * (kTcM * 128 / 16) + (kk & 3) * 2), dv + 128 * kk,
+                         idesc_o, (blk > 0 || kk > 0) ? 1u : 0u);
         tc::mma_commit(bar_o);
         if (blk + 1 < nblocks) ok = issue_s(blk + 1, t_s);
       }
