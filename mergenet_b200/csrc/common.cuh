@@ -237,6 +237,46 @@ __device__ __forceinline__ unsigned long long bitonic_sort_u64_reg(unsigned long
   return key;
 }
 
+// The same sort for n <= 2 * blockDim.x keys, two per thread: thread i
+// holds keys i and i + blockDim.x (k0, k1) and receives those two positions
+// of the sorted order.  The step with partner distance blockDim.x compares
+// a thread's own pair; xbuf holds 4 * blockDim.x keys.
+__device__ __forceinline__ void bitonic_sort_u64_reg2(unsigned long long& k0, unsigned long long& k1,
+                                                      unsigned long long* xbuf, int n) {
+  const int bd = blockDim.x;
+  const int i = threadIdx.x;
+  int parity = 0;
+  auto cmpx = [](unsigned long long key, unsigned long long other, int idx, int k, int j) {
+    const bool up = (idx & k) == 0, lower = (idx & j) == 0;
+    const unsigned long long lo = key < other ? key : other, hi = key < other ? other : key;
+    return (lower == up) ? lo : hi;
+  };
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= bd) {  // partner of i is i + bd: the thread's own other key
+        const bool up = (i & k) == 0;
+        const unsigned long long lo = k0 < k1 ? k0 : k1, hi = k0 < k1 ? k1 : k0;
+        k0 = up ? lo : hi;
+        k1 = up ? hi : lo;
+      } else if (j >= 32) {
+        unsigned long long* buf = xbuf + parity * 2 * bd;
+        buf[i] = k0;
+        buf[i + bd] = k1;
+        __syncthreads();
+        const unsigned long long o0 = buf[i ^ j], o1 = buf[(i + bd) ^ j];
+        parity ^= 1;
+        k0 = cmpx(k0, o0, i, k, j);
+        k1 = cmpx(k1, o1, i + bd, k, j);
+      } else {
+        const unsigned long long o0 = __shfl_xor_sync(MN_FULL_MASK, k0, j);
+        const unsigned long long o1 = __shfl_xor_sync(MN_FULL_MASK, k1, j);
+        k0 = cmpx(k0, o0, i, k, j);
+        k1 = cmpx(k1, o1, i + bd, k, j);
+      }
+    }
+  }
+}
+
 __host__ __device__ inline int next_pow2(int v) {
   int p = 1;
   while (p < v) p <<= 1;

@@ -575,7 +575,7 @@ __global__ void __launch_bounds__(512) route_select_kernel(
 // (model.py:1167-1171).  Also records the per-layer scalars the feature
 // transport needs.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) route_mass_kernel(
+__global__ void __launch_bounds__(512, 2) route_mass_kernel(
     const int32_t* __restrict__ table, int B, int T, int half, int kc, int kin, int L, int k,
     int write_stencil, RouteWs ws, float* __restrict__ size_out, float* __restrict__ center_out,
     float* __restrict__ topk_size, int64_t* __restrict__ topk_idx) {
@@ -715,10 +715,18 @@ __global__ void __launch_bounds__(1024) route_mass_kernel(
     const unsigned int p = (unsigned int)(mk & 0xffffffffu);
     return ((unsigned long long)__float_as_uint(center[1 + p]) << 32) | p;
   };
-  if (np <= (int)blockDim.x) {
-    // one key per thread: shuffles inside a warp, one barrier per wider step
-    const unsigned long long mk = bitonic_sort_u64_reg(mass_key(threadIdx.x), xbuf, np);
-    if ((int)threadIdx.x < np) keys[threadIdx.x] = mk;
+  if (np <= 2 * (int)blockDim.x && nk <= (int)blockDim.x) {
+    // keys in registers: shuffles inside a warp, one barrier per wider step
+    const int bd = blockDim.x, t = threadIdx.x;
+    if (np <= bd) {
+      const unsigned long long mk = bitonic_sort_u64_reg(mass_key(t), xbuf, np);
+      if (t < np) keys[t] = mk;
+    } else {
+      unsigned long long k0 = mass_key(t), k1 = mass_key(t + bd);
+      bitonic_sort_u64_reg2(k0, k1, xbuf, np);
+      keys[t] = k0;
+      keys[t + bd] = k1;
+    }
     __syncthreads();
     const unsigned long long ck = (int)threadIdx.x < k ? centre_key(keys[threadIdx.x]) : ~0ull;
     const unsigned long long sk = bitonic_sort_u64_reg(ck, xbuf, nk);
@@ -1182,7 +1190,7 @@ extern "C" int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev
   const int P = dims->num_patches, T = P + 1;
   if (P <= 0 || P % 2 != 0 || half * 2 != P || dims->grid_h * dims->grid_w != P) return MN_ERR_ARG;
   if (metric_dim > 128 || kc <= 0 || kc > 32 || kin <= 0 || k <= 0 || k > P) return MN_ERR_UNSUPPORTED;
-  if (half > 4 * 1024 || next_pow2(half) > 2048 * 4) return MN_ERR_UNSUPPORTED;
+  if (half > 4 * 512 || next_pow2(half) > 2048 * 4) return MN_ERR_UNSUPPORTED;  // route_mass: 4 receivers per thread
   if (mn_route_workspace_bytes(dims, batch, num_layers) > workspace_bytes) return MN_ERR_WORKSPACE;
   KBudget kb;
   for (int l = 0; l < num_layers; ++l) {
@@ -1199,7 +1207,7 @@ extern "C" int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev
   const int np_sel = next_pow2(half);
   const size_t smem_sel = row_scratch_bytes(np_sel) + (size_t)half * sizeof(float);
   const int np_mass = next_pow2(P), nk = next_pow2(k);
-  const size_t smem_mass = (size_t)2 * T * sizeof(float) + (size_t)(np_mass + nk) * 8 + (size_t)2 * 1024 * 8;
+  const size_t smem_mass = (size_t)2 * T * sizeof(float) + (size_t)(np_mass + nk) * 8 + (size_t)4 * 512 * 8;
   if (smem_sel > 220 * 1024 || smem_mass > 220 * 1024) return MN_ERR_UNSUPPORTED;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -1253,7 +1261,7 @@ extern "C" int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev
 
   const int stencil = stencil_variant(dims);
   cudaFuncSetAttribute(route_mass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_mass);
-  route_mass_kernel<<<batch, 1024, smem_mass, st>>>(dev_table, batch, T, half, kc, kin, num_layers, k,
+  route_mass_kernel<<<batch, 512, smem_mass, st>>>(dev_table, batch, T, half, kc, kin, num_layers, k,
                                                     stencil > 0 ? 1 : 0, ws, size_out, center_out, topk_size,
                                                     topk_idx);
 
