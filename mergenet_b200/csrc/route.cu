@@ -899,6 +899,8 @@ __global__ void __launch_bounds__(448, 2) route_transport_stencil_kernel(
   const int c0 = blockIdx.y * CT;
   const XT* xb = x + (int64_t)b * T * C;
   load_token_tile<XT, CT>(tile, xb, T, C, c0);
+  float* zrow = tile + (int64_t)T * CT;  // one row of zeros after the tile
+  for (int i = threadIdx.x; i < CT; i += blockDim.x) zrow[i] = 0.f;
   __syncthreads();
   const int half_w = grid_w >> 1;
   const int g = threadIdx.x % G;
@@ -908,7 +910,6 @@ __global__ void __launch_bounds__(448, 2) route_transport_stencil_kernel(
   const int rows_per = (grid_h + row_splits - 1) / row_splits;
   const int r_begin = rs * rows_per, r_end = min(grid_h, r_begin + rows_per);
   const int rstride = grid_w * CT;  // floats between grid rows
-  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
   // acc (two float2 halves) += w * v, in the order of the scalar form
   auto fma4 = [](float w, float4 v, float2& lo, float2& hi) {
     const float2 ww = make_float2(w, w);
@@ -927,8 +928,12 @@ __global__ void __launch_bounds__(448, 2) route_transport_stencil_kernel(
       const float* colp1 = tile + (1 + (okr ? c + 1 : c)) * CT + 4 * g;
       const float* colm3 = tile + (1 + (okl3 ? c - 3 : c)) * CT + 4 * g;
       const float* colp3 = tile + (1 + (okr3 ? c + 3 : c)) * CT + 4 * g;
+      // an out-of-grid neighbour reads the zero row: an address select, not
+      // a predicated load and a select per component
+      const float* zero4 = zrow + 4 * g;
       auto ldc = [&](const float* col, bool ok, int r) -> float4 {
-        return (ok && (unsigned)r < (unsigned)grid_h) ? *reinterpret_cast<const float4*>(col + r * rstride) : zero;
+        const float* src = (ok && (unsigned)r < (unsigned)grid_h) ? col + r * rstride : zero4;
+        return *reinterpret_cast<const float4*>(src);
       };
       float4 wl[NW], wr[NW];
       // window slot (ph + u) % NW holds grid row r - DY1 + u while row r is
@@ -1045,7 +1050,7 @@ static void launch_stencil_ct(const void* x, int B, int T, int C, const mn_route
   int splits = std::max(1, std::min(d->grid_h, 448 / per_split));  // <= the kernel's launch bound
   splits = std::min(splits, 4);
   const int threads = ((per_split * splits + 31) / 32) * 32;
-  const size_t smem = (size_t)T * CT * sizeof(float);
+  const size_t smem = (size_t)(T + 1) * CT * sizeof(float);  // tile + zero row
   auto kern = route_transport_stencil_kernel<XT, CT, DY1, DY3>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   kern<<<dim3(B, (C + CT - 1) / CT), threads, smem, st>>>(static_cast<const XT*>(x), B, T, C, d->grid_h,
