@@ -32,9 +32,11 @@ sys.path.insert(0, str(ROOT))
 METRIC = "images/sec mergenet_small_cls fp16 B=256/GPU"
 IMG = 224
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture
-# of a B=128 launch) of the latent attention kernel, per image; the traffic
-# grows in proportion to the batch
-TRAFFIC_LATENT_ATTN = 136.2e6 / 128
+# of a B=128 launch) of the windowed attention kernel with its CLS row and of
+# the latent attention kernel, per image; the traffic grows in proportion to
+# the batch
+TRAFFIC_LOCAL_ATTN = 294.6e6 / 128
+TRAFFIC_LATENT_ATTN = 136.1e6 / 128
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 
 
@@ -227,8 +229,9 @@ def run_b200(args):
     # logits are finite and gathered
     finite = bool(torch.isfinite(gather_logits(logits)).all())
 
-    # roofline of the dominant library kernel: the latent attention over all
-    # 393 carriers with the log-size bias (attn_tc_kernel<half, 128>)
+    # roofline of the dominant library kernel, the windowed local attention
+    # with its CLS row (attn_tc_kernel<half, 160, window>), and of the latent
+    # attention over all 393 carriers with the log-size bias
     nt = 393
     qkv_l = torch.randn(B, nt, 3 * 384, device=dev, dtype=torch.float16) * 0.5
     log_size = torch.rand(B, nt, device=dev).mul_(3.0).log1p_()
@@ -238,10 +241,10 @@ def run_b200(args):
     attn_flops = 4 * B * 6 * nt * nt * 64
     peak, peak_kind = _peaks()
     achieved = attn_bytes / t_attn / 1e9
-    # the windowed local attention (attn_tc_kernel<half, 160> + cls_row_kernel)
     qkv = torch.randn(B, 785, 3 * 384, device=dev, dtype=torch.float16) * 0.5
     t_local = _time_kernel(lambda: mergenet_b200.local_attention_packed(qkv, 6, 16, cls_global=True), stream)
-    local_bytes = qkv.numel() * 2 + B * 785 * 384 * 2
+    local_bytes = qkv.numel() * 2 + B * 785 * 384 * 2  # q, k, v read + o write (fp16)
+    local_achieved = local_bytes / t_local / 1e9
     # the routing op on the same shard (routing HBM GB/s)
     x_embed = torch.randn(B, 785, 384, device=dev)
     metrics = (torch.randn(6, B, 785, 64, device=dev) * 1.3).half()
@@ -266,15 +269,15 @@ def run_b200(args):
                     "d2h_bytes_per_step": host_logits[0].numel() * host_logits.element_size(),
                     "overlap": "H2D of step i+1 on a copy stream during step i's forward"},
             "gpu_launches": ForwardGraph.library_launches(model) * args.steps,
-            "roofline": {"kernel": "attn_tc_kernel<half,64,full,bias> (latent attention, 393 carriers, 6 heads, B=%d)" % B,
-                         "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": TRAFFIC_LATENT_ATTN * B,
-                         "algorithmic_bytes": attn_bytes, "ms_per_launch": t_attn * 1e3,
-                         "tflops": attn_flops / t_attn / 1e12},
-            "local_attention": {"kernel": "attn_tc_kernel<half,160> + cls_row_kernel (window 16)",
-                                "ms_per_call": t_local * 1e3, "algorithmic_bytes": local_bytes,
-                                "achieved_gbs": local_bytes / t_local / 1e9,
-                                "frac": local_bytes / t_local / 1e9 / peak},
+            "roofline": {"kernel": "attn_tc_kernel<half,160,window> with the CLS row (local attention, window 16, "
+                                   "785 tokens, 6 heads, B=%d)" % B,
+                         "bound": "hbm", "achieved": local_achieved, "peak": peak, "unit": "GB/s",
+                         "frac": local_achieved / peak, "peak_kind": peak_kind, "traffic": TRAFFIC_LOCAL_ATTN * B,
+                         "algorithmic_bytes": local_bytes, "ms_per_launch": t_local * 1e3},
+            "latent_attention": {"kernel": "attn_tc_kernel<half,64,full,bias> (393 carriers, 6 heads)",
+                                 "ms_per_call": t_attn * 1e3, "algorithmic_bytes": attn_bytes,
+                                 "achieved_gbs": achieved, "frac": achieved / peak,
+                                 "traffic": TRAFFIC_LATENT_ATTN * B, "tflops": attn_flops / t_attn / 1e12},
             "routing": {"ms_per_call": t_route * 1e3, "algorithmic_bytes": route_bytes,
                         "achieved_gbs": route_bytes / t_route / 1e9, "frac": route_bytes / t_route / 1e9 / peak},
             "cpu_baseline": ({"value": cpu_v, "unit": "images/sec", "cores": os.cpu_count(), "kind": "port",
