@@ -103,11 +103,10 @@ struct TcChunks {
 // query tile 0 after its windowed rows: scores q0 . k_j * scale (+ bias_j),
 // softmax exp(s - max) / sum, then sum_j p_j v_j with 16-byte value loads
 // (8 threads per value row, 16 rows in flight).  `scratch` holds the scores
-// (Nk floats) and the partial sums; q0 is row 0 of the swizzled Q tile, whose
-// 16-byte chunks are in order.
+// (Nk floats) and the partial sums; qrow is the CLS query (global memory).
 template <typename ET>
-__device__ void cls_row_global(const uint8_t* sq, const ET* __restrict__ kg, const ET* __restrict__ vg, int64_t kb,
-                               int64_t kn, int64_t kh, int b, int h, int Nq, int Nk, int H, float scale,
+__device__ void cls_row_global(const ET* __restrict__ qrow, const ET* __restrict__ kg, const ET* __restrict__ vg,
+                               int64_t kb, int64_t kn, int64_t kh, int b, int h, int Nq, int Nk, int H, float scale,
                                const void* __restrict__ bias, int bias_dtype, float* scratch, void* out,
                                int out_dtype) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -115,7 +114,7 @@ __device__ void cls_row_global(const uint8_t* sq, const ET* __restrict__ kg, con
   float* qv = sp + ((Nk + 3) & ~3);            // [64]
   float* part = qv + kTcD;                     // [16][64]
   float* red = part + 16 * kTcD;               // [8]
-  if (tid < kTcD) qv[tid] = to_f32(reinterpret_cast<const ET*>(sq)[tid]);
+  if (tid < kTcD) qv[tid] = to_f32(qrow[tid]);
   __syncthreads();
   const ET* kbh = kg + (int64_t)b * kb + (int64_t)h * kh;
   const ET* vbh = vg + (int64_t)b * kb + (int64_t)h * kh;
@@ -224,8 +223,8 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, int q_order, int kv_order, int Nq, int Nk, int H, int window,
     float scale, const void* __restrict__ bias, int bias_dtype, void* __restrict__ out, int out_dtype,
-    int* __restrict__ err, int cls_global, const ET* __restrict__ kg, const ET* __restrict__ vg, int64_t kb,
-    int64_t kn, int64_t kh) {
+    int* __restrict__ err, int cls_global, const ET* __restrict__ qg, int64_t qb, int64_t qh,
+    const ET* __restrict__ kg, const ET* __restrict__ vg, int64_t kb, int64_t kn, int64_t kh) {
   using S = TcSmem<NB>;
   constexpr int NCH = TcChunks<NB>::kWarp;
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -544,8 +543,289 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
   // 0 was written above and is replaced); every MMA has completed, so the P
   // tile is free scratch
   if (WIN && cls_global && q0 == 0 && all_ok && nblocks > 0)
-    cls_row_global<ET>(sq, kg, vg, kb, kn, kh, b, h, Nq, Nk, H, scale, bias, bias_dtype,
-                       reinterpret_cast<float*>(sp), out, out_dtype);
+    cls_row_global<ET>(qg + (int64_t)b * qb + (int64_t)h * qh, kg, vg, kb, kn, kh, b, h, Nq, Nk, H, scale, bias,
+                       bias_dtype, reinterpret_cast<float*>(sp), out, out_dtype);
+}
+
+// ---------------------------------------------------------------------------
+// Windowed attention (window <= 16: one 160-key band per 128-query tile),
+// persistent: each CTA walks tiles t = blockIdx.x, + gridDim.x, ... in
+// (tile, head, image) order.  The next tile's Q and K are fetched as soon as
+// this tile's S = Q K^T has completed and its V as soon as P.V has, so copy
+// latency overlaps the softmax and epilogue; TMEM, barriers and tensor-map
+// prefetches are set up once per CTA.  Copies are issued from warps 1-3 and
+// the MMAs from thread 0.
+// ---------------------------------------------------------------------------
+template <typename ET, bool BIAS>
+__global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, int q_order, int kv_order, int N, int H, int B, int window,
+    float scale, const void* __restrict__ bias, int bias_dtype, void* __restrict__ out, int out_dtype,
+    int* __restrict__ err, int cls_global, const ET* __restrict__ qg, int64_t qb, int64_t qh,
+    const ET* __restrict__ kg, const ET* __restrict__ vg, int64_t kb, int64_t kn, int64_t kh) {
+  constexpr int NB = 160;
+  using S = TcSmem<NB>;
+  constexpr int NCH = TcChunks<NB>::kWarp;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = base + S::q_off;
+  uint8_t* sk = base + S::k_off;
+  uint8_t* sv = base + S::v_off;
+  uint8_t* sp = base + S::p_off;
+  float* sbias2 = reinterpret_cast<float*>(base + S::bias_off);  // [2][NB]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(base + S::bar_off);
+  uint64_t* bar_s = bar;
+  uint64_t* bar_o = bar + 1;
+  uint64_t* bar_q = bar + 2;
+  uint64_t* bar_k = bar + 3;
+  uint64_t* bar_v = bar + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + S::tmem_slot_off);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  constexpr int ab_bf16 = std::is_same<ET, __nv_bfloat16>::value ? 1 : 0;
+  constexpr uint32_t idesc_o = tc::idesc_f16(ab_bf16, 1, kTcM, kTcD);
+  const float kLog2e = 1.4426950408889634f;
+  const float sl2 = scale * kLog2e;
+  const int ntq = (N + kTcM - 1) / kTcM;
+  const int total = ntq * H * B;
+
+  struct Tile {
+    int q0, h, b, klo, khi;
+  };
+  auto tile_of = [&](int t) {
+    Tile x;
+    x.q0 = (t % ntq) * kTcM;
+    x.h = (t / ntq) % H;
+    x.b = t / (ntq * H);
+    x.klo = max(0, x.q0 - window);
+    x.khi = min(N, x.q0 + kTcM + window);
+    return x;
+  };
+  auto stage_bias = [&](const Tile& x, int buf) {
+    if (BIAS) {
+      float* sb = sbias2 + buf * NB;
+      for (int j = tid; j < NB; j += blockDim.x) {
+        float bv = 0.f;
+        if (x.klo + j < x.khi)
+          bv = to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)x.b * N + x.klo + j))) * kLog2e;
+        sb[j] = bv;
+      }
+    }
+  };
+
+  if (warp == 0) tc::tmem_alloc(tmem_slot, S::kTmemCols);
+  const int t0 = blockIdx.x;
+  if (tid == 0) {
+    for (int i = 0; i < 5; ++i) tc::mbar_init(bar + i, 1);
+    tc::fence_mbar_init();
+    tma::prefetch_map(&tm_q);
+    tma::prefetch_map(&tm_k);
+    tma::prefetch_map(&tm_v);
+    if (t0 < total) {
+      const Tile x = tile_of(t0);
+      tma::expect_tx(bar_q, kTcM * 128);
+      load_rows(tc::smem_u32(sq), &tm_q, q_order, x.h, x.q0, x.b, bar_q);
+      tma::expect_tx(bar_k, NB * 128);
+      load_rows(tc::smem_u32(sk), &tm_k, kv_order, x.h, x.klo, x.b, bar_k);
+      tma::expect_tx(bar_v, NB * 128);
+      load_rows(tc::smem_u32(sv), &tm_v, kv_order, x.h, x.klo, x.b, bar_v);
+    }
+  }
+  if (t0 < total) stage_bias(tile_of(t0), 0);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem, t_o = tmem + NB;
+  const uint32_t lane_sel = (uint32_t)(warp * 32) << 16;
+  bool ok = true;
+  // the last local tile whose Q/K and V copies were issued, for the drain
+  int qk_last = t0 < total ? 0 : -1, v_last = qk_last;
+
+  int i = 0;
+  for (int t = t0; t < total && ok; t += gridDim.x, ++i) {
+    const Tile x = tile_of(t);
+    const int tn = t + gridDim.x;
+    const bool has_next = tn < total;
+    const Tile xn = tile_of(has_next ? tn : t);
+    const int kvalid = x.khi - x.klo;
+    const int kpad = (kvalid + 31) & ~31;
+    const float* sbias = sbias2 + (i & 1) * NB;
+    const int qi = x.q0 + tid;
+
+    if (tid == 0) {
+      // S = Q K^T once this tile's Q and K have landed
+      ok = tc::mbar_wait(bar_q, i & 1, err) && tc::mbar_wait(bar_k, i & 1, err);
+      if (ok) {
+        tc::fence_after_sync();
+        const uint64_t dq = tc::sw128_desc(tc::smem_u32(sq), 16), dk = tc::sw128_desc(tc::smem_u32(sk), 16);
+        const uint32_t idesc_s = tc::idesc_f16(ab_bf16, 0, kTcM, kpad);
+#pragma unroll
+        for (int kk = 0; kk < kTcD / 16; ++kk) tc::mma_f16_ss(t_s, dq + 2 * kk, dk + 2 * kk, idesc_s, kk > 0);
+        tc::mma_commit(bar_s);
+      } else if (err) {
+        atomicOr(err, MN_STATUS_TC_TIMEOUT);
+      }
+    }
+    if (!tc::mbar_wait(bar_s, i & 1, err)) { ok = false; break; }
+    tc::fence_after_sync();
+    // S done: Q and K are free for the next tile
+    if (has_next) {
+      if (tid == 32) {
+        tma::expect_tx(bar_q, kTcM * 128);
+        load_rows(tc::smem_u32(sq), &tm_q, q_order, xn.h, xn.q0, xn.b, bar_q);
+      } else if (tid == 64) {
+        tma::expect_tx(bar_k, NB * 128);
+        load_rows(tc::smem_u32(sk), &tm_k, kv_order, xn.h, xn.klo, xn.b, bar_k);
+      }
+      stage_bias(xn, (i + 1) & 1);
+      qk_last = i + 1;
+    }
+
+    // this row's legal keys relative to klo, and the warp's chunks
+    int jlo = max(0, qi - window - x.klo);
+    int jhi = min(kvalid, qi + window + 1 - x.klo);
+    if (qi >= N) jhi = jlo;
+    const bool has = jlo < jhi;
+    const int wlo = (int)__reduce_min_sync(0xffffffffu, (unsigned)(has ? jlo : NB));
+    const int whi = (int)__reduce_max_sync(0xffffffffu, (unsigned)(has ? jhi : 0));
+    const int c_lo = min(wlo >> 5, TcChunks<NB>::kAll);
+    int nch = whi > wlo ? ((whi + 31) >> 5) - c_lo : 0;
+    if (nch > NCH || c_lo + nch > TcChunks<NB>::kAll) {  // cannot happen for window <= 16
+      nch = max(0, min(NCH, TcChunks<NB>::kAll - c_lo));
+      if (err && (tid & 31) == 0) atomicOr(err, MN_STATUS_TC_TIMEOUT);
+    }
+    float sc[NCH * 32];
+#pragma unroll
+    for (int u = 0; u < NCH; ++u)
+      if (u < nch) tc::tmem_ld32_nowait(t_s + lane_sel + (c_lo + u) * 32, sc + u * 32);
+    tc::tmem_ld_wait<NCH * 32>(sc);
+    // logits (illegal keys -inf) and the row maximum
+    float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+      if (u >= nch) continue;
+      const int cb = (c_lo + u) * 32;
+      const float4* b4 = reinterpret_cast<const float4*>(sbias + cb);
+#pragma unroll
+      for (int i4 = 0; i4 < 8; ++i4) {
+        float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (BIAS) bb = b4[i4];
+        const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = cb + i4 * 4 + e;
+          float& v = sc[u * 32 + i4 * 4 + e];
+          v = (j >= jlo && j < jhi) ? fmaf(v, sl2, bv[e]) : -INFINITY;
+          mx4[e] = fmaxf(mx4[e], v);
+        }
+      }
+    }
+    const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+    const float msub = mx == -INFINITY ? 0.f : mx;
+    // probabilities -> P; chunks outside the warp's range are zero
+    float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+      if (u >= nch) continue;
+      const int c = c_lo + u;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint4 pk;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = fast_ex2(sc[u * 32 + g * 8 + 2 * e] - msub);
+          const float p1 = fast_ex2(sc[u * 32 + g * 8 + 2 * e + 1] - msub);
+          ls4[(2 * e) & 3] += p0;
+          ls4[(2 * e + 1) & 3] += p1;
+          w[e] = pack2<ET>(p0, p1);
+        }
+        const int key8 = c * 4 + g;
+        *reinterpret_cast<uint4*>(sp + (key8 >> 3) * (kTcM * 128) + tc::sw128_off(tid, key8 & 7)) = pk;
+      }
+    }
+    const int c_end = (kpad + 31) >> 5;
+    for (int c = 0; c < c_end; ++c) {
+      if (c >= c_lo && c < c_lo + nch) continue;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int key8 = c * 4 + g;
+        *reinterpret_cast<uint4*>(sp + (key8 >> 3) * (kTcM * 128) + tc::sw128_off(tid, key8 & 7)) =
+            make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    const float l_row = (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after_sync();
+      if (!tc::mbar_wait(bar_v, i & 1, err)) {
+        ok = false;
+        if (err) atomicOr(err, MN_STATUS_TC_TIMEOUT);
+      } else {
+        const uint64_t dp = tc::sw128_desc(tc::smem_u32(sp), 16);
+        const uint64_t dv = tc::sw128_desc(tc::smem_u32(sv), 16384);
+        for (int kk = 0; kk < kpad / 16; ++kk)
+          tc::mma_f16_ss(t_o, dp + (uint64_t)((kk >> 2) * (kTcM * 128 / 16) + (kk & 3) * 2), dv + 128 * kk,
+                         idesc_o, kk > 0 ? 1u : 0u);
+        tc::mma_commit(bar_o);
+      }
+    }
+    if (!tc::mbar_wait(bar_o, i & 1, err)) { ok = false; break; }
+    tc::fence_after_sync();
+    // P.V done: V is free for the next tile
+    if (has_next && tid == 96) {
+      tma::expect_tx(bar_v, NB * 128);
+      load_rows(tc::smem_u32(sv), &tm_v, kv_order, xn.h, xn.klo, xn.b, bar_v);
+    }
+    if (has_next) v_last = i + 1;
+    {
+      const float inv = l_row > 0.f ? 1.0f / l_row : 0.f;
+      const int64_t obase = (((int64_t)x.b * N + qi) * H + x.h) * kTcD;
+#pragma unroll
+      for (int c = 0; c < kTcD / 32; ++c) {
+        float o[32];
+        tc::tmem_ld32(t_o + lane_sel + c * 32, o);  // warp-collective: every row loads
+        if (qi >= N) continue;
+#pragma unroll
+        for (int k2 = 0; k2 < 32; ++k2) o[k2] *= inv;
+        if (out_dtype == MN_F32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + obase + c * 32);
+#pragma unroll
+          for (int k2 = 0; k2 < 8; ++k2)
+            dst[k2] = make_float4(o[4 * k2], o[4 * k2 + 1], o[4 * k2 + 2], o[4 * k2 + 3]);
+        } else if (out_dtype == MN_F16) {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(out) + obase + c * 32);
+#pragma unroll
+          for (int k2 = 0; k2 < 4; ++k2) dst[k2] = pack8<__half>(o + 8 * k2);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + obase + c * 32);
+#pragma unroll
+          for (int k2 = 0; k2 < 4; ++k2) dst[k2] = pack8<__nv_bfloat16>(o + 8 * k2);
+        }
+      }
+    }
+    // the CLS row of this (image, head), by the CTA holding its tile 0; the
+    // P tile is free scratch until the next tile's softmax (barriers around)
+    if (cls_global && x.q0 == 0) {
+      __syncthreads();
+      cls_row_global<ET>(qg + (int64_t)x.b * qb + (int64_t)x.h * qh, kg, vg, kb, kn, kh, x.b, x.h, N, N, H, scale,
+                         bias, bias_dtype, reinterpret_cast<float*>(sp), out, out_dtype);
+      __syncthreads();
+    }
+  }
+  if (tid == 0 && qk_last >= 0) {
+    // every bulk copy issued has landed before the CTA may exit
+    tc::mbar_wait(bar_q, qk_last & 1, nullptr);
+    tc::mbar_wait(bar_k, qk_last & 1, nullptr);
+    tc::mbar_wait(bar_v, v_last & 1, nullptr);
+  }
+  if (!ok && tid == 0 && err) atomicOr(err, MN_STATUS_TC_TIMEOUT);
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, S::kTmemCols);
 }
 
 // 4-D tensor map (d, h, n, b) -- or (d, n, h, b) when heads are strided
@@ -580,12 +860,42 @@ static bool launch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const v
   // the CLS row rides along with query tile 0 when its scratch fits the P tile
   const bool cls = WIN && cls_global && Nq == Nk && Nk <= cls_max_keys<NB>();
   kern<<<grid, 128, smem, st>>>(mq, mk, mv, q_order, kv_order, Nq, Nk, H, window, scale, bias, bias_dtype, out,
-                                out_dtype, err, cls ? 1 : 0, static_cast<const ET*>(k), static_cast<const ET*>(v),
-                                kb, kn, kh);
+                                out_dtype, err, cls ? 1 : 0, static_cast<const ET*>(q), qb, qh,
+                                static_cast<const ET*>(k), static_cast<const ET*>(v), kb, kn, kh);
   *cls_done = cls;
   return true;
 }
 
+template <typename ET>
+static bool launch_win_persistent(const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v,
+                                  int64_t kb, int64_t kn, int64_t kh, int B, int N, int H, int window, float scale,
+                                  const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st,
+                                  bool cls_global, bool* cls_done) {
+  CUtensorMap mq, mk, mv;
+  int q_order = 0, kv_order = 0, v_order = 0;
+  if (!make_head_map<ET>(&mq, &q_order, q, B, N, H, qb, qn, qh, kTcM) ||
+      !make_head_map<ET>(&mk, &kv_order, k, B, N, H, kb, kn, kh, 160) ||
+      !make_head_map<ET>(&mv, &v_order, v, B, N, H, kb, kn, kh, 160))
+    return false;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int total = ((N + kTcM - 1) / kTcM) * H * B;
+  const int grid = std::max(1, std::min(total, 2 * sms));  // two CTAs per SM (TMEM, shared memory)
+  const bool cls = cls_global && N <= cls_max_keys<160>();
+  auto kern = bias ? attn_win_persistent_kernel<ET, true> : attn_win_persistent_kernel<ET, false>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TcSmem<160>::bytes);
+  kern<<<grid, 128, TcSmem<160>::bytes, st>>>(mq, mk, mv, q_order, kv_order, N, H, B, window, scale, bias,
+                                               bias_dtype, out, out_dtype, err, cls ? 1 : 0,
+                                               static_cast<const ET*>(q), qb, qh, static_cast<const ET*>(k),
+                                               static_cast<const ET*>(v), kb, kn, kh);
+  *cls_done = cls;
+  return true;
+}
+
+#ifndef MN_TC_WIN_PERSISTENT
+#define MN_TC_WIN_PERSISTENT 1  // window <= 16 on the persistent kernel
+#endif
 #ifndef MN_TC_SINGLE_BAND
 #define MN_TC_SINGLE_BAND 1  // windows up to 16: the tile's whole key band as one 160-key block
 #endif
@@ -599,9 +909,13 @@ static bool dispatch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const
                         const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st,
                         bool cls_global, bool* cls_done) {
   constexpr int NBM = MN_TC_BLOCK_KEYS;
-  if (MN_TC_SINGLE_BAND && window >= 0 && kTcM + 2 * window <= 160)  // the whole band in one block
+  if (MN_TC_SINGLE_BAND && window >= 0 && kTcM + 2 * window <= 160) {  // the whole band in one block
+    if (MN_TC_WIN_PERSISTENT && Nq == Nk)
+      return launch_win_persistent<ET>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, H, window, scale, bias, bias_dtype,
+                                       out, out_dtype, err, st, cls_global, cls_done);
     return launch_tc<ET, 160, true>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
                                     out, out_dtype, err, st, cls_global, cls_done);
+  }
   if (window >= 0)
     return launch_tc<ET, NBM, true>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
                                     out, out_dtype, err, st, cls_global, cls_done);

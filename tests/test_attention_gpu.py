@@ -140,6 +140,29 @@ def test_local_block_attention_cls_global(dev, dtype):
     torch.testing.assert_close(out.float(), exp, atol=tol, rtol=tol)
 
 
+@pytest.mark.parametrize("dtype,biased,cls", [(torch.float16, True, False), (torch.bfloat16, False, True),
+                                              (torch.float16, False, True)])
+def test_window_many_tiles_per_cta(dev, dtype, biased, cls):
+    """Window 16 at 785 tokens with more (tile, head, image) work items than
+    resident CTAs (12 x 6 x 7 = 504), so each CTA walks several tiles and
+    fetches the next one's rows while finishing the current one."""
+    import mergenet_b200 as mn
+    torch.manual_seed(11 + int(biased) + 2 * int(cls))
+    b, n, h, d = 12, 785, 6, 64
+    qkv = (torch.randn(b, n, 3 * h * d, device=dev) * 0.5).to(dtype)
+    bias = (torch.rand(b, n, device=dev) * 3 + 0.5).log() if biased else None
+    out = mn.local_attention_packed(qkv, h, 16, cls_global=cls, bias=bias)
+    view = qkv.view(b, n, 3, h, d)
+    q, k, v = (view[:, :, i].transpose(1, 2) for i in range(3))
+    exp = reference_bhnd(q, k, v, bias.to(dtype) if biased else None, 16)
+    if cls:
+        exp[:, :, :1] = torch.softmax(q[:, :, :1].float() @ k.float().transpose(-1, -2) / 8.0, -1) @ v.float()
+    exp = exp.transpose(1, 2).reshape(b, n, h * d)
+    tol = 2e-2 if dtype == torch.bfloat16 else 5e-3
+    torch.testing.assert_close(out.float(), exp, atol=tol, rtol=tol)
+    assert mn.attention.attention_status(dev) == 0
+
+
 @pytest.mark.parametrize("tokens,window,biased", [(785, 17, False), (785, 40, True), (300, 100, False),
                                                    (131, 70, True)])
 def test_wide_window_multi_block(dev, tokens, window, biased):
