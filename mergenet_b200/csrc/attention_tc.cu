@@ -201,6 +201,13 @@ constexpr int cls_max_keys() {
   return (int)((TcSmem<NB>::kPAtoms * kTcM * 128) / 4) - (kTcD + 16 * kTcD + 8) - 4;
 }
 
+__device__ __forceinline__ void prefetch_rows(const CUtensorMap* map, int order, int h, int n, int b) {
+  if (order == 0)
+    tma::prefetch_l2_4d(map, 0, h, n, b);
+  else
+    tma::prefetch_l2_4d(map, 0, n, h, b);
+}
+
 // WIN: sliding window (per-row key ranges, masked per element).  Without a
 // window every row sees the same keys, so keys past the end get a -inf bias
 // and no element is masked.  BIAS: a per-key bias is given.
@@ -548,10 +555,115 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// CLS row of the windowed attention, folded into the persistent kernel.
+// Query 0 attends every key (bias_local_attn.py:704-719).  The CTA that
+// processes a (head, image)'s first query tile owns its CLS row: while a tile's
+// K/V rows sit in shared memory, each warp scores the CLS query against 32 of
+// the tile's own 128 keys and folds them into its running softmax state (max,
+// sum, 64 outputs; log2 domain) held in shared memory.  The four warps' states
+// are merged and row 0 is written after the last tile.  When the CTA's range
+// of tiles ends before the (head, image) does, the rest of the keys are read
+// from global memory.
+// ---------------------------------------------------------------------------
+constexpr int kClsState = 2 + kTcD;                               // max, sum, outputs
+constexpr int kClsFloats = 2 * kTcD + 2 * 4 * kClsState;          // two queries, two sets of 4 warp states
+constexpr uint32_t kClsBytes = kClsFloats * 4;
+
+template <typename ET>
+__device__ __forceinline__ float dot8(const uint4& u, const float* __restrict__ q) {
+  const ET* e = reinterpret_cast<const ET*>(&u);
+  const float4 qa = *reinterpret_cast<const float4*>(q), qb = *reinterpret_cast<const float4*>(q + 4);
+  float a = to_f32(e[0]) * qa.x;
+  a = fmaf(to_f32(e[1]), qa.y, a);
+  a = fmaf(to_f32(e[2]), qa.z, a);
+  a = fmaf(to_f32(e[3]), qa.w, a);
+  float b = to_f32(e[4]) * qb.x;
+  b = fmaf(to_f32(e[5]), qb.y, b);
+  b = fmaf(to_f32(e[6]), qb.z, b);
+  b = fmaf(to_f32(e[7]), qb.w, b);
+  return a + b;
+}
+
+// Lane l's CLS logit (log2 domain) for key l of a warp's group of 32 keys;
+// -inf when l >= nvalid.  Keys come from the swizzled K tile (row row0 + l)
+// or, when GLOBAL, from global row key0 + l.  `bl2` is the key's bias.
+template <typename ET, bool GLOBAL>
+__device__ __forceinline__ float cls_warp_score(const float* __restrict__ qc, int nvalid, const uint8_t* sk,
+                                                int row0, const ET* __restrict__ kbh, int64_t kn, int key0,
+                                                float sl2, float bl2) {
+  const int lane = threadIdx.x & 31;
+  if (GLOBAL && nvalid <= 0) return -INFINITY;  // no row of this group exists
+  // tile rows past the valid keys are in bounds (zero-filled): read them
+  // unconditionally and mask afterwards; global rows are clamped to the
+  // group's last key instead
+  const int kr = GLOBAL ? key0 + min(lane, nvalid - 1) : 0;
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int c = 0; c < kTcD / 8; ++c) {
+    const uint4 u = GLOBAL ? __ldg(reinterpret_cast<const uint4*>(kbh + (int64_t)kr * kn) + c)
+                           : *reinterpret_cast<const uint4*>(sk + tc::sw128_off(row0 + lane, c));
+    if (c & 1) a1 += dot8<ET>(u, qc + c * 8);
+    else a0 += dot8<ET>(u, qc + c * 8);
+  }
+  return lane < nvalid ? fmaf(a0 + a1, sl2, bl2) : -INFINITY;
+}
+
+// One warp folds its 32 scored keys (logit s in lane l) into its CLS state
+// `st` (fresh: the state is empty).  For P.V lane (ks = l >> 3, dg = l & 7)
+// takes keys ks*8 .. ks*8+7 and channels dg*8 .. dg*8+7, from the swizzled V
+// tile (rows row0 + key) or, when GLOBAL, global rows key0 + key.
+template <typename ET, bool GLOBAL>
+__device__ __forceinline__ void cls_warp_fold(float s, float* st, bool fresh, int nvalid, const uint8_t* sv,
+                                              int row0, const ET* __restrict__ vbh, int64_t kn, int key0) {
+  const int lane = threadIdx.x & 31;
+  if (GLOBAL && nvalid <= 0) return;  // nothing to fold (never the first group: `fresh` is false here)
+  const float m_old = fresh ? -INFINITY : st[0];
+  const float l_old = fresh ? 0.f : st[1];
+  const float m_new = fmaxf(m_old, warp_max(s));
+  const float msub = m_new == -INFINITY ? 0.f : m_new;
+  const float alpha = fast_ex2(m_old - msub);
+  const float p = lane < nvalid ? fast_ex2(s - msub) : 0.f;
+  const float psum = warp_sum(p);
+  const int ks = lane >> 3, dg = lane & 7;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  uint4 vr[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {  // all eight rows in flight; p = 0 past the valid keys
+    const int kk = ks * 8 + i;
+    vr[i] = GLOBAL ? __ldg(reinterpret_cast<const uint4*>(vbh + (int64_t)(key0 + min(kk, nvalid - 1)) * kn) + dg)
+                   : *reinterpret_cast<const uint4*>(sv + tc::sw128_off(row0 + kk, dg));
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float pk = __shfl_sync(0xffffffffu, p, ks * 8 + i);
+    const ET* e = reinterpret_cast<const ET*>(&vr[i]);
+#pragma unroll
+    for (int k2 = 0; k2 < 8; ++k2) acc[k2] = fmaf(pk, to_f32(e[k2]), acc[k2]);
+  }
+#pragma unroll
+  for (int k2 = 0; k2 < 8; ++k2) {
+    acc[k2] += __shfl_xor_sync(0xffffffffu, acc[k2], 8);
+    acc[k2] += __shfl_xor_sync(0xffffffffu, acc[k2], 16);
+  }
+  __syncwarp();  // every lane has read st[0..1]
+  if (lane < 8) {
+    float* o = st + 2 + lane * 8;
+#pragma unroll
+    for (int k2 = 0; k2 < 8; ++k2) o[k2] = fresh ? acc[k2] : fmaf(o[k2], alpha, acc[k2]);
+  }
+  if (lane == 0) {
+    st[0] = m_new;
+    st[1] = fmaf(l_old, alpha, psum);
+  }
+  __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
 // Windowed attention (window <= 16: one 160-key band per 128-query tile),
-// persistent: each CTA walks tiles t = blockIdx.x, + gridDim.x, ... in
-// (tile, head, image) order.  The next tile's Q and K are fetched as soon as
-// this tile's S = Q K^T has completed and its V as soon as P.V has, so copy
+// persistent: CTA c walks an equal, contiguous range of tiles in (tile, head,
+// image) order.  The next tile's Q is fetched as soon as this tile's
+// S = Q K^T has completed, its K once the softmax is done (at once when there
+// is no CLS row to fold in) and its V as soon as P.V has completed, so copy
 // latency overlaps the softmax and epilogue; TMEM, barriers and tensor-map
 // prefetches are set up once per CTA.  Copies are issued from warps 1-3 and
 // the MMAs from thread 0.
@@ -580,6 +692,8 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
   uint64_t* bar_k = bar + 3;
   uint64_t* bar_v = bar + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + S::tmem_slot_off);
+  float* cls_q = reinterpret_cast<float*>(base + ((S::tmem_slot_off + 8 + 15) & ~15u));  // [2][64]
+  float* cls_st = cls_q + 2 * kTcD;                                                      // [2][4][kClsState]
 
   const int tid = threadIdx.x, warp = tid >> 5;
   constexpr int ab_bf16 = std::is_same<ET, __nv_bfloat16>::value ? 1 : 0;
@@ -588,15 +702,22 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
   const float sl2 = scale * kLog2e;
   const int ntq = (N + kTcM - 1) / kTcM;
   const int total = ntq * H * B;
+  // this CTA's tiles [t_begin, t_end)
+  const int per = total / (int)gridDim.x, extra = total % (int)gridDim.x;
+  const int t_begin = (int)blockIdx.x * per + min((int)blockIdx.x, extra);
+  const int t_end = t_begin + per + ((int)blockIdx.x < extra ? 1 : 0);
+  const bool late_k = cls_global != 0;  // K is read by the CLS fold until the softmax barrier
 
   struct Tile {
-    int q0, h, b, klo, khi;
+    int q0, h, b, klo, khi, qt, unit;
   };
   auto tile_of = [&](int t) {
     Tile x;
-    x.q0 = (t % ntq) * kTcM;
-    x.h = (t / ntq) % H;
-    x.b = t / (ntq * H);
+    x.qt = t % ntq;
+    x.unit = t / ntq;
+    x.q0 = x.qt * kTcM;
+    x.h = x.unit % H;
+    x.b = x.unit / H;
     x.klo = max(0, x.q0 - window);
     x.khi = min(N, x.q0 + kTcM + window);
     return x;
@@ -612,17 +733,20 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
       }
     }
   };
+  auto stage_cls_query = [&](const Tile& x) {  // a (head, image)'s first tile: its CLS query
+    if (cls_global && x.qt == 0 && tid < kTcD)
+      cls_q[(x.unit & 1) * kTcD + tid] = to_f32(qg[(int64_t)x.b * qb + (int64_t)x.h * qh + tid]);
+  };
 
   if (warp == 0) tc::tmem_alloc(tmem_slot, S::kTmemCols);
-  const int t0 = blockIdx.x;
   if (tid == 0) {
     for (int i = 0; i < 5; ++i) tc::mbar_init(bar + i, 1);
     tc::fence_mbar_init();
     tma::prefetch_map(&tm_q);
     tma::prefetch_map(&tm_k);
     tma::prefetch_map(&tm_v);
-    if (t0 < total) {
-      const Tile x = tile_of(t0);
+    if (t_begin < t_end) {
+      const Tile x = tile_of(t_begin);
       tma::expect_tx(bar_q, kTcM * 128);
       load_rows(tc::smem_u32(sq), &tm_q, q_order, x.h, x.q0, x.b, bar_q);
       tma::expect_tx(bar_k, NB * 128);
@@ -631,7 +755,10 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
       load_rows(tc::smem_u32(sv), &tm_v, kv_order, x.h, x.klo, x.b, bar_v);
     }
   }
-  if (t0 < total) stage_bias(tile_of(t0), 0);
+  if (t_begin < t_end) {
+    stage_bias(tile_of(t_begin), 0);
+    stage_cls_query(tile_of(t_begin));
+  }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -639,19 +766,21 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
   const uint32_t t_s = tmem, t_o = tmem + NB;
   const uint32_t lane_sel = (uint32_t)(warp * 32) << 16;
   bool ok = true;
-  // the last local tile whose Q/K and V copies were issued, for the drain
-  int qk_last = t0 < total ? 0 : -1, v_last = qk_last;
+  // the last local tile whose Q, K and V copies were issued, for the drain
+  int q_last = t_begin < t_end ? 0 : -1, k_last = q_last, v_last = q_last;
+  // the unit whose first tile precedes t_begin has its CLS row elsewhere
+  const int first_owned_unit = (t_begin % ntq == 0) ? t_begin / ntq : t_begin / ntq + 1;
 
   int i = 0;
-  for (int t = t0; t < total && ok; t += gridDim.x, ++i) {
+  for (int t = t_begin; t < t_end && ok; ++t, ++i) {
     const Tile x = tile_of(t);
-    const int tn = t + gridDim.x;
-    const bool has_next = tn < total;
-    const Tile xn = tile_of(has_next ? tn : t);
+    const bool has_next = t + 1 < t_end;
+    const Tile xn = tile_of(has_next ? t + 1 : t);
     const int kvalid = x.khi - x.klo;
     const int kpad = (kvalid + 31) & ~31;
     const float* sbias = sbias2 + (i & 1) * NB;
     const int qi = x.q0 + tid;
+    const bool cls_tile = cls_global && x.unit >= first_owned_unit;
 
     if (tid == 0) {
       // S = Q K^T once this tile's Q and K have landed
@@ -667,21 +796,43 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
         atomicOr(err, MN_STATUS_TC_TIMEOUT);
       }
     }
+    // while S = Q K^T runs, the CLS row scores this tile's own keys
+    // [q0, q0 + 128), 32 per warp
+    const int cls_row0 = x.q0 + warp * 32 - x.klo;
+    const int cls_nvalid = max(0, min(32, min(x.q0 + kTcM, N) - (x.q0 + warp * 32)));
+    float cls_s = -INFINITY;
+    if (cls_tile) {
+      if (!tc::mbar_wait(bar_k, i & 1, err)) { ok = false; break; }
+      const float bl2 = (BIAS && (tid & 31) < cls_nvalid) ? sbias[cls_row0 + (tid & 31)] : 0.f;
+      cls_s = cls_warp_score<ET, false>(cls_q + (x.unit & 1) * kTcD, cls_nvalid, sk, cls_row0, nullptr, 0, 0, sl2,
+                                        bl2);
+    }
     if (!tc::mbar_wait(bar_s, i & 1, err)) { ok = false; break; }
     tc::fence_after_sync();
-    // S done: Q and K are free for the next tile
+    // S done: Q (and K, when no CLS fold reads it) are free for the next tile
     if (has_next) {
       if (tid == 32) {
         tma::expect_tx(bar_q, kTcM * 128);
         load_rows(tc::smem_u32(sq), &tm_q, q_order, xn.h, xn.q0, xn.b, bar_q);
-      } else if (tid == 64) {
+      } else if (tid == 64 && !late_k) {
         tma::expect_tx(bar_k, NB * 128);
         load_rows(tc::smem_u32(sk), &tm_k, kv_order, xn.h, xn.klo, xn.b, bar_k);
       }
+      q_last = i + 1;
+      if (!late_k) k_last = i + 1;
       stage_bias(xn, (i + 1) & 1);
-      qk_last = i + 1;
+      stage_cls_query(xn);
     }
-
+    if (cls_global && warp == 3 && t == max(t_begin, t_end - 2)) {
+      // two tiles before the range ends: bring the keys that the last
+      // (head, image)'s CLS row will read from global memory into L2
+      const Tile xl = tile_of(t_end - 1);
+      if (xl.unit >= first_owned_unit)
+        for (int k0 = xl.q0 + kTcM + (tid & 31) * NB; k0 < N; k0 += 32 * NB) {
+          prefetch_rows(&tm_k, kv_order, xl.h, k0, xl.b);
+          prefetch_rows(&tm_v, kv_order, xl.h, k0, xl.b);
+        }
+    }
     // this row's legal keys relative to klo, and the warp's chunks
     int jlo = max(0, qi - window - x.klo);
     int jhi = min(kvalid, qi + window + 1 - x.klo);
@@ -759,6 +910,13 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
+    if (has_next && late_k) {  // every warp is past its reads of K
+      if (tid == 64) {
+        tma::expect_tx(bar_k, NB * 128);
+        load_rows(tc::smem_u32(sk), &tm_k, kv_order, xn.h, xn.klo, xn.b, bar_k);
+      }
+      k_last = i + 1;
+    }
     if (tid == 0) {
       tc::fence_after_sync();
       if (!tc::mbar_wait(bar_v, i & 1, err)) {
@@ -773,14 +931,22 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
         tc::mma_commit(bar_o);
       }
     }
+    if (cls_tile) {  // while P.V runs, the CLS row folds in its scored keys
+      if (!tc::mbar_wait(bar_v, i & 1, err)) { ok = false; break; }
+      cls_warp_fold<ET, false>(cls_s, cls_st + ((x.unit & 1) * 4 + warp) * kClsState, x.qt == 0, cls_nvalid, sv,
+                               cls_row0, nullptr, 0, 0);
+    }
     if (!tc::mbar_wait(bar_o, i & 1, err)) { ok = false; break; }
     tc::fence_after_sync();
-    // P.V done: V is free for the next tile
-    if (has_next && tid == 96) {
-      tma::expect_tx(bar_v, NB * 128);
-      load_rows(tc::smem_u32(sv), &tm_v, kv_order, xn.h, xn.klo, xn.b, bar_v);
+    // P.V done (and, after the barrier, every warp's CLS reads): V is free
+    if (has_next) {
+      if (cls_tile) __syncthreads();
+      if (tid == 96) {
+        tma::expect_tx(bar_v, NB * 128);
+        load_rows(tc::smem_u32(sv), &tm_v, kv_order, xn.h, xn.klo, xn.b, bar_v);
+      }
+      v_last = i + 1;
     }
-    if (has_next) v_last = i + 1;
     {
       const float inv = l_row > 0.f ? 1.0f / l_row : 0.f;
       const int64_t obase = (((int64_t)x.b * N + qi) * H + x.h) * kTcD;
@@ -807,19 +973,44 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
         }
       }
     }
-    // the CLS row of this (image, head), by the CTA holding its tile 0; the
-    // P tile is free scratch until the next tile's softmax (barriers around)
-    if (cls_global && x.q0 == 0) {
-      __syncthreads();
-      cls_row_global<ET>(qg + (int64_t)x.b * qb + (int64_t)x.h * qh, kg, vg, kb, kn, kh, x.b, x.h, N, N, H, scale,
-                         bias, bias_dtype, reinterpret_cast<float*>(sp), out, out_dtype);
-      __syncthreads();
+    // the CLS row is complete after the unit's last tile, or at the end of
+    // this CTA's range (the remaining keys then come from global memory)
+    if (cls_tile && (x.qt == ntq - 1 || t + 1 == t_end)) {
+      float* st = cls_st + ((x.unit & 1) * 4 + warp) * kClsState;
+      const float* qc = cls_q + (x.unit & 1) * kTcD;
+      const ET* kbh = kg + (int64_t)x.b * kb + (int64_t)x.h * kh;
+      const ET* vbh = vg + (int64_t)x.b * kb + (int64_t)x.h * kh;
+      for (int k0 = x.q0 + kTcM; k0 < N; k0 += kTcM) {
+        const int key0 = k0 + warp * 32;
+        const int nvalid = max(0, min(32, N - key0));
+        const int lane = tid & 31;
+        float bl2 = 0.f;
+        if (BIAS && lane < nvalid)
+          bl2 = to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)x.b * N + key0 + lane))) * kLog2e;
+        const float sc0 = cls_warp_score<ET, true>(qc, nvalid, nullptr, 0, kbh, kn, key0, sl2, bl2);
+        cls_warp_fold<ET, true>(sc0, st, false, nvalid, nullptr, 0, vbh, kn, key0);
+      }
+      __syncthreads();  // every warp's state, and this tile's row-0 store, are in
+      if (tid < kTcD) {
+        const float* s0 = cls_st + (x.unit & 1) * 4 * kClsState;
+        float m = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) m = fmaxf(m, s0[w * kClsState]);
+        float l = 0.f, o = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const float a = fast_ex2(s0[w * kClsState] - m);
+          l = fmaf(s0[w * kClsState + 1], a, l);
+          o = fmaf(s0[w * kClsState + 2 + tid], a, o);
+        }
+        store_any(out, out_dtype, ((int64_t)x.b * N * H + x.h) * kTcD + tid, o / l);
+      }
     }
   }
-  if (tid == 0 && qk_last >= 0) {
+  if (tid == 0 && q_last >= 0) {
     // every bulk copy issued has landed before the CTA may exit
-    tc::mbar_wait(bar_q, qk_last & 1, nullptr);
-    tc::mbar_wait(bar_k, qk_last & 1, nullptr);
+    tc::mbar_wait(bar_q, q_last & 1, nullptr);
+    tc::mbar_wait(bar_k, k_last & 1, nullptr);
     tc::mbar_wait(bar_v, v_last & 1, nullptr);
   }
   if (!ok && tid == 0 && err) atomicOr(err, MN_STATUS_TC_TIMEOUT);
@@ -882,10 +1073,12 @@ static bool launch_win_persistent(const void* q, int64_t qb, int64_t qn, int64_t
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int total = ((N + kTcM - 1) / kTcM) * H * B;
   const int grid = std::max(1, std::min(total, 2 * sms));  // two CTAs per SM (TMEM, shared memory)
-  const bool cls = cls_global && N <= cls_max_keys<160>();
+  const bool cls = cls_global;
   auto kern = bias ? attn_win_persistent_kernel<ET, true> : attn_win_persistent_kernel<ET, false>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TcSmem<160>::bytes);
-  kern<<<grid, 128, TcSmem<160>::bytes, st>>>(mq, mk, mv, q_order, kv_order, N, H, B, window, scale, bias,
+  constexpr uint32_t smem = TcSmem<160>::bytes + kClsBytes + 16;
+  static_assert(smem <= 113 * 1024, "two CTAs per SM");
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<grid, 128, smem, st>>>(mq, mk, mv, q_order, kv_order, N, H, B, window, scale, bias,
                                                bias_dtype, out, out_dtype, err, cls ? 1 : 0,
                                                static_cast<const ET*>(q), qb, qh, static_cast<const ET*>(k),
                                                static_cast<const ET*>(v), kb, kn, kh);
