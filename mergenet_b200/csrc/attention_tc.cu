@@ -584,78 +584,124 @@ __device__ __forceinline__ float dot8(const uint4& u, const float* __restrict__ 
   return a + b;
 }
 
-// Lane l's CLS logit (log2 domain) for key l of a warp's group of 32 keys;
-// -inf when l >= nvalid.  Keys come from the swizzled K tile (row row0 + l)
-// or, when GLOBAL, from global row key0 + l.  `bl2` is the key's bias.
-template <typename ET, bool GLOBAL>
-__device__ __forceinline__ float cls_warp_score(const float* __restrict__ qc, int nvalid, const uint8_t* sk,
-                                                int row0, const ET* __restrict__ kbh, int64_t kn, int key0,
-                                                float sl2, float bl2) {
+// Lane l's CLS logits (log2 domain) for key l of G groups of 32 keys each
+// (group g: nv[g] valid keys; -inf past them).  Keys come from the swizzled
+// K tile (row row0 + l, G = 1) or, when GLOBAL, from global rows
+// key0 + g * gstride + l.  `bl2[g]` is the key's bias.
+template <typename ET, bool GLOBAL, int G>
+__device__ __forceinline__ void cls_warp_score(const float* __restrict__ qc, const int* nv, const uint8_t* sk,
+                                               int row0, const ET* __restrict__ kbh, int64_t kn, int key0,
+                                               int gstride, float sl2, const float* bl2, float* s) {
   const int lane = threadIdx.x & 31;
-  if (GLOBAL && nvalid <= 0) return -INFINITY;  // no row of this group exists
-  // tile rows past the valid keys are in bounds (zero-filled): read them
-  // unconditionally and mask afterwards; global rows are clamped to the
-  // group's last key instead
-  const int kr = GLOBAL ? key0 + min(lane, nvalid - 1) : 0;
-  float a0 = 0.f, a1 = 0.f;
+  uint4 kr[G][kTcD / 8];
 #pragma unroll
-  for (int c = 0; c < kTcD / 8; ++c) {
-    const uint4 u = GLOBAL ? __ldg(reinterpret_cast<const uint4*>(kbh + (int64_t)kr * kn) + c)
-                           : *reinterpret_cast<const uint4*>(sk + tc::sw128_off(row0 + lane, c));
-    if (c & 1) a1 += dot8<ET>(u, qc + c * 8);
-    else a0 += dot8<ET>(u, qc + c * 8);
+  for (int g = 0; g < G; ++g) {
+    // tile rows past the valid keys are in bounds (zero-filled): read them
+    // unconditionally and mask afterwards; a global row is clamped to its
+    // group's last key, and an empty group reads nothing
+    if (GLOBAL && nv[g] <= 0) continue;
+    const int r = GLOBAL ? key0 + g * gstride + min(lane, nv[g] - 1) : 0;
+#pragma unroll
+    for (int c = 0; c < kTcD / 8; ++c)
+      kr[g][c] = GLOBAL ? __ldg(reinterpret_cast<const uint4*>(kbh + (int64_t)r * kn) + c)
+                        : *reinterpret_cast<const uint4*>(sk + tc::sw128_off(row0 + lane, c));
   }
-  return lane < nvalid ? fmaf(a0 + a1, sl2, bl2) : -INFINITY;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (GLOBAL && nv[g] <= 0) {
+      s[g] = -INFINITY;
+      continue;
+    }
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int c = 0; c < kTcD / 8; ++c) {
+      if (c & 1) a1 += dot8<ET>(kr[g][c], qc + c * 8);
+      else a0 += dot8<ET>(kr[g][c], qc + c * 8);
+    }
+    s[g] = lane < nv[g] ? fmaf(a0 + a1, sl2, bl2[g]) : -INFINITY;
+  }
 }
 
-// One warp folds its 32 scored keys (logit s in lane l) into its CLS state
-// `st` (fresh: the state is empty).  For P.V lane (ks = l >> 3, dg = l & 7)
-// takes keys ks*8 .. ks*8+7 and channels dg*8 .. dg*8+7, from the swizzled V
-// tile (rows row0 + key) or, when GLOBAL, global rows key0 + key.
-template <typename ET, bool GLOBAL>
-__device__ __forceinline__ void cls_warp_fold(float s, float* st, bool fresh, int nvalid, const uint8_t* sv,
-                                              int row0, const ET* __restrict__ vbh, int64_t kn, int key0) {
+__device__ __forceinline__ float warp_max_f32(float v) {  // one warp-wide reduction instruction
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+// One warp folds its G scored groups (logit s[g] in lane l) into its CLS
+// state, kept in registers: the running max m (warp-uniform), this lane's
+// share l of the running sum, and this lane's unreduced share o[8] of the 64
+// outputs (fresh: the state is empty).  For P.V lane (ks = l >> 3, dg = l & 7)
+// takes keys ks*8 .. ks*8+7 of each group and channels dg*8 .. dg*8+7, from
+// the swizzled V tile (rows row0 + key, G = 1) or, when GLOBAL, global rows
+// key0 + g * gstride + key.
+template <typename ET, bool GLOBAL, int G>
+__device__ __forceinline__ void cls_warp_fold(const float* s, float& m, float& l, float* o, bool fresh, const int* nv,
+                                              const uint8_t* sv, int row0, const ET* __restrict__ vbh, int64_t kn,
+                                              int key0, int gstride) {
   const int lane = threadIdx.x & 31;
-  if (GLOBAL && nvalid <= 0) return;  // nothing to fold (never the first group: `fresh` is false here)
-  const float m_old = fresh ? -INFINITY : st[0];
-  const float l_old = fresh ? 0.f : st[1];
-  const float m_new = fmaxf(m_old, warp_max(s));
+  const float m_old = fresh ? -INFINITY : m;
+  float lm = s[0];
+#pragma unroll
+  for (int g = 1; g < G; ++g) lm = fmaxf(lm, s[g]);
+  const float m_new = fmaxf(m_old, warp_max_f32(lm));
   const float msub = m_new == -INFINITY ? 0.f : m_new;
   const float alpha = fast_ex2(m_old - msub);
-  const float p = lane < nvalid ? fast_ex2(s - msub) : 0.f;
-  const float psum = warp_sum(p);
+  float p[G], ps = 0.f;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    p[g] = lane < nv[g] ? fast_ex2(s[g] - msub) : 0.f;
+    ps += p[g];
+  }
+  l = fresh ? ps : fmaf(l, alpha, ps);
+  m = m_new;
   const int ks = lane >> 3, dg = lane & 7;
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  uint4 vr[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {  // all eight rows in flight; p = 0 past the valid keys
-    const int kk = ks * 8 + i;
-    vr[i] = GLOBAL ? __ldg(reinterpret_cast<const uint4*>(vbh + (int64_t)(key0 + min(kk, nvalid - 1)) * kn) + dg)
-                   : *reinterpret_cast<const uint4*>(sv + tc::sw128_off(row0 + kk, dg));
+  for (int k2 = 0; k2 < 8; ++k2) o[k2] = fresh ? 0.f : o[k2] * alpha;
+  uint4 vr[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {  // every row in flight; p = 0 past the valid keys
+    if (GLOBAL && nv[g] <= 0) continue;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int kk = ks * 8 + i;
+      vr[g][i] = GLOBAL ? __ldg(reinterpret_cast<const uint4*>(vbh + (int64_t)(key0 + g * gstride + min(kk, nv[g] - 1)) *
+                                                                         kn) + dg)
+                        : *reinterpret_cast<const uint4*>(sv + tc::sw128_off(row0 + kk, dg));
+    }
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float pk = __shfl_sync(0xffffffffu, p, ks * 8 + i);
-    const ET* e = reinterpret_cast<const ET*>(&vr[i]);
+  for (int g = 0; g < G; ++g) {
+    if (GLOBAL && nv[g] <= 0) continue;
 #pragma unroll
-    for (int k2 = 0; k2 < 8; ++k2) acc[k2] = fmaf(pk, to_f32(e[k2]), acc[k2]);
+    for (int i = 0; i < 8; ++i) {
+      const float pk = __shfl_sync(0xffffffffu, p[g], ks * 8 + i);
+      const ET* e = reinterpret_cast<const ET*>(&vr[g][i]);
+#pragma unroll
+      for (int k2 = 0; k2 < 8; ++k2) o[k2] = fmaf(pk, to_f32(e[k2]), o[k2]);
+    }
   }
+}
+
+// Reduce a warp's register CLS state and store it to `st` = {max, sum, 64
+// outputs} for the cross-warp merge.
+__device__ __forceinline__ void cls_warp_publish(float m, float l, const float* o, float* st) {
+  const int lane = threadIdx.x & 31;
+  const float lsum = warp_sum(l);
+  float r[8];
 #pragma unroll
   for (int k2 = 0; k2 < 8; ++k2) {
-    acc[k2] += __shfl_xor_sync(0xffffffffu, acc[k2], 8);
-    acc[k2] += __shfl_xor_sync(0xffffffffu, acc[k2], 16);
+    r[k2] = o[k2] + __shfl_xor_sync(0xffffffffu, o[k2], 8);
+    r[k2] += __shfl_xor_sync(0xffffffffu, r[k2], 16);
   }
-  __syncwarp();  // every lane has read st[0..1]
   if (lane < 8) {
-    float* o = st + 2 + lane * 8;
 #pragma unroll
-    for (int k2 = 0; k2 < 8; ++k2) o[k2] = fresh ? acc[k2] : fmaf(o[k2], alpha, acc[k2]);
+    for (int k2 = 0; k2 < 8; ++k2) st[2 + lane * 8 + k2] = r[k2];
   }
   if (lane == 0) {
-    st[0] = m_new;
-    st[1] = fmaf(l_old, alpha, psum);
+    st[0] = m;
+    st[1] = lsum;
   }
-  __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
@@ -733,6 +779,21 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
       }
     }
   };
+  auto cls_combine = [&](const float* s0, int b, int h) {  // merge the four warps' states into row 0
+    if (tid < kTcD) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) m = fmaxf(m, s0[w * kClsState]);
+      float l = 0.f, o = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float a = fast_ex2(s0[w * kClsState] - m);
+        l = fmaf(s0[w * kClsState + 1], a, l);
+        o = fmaf(s0[w * kClsState + 2 + tid], a, o);
+      }
+      store_any(out, out_dtype, ((int64_t)b * N * H + h) * kTcD + tid, o / l);
+    }
+  };
   auto stage_cls_query = [&](const Tile& x) {  // a (head, image)'s first tile: its CLS query
     if (cls_global && x.qt == 0 && tid < kTcD)
       cls_q[(x.unit & 1) * kTcD + tid] = to_f32(qg[(int64_t)x.b * qb + (int64_t)x.h * qh + tid]);
@@ -771,6 +832,8 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
   // the unit whose first tile precedes t_begin has its CLS row elsewhere
   const int first_owned_unit = (t_begin % ntq == 0) ? t_begin / ntq : t_begin / ntq + 1;
 
+  // this warp's CLS state for the (head, image) in progress
+  float cls_m = -INFINITY, cls_l = 0.f, cls_o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   int i = 0;
   for (int t = t_begin; t < t_end && ok; ++t, ++i) {
     const Tile x = tile_of(t);
@@ -804,8 +867,8 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
     if (cls_tile) {
       if (!tc::mbar_wait(bar_k, i & 1, err)) { ok = false; break; }
       const float bl2 = (BIAS && (tid & 31) < cls_nvalid) ? sbias[cls_row0 + (tid & 31)] : 0.f;
-      cls_s = cls_warp_score<ET, false>(cls_q + (x.unit & 1) * kTcD, cls_nvalid, sk, cls_row0, nullptr, 0, 0, sl2,
-                                        bl2);
+      cls_warp_score<ET, false, 1>(cls_q + (x.unit & 1) * kTcD, &cls_nvalid, sk, cls_row0, nullptr, 0, 0, 0, sl2,
+                                   &bl2, &cls_s);
     }
     if (!tc::mbar_wait(bar_s, i & 1, err)) { ok = false; break; }
     tc::fence_after_sync();
@@ -933,8 +996,8 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
     }
     if (cls_tile) {  // while P.V runs, the CLS row folds in its scored keys
       if (!tc::mbar_wait(bar_v, i & 1, err)) { ok = false; break; }
-      cls_warp_fold<ET, false>(cls_s, cls_st + ((x.unit & 1) * 4 + warp) * kClsState, x.qt == 0, cls_nvalid, sv,
-                               cls_row0, nullptr, 0, 0);
+      cls_warp_fold<ET, false, 1>(&cls_s, cls_m, cls_l, cls_o, x.qt == 0, &cls_nvalid, sv, cls_row0, nullptr, 0, 0,
+                                  0);
     }
     if (!tc::mbar_wait(bar_o, i & 1, err)) { ok = false; break; }
     tc::fence_after_sync();
@@ -973,38 +1036,42 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
         }
       }
     }
-    // the CLS row is complete after the unit's last tile, or at the end of
-    // this CTA's range (the remaining keys then come from global memory)
-    if (cls_tile && (x.qt == ntq - 1 || t + 1 == t_end)) {
-      float* st = cls_st + ((x.unit & 1) * 4 + warp) * kClsState;
+    // the CLS row is complete after the unit's last tile
+    if (cls_tile && x.qt == ntq - 1) {
+      cls_warp_publish(cls_m, cls_l, cls_o, cls_st + ((x.unit & 1) * 4 + warp) * kClsState);
+      __syncthreads();  // every warp's state, and this tile's row-0 store, are in
+      cls_combine(cls_st + (x.unit & 1) * 4 * kClsState, x.b, x.h);
+    }
+  }
+  // The range ended inside an owned (head, image): the rest of its keys come
+  // from global memory (outside the tile loop, where registers are free).
+  const bool all_ok = __syncthreads_and(ok ? 1 : 0) != 0;
+  if (all_ok && cls_global && t_begin < t_end) {
+    const Tile x = tile_of(t_end - 1);
+    if (x.unit >= first_owned_unit && x.qt < ntq - 1) {
       const float* qc = cls_q + (x.unit & 1) * kTcD;
       const ET* kbh = kg + (int64_t)x.b * kb + (int64_t)x.h * kh;
       const ET* vbh = vg + (int64_t)x.b * kb + (int64_t)x.h * kh;
-      for (int k0 = x.q0 + kTcM; k0 < N; k0 += kTcM) {
+      constexpr int G = 2;  // chunks of 128 keys per pass: G x 8 row loads in flight per lane
+      for (int k0 = x.q0 + kTcM; k0 < N; k0 += G * kTcM) {
         const int key0 = k0 + warp * 32;
-        const int nvalid = max(0, min(32, N - key0));
         const int lane = tid & 31;
-        float bl2 = 0.f;
-        if (BIAS && lane < nvalid)
-          bl2 = to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)x.b * N + key0 + lane))) * kLog2e;
-        const float sc0 = cls_warp_score<ET, true>(qc, nvalid, nullptr, 0, kbh, kn, key0, sl2, bl2);
-        cls_warp_fold<ET, true>(sc0, st, false, nvalid, nullptr, 0, vbh, kn, key0);
-      }
-      __syncthreads();  // every warp's state, and this tile's row-0 store, are in
-      if (tid < kTcD) {
-        const float* s0 = cls_st + (x.unit & 1) * 4 * kClsState;
-        float m = -INFINITY;
+        int nv[G];
+        float bl2[G], sc[G];
 #pragma unroll
-        for (int w = 0; w < 4; ++w) m = fmaxf(m, s0[w * kClsState]);
-        float l = 0.f, o = 0.f;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const float a = fast_ex2(s0[w * kClsState] - m);
-          l = fmaf(s0[w * kClsState + 1], a, l);
-          o = fmaf(s0[w * kClsState + 2 + tid], a, o);
+        for (int g = 0; g < G; ++g) {
+          nv[g] = max(0, min(32, N - (key0 + g * kTcM)));
+          bl2[g] = 0.f;
+          if (BIAS && lane < nv[g])
+            bl2[g] =
+                to_f32(from_f32<ET>(load_any(bias, bias_dtype, (int64_t)x.b * N + key0 + g * kTcM + lane))) * kLog2e;
         }
-        store_any(out, out_dtype, ((int64_t)x.b * N * H + x.h) * kTcD + tid, o / l);
+        cls_warp_score<ET, true, G>(qc, nv, nullptr, 0, kbh, kn, key0, kTcM, sl2, bl2, sc);
+        cls_warp_fold<ET, true, G>(sc, cls_m, cls_l, cls_o, false, nv, nullptr, 0, vbh, kn, key0, kTcM);
       }
+      cls_warp_publish(cls_m, cls_l, cls_o, cls_st + ((x.unit & 1) * 4 + warp) * kClsState);
+      __syncthreads();
+      cls_combine(cls_st + (x.unit & 1) * 4 * kClsState, x.b, x.h);
     }
   }
   if (tid == 0 && q_last >= 0) {
