@@ -495,9 +495,12 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
         // V: 16 key rows (2 KB) per K step
         const uint64_t dp = tc::sw128_desc(tc::smem_u32(sp), 16);
         const uint64_t dv = tc::sw128_desc(tc::smem_u32(sv + stage * S::kv_stage), 16384);
-        for (int kk = 0; kk < kpad / 16; ++kk)
-          tc::mma_f16_ss(t_o, dp + (uint64_t)((kk >> 2) * (kTcM * 128 / 16) + (kk & 3) * 2), dv + 128 * kk,
-                         idesc_o, (blk > 0 || kk > 0) ? 1u : 0u);
+        const int nsteps = kpad / 16;
+#pragma unroll
+        for (int kk = 0; kk < NB / 16; ++kk)  // unrolled: descriptor offsets are constants
+          if (kk < nsteps)
+            tc::mma_f16_ss(t_o, dp + (uint64_t)((kk >> 2) * (kTcM * 128 / 16) + (kk & 3) * 2), dv + 128 * kk,
+                           idesc_o, (blk > 0 || kk > 0) ? 1u : 0u);
         tc::mma_commit(bar_o);
         if (blk + 1 < nblocks) ok = issue_s(blk + 1, t_s);
       }
@@ -988,9 +991,12 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
       } else {
         const uint64_t dp = tc::sw128_desc(tc::smem_u32(sp), 16);
         const uint64_t dv = tc::sw128_desc(tc::smem_u32(sv), 16384);
-        for (int kk = 0; kk < kpad / 16; ++kk)
-          tc::mma_f16_ss(t_o, dp + (uint64_t)((kk >> 2) * (kTcM * 128 / 16) + (kk & 3) * 2), dv + 128 * kk,
-                         idesc_o, kk > 0 ? 1u : 0u);
+        const int nsteps = kpad / 16;
+#pragma unroll
+        for (int kk = 0; kk < NB / 16; ++kk)  // unrolled: descriptor offsets are constants
+          if (kk < nsteps)
+            tc::mma_f16_ss(t_o, dp + (uint64_t)((kk >> 2) * (kTcM * 128 / 16) + (kk & 3) * 2), dv + 128 * kk,
+                           idesc_o, kk > 0 ? 1u : 0u);
         tc::mma_commit(bar_o);
       }
     }

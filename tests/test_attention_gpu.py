@@ -163,6 +163,27 @@ def test_window_many_tiles_per_cta(dev, dtype, biased, cls):
     assert mn.attention.attention_status(dev) == 0
 
 
+@pytest.mark.parametrize("dtype,biased,out_dtype", [(torch.float16, True, None), (torch.bfloat16, False, None),
+                                                    (torch.float16, False, torch.float32)])
+def test_full_attention_many_tiles(dev, dtype, biased, out_dtype):
+    """Every key of 393, with more (tile, head, image) items than CTAs
+    (40 x 6 x 4 = 960): each CTA walks several images and heads, loading the
+    next one's K and V while the current one's tiles run."""
+    import mergenet_b200 as mn
+    torch.manual_seed(5 + int(biased))
+    b, n, h, d = 40, 393, 6, 64
+    qkv = (torch.randn(b, n, 3 * h * d, device=dev) * 0.5).to(dtype)
+    size = torch.rand(b, n, device=dev) * 3 + 0.05
+    bias = size.log() if biased else None
+    out = mn.local_attention_packed(qkv, h, -1, cls_global=False, bias=bias, out_dtype=out_dtype)
+    q, k, v = qkv.view(b, n, 3, h, d).permute(2, 0, 3, 1, 4).unbind(0)
+    mask = bias.to(dtype).float()[:, None, None, :] if biased else None
+    exp = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(), attn_mask=mask)
+    tol = 2e-2 if dtype == torch.bfloat16 else 5e-3
+    torch.testing.assert_close(out.float(), exp.transpose(1, 2).reshape(b, n, h * d), atol=tol, rtol=tol)
+    assert mn.attention.attention_status(dev) == 0
+
+
 @pytest.mark.parametrize("tokens,window,biased", [(785, 17, False), (785, 40, True), (300, 100, False),
                                                    (131, 70, True)])
 def test_wide_window_multi_block(dev, tokens, window, biased):
@@ -232,7 +253,7 @@ def test_cross_attention_strided_projection_views(dev):
     torch.testing.assert_close(out, exp.transpose(1, 2), atol=5e-3, rtol=5e-3)
 
 
-@pytest.mark.parametrize("n", [393, 130, 17])
+@pytest.mark.parametrize("n", [393, 400, 401, 257, 256, 130, 17, 1])
 def test_latent_proportional_attention(dev, n):
     """The latent blocks' ToMe attention (opentome/timm/tome.py:44-58):
     every key, plus log(size) per key, against SDPA with the float mask."""
