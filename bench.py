@@ -269,8 +269,8 @@ def run_b200(args):
                     "d2h_bytes_per_step": host_logits[0].numel() * host_logits.element_size(),
                     "overlap": "H2D of step i+1 on a copy stream during step i's forward"},
             "gpu_launches": ForwardGraph.library_launches(model) * args.steps,
-            "roofline": {"kernel": "attn_tc_kernel<half,160,window> with the CLS row (local attention, window 16, "
-                                   "785 tokens, 6 heads, B=%d)" % B,
+            "roofline": {"kernel": "attn_win_persistent_kernel<half> with the CLS row folded in (local attention, "
+                                   "window 16, 785 tokens, 6 heads, B=%d)" % B,
                          "bound": "hbm", "achieved": local_achieved, "peak": peak, "unit": "GB/s",
                          "frac": local_achieved / peak, "peak_kind": peak_kind, "traffic": TRAFFIC_LOCAL_ATTN * B,
                          "algorithmic_bytes": local_bytes, "ms_per_launch": t_local * 1e3},

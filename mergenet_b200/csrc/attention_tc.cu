@@ -1092,6 +1092,9 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
   if (warp == 0) tc::tmem_dealloc(tmem, S::kTmemCols);
 }
 
+#ifndef MN_TC_PROMOTE128
+#define MN_TC_PROMOTE128 true  // 128-byte head rows: no 256-byte L2 promotion
+#endif
 // 4-D tensor map (d, h, n, b) -- or (d, n, h, b) when heads are strided
 // wider than tokens -- over a [B, N, H, 64] view with element strides sb, sn,
 // sh; box = `rows` tokens of one head.  *order receives the dimension order.
@@ -1103,7 +1106,7 @@ static bool make_head_map(CUtensorMap* map, int* order, const void* ptr, int B, 
   const cuuint64_t dims[4] = {(cuuint64_t)kTcD, (cuuint64_t)(hn ? H : N), (cuuint64_t)(hn ? N : H), (cuuint64_t)B};
   const cuuint64_t strides[3] = {(cuuint64_t)(hn ? sh : sn) * 2, (cuuint64_t)(hn ? sn : sh) * 2, (cuuint64_t)sb * 2};
   const cuuint32_t box[4] = {(cuuint32_t)kTcD, hn ? 1u : (cuuint32_t)rows, hn ? (cuuint32_t)rows : 1u, 1u};
-  return tma::encode(map, std::is_same<ET, __nv_bfloat16>::value, 4, ptr, dims, strides, box, true);
+  return tma::encode(map, std::is_same<ET, __nv_bfloat16>::value, 4, ptr, dims, strides, box, true, MN_TC_PROMOTE128);
 }
 
 template <typename ET, int NB, bool WIN>
