@@ -35,8 +35,8 @@ IMG = 224
 # of a B=128 launch) of the windowed attention kernel with its CLS row and of
 # the latent attention kernel, per image; the traffic grows in proportion to
 # the batch
-TRAFFIC_LOCAL_ATTN = 294.6e6 / 128
-TRAFFIC_LATENT_ATTN = 136.1e6 / 128
+TRAFFIC_LOCAL_ATTN = 313.3e6 / 128
+TRAFFIC_LATENT_ATTN = 136.3e6 / 128
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 
 
