@@ -141,7 +141,7 @@ def test_local_block_attention_cls_global(dev, dtype):
 
 
 @pytest.mark.parametrize("dtype,biased,cls", [(torch.float16, True, False), (torch.bfloat16, False, True),
-                                              (torch.float16, False, True)])
+                                              (torch.float16, False, True), (torch.float16, True, True)])
 def test_window_many_tiles_per_cta(dev, dtype, biased, cls):
     """Window 16 at 785 tokens with more (tile, head, image) work items than
     resident CTAs (12 x 6 x 7 = 504), so each CTA walks several tiles and
@@ -156,7 +156,10 @@ def test_window_many_tiles_per_cta(dev, dtype, biased, cls):
     q, k, v = (view[:, :, i].transpose(1, 2) for i in range(3))
     exp = reference_bhnd(q, k, v, bias.to(dtype) if biased else None, 16)
     if cls:
-        exp[:, :, :1] = torch.softmax(q[:, :, :1].float() @ k.float().transpose(-1, -2) / 8.0, -1) @ v.float()
+        logits = q[:, :, :1].float() @ k.float().transpose(-1, -2) / 8.0
+        if biased:
+            logits = logits + bias.to(dtype).float()[:, None, None, :]
+        exp[:, :, :1] = torch.softmax(logits, -1) @ v.float()
     exp = exp.transpose(1, 2).reshape(b, n, h * d)
     tol = 2e-2 if dtype == torch.bfloat16 else 5e-3
     torch.testing.assert_close(out.float(), exp, atol=tol, rtol=tol)
