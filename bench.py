@@ -20,6 +20,7 @@ import json
 import os
 import statistics
 import subprocess
+import tempfile
 import sys
 import time
 from pathlib import Path
@@ -54,11 +55,13 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_gpu{index}.csv"
+        # the raw samples go to $MN_CLOCKS_DIR (default: the system temp dir)
+        out = Path(os.environ.get("MN_CLOCKS_DIR", tempfile.gettempdir()))
+        self.path = out / f"mergenet_b200_clocks_gpu{index}.csv"
 
     def __enter__(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
+            self.path.parent.mkdir(parents=True, exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index),

@@ -3,7 +3,7 @@
 TEST INFRASTRUCTURE ONLY.  This package restates, in plain numpy, the
 reference algorithm the CUDA library reproduces.  Only ``tests/``,
 ``__graft_entry__.smoke()`` and the CPU-baseline legs of ``bench.py`` may
-import it, and only as the checker or as the timed CPU baseline; the product
+import it, and only as the parity reference or as the timed CPU baseline; the product
 path (``mergenet_b200``) never calls into it.
 
 Parity is pinned: ``tests/golden/make_golden.py`` runs the reference itself

@@ -1,4 +1,4 @@
-"""numpy restatement of the reference's windowed attention (the checker).
+"""numpy restatement of the reference's windowed attention (the oracle).
 
 TEST INFRASTRUCTURE ONLY -- see ``oracle/__init__.py``.
 

@@ -1,4 +1,4 @@
-"""numpy restatement of MergeNet's DTEM spatial routing (the checker).
+"""numpy restatement of MergeNet's DTEM spatial routing (the oracle).
 
 TEST INFRASTRUCTURE ONLY -- see ``oracle/__init__.py``.
 
