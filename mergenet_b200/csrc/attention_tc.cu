@@ -327,6 +327,7 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
   }
 
   const int qi = q0 + tid;  // this thread's query row
+  const bool live = WIN || q0 + warp * 32 < Nq;  // warp-uniform
   float m_run = -INFINITY, l_run = 0.f;
   // the last phase issued on each copy barrier, for the exit drain
   int k_issued = nblocks > 0 ? 0 : -1, v_issued[2] = {nblocks > 0 ? 0 : -1, -1};
@@ -384,104 +385,108 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
       if (err && (tid & 31) == 0) atomicOr(err, MN_STATUS_TC_TIMEOUT);
     }
 
-    // S rows of the warp's chunks, all loads in flight before one wait
-    float sc[NCH * 32];
+    // a warp whose 32 rows all lie past the last query (the tail tile) has
+    // nothing to compute; its P rows feed only O rows that are never stored
+    if (live) {
+      // S rows of the warp's chunks, all loads in flight before one wait
+      float sc[NCH * 32];
 #pragma unroll
-    for (int u = 0; u < NCH; ++u)
-      if (u < nch) tc::tmem_ld32_nowait(t_s + lane_sel + (c_lo + u) * 32, sc + u * 32);
-    tc::tmem_ld_wait<NCH * 32>(sc);
+      for (int u = 0; u < NCH; ++u)
+        if (u < nch) tc::tmem_ld32_nowait(t_s + lane_sel + (c_lo + u) * 32, sc + u * 32);
+      tc::tmem_ld_wait<NCH * 32>(sc);
 
-    // pass 1: log2-domain logits (illegal keys -inf) and the row maximum
-    float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // pass 1: log2-domain logits (illegal keys -inf) and the row maximum
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-    for (int u = 0; u < NCH; ++u) {
-      if (u >= nch) continue;
-      const int cb = (c_lo + u) * 32;
-      const bool whole = !WIN || __all_sync(0xffffffffu, jlo <= cb && jhi >= cb + 32);
-      const float4* b4 = reinterpret_cast<const float4*>(sbias + cb);
-      if (whole) {
+      for (int u = 0; u < NCH; ++u) {
+        if (u >= nch) continue;
+        const int cb = (c_lo + u) * 32;
+        const bool whole = !WIN || __all_sync(0xffffffffu, jlo <= cb && jhi >= cb + 32);
+        const float4* b4 = reinterpret_cast<const float4*>(sbias + cb);
+        if (whole) {
 #pragma unroll
-        for (int i4 = 0; i4 < 8; ++i4) {
-          float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (BIAS || !WIN) bb = b4[i4];
-          const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+          for (int i4 = 0; i4 < 8; ++i4) {
+            float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (BIAS || !WIN) bb = b4[i4];
+            const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float& x = sc[u * 32 + i4 * 4 + e];
-            x = fmaf(x, sl2, bv[e]);
-            mx4[e] = fmaxf(mx4[e], x);
+            for (int e = 0; e < 4; ++e) {
+              float& x = sc[u * 32 + i4 * 4 + e];
+              x = fmaf(x, sl2, bv[e]);
+              mx4[e] = fmaxf(mx4[e], x);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i4 = 0; i4 < 8; ++i4) {
+            float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (BIAS) bb = b4[i4];
+            const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int j = cb + i4 * 4 + e;
+              float& x = sc[u * 32 + i4 * 4 + e];
+              x = (j >= jlo && j < jhi) ? fmaf(x, sl2, bv[e]) : -INFINITY;
+              mx4[e] = fmaxf(mx4[e], x);
+            }
           }
         }
-      } else {
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      const float m_new = fmaxf(m_run, mx);
+      // keep the running maximum unless it grew by more than 2^8
+      const float m_use = (m_run == -INFINITY || m_new - m_run > kRescaleLog2) ? m_new : m_run;
+      const float corr = (m_run == -INFINITY || m_use == m_run) ? 1.f : fast_ex2(m_run - m_use);
+      const float msub = m_use == -INFINITY ? 0.f : m_use;
+
+      // pass 2: probabilities -> P in shared memory; chunks outside the warp's
+      // range are zero
+      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int i4 = 0; i4 < 8; ++i4) {
-          float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (BIAS) bb = b4[i4];
-          const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+      for (int u = 0; u < NCH; ++u) {
+        if (u >= nch) continue;
+        const int c = c_lo + u;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 pk;
+          uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int j = cb + i4 * 4 + e;
-            float& x = sc[u * 32 + i4 * 4 + e];
-            x = (j >= jlo && j < jhi) ? fmaf(x, sl2, bv[e]) : -INFINITY;
-            mx4[e] = fmaxf(mx4[e], x);
+            const float p0 = fast_ex2(sc[u * 32 + g * 8 + 2 * e] - msub);
+            const float p1 = fast_ex2(sc[u * 32 + g * 8 + 2 * e + 1] - msub);
+            ls4[(2 * e) & 3] += p0;
+            ls4[(2 * e + 1) & 3] += p1;
+            w[e] = pack2<ET>(p0, p1);
           }
+          const int key8 = c * 4 + g;  // 8-key chunk index
+          *reinterpret_cast<uint4*>(sp + (key8 >> 3) * (kTcM * 128) + tc::sw128_off(tid, key8 & 7)) = pk;
         }
       }
-    }
-    const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-    const float m_new = fmaxf(m_run, mx);
-    // keep the running maximum unless it grew by more than 2^8
-    const float m_use = (m_run == -INFINITY || m_new - m_run > kRescaleLog2) ? m_new : m_run;
-    const float corr = (m_run == -INFINITY || m_use == m_run) ? 1.f : fast_ex2(m_run - m_use);
-    const float msub = m_use == -INFINITY ? 0.f : m_use;
-
-    // pass 2: probabilities -> P in shared memory; chunks outside the warp's
-    // range are zero
-    float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+      const int c_end = (kpad + 31) >> 5;  // chunks the P.V MMA reads
+      for (int c = 0; c < c_end; ++c) {
+        if (c >= c_lo && c < c_lo + nch) continue;
 #pragma unroll
-    for (int u = 0; u < NCH; ++u) {
-      if (u >= nch) continue;
-      const int c = c_lo + u;
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        uint4 pk;
-        uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = fast_ex2(sc[u * 32 + g * 8 + 2 * e] - msub);
-          const float p1 = fast_ex2(sc[u * 32 + g * 8 + 2 * e + 1] - msub);
-          ls4[(2 * e) & 3] += p0;
-          ls4[(2 * e + 1) & 3] += p1;
-          w[e] = pack2<ET>(p0, p1);
+        for (int g = 0; g < 4; ++g) {
+          const int key8 = c * 4 + g;
+          *reinterpret_cast<uint4*>(sp + (key8 >> 3) * (kTcM * 128) + tc::sw128_off(tid, key8 & 7)) =
+              make_uint4(0u, 0u, 0u, 0u);
         }
-        const int key8 = c * 4 + g;  // 8-key chunk index
-        *reinterpret_cast<uint4*>(sp + (key8 >> 3) * (kTcM * 128) + tc::sw128_off(tid, key8 & 7)) = pk;
       }
-    }
-    const int c_end = (kpad + 31) >> 5;  // chunks the P.V MMA reads
-    for (int c = 0; c < c_end; ++c) {
-      if (c >= c_lo && c < c_lo + nch) continue;
+      // rescale the running output rows (warp-collective TMEM access: the
+      // whole warp takes part when any of its rows needs it)
+      if (blk > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+        float o[32];
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const int key8 = c * 4 + g;
-        *reinterpret_cast<uint4*>(sp + (key8 >> 3) * (kTcM * 128) + tc::sw128_off(tid, key8 & 7)) =
-            make_uint4(0u, 0u, 0u, 0u);
+        for (int c = 0; c < kTcD / 32; ++c) {
+          tc::tmem_ld32(t_o + lane_sel + c * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= corr;
+          tc::tmem_st32(t_o + lane_sel + c * 32, o);
+        }
       }
+      l_run = l_run * corr + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
+      m_run = m_use;
     }
-    // rescale the running output rows (warp-collective TMEM access: the
-    // whole warp takes part when any of its rows needs it)
-    if (blk > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
-      float o[32];
-#pragma unroll
-      for (int c = 0; c < kTcD / 32; ++c) {
-        tc::tmem_ld32(t_o + lane_sel + c * 32, o);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] *= corr;
-        tc::tmem_st32(t_o + lane_sel + c * 32, o);
-      }
-    }
-    l_run = l_run * corr + ((ls4[0] + ls4[1]) + (ls4[2] + ls4[3]));
-    m_run = m_use;
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
@@ -525,6 +530,7 @@ __global__ void __launch_bounds__(128, TcSmem<NB>::kMinBlocks) attn_tc_kernel(
     const int64_t obase = (((int64_t)b * Nq + qi) * H + h) * kTcD;
 #pragma unroll
     for (int c = 0; c < kTcD / 32; ++c) {
+      if (!live) break;
       float o[32];
       tc::tmem_ld32(t_o + lane_sel + c * 32, o);  // warp-collective: every row loads
       if (qi >= Nq) continue;
@@ -962,7 +968,10 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
         *reinterpret_cast<uint4*>(sp + (key8 >> 3) * (kTcM * 128) + tc::sw128_off(tid, key8 & 7)) = pk;
       }
     }
-    const int c_end = (kpad + 31) >> 5;
+    // a warp whose rows all lie past the last query (the tail tile) leaves
+    // its P rows alone: they feed only O rows that are never stored
+    const bool live = x.q0 + warp * 32 < N;
+    const int c_end = live ? (kpad + 31) >> 5 : 0;
     for (int c = 0; c < c_end; ++c) {
       if (c >= c_lo && c < c_lo + nch) continue;
 #pragma unroll
@@ -1021,6 +1030,7 @@ __global__ void __launch_bounds__(128, 2) attn_win_persistent_kernel(
       const int64_t obase = (((int64_t)x.b * N + qi) * H + x.h) * kTcD;
 #pragma unroll
       for (int c = 0; c < kTcD / 32; ++c) {
+        if (!live) break;
         float o[32];
         tc::tmem_ld32(t_o + lane_sel + c * 32, o);  // warp-collective: every row loads
         if (qi >= N) continue;
