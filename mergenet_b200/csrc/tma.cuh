@@ -3,7 +3,7 @@
 // encoding of fp16 / bf16 tensor maps (the encoder is fetched from the driver
 // through the runtime, so the library does not link libcuda).
 //
-// No copy here uses cluster multicast.
+// Every copy here lands in the issuing CTA's own shared memory.
 #pragma once
 
 #include <cuda.h>  // CUtensorMap and its enums
