@@ -40,9 +40,12 @@ def _strides_bnhd(t: torch.Tensor):
 
 def _launch(q, k, v, bias, window, cls_global, scale, out_dtype):
     """q/k/v in (B, N, H, D) view form (any strides with a unit last stride)."""
-    dev = L.require_cuda(q, k, v, bias)
     if q.shape != k.shape or q.shape != v.shape:
         raise ValueError(f"q/k/v shape mismatch: {q.shape}, {k.shape}, {v.shape}")
+    if bias is not None and tuple(bias.shape) != (q.shape[0], q.shape[1]):
+        # the kernels read bias[b * N + j] for every key j of every image b
+        raise ValueError(f"bias must be (B, N) = {(q.shape[0], q.shape[1])}, got {tuple(bias.shape)}")
+    dev = L.require_cuda(q, k, v, bias)
     if q.dtype != k.dtype or q.dtype != v.dtype:
         raise ValueError("q/k/v must share a dtype")
     if not (q.stride() == k.stride() == v.stride()):
@@ -139,6 +142,8 @@ def local_attention_packed(qkv, num_heads, local_window, cls_global=True, out_dt
     every key; ``bias`` [B, N] adds a per-key bias (rounded to the qkv dtype,
     as SDPA's autocast rounds the float mask)."""
     b, n, c3 = qkv.shape
+    if num_heads <= 0 or c3 % (3 * num_heads) != 0:
+        raise ValueError(f"packed qkv width {c3} is not 3 x num_heads ({num_heads}) x head_dim")
     d = c3 // (3 * num_heads)
     view = qkv.view(b, n, 3, num_heads, d)
     q, k, v = view[:, :, 0], view[:, :, 1], view[:, :, 2]

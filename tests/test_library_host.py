@@ -135,3 +135,20 @@ def test_cpu_tensors_are_rejected():
         mn.ThreTopK(torch.rand(2, 5), 2)
     with pytest.raises(RuntimeError):
         mn.unbiased_local_attention(torch.rand(1, 5, 2, 8), torch.rand(1, 5, 2, 8), torch.rand(1, 5, 2, 8), 1)
+
+
+def test_attention_argument_checks_precede_any_launch():
+    """A per-key bias that is not (B, N) and a packed width that is not
+    3 x heads x head_dim are refused before the device is touched, so the
+    kernels never index past the bias; well-formed host tensors still meet
+    the no-CPU-path error."""
+    import mergenet_b200 as mn
+    qkv = torch.rand(2, 7, 3 * 2 * 8)
+    with pytest.raises(ValueError, match="bias must be"):
+        mn.local_attention_packed(qkv, 2, 1, bias=torch.rand(2, 6))
+    with pytest.raises(ValueError, match="bias must be"):
+        mn.local_attention_packed(qkv, 2, 1, bias=torch.rand(7, 2))
+    with pytest.raises(ValueError, match="packed qkv width"):
+        mn.local_attention_packed(torch.rand(2, 7, 40), 2, 1)
+    with pytest.raises(RuntimeError):
+        mn.local_attention_packed(qkv, 2, 1, bias=torch.rand(2, 7))
