@@ -213,6 +213,7 @@ def run_b200(args):
         barrier()
     t_max = max_over_ranks(start.elapsed_time(end) / 1e3, dev)
     value = world * B * args.steps / t_max
+    fwd.check_status()  # fail closed on any device status the timed replays raised
 
     # end to end through the public call: pinned host images -> device -> logits -> host
     # every step copies its pinned host batch to the device (on a copy stream,

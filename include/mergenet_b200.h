@@ -200,8 +200,8 @@ int mn_dtem_select(int batch, int num_donors, int k_slots, const float* scores,
  * until exit).  Limits: batch * num_donors <= 262144, batch <= 65536,
  * num_donors <= 4096 (MN_ERR_UNSUPPORTED beyond).  Calls that overlap on one
  * GPU share the scratch and race; order them on a single stream.  The first
- * call on a device looks up the scratch address; make it before any stream
- * capture. */
+ * call in each CUDA context (per device, and again after a device reset)
+ * looks up the scratch address; make it before any stream capture. */
 int mn_dtem_select_noalloc(int batch, int num_donors, int k_slots,
                            const float* scores, const uint8_t* allowed, int k,
                            float tau1, float tau2, float* assignment,
@@ -227,9 +227,12 @@ int mn_carrier_scatter(int batch, int k, int num_patches, int channels,
  * window: |i - j| <= window; window < 0 means global attention.
  * cls_global: 1 = row 0 attends to every key (the LocalAttention CLS row).
  * scale: softmax scale (1/sqrt(D) in the reference).
- * fp16 / bf16 with head_dim 64 run on the tensor cores (tcgen05, fp32
- * accumulation, probabilities rounded to the input type for P.V as
- * FlashAttention does); other shapes on CUDA cores in fp32.
+ * The kernels are tcgen05 tensor-core kernels (fp32 accumulation,
+ * probabilities rounded to the input type for P.V as FlashAttention does):
+ * q/k/v must be fp16 or bf16 with head_dim 64 and 16-byte aligned rows
+ * (strides multiples of 8 elements).  Anything else returns
+ * MN_ERR_UNSUPPORTED with nothing launched; so does a CLS-global row with a
+ * window above 16 over more keys than the kernel's CLS scratch holds.
  * status: optional device int; bit 8 set if a tensor-core wait timed out. */
 int mn_local_attention(int batch, int tokens, int heads, int head_dim,
                        int dtype, const void* q, const void* k, const void* v,
@@ -242,7 +245,8 @@ int mn_local_attention(int batch, int tokens, int heads, int head_dim,
  * (|i - j| <= window, window < 0 = every key): the recovery cross-attention
  * core of MyCrossAttention.forward (opentome/models/mergenet/model.py:173-188,
  * 393 carrier queries over the 785 pre-merge tokens).  Strides in elements;
- * out [B, nq, H, D] contiguous. */
+ * out [B, nq, H, D] contiguous.  Same dtype / head_dim / alignment contract
+ * as mn_local_attention (MN_ERR_UNSUPPORTED otherwise). */
 int mn_attention(int batch, int nq, int nk, int heads, int head_dim, int dtype,
                  const void* q, int64_t q_sb, int64_t q_sn, int64_t q_sh,
                  const void* k, const void* v, int64_t kv_sb, int64_t kv_sn,

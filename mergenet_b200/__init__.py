@@ -12,6 +12,7 @@ from .routing import (  # noqa: F401
     build_patch_spatial_adjacency,
     build_patch_spatial_neighbors,
     carrier_scatter,
+    check_status,
     dtem_select,
     route_and_gather,
     sparse_neighbor_dot,

@@ -38,6 +38,20 @@ def _strides_bnhd(t: torch.Tensor):
     return t.stride(0), t.stride(1), t.stride(2)
 
 
+HEAD_DIM = 64  # the tensor-core kernels' head width (the canonical 384 / 6 heads)
+
+
+def _check_head_dim(d):
+    if d != HEAD_DIM:
+        raise ValueError(f"head_dim {d} is not supported: the B200 attention kernels take head_dim {HEAD_DIM} "
+                         "(fp16 / bf16 on the tensor cores)")
+
+
+def _tc_ready(t):
+    """fp16 / bf16 with 16-byte aligned rows (what the TMA tensor maps need)."""
+    return (t.stride(-1) == 1 and all(s % 8 == 0 for s in t.stride()[:-1]) and t.data_ptr() % 16 == 0)
+
+
 def _launch(q, k, v, bias, window, cls_global, scale, out_dtype):
     """q/k/v in (B, N, H, D) view form (any strides with a unit last stride)."""
     if q.shape != k.shape or q.shape != v.shape:
@@ -45,14 +59,19 @@ def _launch(q, k, v, bias, window, cls_global, scale, out_dtype):
     if bias is not None and tuple(bias.shape) != (q.shape[0], q.shape[1]):
         # the kernels read bias[b * N + j] for every key j of every image b
         raise ValueError(f"bias must be (B, N) = {(q.shape[0], q.shape[1])}, got {tuple(bias.shape)}")
+    _check_head_dim(q.shape[-1])
     dev = L.require_cuda(q, k, v, bias)
     if q.dtype != k.dtype or q.dtype != v.dtype:
         raise ValueError("q/k/v must share a dtype")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError(f"q/k/v must be float16 or bfloat16 for the tensor-core kernels, got {q.dtype}")
     if not (q.stride() == k.stride() == v.stride()):
         k = k.contiguous() if k.stride() != q.stride() else k
         v = v.contiguous() if v.stride() != q.stride() else v
         if not (q.stride() == k.stride() == v.stride()):
             q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    if not (_tc_ready(q) and _tc_ready(k) and _tc_ready(v)):
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     b, n, h, d = q.shape
     sb, sn, sh = _strides_bnhd(q)
     out = torch.empty(b, n, h, d, device=dev, dtype=out_dtype)
@@ -82,6 +101,8 @@ def unbiased_local_attention(q, k, v, local_window, *, logical_dim: Optional[int
     d = q.shape[-1]
     scale = 1.0 / math.sqrt(logical_dim if logical_dim is not None else d)
     out_dtype = x_dtype if x_dtype is not None else q.dtype
+    if q.dtype not in (torch.float16, torch.bfloat16):  # the reference casts to fp16 for its kernel (:533-537)
+        q, k, v = q.half(), k.half(), v.half()
     if bnhd:
         return _launch(q, k, v, None, local_window, cls_global, scale, out_dtype)
     o = _launch(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), None, local_window, cls_global, scale,
@@ -115,6 +136,11 @@ def biased_local_attention(q, k, v, bias, local_window, *, logical_dim: Optional
     if training and dropout_p > 0.0:
         raise NotImplementedError("attention dropout is a training feature; the B200 path is inference")
     d_logic = logical_dim if logical_dim is not None else q.shape[-1]
+    if d_logic < q.shape[-1] and q.shape[-1] % 8 != 0:
+        # the reference's generic path (:416-483) then returns all D columns,
+        # the ones past the logical width attention-weighted from v's padding
+        raise ValueError(f"logical_dim {d_logic} below head_dim {q.shape[-1]} needs head_dim % 8 == 0 "
+                         "(the reference's in-place bias-column layout)")
     scale = 1.0 / math.sqrt(d_logic)
     out_dtype = x_dtype if x_dtype is not None else q.dtype
     if q.dtype not in (torch.float16, torch.bfloat16):  # the reference computes in fp16 then
@@ -154,13 +180,21 @@ def local_attention_packed(qkv, num_heads, local_window, cls_global=True, out_dt
 def cross_attention(q, k, v, scale=None, out_dtype=None, window=-1):
     """softmax(q k^T * scale) v with q [B, Nq, H, D] and k/v [B, Nk, H, D]
     (any strides with a unit last stride): the SDPA core of the recovery
-    cross-attention (opentome/models/mergenet/model.py:173-188)."""
-    dev = L.require_cuda(q, k, v)
+    cross-attention (opentome/models/mergenet/model.py:173-188).  fp16 /
+    bf16, head_dim 64 (the tensor-core kernel's contract)."""
     if k.shape != v.shape or q.shape[0] != k.shape[0] or q.shape[2:] != k.shape[2:]:
         raise ValueError(f"shape mismatch: q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)}")
+    _check_head_dim(q.shape[-1])
+    dev = L.require_cuda(q, k, v)
     if not (q.dtype == k.dtype == v.dtype):
         raise ValueError("q/k/v must share a dtype")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError(f"q/k/v must be float16 or bfloat16 for the tensor-core kernel, got {q.dtype}")
     if k.stride() != v.stride():
+        k, v = k.contiguous(), v.contiguous()
+    if not _tc_ready(q):
+        q = q.contiguous()
+    if not (_tc_ready(k) and _tc_ready(v)):
         k, v = k.contiguous(), v.contiguous()
     b, nq, h, d = q.shape
     nk = k.shape[1]

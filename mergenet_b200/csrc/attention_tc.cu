@@ -1132,7 +1132,7 @@ static bool launch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const v
     return false;
   const size_t smem = TcSmem<NB>::bytes;
   auto kern = bias ? attn_tc_kernel<ET, NB, WIN, true> : attn_tc_kernel<ET, NB, WIN, false>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (!ensure_smem(kern, smem)) return false;
   dim3 grid((Nq + kTcM - 1) / kTcM, H, B);
   // the CLS row rides along with query tile 0 when its scratch fits the P tile
   const bool cls = WIN && cls_global && Nq == Nk && Nk <= cls_max_keys<NB>();
@@ -1163,7 +1163,7 @@ static bool launch_win_persistent(const void* q, int64_t qb, int64_t qn, int64_t
   auto kern = bias ? attn_win_persistent_kernel<ET, true> : attn_win_persistent_kernel<ET, false>;
   constexpr uint32_t smem = TcSmem<160>::bytes + kClsBytes + 16;
   static_assert(smem <= 113 * 1024, "two CTAs per SM");
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (!ensure_smem(kern, smem)) return false;
   kern<<<grid, 128, smem, st>>>(mq, mk, mv, q_order, kv_order, N, H, B, window, scale, bias,
                                                bias_dtype, out, out_dtype, err, cls ? 1 : 0,
                                                static_cast<const ET*>(q), qb, qh, static_cast<const ET*>(k),
@@ -1202,19 +1202,35 @@ static bool dispatch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const
                                    out, out_dtype, err, st, cls_global, cls_done);
 }
 
+// Whether the tensor-core kernels cover a call: fp16 / bf16, head_dim 64,
+// 16-byte aligned rows, and (for the CLS-global row) a window the persistent
+// kernel takes or few enough keys for the multi-block kernel's CLS scratch.
+bool attention_tc_supported(int dtype, const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k,
+                            const void* v, int64_t kb, int64_t kn, int64_t kh, int Nq, int Nk, int D, int window,
+                            bool cls_global) {
+  if (D != kTcD || (dtype != MN_F16 && dtype != MN_BF16)) return false;
+  auto aligned = [](const void* p, int64_t s1, int64_t s2, int64_t s3) {
+    return (reinterpret_cast<uintptr_t>(p) % 16 == 0) && s1 % 8 == 0 && s2 % 8 == 0 && s3 % 8 == 0;
+  };
+  if (!aligned(q, qb, qn, qh) || !aligned(k, kb, kn, kh) || !aligned(v, kb, kn, kh)) return false;
+  if (cls_global) {
+    if (Nq != Nk || window < 0) return false;
+    const bool band = MN_TC_SINGLE_BAND && kTcM + 2 * window <= 160;
+    if (band && !MN_TC_WIN_PERSISTENT && Nk > cls_max_keys<160>()) return false;
+    if (!band && Nk > cls_max_keys<MN_TC_BLOCK_KEYS>()) return false;
+  }
+  return true;
+}
+
 // Host-side dispatch used by mn_local_attention / mn_attention.  Returns
-// false when the shape is not one the tensor-core kernel covers.
+// false when the shape is not one the tensor-core kernel covers (nothing is
+// launched then).
 bool attention_tc(int dtype, const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v,
                   int64_t kb, int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int D, int window, float scale,
                   const void* bias, int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st,
                   bool cls_global, bool* cls_done) {
   *cls_done = false;
-  if (D != kTcD || (dtype != MN_F16 && dtype != MN_BF16)) return false;
-  // 16-byte aligned rows for the vector loads
-  auto aligned = [](const void* p, int64_t s1, int64_t s2, int64_t s3) {
-    return (reinterpret_cast<uintptr_t>(p) % 16 == 0) && s1 % 8 == 0 && s2 % 8 == 0 && s3 % 8 == 0;
-  };
-  if (!aligned(q, qb, qn, qh) || !aligned(k, kb, kn, kh) || !aligned(v, kb, kn, kh)) return false;
+  if (!attention_tc_supported(dtype, q, qb, qn, qh, k, v, kb, kn, kh, Nq, Nk, D, window, cls_global)) return false;
   if (dtype == MN_F16)
     return dispatch_tc<__half>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype, out,
                                out_dtype, err, st, cls_global, cls_done);

@@ -6,6 +6,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "../../include/mergenet_b200.h"
 
 #define MN_FULL_MASK 0xffffffffu
@@ -36,6 +40,35 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
 }
 
 namespace mn {
+
+// ------------------------------------------------- dynamic shared memory
+// Make sure `func` may launch with `bytes` of dynamic shared memory on the
+// current device.  cudaFuncAttributeMaxDynamicSharedMemorySize is a
+// process-wide setting per (device, kernel): if two host threads each set it
+// to their own size before launching, one can lower the limit between the
+// other's set and its launch.  Here the limit is only ever raised, under one
+// lock, and the largest value set so far is remembered, so a launch never
+// finds a limit below what it asked for.  Returns false if the driver
+// refuses the size (nothing should be launched then).
+inline bool ensure_dynamic_smem(const void* func, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, size_t> set_so_far;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  size_t& cur = set_so_far[{dev, func}];
+  if (bytes <= cur) return true;
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess) {
+    cudaGetLastError();  // the refusal is reported by the return value, not left sticky
+    return false;
+  }
+  cur = bytes;
+  return true;
+}
+template <typename F>
+inline bool ensure_smem(F* func, size_t bytes) {
+  return ensure_dynamic_smem(reinterpret_cast<const void*>(func), bytes);
+}
 
 // ---------------------------------------------------------------- dtype I/O
 template <int DT> struct Elem;

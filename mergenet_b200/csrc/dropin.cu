@@ -3,6 +3,7 @@
 // odd grids): the fused path in route.cu covers only the canonical eval
 // grouping.
 #include <algorithm>
+#include <map>
 #include <mutex>
 
 #include "common.cuh"
@@ -409,7 +410,7 @@ extern "C" int mn_sparse_weighted_transport(int batch, int num_donors, int num_r
   const dim3 grid(batch, (channels + CC - 1) / CC);
   int rc = dispatch_dtype(dtype, [&](auto tag) {
     using ET = decltype(tag);
-    cudaFuncSetAttribute(transport_kernel<ET>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (!ensure_smem(transport_kernel<ET>, smem)) return;  // reported by launch_status below
     transport_kernel<ET><<<grid, 512, smem, st>>>(static_cast<const ET*>(assignment), static_cast<const ET*>(values),
                                                   receiver_indices, receiver_valid, num_donors, num_receivers, k,
                                                   channels, CC, static_cast<ET*>(out), status);
@@ -456,10 +457,10 @@ extern "C" int mn_thre_topk(int rows, int n, const float* x, int k, float temper
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int parts = thre_topk_parts((int64_t)rows * n);
   float* partials = static_cast<float*>(workspace);
-  minmax_partials_kernel<<<parts, 256, 0, st>>>(x, (int64_t)rows * n, partials);
   const int np = next_pow2(n);
   const size_t smem = row_scratch_bytes(np) + (size_t)n * sizeof(float);
-  cudaFuncSetAttribute(thre_topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (!ensure_smem(thre_topk_rows_kernel, smem)) return MN_ERR_LAUNCH;
+  minmax_partials_kernel<<<parts, 256, 0, st>>>(x, (int64_t)rows * n, partials);
   thre_topk_rows_kernel<<<rows, 512, smem, st>>>(x, n, k, temperature, partials, parts, y, status);
   return launch_status();
 }
@@ -485,13 +486,13 @@ extern "C" int mn_dtem_select(int batch, int num_donors, int k_slots, const floa
   int* counts = reinterpret_cast<int*>(energy + rows);
   float* partials = reinterpret_cast<float*>(counts + batch);
   const int parts = thre_topk_parts(rows);
+  const int np = next_pow2(num_donors);
+  const size_t smem = row_scratch_bytes(np) + (size_t)num_donors * sizeof(float);
+  if (!ensure_smem(select_rows_kernel, smem)) return MN_ERR_LAUNCH;
   cudaMemsetAsync(counts, 0, (size_t)batch * sizeof(int), st);
   select_energy_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(scores, allowed, (int)rows, k_slots, tau1,
                                                                    energy, counts, num_donors);
   minmax_partials_kernel<<<parts, 256, 0, st>>>(energy, rows, partials);
-  const int np = next_pow2(num_donors);
-  const size_t smem = row_scratch_bytes(np) + (size_t)num_donors * sizeof(float);
-  cudaFuncSetAttribute(select_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   select_rows_kernel<<<batch, 512, smem, st>>>(scores, allowed, num_donors, k_slots, k, tau1, tau2, energy, counts,
                                                partials, parts, assignment, status);
   return launch_status();
@@ -536,9 +537,12 @@ extern "C" int mn_carrier_scatter(int batch, int k, int num_patches, int channel
 // call (cleared with cudaMemsetAsync, which allocates nothing); the other
 // scratch is fully rewritten by each call.
 //
-// The first call on each device looks up the array's device address with
-// cudaGetSymbolAddress while that device is current (a host-side lookup,
-// cached per device); make that first call before any stream capture.
+// The first call in each CUDA context looks up the array's device address
+// with cudaGetSymbolAddress while that context's device is current (a
+// host-side lookup, cached per context); make that first call before any
+// stream capture.  The cache is keyed by the driver context, so a device
+// reset (a new primary context) triggers a fresh lookup instead of reusing a
+// stale address.
 // ---------------------------------------------------------------------------
 namespace {
 constexpr int64_t kNoAllocMaxRows = 262144;
@@ -549,21 +553,46 @@ constexpr size_t kNoAllocScratchBytes =
     (size_t)kNoAllocMaxParts * 2 * sizeof(float);
 static __device__ __align__(256) unsigned char g_select_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 128;
 std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+std::map<void*, void*> g_scratch_addr;  // driver context -> address of g_select_scratch in it
 
-// Device address of g_select_scratch on the current device (looked up once).
+// The current driver context (CUcontext), through the runtime's driver entry
+// point so the library needs no link-time libcuda.
+void* current_context() {
+  using GetCtx = int (*)(void**);
+  static GetCtx fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<GetCtx>(nullptr);
+    return reinterpret_cast<GetCtx>(p);
+  }();
+  void* ctx = nullptr;
+  if (!fn || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
+
+// Device address of g_select_scratch in the current context (looked up once
+// per context).
 int select_scratch_address(void** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MN_ERR_LAUNCH;
+  void* ctx = current_context();
+  if (!ctx) {
+    // no context is current yet: the symbol lookup initialises the current
+    // device's primary context (and allocates nothing)
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_select_scratch) != cudaSuccess) return MN_ERR_LAUNCH;
+    ctx = current_context();
+    if (!ctx) return MN_ERR_LAUNCH;
+  }
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+  auto it = g_scratch_addr.find(ctx);
+  if (it == g_scratch_addr.end()) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_select_scratch) != cudaSuccess || p == nullptr) return MN_ERR_LAUNCH;
-    g_scratch_addr[dev] = p;
+    it = g_scratch_addr.emplace(ctx, p).first;
   }
-  *out = g_scratch_addr[dev];
+  *out = it->second;
   return MN_OK;
 }
 }  // namespace
@@ -585,13 +614,13 @@ extern "C" int mn_dtem_select_noalloc(int batch, int num_donors, int k_slots, co
   float* energy = static_cast<float*>(scratch);
   int* counts = reinterpret_cast<int*>(energy + rows);
   float* partials = reinterpret_cast<float*>(counts + batch);
+  const int np = next_pow2(num_donors);
+  const size_t smem = row_scratch_bytes(np) + (size_t)num_donors * sizeof(float);
+  if (!ensure_smem(select_rows_kernel, smem)) return MN_ERR_LAUNCH;
   cudaMemsetAsync(counts, 0, (size_t)batch * sizeof(int), st);
   select_energy_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(scores, allowed, (int)rows, k_slots, tau1,
                                                                    energy, counts, num_donors);
   minmax_partials_kernel<<<parts, 256, 0, st>>>(energy, rows, partials);
-  const int np = next_pow2(num_donors);
-  const size_t smem = row_scratch_bytes(np) + (size_t)num_donors * sizeof(float);
-  cudaFuncSetAttribute(select_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   select_rows_kernel<<<batch, 512, smem, st>>>(scores, allowed, num_donors, k_slots, k, tau1, tau2, energy, counts,
                                                partials, parts, assignment, status);
   return launch_status();

@@ -273,7 +273,7 @@ static int launch(int M, int N, int K, const void* a, int64_t lda, const void* w
   const int tiles = ((M + BM - 1) / BM) * (N / BN);
   const int grid = std::max(1, std::min(tiles, sms));
   auto kern = gemm_tc_kernel<BN, EPI>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<BN>::bytes);
+  if (!ensure_smem(kern, Cfg<BN>::bytes)) return MN_ERR_LAUNCH;
   kern<<<grid, kThreads, Cfg<BN>::bytes, st>>>(ma, mw, mo, M, N, K, static_cast<const __half*>(bias), status);
   return MN_OK;
 }

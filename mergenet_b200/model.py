@@ -128,7 +128,7 @@ class MergeNetSmall(nn.Module):
         self.encode_cross_attention = CrossAttention(embed_dim, num_heads)
         self._plans = {}
         self._half = None
-        self._kv16 = None
+        self._kv32 = None
         self._patch_w16 = None
 
     # ------------------------------------------------------------------ init
@@ -164,9 +164,7 @@ class MergeNetSmall(nn.Module):
         self.encode_cross_attention.out_proj.bias.zero_()
         tn(self.head.weight)
         self.head.bias.zero_()
-        self._half = None
-        self._kv16 = None
-        self._patch_w16 = None
+        self._reset_caches()
         return self
 
     # ------------------------------------------------------------- execution
@@ -185,7 +183,7 @@ class MergeNetSmall(nn.Module):
 
     def _reset_caches(self):
         self._half = None
-        self._kv16 = None
+        self._kv32 = None
         self._patch_w16 = None
 
     def load_state_dict(self, state_dict, strict=True, assign=False):
@@ -232,29 +230,27 @@ class MergeNetSmall(nn.Module):
         return self._linear16(f, prefix + ".mlp.fc2", blk.mlp.fc2).view(*shp[:-1], -1)
 
     def _cross(self, topk_x, x_embed):
-        """MyCrossAttention (model.py:122-221).  The q/k/v projections feed an
-        fp16 attention (SDPA autocasts its inputs), so they run as fp16 GEMMs
-        with fp32 accumulation on LayerNorm outputs rounded to fp16; the
-        out-projection keeps an fp32 result (TF32 tensor cores)."""
+        """MyCrossAttention (model.py:122-221) as the reference runs it under
+        fp16 autocast: fp32 LayerNorms, q/k/v projections in true fp32 (the
+        reference turns autocast off for them, :140-145; TF32 is switched off
+        here), the attention on fp16 operands (SDPA autocasts them, :178-186)
+        with an fp16 context widened to fp32, and the out-projection in fp32
+        (:215-219)."""
         ca = self.encode_cross_attention
         b, nq, c = topk_x.shape
         nk = x_embed.shape[1]
         hd = c // self.num_heads
-        w16 = self._weights16()
-        qn = add_layernorm(topk_x, None, ca.q_norm)[1]
-        kvn = add_layernorm(x_embed, None, ca.kv_norm)[1]
-        q = F.linear(qn, w16["encode_cross_attention.q_proj.weight"], w16["encode_cross_attention.q_proj.bias"])
-        if self._kv16 is None:
-            self._kv16 = (torch.cat([ca.k_proj.weight, ca.v_proj.weight]).half(),
-                          torch.cat([ca.k_proj.bias, ca.v_proj.bias]).half())
-        kv = F.linear(kvn, *self._kv16).view(b, nk, 2, self.num_heads, hd)
-        ctx = cross_attention(q.view(b, nq, self.num_heads, hd), kv[:, :, 0], kv[:, :, 1], out_dtype=torch.float32)
-        prev = torch.backends.cuda.matmul.allow_tf32
-        torch.backends.cuda.matmul.allow_tf32 = True
-        try:
-            out = F.linear(ctx.view(b, nq, c), ca.out_proj.weight, ca.out_proj.bias)
-        finally:
-            torch.backends.cuda.matmul.allow_tf32 = prev
+        qn = F.layer_norm(topk_x, (c,), ca.q_norm.weight, ca.q_norm.bias, ca.q_norm.eps)
+        kvn = F.layer_norm(x_embed, (c,), ca.kv_norm.weight, ca.kv_norm.bias, ca.kv_norm.eps)
+        if self._kv32 is None:
+            self._kv32 = (torch.cat([ca.k_proj.weight, ca.v_proj.weight]).contiguous(),
+                          torch.cat([ca.k_proj.bias, ca.v_proj.bias]).contiguous())
+        with _true_fp32_matmul():
+            q = F.linear(qn, ca.q_proj.weight, ca.q_proj.bias).half()
+            kv = F.linear(kvn, *self._kv32).half().view(b, nk, 2, self.num_heads, hd)
+            ctx = cross_attention(q.view(b, nq, self.num_heads, hd), kv[:, :, 0], kv[:, :, 1],
+                                  out_dtype=torch.float16)
+            out = F.linear(ctx.view(b, nq, c).float(), ca.out_proj.weight, ca.out_proj.bias)
         return out
 
     def _embed(self, images, w16, norm1):
@@ -282,10 +278,16 @@ class MergeNetSmall(nn.Module):
         return embed_layernorm(emb.view(b, gh * gw, -1), vit.pos_embed[0], vit.cls_token.view(-1), norm1)
 
     @torch.no_grad()
-    def forward(self, images, return_intermediates=False):
+    def forward(self, images, return_intermediates=False, check=None):
         """images [B, 3, H, W] -> (logits [B, classes] fp16, aux dict).
         ``return_intermediates`` adds the tensors handed between stages
-        (x_embed, metrics, topk_x, topk_size) to aux, for checking."""
+        (x_embed, metrics, topk_x, topk_size, x_trace) to aux, for checking.
+
+        The routing and attention kernels report data conditions and wait
+        timeouts in device status words.  ``check`` (default: unless a CUDA
+        graph is being captured) reads them at the end of the forward and
+        raises, as the reference's budget assert fails closed
+        (dtem.py:1536-1546); otherwise ``check_status`` reads them later."""
         if not images.is_cuda:
             raise RuntimeError("MergeNetSmall runs on CUDA (there is no CPU path)")
         w16 = self._weights16()
@@ -310,9 +312,11 @@ class MergeNetSmall(nn.Module):
         _, _, raw = add_layernorm(x, y, None, x_out=x, want_ln=False, want_raw=True)
         self._metric(raw, depth - 1, metrics, w16)
         x_embed = x
-        route = self._plan(x.device)(x_embed, metrics)
+        route = self._plan(x.device)(x_embed, metrics, check=False)
+        self._route_status = route.status
         topk_x = route.topk_x
         x_trace = self._cross(topk_x, x_embed) + topk_x
+        x_trace_in = x_trace.clone() if return_intermediates else None
         log_size = route.topk_size.log()
         y = None
         for i, blk in enumerate(self.latent.vit.blocks):
@@ -321,19 +325,43 @@ class MergeNetSmall(nn.Module):
             _, h, _ = add_layernorm(x_trace, p, blk.norm2, x_out=x_trace)
             y = self._mlp(h, f"latent.vit.blocks.{i}", blk)
         lv = self.latent.vit
-        cls = x_trace[:, 0] + y[:, 0].float()
-        cls = F.layer_norm(cls, (c,), lv.norm.weight, lv.norm.bias, lv.norm.eps)
+        # the latent encoder's final norm over every carrier row (fp32 under
+        # autocast); the head reads the CLS row (model.py:1195-1198)
+        x_latent = F.layer_norm(torch.add(x_trace, y), (c,), lv.norm.weight, lv.norm.bias, lv.norm.eps)
+        cls = x_latent[:, 0]
         logits = self._linear16(cls, "head", self.head)
         aux = {
+            # soft merging keeps every token in place, so each local layer
+            # hands on all T tokens (model.py:589)
+            "token_counts_local": [n] * depth,
             "token_strength_no_cls": route.size[:, 1:],
             "topk_patch_indices": route.topk_idx,
             "retained_tokens": int(route.topk_idx.shape[1]),
             "cls_feature": cls,
+            "latent_tokens": x_latent[:, 1:],
         }
         if return_intermediates:
             aux.update(x_embed=x_embed, metrics=metrics, topk_x=topk_x, topk_size=route.topk_size,
-                       token_center=route.center)
+                       token_center=route.center, x_trace=x_trace_in)
+        if check is None:
+            check = not torch.cuda.is_current_stream_capturing()
+        if check:
+            self.check_status()
         return logits, aux
+
+    def check_status(self, route_status=None):
+        """Raise if the last forward's routing (or the routing call whose
+        status word is given) flagged a data condition, or an attention
+        kernel's bounded wait gave up (reads the device status words, which
+        synchronises)."""
+        from .attention import attention_status
+        from .routing import check_status
+        status = route_status if route_status is not None else getattr(self, "_route_status", None)
+        if status is not None:
+            check_status(status)
+            st = attention_status(status.device)
+            if st:
+                raise RuntimeError(f"attention kernel status {st:#x} (a bounded tensor-core wait gave up)")
 
 
 class ForwardGraph:
@@ -365,6 +393,13 @@ class ForwardGraph:
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self.logits, self.aux = model(images)
+        self._route_status = model._route_status  # the captured routing call's status word
+
+    def check_status(self):
+        """Raise if a replay's routing or attention kernels flagged a data
+        condition (reads the device status words, which synchronises).  The
+        replay itself never reads them, so timing loops stay asynchronous."""
+        self.model.check_status(self._route_status)
 
     def __call__(self, images=None):
         if images is not None and images is not self.images:
@@ -424,6 +459,20 @@ class ForwardGraph:
         and the four routing kernels."""
         nl, nt = len(model.local.vit.blocks), len(model.latent.vit.blocks)
         return 1 + (2 * nl + 1 + 2 + 2 * nt) + (nl + nt + 1) + 4
+
+
+class _true_fp32_matmul:
+    """fp32 GEMMs in IEEE fp32 (no TF32) inside the block, whatever the
+    process-wide setting; restores it on exit."""
+
+    def __enter__(self):
+        self.prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        return self
+
+    def __exit__(self, *exc):
+        torch.backends.cuda.matmul.allow_tf32 = self.prev
+        return False
 
 
 def embed_layernorm(emb, pos, cls, ln):

@@ -185,6 +185,19 @@ def _raise_status(status, what):
                            "merge budget")
     if s & L.MN_STATUS_TOO_MANY_EDGES:
         raise ValueError(f"{what}: receiver index out of range")
+    if s & L.MN_STATUS_DEGENERATE_RANGE:
+        raise RuntimeError(f"{what}: ThreTopK energy range is empty or not finite (global max == min); "
+                           "the soft top-k threshold is undefined")
+    if s:
+        raise RuntimeError(f"{what}: device status {s:#x}")
+
+
+def _default_check(check):
+    """check=None: read the status word now unless a CUDA graph is being
+    captured (then the caller reads it after the replay)."""
+    if check is None:
+        return not torch.cuda.is_current_stream_capturing()
+    return bool(check)
 
 
 def ThreTopK(x, k, temperature=30.0):  # noqa: N802 - reference name
@@ -274,8 +287,16 @@ class RoutePlan:
     def workspace_bytes(self, batch):
         return int(L.lib().mn_route_workspace_bytes(ctypes.byref(self.dims), batch, len(self.r_list)))
 
-    def __call__(self, x, metrics, out=None, workspace=None, status=None):
-        """x [B, T, C] (fp32/fp16/bf16), metrics [L, B, T, Cm] -> RouteResult."""
+    def __call__(self, x, metrics, out=None, workspace=None, status=None, check=None):
+        """x [B, T, C] (fp32/fp16/bf16), metrics [L, B, T, Cm] -> RouteResult.
+
+        The kernels report data conditions (an infeasible merge budget, an
+        empty ThreTopK range, a table error) in the device status word.
+        ``check=True`` reads it after the launch and raises (one
+        synchronisation), as the reference's budget assert fails closed
+        (dtem.py:1536-1546); ``check=False`` leaves ``RouteResult.status`` for
+        the caller to read later with ``check_status``.  The default reads it
+        unless a CUDA graph is being captured."""
         L.require_cuda(x, metrics)
         if x.device != self.device:
             raise ValueError(f"plan lives on {self.device}, inputs on {x.device}")
@@ -305,7 +326,17 @@ class RoutePlan:
                                          L.ptr(topk_size), L.ptr(topk_idx), L.ptr(size), L.ptr(center),
                                          L.ptr(status), L.stream_of(x))
         L.check(rc, "mn_route_and_gather")
-        return RouteResult(topk_x, topk_size, topk_idx, size, center, status)
+        res = RouteResult(topk_x, topk_size, topk_idx, size, center, status)
+        if _default_check(check):
+            check_status(res)
+        return res
+
+
+def check_status(result):
+    """Raise if the routing call behind ``result`` (a RouteResult, or its
+    status tensor) flagged a data condition on the device."""
+    status = result.status if isinstance(result, RouteResult) else result
+    _raise_status(status, "mn_route_and_gather")
 
 
 def route_and_gather(x_embed, metrics, grid_size, radius=3.0, r_list=None):

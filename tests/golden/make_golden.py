@@ -1,10 +1,10 @@
 #!/usr/bin/env python3
 """Generate golden fixtures by running the MergeNet reference itself.
 
-Run in a container that has the reference checkout (read-only) at
-$MERGENET_REFERENCE (default /root/reference):
+Run where a checkout of the reference is available (read-only), naming it
+in $MERGENET_REFERENCE:
 
-    python tests/golden/make_golden.py
+    MERGENET_REFERENCE=<path to the MergeNet checkout> python tests/golden/make_golden.py
 
 The reference's routing modules import timm at module level; timm is not
 installed, so ``timm_shim/`` (inert placeholders written for this repository)
@@ -27,7 +27,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("MERGENET_REFERENCE", "/root/reference"))
+if "MERGENET_REFERENCE" not in os.environ:
+    raise SystemExit("set MERGENET_REFERENCE to the MergeNet reference checkout")
+REF = Path(os.environ["MERGENET_REFERENCE"])
 sys.path.insert(0, str(HERE))
 sys.path.insert(0, str(HERE / "timm_shim"))
 sys.path.insert(0, str(REF))

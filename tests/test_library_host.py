@@ -134,7 +134,7 @@ def test_cpu_tensors_are_rejected():
     with pytest.raises(RuntimeError):
         mn.ThreTopK(torch.rand(2, 5), 2)
     with pytest.raises(RuntimeError):
-        mn.unbiased_local_attention(torch.rand(1, 5, 2, 8), torch.rand(1, 5, 2, 8), torch.rand(1, 5, 2, 8), 1)
+        mn.unbiased_local_attention(torch.rand(1, 5, 2, 64), torch.rand(1, 5, 2, 64), torch.rand(1, 5, 2, 64), 1)
 
 
 def test_attention_argument_checks_precede_any_launch():
@@ -143,7 +143,7 @@ def test_attention_argument_checks_precede_any_launch():
     kernels never index past the bias; well-formed host tensors still meet
     the no-CPU-path error."""
     import mergenet_b200 as mn
-    qkv = torch.rand(2, 7, 3 * 2 * 8)
+    qkv = torch.rand(2, 7, 3 * 2 * 64)
     with pytest.raises(ValueError, match="bias must be"):
         mn.local_attention_packed(qkv, 2, 1, bias=torch.rand(2, 6))
     with pytest.raises(ValueError, match="bias must be"):
@@ -152,3 +152,18 @@ def test_attention_argument_checks_precede_any_launch():
         mn.local_attention_packed(torch.rand(2, 7, 40), 2, 1)
     with pytest.raises(RuntimeError):
         mn.local_attention_packed(qkv, 2, 1, bias=torch.rand(2, 7))
+
+
+def test_attention_shapes_outside_the_kernels_are_refused():
+    """One backend: head_dim other than 64 is a ValueError before any device
+    work, and so is the reference's generic-path case logical_dim < head_dim
+    with head_dim % 8 != 0 (it would return head_dim columns there)."""
+    import mergenet_b200 as mn
+    t = torch.rand(1, 9, 2, 16)
+    with pytest.raises(ValueError, match="head_dim 16"):
+        mn.unbiased_local_attention(t, t, t, 2)
+    t65 = torch.rand(1, 9, 2, 65)
+    with pytest.raises(ValueError, match="head_dim % 8"):
+        mn.biased_local_attention(t65, t65, t65, torch.rand(1, 9), 2, logical_dim=64, input_layout="BNHD")
+    with pytest.raises(ValueError, match="head_dim 32"):
+        mn.cross_attention(torch.rand(1, 3, 2, 32), torch.rand(1, 5, 2, 32), torch.rand(1, 5, 2, 32))

@@ -49,21 +49,38 @@ def torch_local_encoder(model, images):
 
 
 @torch.no_grad()
-def torch_after_routing(model, x_embed, topk_x, topk_size):
-    """Recovery cross-attention (fp32 projections, SDPA on fp16 operands),
-    six latent blocks with proportional attention and the head, restated with
-    PyTorch ops from the routing outputs (model.py:1190-1198)."""
+def torch_recovery(model, x_embed, topk_x):
+    """MyCrossAttention + residual (model.py:122-221, :1193) restated with
+    PyTorch ops as the reference runs it under fp16 autocast: fp32
+    LayerNorms, IEEE fp32 q/k/v projections, attention on fp16 operands with
+    an fp16 context, fp32 out-projection."""
     b, nq, c = topk_x.shape
     heads = model.num_heads
     hd = c // heads
     ca = model.encode_cross_attention
-    q = F.linear(F.layer_norm(topk_x, (c,), ca.q_norm.weight, ca.q_norm.bias), ca.q_proj.weight, ca.q_proj.bias)
-    kv = F.layer_norm(x_embed, (c,), ca.kv_norm.weight, ca.kv_norm.bias)
-    k = F.linear(kv, ca.k_proj.weight, ca.k_proj.bias)
-    v = F.linear(kv, ca.v_proj.weight, ca.v_proj.bias)
-    split = lambda t: t.half().view(b, -1, heads, hd).transpose(1, 2).float()  # noqa: E731
-    ctx = torch.softmax(split(q) @ split(k).transpose(-1, -2) / math.sqrt(hd), -1) @ split(v)
-    xt = F.linear(ctx.transpose(1, 2).reshape(b, -1, c), ca.out_proj.weight, ca.out_proj.bias) + topk_x
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        q = F.linear(F.layer_norm(topk_x, (c,), ca.q_norm.weight, ca.q_norm.bias), ca.q_proj.weight, ca.q_proj.bias)
+        kv = F.layer_norm(x_embed, (c,), ca.kv_norm.weight, ca.kv_norm.bias)
+        k = F.linear(kv, ca.k_proj.weight, ca.k_proj.bias)
+        v = F.linear(kv, ca.v_proj.weight, ca.v_proj.bias)
+        split = lambda t: t.half().view(b, -1, heads, hd).transpose(1, 2).float()  # noqa: E731
+        ctx = torch.softmax(split(q) @ split(k).transpose(-1, -2) / math.sqrt(hd), -1) @ split(v)
+        ctx = ctx.half().float().transpose(1, 2).reshape(b, -1, c)  # SDPA's fp16 output, widened
+        return F.linear(ctx, ca.out_proj.weight, ca.out_proj.bias) + topk_x
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+@torch.no_grad()
+def torch_after_routing(model, x_trace, topk_size):
+    """Six latent blocks with proportional attention and the head, restated
+    with PyTorch ops from the recovery output (model.py:1195-1198)."""
+    b, nq, c = x_trace.shape
+    heads = model.num_heads
+    hd = c // heads
+    xt = x_trace
     log_size = topk_size.log().half()[:, None, None, :]
     for i, blk in enumerate(model.latent.vit.blocks):
         # ToMeBlock with proportional attention (opentome/timm/tome.py:89-143)
@@ -77,14 +94,30 @@ def torch_after_routing(model, x_embed, topk_x, topk_size):
         xt = xt + model._linear16(h, f"latent.vit.blocks.{i}.mlp.fc2", blk.mlp.fc2)
     lv = model.latent.vit
     cls = F.layer_norm(xt[:, 0], (c,), lv.norm.weight, lv.norm.bias, lv.norm.eps)
-    return model._linear16(cls, "head", model.head)
+    tokens = F.layer_norm(xt[:, 1:], (c,), lv.norm.weight, lv.norm.bias, lv.norm.eps)
+    return model._linear16(cls, "head", model.head), tokens
+
+
+@torch.no_grad()
+def live_out_proj(model, seed=0):
+    """The reference zero-initialises the cross-attention out-projection
+    (model.py:822-829), which would hide the recovery path from the logits;
+    give it random weights so every check below sees it."""
+    g = torch.Generator().manual_seed(seed)
+    op = model.encode_cross_attention.out_proj
+    op.weight.copy_(torch.randn(op.weight.shape, generator=g) * 0.05)
+    op.bias.copy_(torch.randn(op.bias.shape, generator=g) * 0.05)
+    model._reset_caches()
+    return model
 
 
 def check_forward(model, images):
     """Stage-by-stage parity of one forward: local encoder vs the PyTorch
     restatement (fp16 tolerance), routing on the model's own x_embed/metrics
-    vs the oracle (exact carriers), logits vs the restatement of the
-    post-routing stages fed with the model's routing outputs (1e-2)."""
+    vs the oracle (exact carriers), the recovery cross-attention output vs
+    its fp32 restatement (2e-3, and large enough that a zeroed
+    cross-attention would fail), logits vs the restatement of the latent
+    stage fed with the model's recovery output (1e-2)."""
     logits, aux = model(images, return_intermediates=True)
     x_ref = torch_local_encoder(model, images)
     err = ((aux["x_embed"] - x_ref).abs().max() / x_ref.abs().max()).item()
@@ -96,9 +129,17 @@ def check_forward(model, images):
     assert not mism, mism
     rel = np.abs(aux["topk_x"].cpu().numpy() - route["topk_x"]).max() / np.abs(route["topk_x"]).max()
     assert rel <= 2e-3, rel
-    exp = torch_after_routing(model, aux["x_embed"], aux["topk_x"], aux["topk_size"])
+    rec = torch_recovery(model, aux["x_embed"], aux["topk_x"])
+    scale = rec.abs().max()
+    rerr = ((aux["x_trace"] - rec).abs().max() / scale).item()
+    assert rerr <= 2e-3, f"recovery cross-attention rel err {rerr}"
+    contrib = ((rec - aux["topk_x"]).abs().max() / scale).item()
+    assert contrib >= 0.05, f"cross-attention contributes only {contrib} of the recovery output"
+    exp, tokens = torch_after_routing(model, aux["x_trace"], aux["topk_size"])
     lerr = ((logits.float() - exp.float()).abs().max() / exp.float().abs().max()).item()
     assert lerr <= 1e-2, f"logits rel err {lerr}"
+    terr = ((aux["latent_tokens"] - tokens).abs().max() / tokens.abs().max()).item()
+    assert terr <= 1e-2, f"latent tokens rel err {terr}"
     return logits, aux
 
 
@@ -108,7 +149,8 @@ def test_reference_smoke_config(dev):
     from mergenet_b200.model import MergeNetSmall
     torch.manual_seed(20260809)
     model = MergeNetSmall(img_size=32, patch_size=8, num_classes=10, metric_dim=16, local_depth=2,
-                          latent_depth=2, local_window=2).init_weights(0).to(dev).eval()
+                          latent_depth=2, local_window=2).init_weights(0)
+    model = live_out_proj(model).to(dev).eval()
     images = torch.randn(2, 3, 32, 32, device=dev)
     first, aux1 = check_forward(model, images)
     second, aux2 = model(images)
@@ -121,7 +163,7 @@ def test_reference_smoke_config(dev):
 def test_canonical_forward_stages(dev):
     """Canonical 224x224 model, stage by stage."""
     from mergenet_b200.model import MergeNetSmall
-    model = MergeNetSmall().init_weights(0).to(dev).eval()
+    model = live_out_proj(MergeNetSmall().init_weights(0)).to(dev).eval()
     g = torch.Generator(device=dev).manual_seed(3)
     images = torch.randn(4, 3, 224, 224, device=dev, generator=g)
     logits, aux = check_forward(model, images)

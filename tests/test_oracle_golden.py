@@ -60,10 +60,8 @@ def test_oracle_select_and_score(golden_dir):
     np.testing.assert_allclose(scores, g["scores"], rtol=0, atol=1e-5)
     np.testing.assert_array_equal(ridx, g["receiver_indices"])
     np.testing.assert_array_equal(rvalid, g["receiver_valid"])
-    an = O.normalize_metric(g["a"]) * 0 + g["a"]  # _select receives already-normalised a/b in the merge
     assign, _, _ = O.select(3, scores, rvalid)
     np.testing.assert_allclose(assign, g["assign"], rtol=0, atol=2e-6)
-    del an
 
 
 def test_oracle_transport(golden_dir):
@@ -88,3 +86,17 @@ def test_parse_r_schedule():
     assert canonical_r_list((28, 28)) == [65, 65, 65, 65, 65, 67]
     assert canonical_r_list((48, 48)) == [192] * 6
     assert O.parse_r(3, [1, 2]) == [1, 2, 0]
+
+
+def test_oracle_attention_matches_reference_naive(golden_dir):
+    """oracle/attention.py against the reference's unfold implementations
+    (naive_unbiased_local_attention / naive_biased_local_attention) on all
+    three fixture cases; those take a pre-scaled q, so the scale is 1."""
+    from oracle.attention import local_attention
+    g = np.load(golden_dir / "attention.npz")
+    for i in range(3):
+        q, k, v, bias = (g[f"{n}{i}"] for n in ("q", "k", "v", "bias"))
+        w = int(g[f"window{i}"])
+        np.testing.assert_allclose(local_attention(q, k, v, w, scale=1.0), g[f"unbiased{i}"], rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(local_attention(q, k, v, w, bias=bias, scale=1.0), g[f"biased{i}"],
+                                   rtol=1e-5, atol=1e-5)
