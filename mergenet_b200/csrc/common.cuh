@@ -239,72 +239,55 @@ __device__ __forceinline__ void bitonic_sort_u64(unsigned long long* s, int n) {
   }
 }
 
-// Bitonic sort of n keys (n a power of two, n <= blockDim.x, blockDim.x a
-// power of two), one key per thread: thread i passes key i and receives the
-// i-th smallest.  Exchanges with a partner less than 32 away use warp
-// shuffles; wider ones go through `xbuf` (2 * blockDim.x keys of shared
-// memory, double-buffered so each costs one barrier).  Every thread of the
-// block must call it; threads i >= n sort padding among themselves.
-__device__ __forceinline__ unsigned long long bitonic_sort_u64_reg(unsigned long long key, unsigned long long* xbuf,
-                                                                   int n) {
-  const int i = threadIdx.x;
-  int parity = 0;
-  for (int k = 2; k <= n; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      unsigned long long other;
-      if (j >= 32) {
-        unsigned long long* buf = xbuf + parity * blockDim.x;
-        buf[i] = key;
-        __syncthreads();
-        other = buf[i ^ j];
-        parity ^= 1;
-      } else {
-        other = __shfl_xor_sync(MN_FULL_MASK, key, j);
-      }
-      const bool up = (i & k) == 0;      // ascending run
-      const bool lower = (i & j) == 0;   // lower index of the pair
-      const unsigned long long lo = key < other ? key : other, hi = key < other ? other : key;
-      key = (lower == up) ? lo : hi;
-    }
-  }
-  return key;
-}
-
-// The same sort for n <= 2 * blockDim.x keys, two per thread: thread i
-// holds keys i and i + blockDim.x (k0, k1) and receives those two positions
-// of the sorted order.  The step with partner distance blockDim.x compares
-// a thread's own pair; xbuf holds 4 * blockDim.x keys.
-__device__ __forceinline__ void bitonic_sort_u64_reg2(unsigned long long& k0, unsigned long long& k1,
-                                                      unsigned long long* xbuf, int n) {
+// Bitonic sort of n keys (n a power of two, n <= R * blockDim.x,
+// blockDim.x a power of two >= 32) held in registers: thread i holds the
+// keys at positions i + r * blockDim.x (r = 0 .. R-1) in kv[r] and receives
+// those positions of the ascending order.  Positions at or past n must hold
+// keys that sort last (~0 for integers, +inf for floats).  Partners R * blockDim.x / 2 .. blockDim.x apart
+// are the thread's own registers, partners under 32 apart are reached by warp
+// shuffles, and the steps in between exchange through `xbuf` (2 * R *
+// blockDim.x keys of shared memory, double-buffered: one barrier per step).
+// Every thread of the block must call it with the same n.
+template <int R, typename K>
+__device__ __forceinline__ void bitonic_sort_regs(K (&kv)[R], K* xbuf, int n) {
   const int bd = blockDim.x;
   const int i = threadIdx.x;
   int parity = 0;
-  auto cmpx = [](unsigned long long key, unsigned long long other, int idx, int k, int j) {
+  auto pick = [](K key, K other, int idx, int k, int j) {
     const bool up = (idx & k) == 0, lower = (idx & j) == 0;
-    const unsigned long long lo = key < other ? key : other, hi = key < other ? other : key;
+    const K lo = key > other ? other : key, hi = key > other ? key : other;
     return (lower == up) ? lo : hi;
   };
   for (int k = 2; k <= n; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
-      if (j >= bd) {  // partner of i is i + bd: the thread's own other key
-        const bool up = (i & k) == 0;
-        const unsigned long long lo = k0 < k1 ? k0 : k1, hi = k0 < k1 ? k1 : k0;
-        k0 = up ? lo : hi;
-        k1 = up ? hi : lo;
+      if (j >= bd) {  // partner r ^ (j / bd) of the thread's own keys
+#pragma unroll
+        for (int t = 1; t < R; t <<= 1) {
+          if (j == t * bd) {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              if ((r & t) == 0) {
+                const bool up = ((i + r * bd) & k) == 0;
+                const K a = kv[r], b = kv[r | t];
+                const bool sw = up ? (a > b) : (a < b);
+                kv[r] = sw ? b : a;
+                kv[r | t] = sw ? a : b;
+              }
+            }
+          }
+        }
       } else if (j >= 32) {
-        unsigned long long* buf = xbuf + parity * 2 * bd;
-        buf[i] = k0;
-        buf[i + bd] = k1;
+        K* buf = xbuf + parity * R * bd;
+#pragma unroll
+        for (int r = 0; r < R; ++r) buf[i + r * bd] = kv[r];
         __syncthreads();
-        const unsigned long long o0 = buf[i ^ j], o1 = buf[(i + bd) ^ j];
+#pragma unroll
+        for (int r = 0; r < R; ++r) kv[r] = pick(kv[r], buf[(i + r * bd) ^ j], i + r * bd, k, j);
         parity ^= 1;
-        k0 = cmpx(k0, o0, i, k, j);
-        k1 = cmpx(k1, o1, i + bd, k, j);
       } else {
-        const unsigned long long o0 = __shfl_xor_sync(MN_FULL_MASK, k0, j);
-        const unsigned long long o1 = __shfl_xor_sync(MN_FULL_MASK, k1, j);
-        k0 = cmpx(k0, o0, i, k, j);
-        k1 = cmpx(k1, o1, i + bd, k, j);
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          kv[r] = pick(kv[r], __shfl_xor_sync(MN_FULL_MASK, kv[r], j), i + r * bd, k, j);
       }
     }
   }

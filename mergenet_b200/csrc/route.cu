@@ -189,168 +189,7 @@ __global__ void __launch_bounds__(512) route_score_kernel(
 }
 
 
-// ---------------------------------------------------------------------------
-// route_score_fast: same contract as route_score for Cm a multiple of 8.  The
-// band's raw metric rows (both parities) arrive in shared memory through
-// cp.async in one shot; receivers are normalised from there into fp32 rows,
-// and each warp scores four donors at a time with eight lanes per donor
-// (Cm / 8 channels per lane, three-step shuffle reductions).
-// ---------------------------------------------------------------------------
 constexpr int kMaxKc = 16;
-
-template <int MDT, int CPL>
-__global__ void __launch_bounds__(512) route_score_fast_kernel(
-    const typename Elem<MDT>::T* __restrict__ metrics, const int32_t* __restrict__ table, int B, int T, int grid_w,
-    int half, int kc, int kin, Banding band, float tau1, RouteWs ws, int* status) {
-  using ET = typename Elem<MDT>::T;
-  constexpr int Cm = 8 * CPL;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ float red[64];
-  const int l = blockIdx.y;
-  const int b = blockIdx.x / band.bands;
-  const int bi = blockIdx.x % band.bands;
-  const int q = l & 1;
-  const int dp = q ? 0 : 1, rp = 1 - dp;
-  const ParityTables pt = parity_tables(table, half, kc, kin, q);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  const int grp = lane >> 3, sl = lane & 7;
-  const int grid_h = (2 * half) / grid_w;
-  const int r0 = bi * band.rows, r1 = min(grid_h, r0 + band.rows);
-  const int p_lo = r0 * grid_w, p_hi = r1 * grid_w;
-  const int d_lo = (p_lo - dp + 1) >> 1, d_hi = (p_hi - dp + 1) >> 1;
-  const int rr0 = max(0, r0 - band.radius_rows), rr1 = min(grid_h, r1 + band.radius_rows);
-  const int s_lo = (rr0 * grid_w - rp + 1) >> 1, s_hi = (rr1 * grid_w - rp + 1) >> 1;
-  const int t_lo = 1 + rr0 * grid_w, t_hi = 1 + rr1 * grid_w;  // raw token rows held
-  ET* raw = reinterpret_cast<ET*>(smem_raw);
-  const size_t raw_bytes = (((size_t)(t_hi - t_lo) * Cm * sizeof(ET)) + 15) & ~size_t(15);
-  float* nrm = reinterpret_cast<float*>(smem_raw + raw_bytes);  // [s_hi - s_lo][Cm]
-
-  const ET* mbase = metrics + ((int64_t)l * B + b) * (int64_t)T * Cm;
-  {
-    const uint32_t sb = static_cast<uint32_t>(__cvta_generic_to_shared(raw));
-    const char* src = reinterpret_cast<const char*>(mbase + (int64_t)t_lo * Cm);
-    const int nvec = (int)(((size_t)(t_hi - t_lo) * Cm * sizeof(ET)) / 16);
-    for (int i = threadIdx.x; i < nvec; i += blockDim.x)
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sb + 16u * i), "l"(src + 16 * (int64_t)i)
-                   : "memory");
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-  }
-  __syncthreads();
-
-  auto load_norm = [&](int token, float* v) {  // this lane's CPL channels, normalised
-    const ET* row = raw + (int64_t)(token - t_lo) * Cm + sl * CPL;
-    constexpr int VB = CPL * (int)sizeof(ET);  // bytes of this lane's slice
-    if (VB % 16 == 0) {
-#pragma unroll
-      for (int w = 0; w < VB / 16; ++w) {
-        const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(row) + 16 * w);
-        const ET* e = reinterpret_cast<const ET*>(&u);
-#pragma unroll
-        for (int i = 0; i < 16 / (int)sizeof(ET); ++i) v[w * (16 / (int)sizeof(ET)) + i] = to_f32(e[i]);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < CPL; ++i) v[i] = to_f32(row[i]);
-    }
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < CPL; ++i) ss = fmaf(v[i], v[i], ss);
-    ss += __shfl_xor_sync(MN_FULL_MASK, ss, 1);
-    ss += __shfl_xor_sync(MN_FULL_MASK, ss, 2);
-    ss += __shfl_xor_sync(MN_FULL_MASK, ss, 4);
-    const float nr = fmaxf(sqrtf(ss), 1e-6f);
-#pragma unroll
-    for (int i = 0; i < CPL; ++i) v[i] = v[i] / nr;
-  };
-
-  // receivers -> normalised fp32 rows
-  for (int s0 = s_lo + warp * 4; s0 < s_hi; s0 += nwarps * 4) {
-    const int s = s0 + grp;
-    const bool live = s < s_hi;
-    float v[CPL];
-    load_norm(live ? 1 + 2 * s + rp : t_lo, v);
-    if (live) {
-      float* dst = nrm + (int64_t)(s - s_lo) * Cm + sl * CPL;
-#pragma unroll
-      for (int i = 0; i < CPL; ++i) dst[i] = v[i];
-    }
-  }
-  __syncthreads();
-
-  float emin = INFINITY, emax = -INFINITY;
-  const int64_t lb = (int64_t)l * B + b;
-  float* sc_out = ws.assign + lb * half * kc;
-  float* e_out = ws.energy + lb * half;
-  const bool unit_tau = tau1 == 1.0f;
-  for (int d0 = d_lo + warp * 4; d0 < d_hi; d0 += nwarps * 4) {
-    const int d = d0 + grp;
-    const bool live = d < d_hi;
-    float a[CPL];
-    load_norm(live ? 1 + 2 * d + dp : t_lo, a);
-    const int32_t* srx = pt.slot_rx + (int64_t)(live ? d : d_lo) * kc;
-    int slot[kMaxKc];
-#pragma unroll
-    for (int c = 0; c < kMaxKc; ++c) slot[c] = (c < kc) ? __ldg(srx + c) : -1;  // all in flight together
-    float sc[kMaxKc];
-#pragma unroll
-    for (int c = 0; c < kMaxKc; ++c) {
-      const int s = slot[c];
-      const bool valid = live && s >= 0;
-      if (__any_sync(MN_FULL_MASK, valid)) {
-        const bool inside = valid && s >= s_lo && s < s_hi;
-        if (valid && !inside && status) atomicOr(status, MN_STATUS_TOO_MANY_EDGES);
-        const float* rv = nrm + (int64_t)((inside ? s : s_lo) - s_lo) * Cm + sl * CPL;
-        float acc = 0.f;
-        if (CPL % 4 == 0) {
-#pragma unroll
-          for (int w = 0; w < CPL / 4; ++w) {
-            const float4 r4 = *reinterpret_cast<const float4*>(rv + 4 * w);
-            acc = fmaf(a[4 * w], r4.x, acc);
-            acc = fmaf(a[4 * w + 1], r4.y, acc);
-            acc = fmaf(a[4 * w + 2], r4.z, acc);
-            acc = fmaf(a[4 * w + 3], r4.w, acc);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < CPL; ++i) acc = fmaf(a[i], rv[i], acc);
-        }
-        acc += __shfl_xor_sync(MN_FULL_MASK, acc, 1);
-        acc += __shfl_xor_sync(MN_FULL_MASK, acc, 2);
-        acc += __shfl_xor_sync(MN_FULL_MASK, acc, 4);
-        // logits = scores / tau1 (dtem.py:1557); exact without a division at tau1 == 1
-        sc[c] = inside ? (unit_tau ? acc : acc / tau1) : -INFINITY;
-      } else {
-        sc[c] = -INFINITY;
-      }
-    }
-    float m = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < kMaxKc; ++c) m = fmaxf(m, sc[c]);
-    float e = 0.f;
-    if (m != -INFINITY) {
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < kMaxKc; ++c)
-        if (sc[c] != -INFINITY) sum += expf(sc[c] - m);
-      e = expf(logf(sum) + m);
-    }
-    if (live) {
-      float* dst = sc_out + (int64_t)d * kc;
-#pragma unroll
-      for (int c = 0; c < kMaxKc; ++c)  // lane sl writes the slots c == sl (mod 8)
-        if ((c & 7) == sl && c < kc) dst[c] = sc[c];
-      if (sl == 0) e_out[d] = e;
-      emin = fminf(emin, e);
-      emax = fmaxf(emax, e);
-    }
-  }
-  block_minmax(emin, emax, red);
-  if (threadIdx.x == 0) {
-    float* p = ws.partials + (lb * band.bands + bi) * 2;
-    p[0] = emin;
-    p[1] = emax;
-  }
-}
 
 // ---------------------------------------------------------------------------
 // route_score_lane: the same scores with one thread per donor.  The band's
@@ -497,11 +336,15 @@ __global__ void __launch_bounds__(kLaneScoreThreads, 2) route_score_lane_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// route_select: one CTA per (image, layer).  Global ThreTopK range over the
-// whole batch for this layer (thetopk.py:12-13), per-row threshold, then the
-// masked softmax x row k-hot and the clamp-normalise (dtem.py:1568-1579).
+// route_select: one CTA per (image, layer), kSelectThreads threads.  Global
+// ThreTopK range over the whole batch for this layer (thetopk.py:12-13), the
+// per-row threshold (block-wide, keys sorted in registers), then the masked
+// softmax x row k-hot and the clamp-normalise of every donor row
+// (dtem.py:1568-1579), with the row's slots in registers.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) route_select_kernel(
+constexpr int kSelectThreads = 256;
+
+__global__ void __launch_bounds__(kSelectThreads) route_select_kernel(
     const int32_t* __restrict__ table, int B, int half, int kc, int kin, int bands,
     KBudget kb, float tau2, RouteWs ws, int* status) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -529,53 +372,107 @@ __global__ void __launch_bounds__(512) route_select_kernel(
   const float* e = ws.energy + lb * half;
   for (int d = threadIdx.x; d < half; d += blockDim.x) xrow[d] = e[d] / range * tau2;
   __syncthreads();
-  const int k = kb.v[l];
-  const float lam = thre_topk_lambda(xrow, half, np, k, rs);
+  const float lam = thre_topk_lambda(xrow, half, np, kb.v[l], rs);
 
   float* asg = ws.assign + lb * half * kc;
   float* asum = ws.asum + lb * half;
   for (int d = threadIdx.x; d < half; d += blockDim.x) {
     float* row = asg + (int64_t)d * kc;
     const int32_t* srx = pt.slot_rx + (int64_t)d * kc;
-    int cnt = 0;
-    float m = -INFINITY;
-    for (int c = 0; c < kc; ++c) {
-      if (srx[c] < 0) break;
-      ++cnt;
-      m = fmaxf(m, row[c]);
+    float sc[kMaxKc];
+    int sl[kMaxKc];
+#pragma unroll
+    for (int c = 0; c < kMaxKc; ++c) {  // every load in flight before any use
+      sc[c] = c < kc ? row[c] : -INFINITY;
+      sl[c] = c < kc ? __ldg(srx + c) : -1;
     }
-    if (cnt == 0) { asum[d] = 0.f; continue; }
+    int cnt = 0;  // legal slots come first (the compact table's order)
+#pragma unroll
+    for (int c = 0; c < kMaxKc; ++c)
+      if (cnt == c && sl[c] >= 0) ++cnt;
+    if (cnt == 0) {
+      asum[d] = 0.f;
+      continue;
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kMaxKc; ++c)
+      if (c < cnt) m = fmaxf(m, sc[c]);
     const float y = thre_topk_map(xrow[d], lam);  // row k-hot (valid row)
     float sum = 0.f;
-    for (int c = 0; c < cnt; ++c) sum += expf(row[c] - m);
+#pragma unroll
+    for (int c = 0; c < kMaxKc; ++c)
+      if (c < cnt) sum += expf(sc[c] - m);
     const float inv = 1.0f / sum;
-    float khot[32];
     float ks = 0.f;
-    for (int c = 0; c < cnt; ++c) {
-      float p = expf(row[c] - m) * inv;
-      khot[c] = p * y;
-      ks += khot[c];
+#pragma unroll
+    for (int c = 0; c < kMaxKc; ++c) {
+      if (c < cnt) {
+        sc[c] = (expf(sc[c] - m) * inv) * y;  // khot
+        ks += sc[c];
+      }
     }
     const float tmp = fmaxf(ks - 1.0f, 0.0f) + 1.0f;
     float as = 0.f;
-    for (int c = 0; c < cnt; ++c) {
-      float v = khot[c] / tmp;
-      row[c] = v;
-      as += v;
+#pragma unroll
+    for (int c = 0; c < kMaxKc; ++c) {
+      if (c < kc) {
+        const float v = c < cnt ? sc[c] / tmp : 0.f;
+        row[c] = v;
+        as += v;
+      }
     }
-    for (int c = cnt; c < kc; ++c) row[c] = 0.f;
     asum[d] = as;
   }
 }
 
 // ---------------------------------------------------------------------------
-// route_mass: one CTA per image.  Mass and centre-of-mass chain over the
-// layers (dtem.py:1978-1983, :2016-2025, :2027-2044, interleave :2196-2222),
-// then the exact top-k by mass and the centre-of-mass ordering
-// (model.py:1167-1171).  Also records the per-layer scalars the feature
-// transport needs.
+// route_mass: one CTA per image, kMassThreads threads.  Mass and
+// centre-of-mass chain over the layers (dtem.py:1978-1983, :2016-2025,
+// :2027-2044, interleave :2196-2222), then the exact top-k by mass and the
+// centre-of-mass ordering (model.py:1167-1171).  A receiver's update reads
+// only its own state and its donors' old masses and centres, and a donor's
+// only its own mass, so each layer updates the receivers in place, then
+// (after a barrier) the donors.  It also writes the coefficients of the
+// feature transport.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(512, 2) route_mass_kernel(
+constexpr int kMassThreads = 512;
+
+__host__ __device__ inline size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
+__host__ __device__ inline size_t mass_smem_bytes(int T, int k) {
+  const int np = next_pow2(T - 1), nk = next_pow2(k);
+  const int nx = np > kMassThreads ? np : kMassThreads;
+  return align16((size_t)2 * T * 4) + (size_t)(np + nk) * 8 + (size_t)2 * nx * 8;
+}
+
+// Sort the n keys key_of(0 .. n-1) (n a power of two <= R * bd) into out[0 .. n).
+template <int R, typename KeyOf>
+__device__ __forceinline__ void sort_carrier_keys(int n, int bd, KeyOf key_of, unsigned long long* out,
+                                                  unsigned long long* xbuf) {
+  unsigned long long kv[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int idx = threadIdx.x + r * bd;
+    kv[r] = idx < n ? key_of(idx) : ~0ull;
+  }
+  bitonic_sort_regs<R>(kv, xbuf, n);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int idx = threadIdx.x + r * bd;
+    if (idx < n) out[idx] = kv[r];
+  }
+}
+template <typename KeyOf>
+__device__ __forceinline__ void sort_carrier_keys_any(int n, int bd, KeyOf key_of, unsigned long long* out,
+                                                      unsigned long long* xbuf) {
+  const int r = n > bd ? n / bd : 1;
+  if (r == 1) sort_carrier_keys<1>(n, bd, key_of, out, xbuf);
+  else if (r == 2) sort_carrier_keys<2>(n, bd, key_of, out, xbuf);
+  else if (r == 4) sort_carrier_keys<4>(n, bd, key_of, out, xbuf);
+  else sort_carrier_keys<8>(n, bd, key_of, out, xbuf);
+}
+
+__global__ void __launch_bounds__(kMassThreads, 2) route_mass_kernel(
     const int32_t* __restrict__ table, int B, int T, int half, int kc, int kin, int L, int k,
     int write_stencil, RouteWs ws, float* __restrict__ size_out, float* __restrict__ center_out,
     float* __restrict__ topk_size, int64_t* __restrict__ topk_idx) {
@@ -583,8 +480,10 @@ __global__ void __launch_bounds__(512, 2) route_mass_kernel(
   float* size = reinterpret_cast<float*>(smem_raw);  // [T]
   float* center = size + T;                          // [T]
   const int P = T - 1;
-  const int np = next_pow2(P);
-  unsigned long long* keys = reinterpret_cast<unsigned long long*>(center + T);  // 8T bytes above base
+  const int np = next_pow2(P), nk = next_pow2(k);
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw + align16((size_t)2 * T * 4));
+  unsigned long long* keys2 = keys + np;
+  unsigned long long* xbuf = keys2 + nk;  // exchange buffers of the sorts
   const int b = blockIdx.x;
   const float eps = 1.1920928955078125e-07f;  // torch.finfo(float32).eps
 
@@ -599,25 +498,24 @@ __global__ void __launch_bounds__(512, 2) route_mass_kernel(
     const int64_t lb = (int64_t)l * B + b;
     const float* asg = ws.assign + lb * half * kc;
     const float* asum = ws.asum + lb * half;
-    float* wa_rec = ws.wa_old + lb * half;
-    float* wb_rec = ws.wb_old + lb * half;
-    float* ws_rec = ws.wb_safe + lb * half;
-    // new values computed from the old state, written after a barrier
-    float nv_b[4], nc_b[4], nv_a[4];
-    int cnt = 0;
-    for (int i = threadIdx.x; i < half; i += blockDim.x, ++cnt) {
+    // receivers, in place (they read donors' old masses and centres only)
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
       const int tb = 1 + 2 * i + rp;
       const float wb = size[tb], cb = center[tb];
       float contrib = 0.f, ccontrib = 0.f;
       const int32_t* in = pt.rx_in + (int64_t)i * kin;
-      // the in-edges' assignment weights, all loads in flight before the
-      // sums (which keep the reference's sequential order)
-      int ev[kMaxKin];
-      float wv[kMaxKin];
+      const int32_t* off = pt.rx_off + (int64_t)i * kin;
+      // the in-edges in the reference's sequential scatter order; with up to
+      // kMaxKin of them every load is in flight before the sums
       const bool fast_in = kin <= kMaxKin;
+      int ev[kMaxKin], ov[kMaxKin];
+      float wv[kMaxKin];
       if (fast_in) {
 #pragma unroll
-        for (int j = 0; j < kMaxKin; ++j) ev[j] = j < kin ? __ldg(in + j) : -1;
+        for (int j = 0; j < kMaxKin; ++j) {
+          ev[j] = j < kin ? __ldg(in + j) : -1;
+          ov[j] = (write_stencil && j < kin) ? __ldg(off + j) : -1;
+        }
 #pragma unroll
         for (int j = 0; j < kMaxKin; ++j) wv[j] = ev[j] >= 0 ? __ldg(asg + ev[j]) : 0.f;
 #pragma unroll
@@ -630,12 +528,11 @@ __global__ void __launch_bounds__(512, 2) route_mass_kernel(
         }
       } else {
         for (int j = 0; j < kin; ++j) {
-          int e = in[j];
+          const int e = __ldg(in + j);
           if (e < 0) break;
-          int d = e / kc;
-          float w = asg[e];
-          int ta = 1 + 2 * d + dp;
-          float wa = size[ta];
+          const float w = __ldg(asg + e);
+          const int ta = 1 + 2 * (e / kc) + dp;
+          const float wa = size[ta];
           contrib = __fadd_rn(contrib, __fmul_rn(w, wa));
           ccontrib = __fadd_rn(ccontrib, __fmul_rn(w, __fmul_rn(wa, center[ta])));
         }
@@ -644,55 +541,46 @@ __global__ void __launch_bounds__(512, 2) route_mass_kernel(
       const float wsafe = fmaxf(wbn, eps);
       if (write_stencil) {
         // x_s <- alpha * x_s + sum_j c_j * x_dj, the same update scaled by
-        // 1 / wb_safe once per coefficient instead of once per channel
-        float* cf = ws.cf + (lb * half + i) * kStencilSlots;
-        float slots[kStencilSlots];
+        // 1 / wb_safe once per coefficient instead of once per channel.
+        // Chunk-major: slot u of receiver i at ((lb * 4 + u / 4) * half + i) * 4 + u % 4;
+        // absent slots are zero (written first, then the present edges).
+        float* cf = ws.cf + (lb * 4 * half + i) * 4;
+        auto cf_slot = [&](int u) -> float* { return cf + (int64_t)(u >> 2) * half * 4 + (u & 3); };
 #pragma unroll
-        for (int u = 0; u < kStencilSlots; ++u) slots[u] = 0.f;
-        slots[0] = wb / wsafe;
-        const int32_t* off = pt.rx_off + (int64_t)i * kin;
+        for (int w = 0; w < kStencilSlots / 4; ++w)
+          *reinterpret_cast<float4*>(cf + (int64_t)w * half * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *cf_slot(0) = wb / wsafe;
         if (fast_in) {
 #pragma unroll
           for (int j = 0; j < kMaxKin; ++j) {
             if (ev[j] < 0) break;
-            const int o = __ldg(off + j);
             const float v = (wv[j] * size[1 + 2 * (ev[j] / kc) + dp]) / wsafe;
-#pragma unroll
-            for (int u = 1; u < kStencilSlots; ++u)
-              if (o == u - 1) slots[u] = v;
+            if (ov[j] >= 0 && ov[j] + 1 < kStencilSlots) *cf_slot(ov[j] + 1) = v;
           }
         } else {
           for (int j = 0; j < kin; ++j) {
-            int e = in[j];
+            const int e = __ldg(in + j);
             if (e < 0) break;
-            const int o = off[j];
-            const float v = (asg[e] * size[1 + 2 * (e / kc) + dp]) / wsafe;
-#pragma unroll
-            for (int u = 1; u < kStencilSlots; ++u)
-              if (o == u - 1) slots[u] = v;
+            const int o = __ldg(off + j);
+            const float v = (__ldg(asg + e) * size[1 + 2 * (e / kc) + dp]) / wsafe;
+            if (o >= 0 && o + 1 < kStencilSlots) *cf_slot(o + 1) = v;
           }
         }
-#pragma unroll
-        for (int u = 0; u < kStencilSlots; u += 4)
-          *reinterpret_cast<float4*>(cf + u) = make_float4(slots[u], slots[u + 1], slots[u + 2], slots[u + 3]);
+      } else {
+        // the table-driven transport reads the old masses of both sides
+        ws.wb_old[lb * half + i] = wb;
+        ws.wb_safe[lb * half + i] = wsafe;
+        ws.wa_old[lb * half + i] = size[1 + 2 * i + dp];  // donor i, not yet updated
       }
-      nv_b[cnt] = wbn;
-      nc_b[cnt] = __fdiv_rn(__fadd_rn(__fmul_rn(wb, cb), ccontrib), wsafe);
-      wb_rec[i] = wb;
-      ws_rec[i] = wsafe;
-      // donor i of this layer
-      const int ta = 1 + 2 * i + dp;
-      const float wa = size[ta];
-      wa_rec[i] = wa;
-      const float tmp = __fsub_rn(1.0f, asum[i]);
-      nv_a[cnt] = __fmul_rn(wa, fminf(fmaxf(tmp, 0.f), 1.f));
+      size[tb] = wbn;
+      center[tb] = __fdiv_rn(__fadd_rn(__fmul_rn(wb, cb), ccontrib), wsafe);
     }
     __syncthreads();
-    cnt = 0;
-    for (int i = threadIdx.x; i < half; i += blockDim.x, ++cnt) {
-      size[1 + 2 * i + rp] = nv_b[cnt];
-      center[1 + 2 * i + rp] = nc_b[cnt];
-      size[1 + 2 * i + dp] = nv_a[cnt];
+    // donors (their own old mass and assignment row sum only)
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+      const int ta = 1 + 2 * i + dp;
+      const float tmp = __fsub_rn(1.0f, __ldg(asum + i));
+      size[ta] = __fmul_rn(size[ta], fminf(fmaxf(tmp, 0.f), 1.f));
     }
     if (threadIdx.x == 0) center[0] = 0.f;  // CLS centre after the first layer
     __syncthreads();
@@ -702,44 +590,22 @@ __global__ void __launch_bounds__(512, 2) route_mass_kernel(
     center_out[(int64_t)b * T + t] = center[t];
   }
   // exact top-k by (mass desc, patch asc): key = (~bits(mass) << 32) | patch
-  const int nk = next_pow2(k);
-  unsigned long long* keys2 = keys + np;
-  unsigned long long* xbuf = keys2 + nk;  // [2][blockDim.x] exchange buffers
   auto mass_key = [&](int i) -> unsigned long long {
     if (i >= P) return ~0ull;
     const unsigned int bits = __float_as_uint(size[1 + i]);
     return ((unsigned long long)(~bits) << 32) | (unsigned int)i;
   };
+  const int bd = blockDim.x;
+  sort_carrier_keys_any(np, bd, mass_key, keys, xbuf);
+  __syncthreads();
   // re-key the k winners by (centre asc, patch asc); centres are >= 0
-  auto centre_key = [&](unsigned long long mk) -> unsigned long long {
-    const unsigned int p = (unsigned int)(mk & 0xffffffffu);
+  auto centre_key = [&](int i) -> unsigned long long {
+    if (i >= k) return ~0ull;
+    const unsigned int p = (unsigned int)(keys[i] & 0xffffffffu);
     return ((unsigned long long)__float_as_uint(center[1 + p]) << 32) | p;
   };
-  if (np <= 2 * (int)blockDim.x && nk <= (int)blockDim.x) {
-    // keys in registers: shuffles inside a warp, one barrier per wider step
-    const int bd = blockDim.x, t = threadIdx.x;
-    if (np <= bd) {
-      const unsigned long long mk = bitonic_sort_u64_reg(mass_key(t), xbuf, np);
-      if (t < np) keys[t] = mk;
-    } else {
-      unsigned long long k0 = mass_key(t), k1 = mass_key(t + bd);
-      bitonic_sort_u64_reg2(k0, k1, xbuf, np);
-      keys[t] = k0;
-      keys[t + bd] = k1;
-    }
-    __syncthreads();
-    const unsigned long long ck = (int)threadIdx.x < k ? centre_key(keys[threadIdx.x]) : ~0ull;
-    const unsigned long long sk = bitonic_sort_u64_reg(ck, xbuf, nk);
-    if ((int)threadIdx.x < nk) keys2[threadIdx.x] = sk;
-    __syncthreads();
-  } else {
-    for (int i = threadIdx.x; i < np; i += blockDim.x) keys[i] = mass_key(i);
-    __syncthreads();
-    bitonic_sort_u64(keys, np);
-    for (int i = threadIdx.x; i < nk; i += blockDim.x) keys2[i] = i < k ? centre_key(keys[i]) : ~0ull;
-    __syncthreads();
-    bitonic_sort_u64(keys2, nk);
-  }
+  sort_carrier_keys_any(nk, bd, centre_key, keys2, xbuf);
+  __syncthreads();
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
     unsigned int p = (unsigned int)(keys2[i] & 0xffffffffu);
     topk_idx[(int64_t)b * k + i] = p;
@@ -881,20 +747,32 @@ __global__ void __launch_bounds__(256) route_transport_kernel(
 // route_transport_stencil: the same per-layer update for even-width grids,
 // where receivers fill whole grid columns and a receiver's donors sit at odd
 // column offsets dx in {-3,-1,1,3} and |dy| <= DY1 (|dx| = 1) or DY3
-// (|dx| = 3).  A thread owns 4 channels of one receiver column and walks its
-// rows with a sliding window of the two neighbouring donor columns, so every
-// donor value it loads serves 2*DY1+1 receivers.  The coefficients
-// (alpha = wb_old / wb_safe, c = assign * wa_old / wb_safe) come from
-// route_mass in stencil order.
+// (|dx| = 3).  The coefficients (alpha = wb_old / wb_safe, c = assign *
+// wa_old / wb_safe) come from route_mass in stencil order, chunk-major: the
+// 16-byte chunk w of receiver s at ((layer * B + b) * 4 + w) * half + s, so
+// the chunks a warp reads for consecutive receivers are contiguous.
+//
+// The kernel is bound by the L1 data pipe (shared-memory wavefronts), so the
+// work is shaped for reuse per shared-memory load: a thread owns 4 channels
+// of a PAIR of receiver columns c and c + 2 and walks their rows with a
+// sliding window over the three donor columns c - 1, c + 1, c + 3.  Every
+// window value it loads serves 2 * DY1 + 1 rows, and the middle column serves
+// both receivers; column c + 3 also gives c its dx = +3 donors and c - 1
+// gives c + 2 its dx = -3 donors, so only c - 3 and c + 5 are extra loads.
+// The next row's coefficient lines are prefetched into L1 one row ahead.
 // ---------------------------------------------------------------------------
+constexpr int kPairThreads = 256;
+constexpr int kPairSplits = 4;
+
 template <typename XT, int CT, int DY1, int DY3>
-__global__ void __launch_bounds__(448, 2) route_transport_stencil_kernel(
+__global__ void __launch_bounds__(kPairThreads, 2) route_transport_stencil_kernel(
     const XT* __restrict__ x, int B, int T, int C, int grid_h, int grid_w, int half, int L, int k,
     int row_splits, RouteWs ws, XT* __restrict__ topk_x) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* tile = reinterpret_cast<float*>(smem_raw);  // [T][CT]
   constexpr int G = CT / 4;                           // float4 channel groups
   constexpr int NW = 2 * DY1 + 1;                     // window rows
+  static_assert(DY3 <= DY1, "the dx = 3 donors of one column lie inside the next pair column's window");
   const int b = blockIdx.x;
   const int c0 = blockIdx.y * CT;
   const XT* xb = x + (int64_t)b * T * C;
@@ -903,76 +781,113 @@ __global__ void __launch_bounds__(448, 2) route_transport_stencil_kernel(
   for (int i = threadIdx.x; i < CT; i += blockDim.x) zrow[i] = 0.f;
   __syncthreads();
   const int half_w = grid_w >> 1;
+  const int npairs = (half_w + 1) >> 1;
   const int g = threadIdx.x % G;
-  const int cr = (threadIdx.x / G) % half_w;
-  const int rs = threadIdx.x / (G * half_w);
+  const int pr = (threadIdx.x / G) % npairs;
+  const int rs = threadIdx.x / (G * npairs);
   const bool active = rs < row_splits;
   const int rows_per = (grid_h + row_splits - 1) / row_splits;
-  const int r_begin = rs * rows_per, r_end = min(grid_h, r_begin + rows_per);
+  const int r_begin = rs * rows_per, r_end = active ? min(grid_h, r_begin + rows_per) : r_begin;
   const int rstride = grid_w * CT;  // floats between grid rows
-  // acc (two float2 halves) += w * v, in the order of the scalar form
+  const float* zero4 = zrow + 4 * g;
+  const int64_t cf_chunk = (int64_t)half * 4;  // floats between chunks w and w + 1
+  // acc (two float2 halves) += w * v
   auto fma4 = [](float w, float4 v, float2& lo, float2& hi) {
     const float2 ww = make_float2(w, w);
     lo = ffma2(ww, make_float2(v.x, v.y), lo);
     hi = ffma2(ww, make_float2(v.z, v.w), hi);
   };
   for (int l = 0; l < L; ++l) {
-    const int rp = (l & 1) ? 1 : 0;  // receiver patch parity = column parity
-    const int c = 2 * cr + rp;
-    const float* cfl = ws.cf + ((int64_t)l * B + b) * half * kStencilSlots;
-    if (active && r_begin < r_end) {
-      // donor columns c -/+ 1 (window) and c -/+ 3; a column outside the grid
-      // reads as zero (its coefficients are zero too)
-      const bool okl = c >= 1, okr = c + 1 < grid_w, okl3 = c >= 3, okr3 = c + 3 < grid_w;
-      const float* colm1 = tile + (1 + (okl ? c - 1 : c)) * CT + 4 * g;
-      const float* colp1 = tile + (1 + (okr ? c + 1 : c)) * CT + 4 * g;
-      const float* colm3 = tile + (1 + (okl3 ? c - 3 : c)) * CT + 4 * g;
-      const float* colp3 = tile + (1 + (okr3 ? c + 3 : c)) * CT + 4 * g;
-      // an out-of-grid neighbour reads the zero row: an address select, not
-      // a predicated load and a select per component
-      const float* zero4 = zrow + 4 * g;
-      auto ldc = [&](const float* col, bool ok, int r) -> float4 {
-        const float* src = (ok && (unsigned)r < (unsigned)grid_h) ? col + r * rstride : zero4;
-        return *reinterpret_cast<const float4*>(src);
-      };
-      float4 wl[NW], wr[NW];
-      // window slot (ph + u) % NW holds grid row r - DY1 + u while row r is
-      // processed at unrolled phase ph; the row loop advances NW rows at a time
+    const int rp = l & 1;       // receiver patch parity = column parity
+    const int ca = 4 * pr + rp;  // the pair's columns ca and cb = ca + 2
+    const int cb = ca + 2;
+    const bool has_b = cb < grid_w;
+    // a column outside the grid reads the zero row (its coefficients are zero)
+    auto colp = [&](int c) -> const float* {
+      return (c >= 0 && c < grid_w) ? tile + (1 + c) * CT + 4 * g : nullptr;
+    };
+    const float* w0 = colp(ca - 1);
+    const float* w1 = colp(ca + 1);
+    const float* w2 = colp(ca + 3);
+    const float* e0 = colp(ca - 3);
+    const float* e1 = colp(ca + 5);
+    auto ldc = [&](const float* col, int r) -> float4 {
+      const float* src = (col != nullptr && (unsigned)r < (unsigned)grid_h) ? col + r * rstride : zero4;
+      return *reinterpret_cast<const float4*>(src);
+    };
+    const float* cfl = ws.cf + ((int64_t)l * B + b) * 4 * cf_chunk;
+    // coefficients of row r for both receivers (chunk-major, 16 bytes each)
+    auto load_cf = [&](int r, float4* qa, float4* qb) {
+      const int sa = (r * grid_w + ca) >> 1;  // receiver of column ca; cb's is sa + 1
 #pragma unroll
-      for (int u = 0; u < NW - 1; ++u) {
-        wl[u] = ldc(colm1, okl, r_begin - DY1 + u);
-        wr[u] = ldc(colp1, okr, r_begin - DY1 + u);
+      for (int w = 0; w < 4; ++w) {
+        qa[w] = __ldg(reinterpret_cast<const float4*>(cfl + w * cf_chunk + (int64_t)sa * 4));
+        qb[w] = has_b ? __ldg(reinterpret_cast<const float4*>(cfl + w * cf_chunk + (int64_t)(sa + 1) * 4))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      for (int rb = r_begin; rb < r_end; rb += NW) {
+    };
+    float4 v0[NW], v1[NW], v2[NW];
 #pragma unroll
-        for (int ph = 0; ph < NW; ++ph) {
-          const int r = rb + ph;
-          if (r < r_end) {
-            wl[(ph + NW - 1) % NW] = ldc(colm1, okl, r + DY1);
-            wr[(ph + NW - 1) % NW] = ldc(colp1, okr, r + DY1);
-            const int s = (r * grid_w + c) >> 1;
-            const float4* cfp = reinterpret_cast<const float4*>(cfl + (int64_t)s * kStencilSlots);
-            const float4 q0 = __ldg(cfp), q1 = __ldg(cfp + 1), q2 = __ldg(cfp + 2), q3 = __ldg(cfp + 3);
-            const float cw[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
-                                  q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
-            float4* own = reinterpret_cast<float4*>(tile + (1 + r * grid_w + c) * CT + 4 * g);
-            const float4 xo = *own;
-            float2 lo = make_float2(cw[0] * xo.x, cw[0] * xo.y), hi = make_float2(cw[0] * xo.z, cw[0] * xo.w);
-            int j = 1;
-            if (DY3 >= 0) {
+    for (int u = 0; u < NW - 1; ++u) {
+      v0[u] = ldc(w0, r_begin - DY1 + u);
+      v1[u] = ldc(w1, r_begin - DY1 + u);
+      v2[u] = ldc(w2, r_begin - DY1 + u);
+    }
+    for (int rb = r_begin; rb < r_end; rb += NW) {
 #pragma unroll
-              for (int dy = -DY3; dy <= DY3; ++dy) fma4(cw[j++], ldc(colm3, okl3, r + dy), lo, hi);
+      for (int ph = 0; ph < NW; ++ph) {
+        const int r = rb + ph;
+        if (r < r_end) {
+          const int sa = (r * grid_w + ca) >> 1;  // receiver of column ca; cb's is sa + 1
+          if (r + 1 < r_end && g < 4)  // next row's chunk g of both receivers -> L1
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(cfl + g * cf_chunk + (int64_t)(sa + half_w) * 4));
+          float4 qa[4], qb[4];
+          load_cf(r, qa, qb);
+          v0[(ph + NW - 1) % NW] = ldc(w0, r + DY1);
+          v1[(ph + NW - 1) % NW] = ldc(w1, r + DY1);
+          v2[(ph + NW - 1) % NW] = ldc(w2, r + DY1);
+          const float cwa[16] = {qa[0].x, qa[0].y, qa[0].z, qa[0].w, qa[1].x, qa[1].y, qa[1].z, qa[1].w,
+                                 qa[2].x, qa[2].y, qa[2].z, qa[2].w, qa[3].x, qa[3].y, qa[3].z, qa[3].w};
+          const float cwb[16] = {qb[0].x, qb[0].y, qb[0].z, qb[0].w, qb[1].x, qb[1].y, qb[1].z, qb[1].w,
+                                 qb[2].x, qb[2].y, qb[2].z, qb[2].w, qb[3].x, qb[3].y, qb[3].z, qb[3].w};
+          float4* own_a = reinterpret_cast<float4*>(tile + (1 + r * grid_w + ca) * CT + 4 * g);
+          float4* own_b = reinterpret_cast<float4*>(tile + (1 + r * grid_w + (has_b ? cb : ca)) * CT + 4 * g);
+          const float4 xa = *own_a, xbv = *own_b;
+          float2 la = make_float2(cwa[0] * xa.x, cwa[0] * xa.y), ha = make_float2(cwa[0] * xa.z, cwa[0] * xa.w);
+          float2 lb = make_float2(cwb[0] * xbv.x, cwb[0] * xbv.y), hb = make_float2(cwb[0] * xbv.z, cwb[0] * xbv.w);
+          int j = 1;
+          // column ca: dx = -3 (extra column), -1 (v0), +1 (v1), +3 (v2 rows |dy| <= DY3)
+          // column cb: dx = -3 (v0 rows |dy| <= DY3), -1 (v1), +1 (v2), +3 (extra column)
+          if (DY3 >= 0) {
+#pragma unroll
+            for (int dy = -DY3; dy <= DY3; ++dy) {
+              fma4(cwa[j], ldc(e0, r + dy), la, ha);
+              fma4(cwb[j], v0[(ph + DY1 + dy) % NW], lb, hb);
+              ++j;
             }
-#pragma unroll
-            for (int u = 0; u < NW; ++u) fma4(cw[j++], wl[(ph + u) % NW], lo, hi);
-#pragma unroll
-            for (int u = 0; u < NW; ++u) fma4(cw[j++], wr[(ph + u) % NW], lo, hi);
-            if (DY3 >= 0) {
-#pragma unroll
-              for (int dy = -DY3; dy <= DY3; ++dy) fma4(cw[j++], ldc(colp3, okr3, r + dy), lo, hi);
-            }
-            *own = make_float4(lo.x, lo.y, hi.x, hi.y);
           }
+#pragma unroll
+          for (int u = 0; u < NW; ++u) {
+            fma4(cwa[j], v0[(ph + u) % NW], la, ha);
+            fma4(cwb[j], v1[(ph + u) % NW], lb, hb);
+            ++j;
+          }
+#pragma unroll
+          for (int u = 0; u < NW; ++u) {
+            fma4(cwa[j], v1[(ph + u) % NW], la, ha);
+            fma4(cwb[j], v2[(ph + u) % NW], lb, hb);
+            ++j;
+          }
+          if (DY3 >= 0) {
+#pragma unroll
+            for (int dy = -DY3; dy <= DY3; ++dy) {
+              fma4(cwa[j], v2[(ph + DY1 + dy) % NW], la, ha);
+              fma4(cwb[j], ldc(e1, r + dy), lb, hb);
+              ++j;
+            }
+          }
+          *own_a = make_float4(la.x, la.y, ha.x, ha.y);
+          if (has_b) *own_b = make_float4(lb.x, lb.y, hb.x, hb.y);
         }
       }
     }
@@ -1012,7 +927,7 @@ extern "C" size_t mn_route_workspace_bytes(const mn_route_dims* dims, int batch,
 }
 
 template <typename XT>
-static void launch_transport(const void* x, const int32_t* table, int B, int T, int C, int half, int kc,
+static bool launch_transport(const void* x, const int32_t* table, int B, int T, int C, int half, int kc,
                              int kin, int L, int k, const RouteWs& ws, void* topk_x, int ct,
                              cudaStream_t st) {
   size_t smem = (size_t)T * ct * sizeof(float);
@@ -1020,22 +935,23 @@ static void launch_transport(const void* x, const int32_t* table, int B, int T, 
   const XT* xp = static_cast<const XT*>(x);
   XT* op = static_cast<XT*>(topk_x);
   if (ct == 32) {
-    cudaFuncSetAttribute(route_transport_kernel<XT, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (!ensure_smem(route_transport_kernel<XT, 32>, smem)) return false;
     route_transport_kernel<XT, 32><<<grid, 256, smem, st>>>(xp, table, B, T, C, half, kc, kin, L, k, ws, op);
   } else if (ct == 16) {
-    cudaFuncSetAttribute(route_transport_kernel<XT, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (!ensure_smem(route_transport_kernel<XT, 16>, smem)) return false;
     route_transport_kernel<XT, 16><<<grid, 256, smem, st>>>(xp, table, B, T, C, half, kc, kin, L, k, ws, op);
   } else {
-    cudaFuncSetAttribute(route_transport_kernel<XT, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (!ensure_smem(route_transport_kernel<XT, 8>, smem)) return false;
     route_transport_kernel<XT, 8><<<grid, 256, smem, st>>>(xp, table, B, T, C, half, kc, kin, L, k, ws, op);
   }
+  return true;
 }
 
 // Which compiled stencil fits the geometry: 1 = (DY1 2, DY3 0) radius 3,
 // 2 = (1, none) radius in [sqrt 2, sqrt 5), 3 = (0, none); 0 = generic path.
 static int stencil_variant(const mn_route_dims* d) {
-  // 8 channel groups per receiver column must fit the 448-thread launch bound
-  if (d->grid_w % 2 != 0 || (d->grid_w / 2) * 8 > 448) return 0;
+  // 8 channel groups per receiver-column pair must fit the launch bound
+  if (d->grid_w % 2 != 0 || ((d->grid_w / 2 + 1) / 2) * 8 > kPairThreads) return 0;
   if (d->stencil_dy1 == 2 && d->stencil_dy3 == 0) return 1;
   if (d->stencil_dy1 == 1 && d->stencil_dy3 == -1) return 2;
   if (d->stencil_dy1 == 0 && d->stencil_dy3 == -1) return 3;
@@ -1043,94 +959,35 @@ static int stencil_variant(const mn_route_dims* d) {
 }
 
 template <typename XT, int CT, int DY1, int DY3>
-static void launch_stencil_ct(const void* x, int B, int T, int C, const mn_route_dims* d, int L, int k,
+static bool launch_stencil_ct(const void* x, int B, int T, int C, const mn_route_dims* d, int L, int k,
                               const RouteWs& ws, void* topk_x, cudaStream_t st) {
   const int half_w = d->grid_w / 2;
-  const int per_split = (CT / 4) * half_w;
-  int splits = std::max(1, std::min(d->grid_h, 448 / per_split));  // <= the kernel's launch bound
-  splits = std::min(splits, 4);
+  const int per_split = (CT / 4) * ((half_w + 1) / 2);  // threads per row split
+  int splits = std::max(1, std::min(d->grid_h, kPairThreads / per_split));  // <= the kernel's launch bound
+  splits = std::min(splits, kPairSplits);
   const int threads = ((per_split * splits + 31) / 32) * 32;
   const size_t smem = (size_t)(T + 1) * CT * sizeof(float);  // tile + zero row
   auto kern = route_transport_stencil_kernel<XT, CT, DY1, DY3>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (!ensure_smem(kern, smem)) return false;
   kern<<<dim3(B, (C + CT - 1) / CT), threads, smem, st>>>(static_cast<const XT*>(x), B, T, C, d->grid_h,
                                                             d->grid_w, d->half, L, k, splits, ws,
                                                             static_cast<XT*>(topk_x));
+  return true;
 }
 
 template <typename XT>
-static void launch_stencil(int variant, const void* x, int B, int T, int C, const mn_route_dims* d, int L, int k,
+static bool launch_stencil(int variant, const void* x, int B, int T, int C, const mn_route_dims* d, int L, int k,
                            const RouteWs& ws, void* topk_x, cudaStream_t st) {
   const bool wide = (size_t)T * 32 * sizeof(float) <= 200 * 1024;
   if (variant == 1) {
-    if (wide) launch_stencil_ct<XT, 32, 2, 0>(x, B, T, C, d, L, k, ws, topk_x, st);
-    else launch_stencil_ct<XT, 16, 2, 0>(x, B, T, C, d, L, k, ws, topk_x, st);
+    if (wide) return launch_stencil_ct<XT, 32, 2, 0>(x, B, T, C, d, L, k, ws, topk_x, st);
+    else return launch_stencil_ct<XT, 16, 2, 0>(x, B, T, C, d, L, k, ws, topk_x, st);
   } else if (variant == 2) {
-    if (wide) launch_stencil_ct<XT, 32, 1, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
-    else launch_stencil_ct<XT, 16, 1, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
+    if (wide) return launch_stencil_ct<XT, 32, 1, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
+    else return launch_stencil_ct<XT, 16, 1, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
   } else {
-    if (wide) launch_stencil_ct<XT, 32, 0, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
-    else launch_stencil_ct<XT, 16, 0, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
-  }
-}
-
-// Banding for route_score_fast: the fewest bands whose raw rows + normalised
-// receivers fit the shared-memory budget.
-static Banding make_fast_banding(int grid_h, int grid_w, int radius_rows, int Cm, int esize, size_t* smem_out) {
-  Banding bd;
-  bd.radius_rows = radius_rows;
-  bd.cap = 0;
-  const size_t budget = 200 * 1024;
-  for (int nb = 1; nb <= grid_h; ++nb) {
-    const int rows = (grid_h + nb - 1) / nb;
-    const int need_rows = (nb == 1) ? grid_h : std::min(grid_h, rows + 2 * radius_rows);
-    const size_t raw = (((size_t)need_rows * grid_w * Cm * esize) + 15) & ~size_t(15);
-    const size_t nrm = ((size_t)(need_rows * grid_w + 1) / 2 + 1) * Cm * 4;
-    if (raw + nrm <= budget) {
-      bd.bands = (grid_h + rows - 1) / rows;
-      bd.rows = rows;
-      *smem_out = raw + nrm;
-      return bd;
-    }
-  }
-  bd.bands = -1;
-  bd.rows = 0;
-  *smem_out = 0;
-  return bd;
-}
-
-template <int MDT, int CPL>
-static void launch_score_fast_cpl(const void* metrics, const int32_t* table, int B, int T, int grid_w, int half,
-                                  int kc, int kin, const Banding& bd, size_t smem, float tau1, const RouteWs& ws, int L,
-                                  int* status, cudaStream_t st) {
-  using ET = typename Elem<MDT>::T;
-  auto kern = route_score_fast_kernel<MDT, CPL>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kern<<<dim3(B * bd.bands, L), 512, smem, st>>>(static_cast<const ET*>(metrics), table, B, T, grid_w, half, kc, kin,
-                                                 bd, tau1, ws, status);
-}
-
-// Whether route_score_fast covers the shape (and its banding).
-static bool fast_score_plan(int Cm, int kc, int grid_h, int grid_w, int radius_rows, int esize, Banding* bd,
-                            size_t* smem) {
-  if (Cm % 8 != 0 || kc > kMaxKc) return false;
-  const int cpl = Cm / 8;
-  if (cpl != 1 && cpl != 2 && cpl != 4 && cpl != 8 && cpl != 16) return false;
-  *bd = make_fast_banding(grid_h, grid_w, radius_rows, Cm, esize, smem);
-  return bd->bands > 0;
-}
-
-template <int MDT>
-static void launch_score_fast(const void* metrics, const int32_t* table, int B, int T, int Cm, int grid_w, int half,
-                              int kc, int kin, const Banding& bd, size_t smem, float tau1, const RouteWs& ws, int L,
-                              int* status, cudaStream_t st) {
-  const int cpl = Cm / 8;
-  switch (cpl) {
-    case 1: launch_score_fast_cpl<MDT, 1>(metrics, table, B, T, grid_w, half, kc, kin, bd, smem, tau1, ws, L, status, st); break;
-    case 2: launch_score_fast_cpl<MDT, 2>(metrics, table, B, T, grid_w, half, kc, kin, bd, smem, tau1, ws, L, status, st); break;
-    case 4: launch_score_fast_cpl<MDT, 4>(metrics, table, B, T, grid_w, half, kc, kin, bd, smem, tau1, ws, L, status, st); break;
-    case 8: launch_score_fast_cpl<MDT, 8>(metrics, table, B, T, grid_w, half, kc, kin, bd, smem, tau1, ws, L, status, st); break;
-    default: launch_score_fast_cpl<MDT, 16>(metrics, table, B, T, grid_w, half, kc, kin, bd, smem, tau1, ws, L, status, st); break;
+    if (wide) return launch_stencil_ct<XT, 32, 0, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
+    else return launch_stencil_ct<XT, 16, 0, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
   }
 }
 
@@ -1156,26 +1013,28 @@ static bool lane_score_plan(int Cm, int kc, int grid_h, int grid_w, int radius_r
 }
 
 template <int MDT>
-static void launch_score_lane(const void* metrics, const int32_t* table, int B, int T, int Cm, int grid_w, int half,
+static bool launch_score_lane(const void* metrics, const int32_t* table, int B, int T, int Cm, int grid_w, int half,
                               int kc, int kin, const Banding& bd, size_t smem, float tau1, const RouteWs& ws, int L,
                               int* status, cudaStream_t st) {
   using ET = typename Elem<MDT>::T;
   auto kern = Cm == 64 ? route_score_lane_kernel<MDT, 64> : route_score_lane_kernel<MDT, 32>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (!ensure_smem(kern, smem)) return false;
   kern<<<dim3(B * bd.bands, L), kLaneScoreThreads, smem, st>>>(static_cast<const ET*>(metrics), table, B, T, grid_w,
                                                                half, kc, kin, bd, tau1, ws, status);
+  return true;
 }
 
 template <int MDT>
-static void launch_score(const void* metrics, const int32_t* table, int B, int T, int Cm, int grid_w,
+static bool launch_score(const void* metrics, const int32_t* table, int B, int T, int Cm, int grid_w,
                          int half, int kc, int kin, const Banding& bd, float tau1, const RouteWs& ws,
                          int L, int* status, cudaStream_t st) {
   using ET = typename Elem<MDT>::T;
   size_t smem = (size_t)bd.cap * Cm * sizeof(float);
   dim3 grid(B * bd.bands, L);
-  cudaFuncSetAttribute(route_score_kernel<MDT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (!ensure_smem(route_score_kernel<MDT>, smem)) return false;
   route_score_kernel<MDT><<<grid, 512, smem, st>>>(static_cast<const ET*>(metrics), table, B, T, Cm,
                                                     grid_w, half, kc, kin, bd, tau1, ws, status);
+  return true;
 }
 
 extern "C" int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev_table, int batch,
@@ -1211,9 +1070,9 @@ extern "C" int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev
   if ((size_t)T * ct * sizeof(float) > 220 * 1024) return MN_ERR_UNSUPPORTED;
   const int np_sel = next_pow2(half);
   const size_t smem_sel = row_scratch_bytes(np_sel) + (size_t)half * sizeof(float);
-  const int np_mass = next_pow2(P), nk = next_pow2(k);
-  const size_t smem_mass = (size_t)2 * T * sizeof(float) + (size_t)(np_mass + nk) * 8 + (size_t)4 * 512 * 8;
-  if (smem_sel > 220 * 1024 || smem_mass > 220 * 1024) return MN_ERR_UNSUPPORTED;
+  const size_t smem_mass = mass_smem_bytes(T, k);
+  if (smem_sel > 220 * 1024 || smem_mass > 220 * 1024 || kc > kMaxKc || next_pow2(P) > 8 * kMassThreads)
+    return MN_ERR_UNSUPPORTED;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   float* f = static_cast<float*>(workspace);
@@ -1230,59 +1089,51 @@ extern "C" int mn_route_and_gather(const mn_route_dims* dims, const int32_t* dev
   ws.carrier_tok = reinterpret_cast<int32_t*>(f);
 
   cudaGetLastError();  // clear any stale error so the check below is ours
-  Banding fbd, lbd;
-  size_t fsmem = 0, lsmem = 0;
-  const int esize = metric_dtype == MN_F32 ? 4 : 2;
+  Banding lbd;
+  size_t lsmem = 0;
   const bool lane = reinterpret_cast<uintptr_t>(metrics) % 16 == 0 &&  // 16-byte row loads
                     lane_score_plan(metric_dim, kc, dims->grid_h, dims->grid_w, dims->radius_rows, &lbd, &lsmem);
-  const bool fast = !lane &&
-                    fast_score_plan(metric_dim, kc, dims->grid_h, dims->grid_w, dims->radius_rows, esize, &fbd, &fsmem);
-  const int bands_used = lane ? lbd.bands : fast ? fbd.bands : bd.bands;
+  const int bands_used = lane ? lbd.bands : bd.bands;
+  bool ok;
   if (lane) {
     if (metric_dtype == MN_F16)
-      launch_score_lane<MN_F16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, lbd, lsmem, tau1, ws, num_layers, status, st);
+      ok = launch_score_lane<MN_F16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, lbd, lsmem, tau1, ws, num_layers, status, st);
     else if (metric_dtype == MN_BF16)
-      launch_score_lane<MN_BF16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, lbd, lsmem, tau1, ws, num_layers, status, st);
+      ok = launch_score_lane<MN_BF16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, lbd, lsmem, tau1, ws, num_layers, status, st);
     else
-      launch_score_lane<MN_F32>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, lbd, lsmem, tau1, ws, num_layers, status, st);
-  } else if (fast) {
-    if (metric_dtype == MN_F16)
-      launch_score_fast<MN_F16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, fbd, fsmem, tau1, ws, num_layers, status, st);
-    else if (metric_dtype == MN_BF16)
-      launch_score_fast<MN_BF16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, fbd, fsmem, tau1, ws, num_layers, status, st);
-    else
-      launch_score_fast<MN_F32>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, fbd, fsmem, tau1, ws, num_layers, status, st);
+      ok = launch_score_lane<MN_F32>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, lbd, lsmem, tau1, ws, num_layers, status, st);
   } else if (metric_dtype == MN_F16) {
-    launch_score<MN_F16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, bd, tau1, ws, num_layers, status, st);
+    ok = launch_score<MN_F16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, bd, tau1, ws, num_layers, status, st);
   } else if (metric_dtype == MN_BF16) {
-    launch_score<MN_BF16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, bd, tau1, ws, num_layers, status, st);
+    ok = launch_score<MN_BF16>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, bd, tau1, ws, num_layers, status, st);
   } else {
-    launch_score<MN_F32>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, bd, tau1, ws, num_layers, status, st);
+    ok = launch_score<MN_F32>(metrics, dev_table, batch, T, metric_dim, dims->grid_w, half, kc, kin, bd, tau1, ws, num_layers, status, st);
   }
+  if (!ok) return MN_ERR_LAUNCH;  // nothing launched: the driver refused a shared-memory size
 
-  cudaFuncSetAttribute(route_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_sel);
-  route_select_kernel<<<dim3(batch, num_layers), 512, smem_sel, st>>>(dev_table, batch, half, kc, kin,
-                                                                       bands_used, kb, tau2, ws, status);
-
+  if (!ensure_smem(route_select_kernel, smem_sel) || !ensure_smem(route_mass_kernel, smem_mass))
+    return MN_ERR_LAUNCH;
+  route_select_kernel<<<dim3(batch, num_layers), kSelectThreads, smem_sel, st>>>(dev_table, batch, half, kc, kin,
+                                                                                 bands_used, kb, tau2, ws, status);
   const int stencil = stencil_variant(dims);
-  cudaFuncSetAttribute(route_mass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_mass);
-  route_mass_kernel<<<batch, 512, smem_mass, st>>>(dev_table, batch, T, half, kc, kin, num_layers, k,
-                                                    stencil > 0 ? 1 : 0, ws, size_out, center_out, topk_size,
-                                                    topk_idx);
+  route_mass_kernel<<<batch, kMassThreads, smem_mass, st>>>(dev_table, batch, T, half, kc, kin, num_layers, k,
+                                                            stencil > 0 ? 1 : 0, ws, size_out, center_out,
+                                                            topk_size, topk_idx);
 
   if (stencil > 0) {
     if (x_dtype == MN_F16)
-      launch_stencil<__half>(stencil, x, batch, T, channels, dims, num_layers, k, ws, topk_x, st);
+      ok = launch_stencil<__half>(stencil, x, batch, T, channels, dims, num_layers, k, ws, topk_x, st);
     else if (x_dtype == MN_BF16)
-      launch_stencil<__nv_bfloat16>(stencil, x, batch, T, channels, dims, num_layers, k, ws, topk_x, st);
+      ok = launch_stencil<__nv_bfloat16>(stencil, x, batch, T, channels, dims, num_layers, k, ws, topk_x, st);
     else
-      launch_stencil<float>(stencil, x, batch, T, channels, dims, num_layers, k, ws, topk_x, st);
+      ok = launch_stencil<float>(stencil, x, batch, T, channels, dims, num_layers, k, ws, topk_x, st);
   } else if (x_dtype == MN_F16) {
-    launch_transport<__half>(x, dev_table, batch, T, channels, half, kc, kin, num_layers, k, ws, topk_x, ct, st);
+    ok = launch_transport<__half>(x, dev_table, batch, T, channels, half, kc, kin, num_layers, k, ws, topk_x, ct, st);
   } else if (x_dtype == MN_BF16) {
-    launch_transport<__nv_bfloat16>(x, dev_table, batch, T, channels, half, kc, kin, num_layers, k, ws, topk_x, ct, st);
+    ok = launch_transport<__nv_bfloat16>(x, dev_table, batch, T, channels, half, kc, kin, num_layers, k, ws, topk_x, ct, st);
   } else {
-    launch_transport<float>(x, dev_table, batch, T, channels, half, kc, kin, num_layers, k, ws, topk_x, ct, st);
+    ok = launch_transport<float>(x, dev_table, batch, T, channels, half, kc, kin, num_layers, k, ws, topk_x, ct, st);
   }
+  if (!ok) return MN_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
 }

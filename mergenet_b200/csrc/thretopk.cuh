@@ -9,6 +9,7 @@
 #pragma once
 
 #include <climits>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -44,9 +45,32 @@ __device__ __forceinline__ RowScratch carve_row_scratch(unsigned char* base, int
 // size must divide np (np >= blockDim.x) or be larger than np.
 __device__ __noinline__ static float thre_topk_lambda(const float* x, int n, int np, int k, RowScratch s) {
   const int tid = threadIdx.x;
-  for (int i = tid; i < np; i += blockDim.x) s.xs[i] = (i < n) ? x[i] : INFINITY;
-  __syncthreads();
-  bitonic_sort_f32(s.xs, np);
+  const int per_thread = np / (int)blockDim.x;
+  if (np % (int)blockDim.x == 0 && (per_thread == 1 || per_thread == 2 || per_thread == 4) && blockDim.x >= 32) {
+    // keys in registers, exchanged by shuffles and (for partners 32 .. blockDim
+    // apart) through the scan buffer, which is free until the scans
+    float* xb = reinterpret_cast<float*>(s.dbuf);
+    auto run = [&](auto tag) {
+      constexpr int R = decltype(tag)::value;
+      float kv[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int i = tid + r * blockDim.x;
+        kv[r] = (i < n) ? x[i] : INFINITY;
+      }
+      bitonic_sort_regs<R>(kv, xb, np);
+#pragma unroll
+      for (int r = 0; r < R; ++r) s.xs[tid + r * blockDim.x] = kv[r];
+    };
+    if (per_thread == 1) run(std::integral_constant<int, 1>{});
+    else if (per_thread == 2) run(std::integral_constant<int, 2>{});
+    else run(std::integral_constant<int, 4>{});
+    __syncthreads();
+  } else {
+    for (int i = tid; i < np; i += blockDim.x) s.xs[i] = (i < n) ? x[i] : INFINITY;
+    __syncthreads();
+    bitonic_sort_f32(s.xs, np);
+  }
   const double xmax = (double)s.xs[n - 1];
   const double xmin = (double)s.xs[0];
   // per-thread chunk for the scans

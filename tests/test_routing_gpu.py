@@ -50,6 +50,26 @@ def test_fused_route_matches_reference(dev, golden_dir, name):
         assert rel_err(res.topk_x.cpu().numpy(), g["topk_x"]) <= 2e-3
 
 
+@pytest.mark.parametrize("grid,radius,metric_dim", [((4, 5), 2.0, 16), ((6, 7), 3.0, 48), ((5, 6), 3.0, 40)])
+def test_fused_route_other_shapes(dev, grid, radius, metric_dim):
+    """Shapes off the canonical path, against the oracle: odd grid widths
+    (the table-driven transport), an even width whose receiver columns do not
+    pair up (the stencil's column pairs with a missing partner), receiver
+    in-degree above the unrolled 12 (6x7 at radius 3), and metric widths the
+    one-thread-per-donor scorer does not take (16, 48, 40)."""
+    import mergenet_b200 as mn
+    r_list = canonical_r_list(grid)
+    x, metrics = routing_inputs(5, 3, grid, 40, metric_dim)
+    ref = O.route_and_gather(x, metrics, r_list, O.Geometry(grid, radius))
+    plan = mn.RoutePlan(grid, radius, r_list, device=dev)
+    res = plan(torch.from_numpy(x).to(dev), torch.from_numpy(metrics).to(dev))
+    mism = carrier_mismatches(res.topk_idx.cpu().numpy(), ref["topk_idx"], ref["center"])
+    assert not mism, mism
+    np.testing.assert_allclose(res.size.cpu().numpy(), ref["size"], rtol=3e-5, atol=3e-5)
+    np.testing.assert_allclose(res.center.cpu().numpy(), ref["center"], rtol=0, atol=2e-3)
+    assert rel_err(res.topk_x.cpu().numpy(), ref["topk_x"]) <= 2e-3
+
+
 def test_fused_route_fp16_tokens(dev, golden_dir):
     """Config-2 storage mode: fp16 tokens in, fp16 carriers out, fp32 math."""
     import mergenet_b200 as mn
