@@ -21,7 +21,9 @@ from .routing import (  # noqa: F401
     sparse_weighted_transport,
     sparse_weighted_transport_pair,
 )
+from .dtem import DTEMMergeBlock, build_eval_group_indices, make_merge_block  # noqa: F401
 from .attention import (  # noqa: F401
+    LocalAttention,
     biased_local_attention,
     cross_attention,
     local_attention_packed,

@@ -207,3 +207,51 @@ def cross_attention(q, k, v, scale=None, out_dtype=None, window=-1):
                                  ksb, ksn, ksh, int(window), scale, L.ptr(out), L.dtype_code(out_dtype),
                                  L.ptr(_status(dev)), L.stream_of(q)), "mn_attention")
     return out
+
+
+class LocalAttention(torch.nn.Module):
+    """Drop-in for the reference's LocalAttention module
+    (opentome/timm/bias_local_attn.py:633-724): the same constructor
+    arguments and parameter names (``qkv``, ``q_norm``, ``k_norm``, ``proj``),
+    so its state dict loads as is.  The forward computes the qkv projection,
+    then the windowed attention over the flat sequence with the global CLS
+    row (``cls_global``) in one tensor-core kernel reading q/k/v in place from
+    the packed projection, then the output projection.  As in the reference,
+    fp32 q/k/v are rounded to fp16 for the attention (the reference's
+    FlashAttention call); its CLS row is computed in the same kernel here.
+    Inference only (attention dropout is a training feature)."""
+
+    def __init__(self, dim, num_heads=8, qkv_bias=False, qk_norm=False, attn_drop=0.0, proj_drop=0.0,
+                 norm_layer=torch.nn.LayerNorm, local_window=16, cls_global=False):
+        super().__init__()
+        if dim % num_heads != 0:
+            raise AssertionError("dim should be divisible by num_heads")
+        self.num_heads = num_heads
+        self.head_dim = dim // num_heads
+        self.scale = self.head_dim ** -0.5
+        self.fused_attn = False
+        self.local_window = local_window
+        self.cls_global = cls_global
+        self.qkv = torch.nn.Linear(dim, dim * 3, bias=qkv_bias)
+        self.q_norm = norm_layer(self.head_dim) if qk_norm else torch.nn.Identity()
+        self.k_norm = norm_layer(self.head_dim) if qk_norm else torch.nn.Identity()
+        self.attn_drop = torch.nn.Dropout(attn_drop)
+        self.proj = torch.nn.Linear(dim, dim)
+        self.proj_drop = torch.nn.Dropout(proj_drop)
+
+    def forward(self, x):
+        if self.training and self.attn_drop.p > 0.0:
+            raise NotImplementedError("attention dropout is a training feature; the B200 path is inference")
+        b, n, c = x.shape
+        qkv = self.qkv(x)
+        cls = self.cls_global and self.local_window >= 0 and n > 1
+        if isinstance(self.q_norm, torch.nn.Identity) and isinstance(self.k_norm, torch.nn.Identity):
+            packed = qkv if qkv.dtype in (torch.float16, torch.bfloat16) else qkv.half()
+            out = local_attention_packed(packed, self.num_heads, self.local_window, cls_global=cls,
+                                         out_dtype=qkv.dtype)
+        else:
+            q, k, v = qkv.view(b, n, 3, self.num_heads, self.head_dim).unbind(2)
+            q, k = self.q_norm(q), self.k_norm(k)
+            out = unbiased_local_attention(q, k, v, self.local_window, x_dtype=qkv.dtype,
+                                           cls_global=cls).reshape(b, n, c)
+        return self.proj_drop(self.proj(out))

@@ -1,0 +1,129 @@
+"""The module-level drop-ins driven the way the reference's callers drive them.
+
+DTEMMergeBlock runs the reference's merge loop (LocalEncoder.forward,
+opentome/models/mergenet/model.py:574-590) and carrier block (:1157-1183) on
+CUDA tensors, and is checked against the fixtures make_golden.py recorded
+from the reference's own DTEMBlock._merge_train / _select: per layer the
+assignment and the ``_tome_info`` side effects (assign_layout,
+assign_b_indices, assign_valid_mask), then the masses, token_center and the
+carriers.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import carrier_mismatches, rel_err
+from inputs import routing_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import mergenet_b200  # noqa: F401
+    return torch.device("cuda", 0)
+
+
+def run_reference_loop(block, x, metrics, r_list):
+    """make_golden.run_routing's loop, on the drop-in block: the six
+    _merge_train calls with merge_layer_index set per layer, recording what
+    _select leaves in _tome_info, then the carrier block's tensor ops."""
+    layers = []
+    original = block._select
+
+    def recording_select(k, a, b, a_orig_idx=None, b_orig_idx=None):
+        assign, out = original(k, a, b, a_orig_idx, b_orig_idx)
+        info = block._tome_info
+        layers.append(dict(layout=info["assign_layout"], assign=assign.cpu().numpy(),
+                           receiver_indices=info["assign_b_indices"].cpu().numpy(),
+                           receiver_valid=info["assign_valid_mask"].cpu().numpy()))
+        return assign, out
+
+    block._select = recording_select
+    bsz, t, _ = x.shape
+    size = torch.ones(bsz, t, 1, device=x.device)
+    n = t
+    for i, r in enumerate(r_list):
+        block._tome_info["merge_layer_index"] = i
+        x, size, n, _, _ = block._merge_train(x, size, r, n, {"metric": metrics[i]})
+    center = block._tome_info["token_center"]
+    k = t - sum(r_list) - 1
+    strength = size[..., 0][:, 1:]
+    _, topk_indices = torch.topk(strength, k, dim=1, largest=True, sorted=False)
+    order = torch.argsort(torch.gather(center[:, 1:], 1, topk_indices), dim=1)
+    topk = torch.gather(topk_indices, 1, order)
+    topk_x = torch.cat([x[:, :1], torch.gather(x, 1, (topk + 1).unsqueeze(-1).expand(-1, -1, x.shape[-1]))], 1)
+    return layers, size[..., 0], center, topk, topk_x
+
+
+@pytest.mark.parametrize("name", ["route_c1", "route_g3x6", "route_g4x4"])
+def test_merge_block_through_the_reference_loop(dev, golden_dir, name):
+    import mergenet_b200 as mn
+    g = np.load(golden_dir / f"{name}.npz")
+    grid = tuple(int(v) for v in g["grid"])
+    r_list = [int(v) for v in g["r_list"]]
+    x, metrics = routing_inputs(int(g["seed"]), int(g["batch"]), grid, int(g["channels"]), int(g["metric_dim"]),
+                                layers=len(r_list))
+    block = mn.make_merge_block(grid, float(g["radius"]), device=dev)
+    layers, size, center, topk, topk_x = run_reference_loop(
+        block, torch.from_numpy(x).to(dev), torch.from_numpy(metrics).to(dev), r_list)
+    assert len(layers) == len(r_list)
+    for i, layer in enumerate(layers):
+        assert layer["layout"] == "spatial_sparse"
+        if f"assign_{i}" in g:
+            np.testing.assert_array_equal(layer["receiver_indices"], g[f"receiver_indices_{i}"])
+            np.testing.assert_array_equal(layer["receiver_valid"], g[f"receiver_valid_{i}"])
+            np.testing.assert_allclose(layer["assign"], g[f"assign_{i}"], rtol=0, atol=5e-6)
+    np.testing.assert_allclose(size.cpu().numpy(), g["size"], rtol=3e-5, atol=3e-5)
+    np.testing.assert_allclose(center.cpu().numpy(), g["center"], rtol=0, atol=2e-3)
+    mism = carrier_mismatches(topk.cpu().numpy(), g["topk_idx"], g["center"])
+    assert not mism, mism
+    if "topk_x" in g:
+        assert rel_err(topk_x.cpu().numpy(), g["topk_x"]) <= 2e-3
+
+
+def test_merge_block_matches_fused_route(dev):
+    """The function-level path (six DTEMMergeBlock layers) and the fused
+    RoutePlan give the same carriers, masses and centres on one input."""
+    import mergenet_b200 as mn
+    from inputs import canonical_r_list
+    grid = (28, 28)
+    r_list = canonical_r_list(grid)
+    x, metrics = routing_inputs(11, 3, grid, 64, 64)
+    xt, mt = torch.from_numpy(x).to(dev), torch.from_numpy(metrics).to(dev)
+    block = mn.make_merge_block(grid, 3.0, device=dev)
+    _, size, center, topk, topk_x = run_reference_loop(block, xt, mt, r_list)
+    res = mn.RoutePlan(grid, 3.0, r_list, device=dev)(xt, mt)
+    mism = carrier_mismatches(res.topk_idx.cpu().numpy(), topk.cpu().numpy(), center.cpu().numpy())
+    assert not mism, mism
+    torch.testing.assert_close(res.size, size, rtol=3e-5, atol=3e-5)
+    torch.testing.assert_close(res.center, center, rtol=0, atol=2e-3)
+    assert rel_err(res.topk_x.cpu().numpy(), topk_x.cpu().numpy()) <= 2e-3
+
+
+@pytest.mark.parametrize("dtype,cls_global", [(torch.float16, True), (torch.bfloat16, False)])
+def test_local_attention_module(dev, dtype, cls_global):
+    """LocalAttention (bias_local_attn.py:633-724) with the reference's
+    parameter names, against its forward restated in PyTorch: qkv Linear,
+    band-masked softmax over |i - j| <= 16 in fp32, CLS row over every key,
+    proj Linear."""
+    import math
+    import mergenet_b200 as mn
+    torch.manual_seed(3)
+    mod = mn.LocalAttention(384, num_heads=6, qkv_bias=True, local_window=16, cls_global=cls_global).to(dev, dtype)
+    x = torch.randn(2, 785, 384, device=dev, dtype=dtype)
+    with torch.no_grad():
+        out = mod(x)
+        qkv = mod.qkv(x).view(2, 785, 3, 6, 64).permute(2, 0, 3, 1, 4).float()
+        q, k, v = qkv.unbind(0)
+        s = q @ k.transpose(-1, -2) / math.sqrt(64)
+        pos = torch.arange(785, device=dev)
+        band = (pos[:, None] - pos[None, :]).abs() <= 16
+        if cls_global:
+            band[0] = True
+        a = torch.softmax(s.masked_fill(~band, float("-inf")), -1) @ v
+        want = mod.proj(a.transpose(1, 2).reshape(2, 785, 384).to(dtype)).float()
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-2
+    assert ((out.float() - want).abs().max() / want.abs().max()).item() <= tol
+    assert sorted(n for n, _ in mod.named_parameters()) == ["proj.bias", "proj.weight", "qkv.bias", "qkv.weight"]

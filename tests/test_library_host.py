@@ -167,3 +167,36 @@ def test_attention_shapes_outside_the_kernels_are_refused():
         mn.biased_local_attention(t65, t65, t65, torch.rand(1, 9), 2, logical_dim=64, input_layout="BNHD")
     with pytest.raises(ValueError, match="head_dim 32"):
         mn.cross_attention(torch.rand(1, 3, 2, 32), torch.rand(1, 5, 2, 32), torch.rand(1, 5, 2, 32))
+
+
+def test_merge_block_refuses_paths_it_does_not_implement():
+    """DTEMMergeBlock covers the inference path only; the others are refused
+    before any device work."""
+    import mergenet_b200 as mn
+    block = mn.DTEMMergeBlock({"window_size": 0, "dtem_spatial_radius": 3.0, "dtem_spatial_backend": "sparse",
+                               "tau2": 30.0})
+    x = torch.zeros(1, 5, 8)
+    size = torch.ones(1, 5, 1)
+    with pytest.raises(NotImplementedError, match="inference"):
+        block.train()._merge_train(x, size, 1, 5, {"metric": torch.ones(1, 5, 4)})
+    block.eval()
+    block._tome_info["dtem_spatial_backend"] = "dense"
+    with pytest.raises(NotImplementedError, match="sparse backend"):
+        block._merge_train(x, size, 1, 5, {"metric": torch.ones(1, 5, 4)})
+    block._tome_info.update(dtem_spatial_backend="sparse", source_trace_mode="matrix")
+    with pytest.raises(NotImplementedError, match="source"):
+        block._merge_train(x, size, 1, 5, {"metric": torch.ones(1, 5, 4)})
+
+
+def test_eval_group_indices_follow_the_layer_parity():
+    """build_dtem_eval_group_indices (dtem.py:1125-1188): even layers donate
+    the odd positions, odd layers the even ones; 'seeded' is batch-shared."""
+    import mergenet_b200 as mn
+    a0, b0 = mn.build_eval_group_indices(6, 2, "cpu", "alternating_per_layer", layer_index=0)
+    a1, b1 = mn.build_eval_group_indices(6, 2, "cpu", "alternating_per_layer_fast", layer_index=1)
+    assert a0[0].tolist() == [1, 3, 5] and b0[0].tolist() == [0, 2, 4]
+    assert a1[0].tolist() == [0, 2, 4] and b1[0].tolist() == [1, 3, 5]
+    s0, _ = mn.build_eval_group_indices(10, 3, "cpu", "seeded", seed=4, layer_index=2)
+    assert torch.equal(s0[0], s0[2])
+    with pytest.raises(ValueError):
+        mn.build_eval_group_indices(6, 2, "cpu", "random")
