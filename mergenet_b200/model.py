@@ -508,6 +508,65 @@ def add_layernorm(x, y, ln, x_out=None, want_ln=True, want_raw=False):
     return x_out, h_ln, h_raw
 
 
-def mergenet_small_cls(**kwargs):
-    """Factory with the reference's canonical single-branch defaults."""
-    return MergeNetSmall(**kwargs)
+# The reference factory's canonical kwargs (opentome/models/mergenet/model.py:
+# 24-50), the values this implementation runs.  Keys marked "training" only
+# change training behaviour and are accepted and ignored at inference.
+MERGENET_SMALL_CANONICAL_KWARGS = {
+    "img_size": 224, "patch_size": 8, "local_depth": 6, "latent_depth": 6, "lambda_local": 2.0,
+    "total_merge_latent": 0, "dtem_window_size": 0, "dtem_spatial_radius": 3.0,
+    "dtem_spatial_metric": "euclidean", "dtem_spatial_backend": "sparse", "dtem_r": 2, "use_softkmax": True,
+    "swa_size": 256, "dtem_feat_dim": 64, "dtem_t": 1, "dtem_train_grouping": "random_per_sample",
+    "dtem_train_grouping_seed": 0, "dtem_eval_grouping": "alternating_per_layer_fast", "dtem_eval_grouping_seed": 0,
+    "metric_grad_scale": 0.1, "source_trace_mode": "center", "local_block_window": 16, "local_cls_global": True,
+    "soft_topk": True, "soft_topk_aux_weight": 0.05,
+}
+_TRAINING_ONLY = ("dtem_r", "swa_size", "dtem_train_grouping", "dtem_train_grouping_seed", "metric_grad_scale",
+                  "soft_topk", "soft_topk_aux_weight", "drop_rate", "attn_drop_rate", "drop_path_rate")
+# settings whose other values select paths this implementation does not run
+_FIXED = {
+    "total_merge_latent": (0,), "dtem_window_size": (0, None), "dtem_spatial_metric": ("euclidean",),
+    # the dense and sparse backends give the same assignment (the reference's
+    # own tests pin them to 3e-10); the fused kernels compute the sparse form
+    "dtem_spatial_backend": ("sparse", "dense"), "use_softkmax": (True,), "dtem_t": (1,),
+    # both eval groupings build the same partition (dtem.py:1125-1188)
+    "dtem_eval_grouping": ("alternating_per_layer", "alternating_per_layer_fast"),
+    "source_trace_mode": ("center", "none"), "local_cls_global": (True,),
+}
+
+
+def mergenet_small_cls(pretrained=False, **kwargs):
+    """The reference's ``mergenet_small_cls`` factory
+    (opentome/models/mergenet/model.py:1602-1607) on the B200 kernels: the
+    same keyword arguments and canonical defaults, and a module whose state
+    dict has the reference's parameter names and shapes.  Pretrained weights
+    are loaded with ``load_state_dict`` from a reference checkpoint
+    (downloading them is not supported).  Keyword values that select paths
+    other than the canonical inference path raise ``NotImplementedError``."""
+    if pretrained:
+        raise NotImplementedError("load a reference checkpoint with load_state_dict(strict=True) instead")
+    cfg = dict(MERGENET_SMALL_CANONICAL_KWARGS)
+    num_classes = kwargs.pop("num_classes", 1000)
+    unknown = set(kwargs) - set(cfg) - set(_TRAINING_ONLY)
+    if unknown:
+        raise TypeError(f"mergenet_small_cls got unexpected keyword arguments {sorted(unknown)}")
+    cfg.update(kwargs)
+    for key, allowed in _FIXED.items():
+        if cfg[key] not in allowed:
+            raise NotImplementedError(f"{key}={cfg[key]!r} is not on the B200 path (supported: {allowed})")
+    if cfg["dtem_spatial_radius"] is None:
+        raise NotImplementedError("global DTEM candidates without a spatial radius are not on the B200 path")
+    return MergeNetSmall(img_size=cfg["img_size"], patch_size=cfg["patch_size"], local_depth=cfg["local_depth"],
+                         latent_depth=cfg["latent_depth"], num_classes=num_classes, metric_dim=cfg["dtem_feat_dim"],
+                         spatial_radius=float(cfg["dtem_spatial_radius"]), local_window=cfg["local_block_window"],
+                         lambda_local=cfg["lambda_local"])
+
+
+try:  # register under the reference's name when timm is importable
+    from timm.models.registry import register_model as _register_model  # type: ignore
+except Exception:  # timm is optional
+    _register_model = None
+if _register_model is not None:
+    try:
+        _register_model(mergenet_small_cls)
+    except Exception:  # another module already registered the name
+        pass

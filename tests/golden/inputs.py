@@ -43,3 +43,35 @@ def attention_inputs(seed, batch, tokens, heads, head_dim, std=0.02, dtype=np.fl
                for _ in range(3))
     bias = rng.standard_normal((batch, tokens), dtype=np.float32) * np.float32(std)
     return q.astype(dtype), k.astype(dtype), v.astype(dtype), bias.astype(dtype)
+
+
+def model_weights(shapes, seed=0):
+    """A full set of model weights as a pure function of (seed, parameter
+    name, shape): {name: float32 array}.  Each tensor draws from its own
+    PCG64 stream keyed by a CRC of its name, so the set does not depend on
+    the order of the names.  1-D norm weights ~ 1 + N(0, 0.05^2); biases,
+    position embedding and CLS token ~ N(0, 0.02^2); weight matrices and the
+    patch kernel ~ N(0, 1 / fan_in).  The recovery out-projection is not
+    zero here, so it takes part in every comparison."""
+    import zlib
+    out = {}
+    for name, shape in shapes.items():
+        rng = np.random.default_rng([int(seed), zlib.crc32(name.encode())])
+        shape = tuple(int(v) for v in shape)
+        z = rng.standard_normal(shape, dtype=np.float32)
+        leaf = name.rsplit(".", 1)[-1]
+        if len(shape) == 1 and "norm" in name and leaf == "weight":
+            w = 1.0 + 0.05 * z
+        elif leaf == "bias" or leaf in ("pos_embed", "cls_token"):
+            w = 0.02 * z
+        else:
+            fan_in = int(np.prod(shape[1:])) if len(shape) > 1 else shape[0]
+            w = z / np.sqrt(fan_in)
+        out[name] = w.astype(np.float32)
+    return out
+
+
+def model_images(seed, batch, size=224):
+    """Synthetic N(0, 1) images [B, 3, size, size]."""
+    rng = np.random.default_rng([int(seed), 224])
+    return rng.standard_normal((batch, 3, size, size), dtype=np.float32)

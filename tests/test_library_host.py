@@ -200,3 +200,34 @@ def test_eval_group_indices_follow_the_layer_parity():
     assert torch.equal(s0[0], s0[2])
     with pytest.raises(ValueError):
         mn.build_eval_group_indices(6, 2, "cpu", "random")
+
+
+def test_state_dict_matches_the_reference_model(golden_dir):
+    """The reference's own mergenet_small_cls (built by make_model_golden.py)
+    has exactly our parameter names and shapes, so its checkpoints load with
+    strict=True; the geometry buffers are not persistent, as in the
+    reference (model.py:350-364)."""
+    import numpy as np
+    from inputs import model_weights
+    from mergenet_b200.model import mergenet_small_cls
+    g = np.load(golden_dir / "model_small_cls.npz")
+    ref = dict(zip(g["param_names"].tolist(), g["param_shapes"].tolist()))
+    model = mergenet_small_cls()
+    ours = {k: ",".join(map(str, tuple(v.shape))) for k, v in model.state_dict().items()}
+    assert ours == ref
+    weights = model_weights({k: tuple(int(x) for x in v.split(",")) for k, v in ref.items()}, seed=0)
+    model.load_state_dict({k: torch.from_numpy(v) for k, v in weights.items()}, strict=True)
+
+
+def test_factory_accepts_the_reference_kwargs_and_refuses_other_paths():
+    from mergenet_b200.model import MERGENET_SMALL_CANONICAL_KWARGS, mergenet_small_cls
+    m = mergenet_small_cls(num_classes=10, **MERGENET_SMALL_CANONICAL_KWARGS)
+    assert m.grid == (28, 28) and m.r_list == [65, 65, 65, 65, 65, 67] and m.local_window == 16
+    m48 = mergenet_small_cls(img_size=384)
+    assert m48.grid == (48, 48) and m48.r_list == [192] * 6
+    with pytest.raises(NotImplementedError):
+        mergenet_small_cls(total_merge_latent=4)
+    with pytest.raises(NotImplementedError):
+        mergenet_small_cls(dtem_window_size=8)
+    with pytest.raises(TypeError):
+        mergenet_small_cls(not_an_argument=1)
