@@ -172,6 +172,168 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def measure_kernels(model, B, dev, stream, extra=True):
+    """Per-kernel timings (CUDA events on the launching stream) of the
+    library kernels one forward uses, each against its roofline, plus the
+    config-2 routing op and the config-3 biased block at B=128, and the
+    reference's own GPU kernels for the same work (FlashAttention-2 and
+    PyTorch SDPA, what the reference calls) timed on the same device.
+
+    Algorithmic bytes (HBM-bound kernels) and FLOPs (tensor-bound) per
+    launch are computed from the shapes; `traffic` is the ncu DRAM bytes of
+    one launch scaled by the batch (profiles/ summaries give the capture)."""
+    import mergenet_b200
+    from mergenet_b200.model import add_layernorm
+    peak, peak_kind = _peaks()
+    tf_peak = _tf_peak()
+    out = {}
+    # latent attention (393 carriers, log-size bias): the largest attention
+    # kernel by launch-list share; HBM-bound at this size
+    nt = 393
+    qkv_l = torch.randn(B, nt, 3 * 384, device=dev, dtype=torch.float16) * 0.5
+    log_size = torch.rand(B, nt, device=dev).mul_(3.0).log1p_()
+    t = _time_kernel(lambda: mergenet_b200.local_attention_packed(qkv_l, 6, -1, cls_global=False, bias=log_size),
+                     stream)
+    byt = qkv_l.numel() * 2 + log_size.numel() * 4 + B * nt * 384 * 2  # q,k,v,bias read + o written
+    flops = 4 * B * 6 * nt * nt * 64
+    out["roofline"] = {"kernel": f"attn_tc_kernel<half,64,full,bias> (latent attention, 393 carriers, 6 heads, "
+                                 f"B={B})", "bound": "hbm", "achieved": byt / t / 1e9, "peak": peak, "unit": "GB/s",
+                       "frac": byt / t / 1e9 / peak, "peak_kind": peak_kind, "traffic": TRAFFIC_LATENT_ATTN * B,
+                       "algorithmic_bytes": byt, "ms_per_launch": t * 1e3, "tflops": flops / t / 1e12}
+    # windowed local attention with the CLS row
+    qkv = torch.randn(B, 785, 3 * 384, device=dev, dtype=torch.float16) * 0.5
+    t = _time_kernel(lambda: mergenet_b200.local_attention_packed(qkv, 6, 16, cls_global=True), stream)
+    byt = qkv.numel() * 2 + B * 785 * 384 * 2
+    out["local_attention"] = {"kernel": "attn_win_persistent_kernel<half> (window 16 + CLS row, 785 tokens)",
+                              "ms_per_launch": t * 1e3, "algorithmic_bytes": byt, "achieved_gbs": byt / t / 1e9,
+                              "frac": byt / t / 1e9 / peak, "traffic": TRAFFIC_LOCAL_ATTN * B}
+    # recovery cross-attention core: 393 queries over 785 keys
+    q = torch.randn(B, 393, 6, 64, device=dev, dtype=torch.float16)
+    kv = torch.randn(B, 785, 2, 6, 64, device=dev, dtype=torch.float16)
+    t = _time_kernel(lambda: mergenet_b200.cross_attention(q, kv[:, :, 0], kv[:, :, 1], out_dtype=torch.float16),
+                     stream)
+    flops = 4 * B * 6 * 393 * 785 * 64
+    out["cross_attention"] = {"kernel": "attn_tc_kernel<half,64,full> (393 x 785)", "ms_per_launch": t * 1e3,
+                              "tflops": flops / t / 1e12, "frac_of_bf16_peak": flops / t / 1e12 / tf_peak}
+    # fused residual add + LayerNorm (27 launches per forward)
+    x = torch.randn(B * 785, 384, device=dev)
+    y = torch.randn(B * 785, 384, device=dev).half()
+    ln = torch.nn.LayerNorm(384).to(dev)
+    t = _time_kernel(lambda: add_layernorm(x, y, ln, x_out=x), stream)
+    byt = x.numel() * (4 + 2 + 4 + 2)
+    out["add_layernorm"] = {"kernel": "add_layernorm_kernel<384> (785 x B rows)", "ms_per_launch": t * 1e3,
+                            "algorithmic_bytes": byt, "achieved_gbs": byt / t / 1e9, "frac": byt / t / 1e9 / peak}
+    # the routing call on the model's shard (fp32 residual stream)
+    x_embed = torch.randn(B, 785, 384, device=dev)
+    metrics = (torch.randn(6, B, 785, 64, device=dev) * 1.3).half()
+    plan = model._plan(dev)
+    ws = torch.empty(plan.workspace_bytes(B), dtype=torch.uint8, device=dev)
+    t = _time_kernel(lambda: plan(x_embed, metrics, workspace=ws, check=False), stream)
+    byt = B * (6 * 785 * 64 * 2 + 785 * 384 * 4 + 393 * 384 * 4 + 785 * 4 * 3 + 392 * 8)
+    out["routing"] = {"ms_per_call": t * 1e3, "algorithmic_bytes": byt, "achieved_gbs": byt / t / 1e9,
+                      "frac": byt / t / 1e9 / peak,
+                      "fp32_fma_per_call": 6 * B * 392 * 384 * 13,
+                      "transport_fma_floor_ms": 6 * B * 392 * 384 * 13 * 2 / 74.4e12 * 1e3}
+    if not extra:
+        return out
+    # config 2: the isolated routing op, fp16 tokens [128, 785, 384], with the
+    # scatter back to [128, 784, 384]; 2.41 MB per image (tokens, metrics,
+    # carriers, scatter read and write)
+    b2 = 128
+    x2 = torch.randn(b2, 785, 384, device=dev).half()
+    m2 = (torch.randn(6, b2, 785, 64, device=dev) * 1.3).half()
+    ws2 = torch.empty(plan.workspace_bytes(b2), dtype=torch.uint8, device=dev)
+
+    def op2():
+        r = plan(x2, m2, workspace=ws2, check=False)
+        return mergenet_b200.carrier_scatter(r.topk_x, r.topk_idx, 784)
+    t = _time_kernel(op2, stream)
+    byt = b2 * (784 * 384 * 2 + 6 * 784 * 64 * 2 + 392 * 384 * 2 + 392 * 384 * 2 + 784 * 384 * 2)
+    out["config2_routing_op"] = {"workload": "fp16 tokens [128, 785, 384]: score, select, 6-layer transport, top-392 "
+                                             "gather, scatter back to [128, 784, 384]",
+                                 "ms_per_call": t * 1e3, "algorithmic_bytes": byt, "achieved_gbs": byt / t / 1e9,
+                                 "frac": byt / t / 1e9 / peak}
+    # config 3: biased local attention block, B=128, window 16, CLS global
+    g = torch.Generator(device=dev).manual_seed(3)
+    qkv3 = (torch.randn(128, 785, 3 * 384, device=dev, generator=g) * 0.02).half()
+    bias3 = (torch.randn(128, 785, device=dev, generator=g) * 0.02)
+    t = _time_kernel(lambda: mergenet_b200.local_attention_packed(qkv3, 6, 16, cls_global=True, bias=bias3), stream)
+    byt = qkv3.numel() * 2 + bias3.numel() * 4 + 128 * 785 * 384 * 2
+    out["config3_biased_local_attention"] = {"workload": "q,k,v [128, 785, 6, 64] fp16, per-key bias, window 16, "
+                                                         "CLS global", "ms_per_call": t * 1e3,
+                                             "algorithmic_bytes": byt, "achieved_gbs": byt / t / 1e9,
+                                             "frac": byt / t / 1e9 / peak}
+    # the reference's GPU kernels for the same attention work
+    ref = {}
+    try:
+        from flash_attn import flash_attn_func
+        v = qkv.view(B, 785, 3, 6, 64)
+
+        def ref_local():
+            o = flash_attn_func(v[:, :, 0], v[:, :, 1], v[:, :, 2], window_size=(16, 16))
+            cls = torch.nn.functional.scaled_dot_product_attention(
+                v[:, :1, 0].transpose(1, 2), v[:, :, 1].transpose(1, 2), v[:, :, 2].transpose(1, 2))
+            o = o.clone()
+            o[:, :1] = cls.transpose(1, 2)
+            return o
+        ref["local_attention_flash_attn_plus_sdpa_cls_ms"] = _time_kernel(ref_local, stream) * 1e3
+    except Exception as exc:  # noqa: BLE001 - report, do not fail the bench
+        ref["flash_attn"] = f"unavailable: {type(exc).__name__}"
+    lv = qkv_l.view(B, nt, 3, 6, 64)
+    mask = log_size.half()[:, None, None, :]
+    ref["latent_attention_sdpa_ms"] = _time_kernel(lambda: torch.nn.functional.scaled_dot_product_attention(
+        lv[:, :, 0].transpose(1, 2), lv[:, :, 1].transpose(1, 2), lv[:, :, 2].transpose(1, 2), attn_mask=mask),
+        stream) * 1e3
+    ref["cross_attention_sdpa_ms"] = _time_kernel(lambda: torch.nn.functional.scaled_dot_product_attention(
+        q.transpose(1, 2), kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2)), stream) * 1e3
+    out["reference_gpu_kernels"] = ref
+    out["config5_highres_bf16"] = config5(dev, stream, peak)
+    return out
+
+
+def config5(dev, stream, peak, batch=64, steps=5):
+    """Config 5: 384 x 384 images, patch 8 (48 x 48 grid, 2305 tokens, 1152
+    carriers), bf16 autocast semantics, B=64 per GPU: the forward's
+    images/sec (CUDA-graph replays, CUDA events) and its three largest library
+    kernels against the HBM roofline."""
+    import mergenet_b200
+    from mergenet_b200.model import ForwardGraph, mergenet_small_cls
+    model = mergenet_small_cls(img_size=384, compute_dtype=torch.bfloat16).init_weights(0).to(dev).eval()
+    images = torch.randn(batch, 3, 384, 384, device=dev, generator=torch.Generator(device=dev).manual_seed(9))
+    fwd = ForwardGraph(model, images, warmup=2)
+    t = _time_kernel(lambda: fwd(), stream, iters=steps)
+    fwd.check_status()
+    res = {"workload": "mergenet_small_cls, 384x384 images, patch 8 (48x48 grid, 2305 tokens, 1152 carriers), bf16, "
+                       f"B={batch}", "images_per_sec": batch / t, "ms_per_step": t * 1e3}
+    n, c = 2305, 384
+    qkv = torch.randn(batch, n, 3 * c, device=dev).mul_(0.5).bfloat16()
+    tk = _time_kernel(lambda: mergenet_b200.local_attention_packed(qkv, 6, 16, cls_global=True), stream)
+    byt = qkv.numel() * 2 + batch * n * c * 2
+    res["local_attention"] = {"ms_per_launch": tk * 1e3, "frac": byt / tk / 1e9 / peak}
+    nt = 1153
+    lat = torch.randn(batch, nt, 3 * c, device=dev).mul_(0.5).bfloat16()
+    ls = torch.rand(batch, nt, device=dev).add_(0.1).log()
+    tk = _time_kernel(lambda: mergenet_b200.local_attention_packed(lat, 6, -1, cls_global=False, bias=ls), stream)
+    byt = lat.numel() * 2 + ls.numel() * 4 + batch * nt * c * 2
+    res["latent_attention"] = {"ms_per_launch": tk * 1e3, "frac": byt / tk / 1e9 / peak,
+                               "tflops": 4 * batch * 6 * nt * nt * 64 / tk / 1e12}
+    plan = model._plan(dev)
+    x = torch.randn(batch, n, c, device=dev)
+    m = torch.randn(6, batch, n, 64, device=dev).mul_(1.3).bfloat16()
+    ws = torch.empty(plan.workspace_bytes(batch), dtype=torch.uint8, device=dev)
+    tk = _time_kernel(lambda: plan(x, m, workspace=ws, check=False), stream)
+    byt = batch * (6 * n * 64 * 2 + n * c * 4 + (nt) * c * 4 + n * 4 * 3 + (nt - 1) * 8)
+    res["routing"] = {"ms_per_call": tk * 1e3, "frac": byt / tk / 1e9 / peak}
+    return res
+
+
+def _tf_peak():
+    try:
+        return float(json.loads(PEAKS.read_text())["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
 def run_b200(args):
     world, rank, local = _dist()
     torch.cuda.set_device(local)
@@ -233,29 +395,7 @@ def run_b200(args):
     # logits are finite and gathered
     finite = bool(torch.isfinite(gather_logits(logits)).all())
 
-    # roofline of the dominant library kernel, the windowed local attention
-    # with its CLS row (attn_tc_kernel<half, 160, window>), and of the latent
-    # attention over all 393 carriers with the log-size bias
-    nt = 393
-    qkv_l = torch.randn(B, nt, 3 * 384, device=dev, dtype=torch.float16) * 0.5
-    log_size = torch.rand(B, nt, device=dev).mul_(3.0).log1p_()
-    t_attn = _time_kernel(lambda: mergenet_b200.local_attention_packed(qkv_l, 6, -1, cls_global=False,
-                                                                         bias=log_size), stream)
-    attn_bytes = qkv_l.numel() * 2 + log_size.numel() * 4 + B * nt * 384 * 2  # q,k,v,bias read + o write
-    attn_flops = 4 * B * 6 * nt * nt * 64
-    peak, peak_kind = _peaks()
-    achieved = attn_bytes / t_attn / 1e9
-    qkv = torch.randn(B, 785, 3 * 384, device=dev, dtype=torch.float16) * 0.5
-    t_local = _time_kernel(lambda: mergenet_b200.local_attention_packed(qkv, 6, 16, cls_global=True), stream)
-    local_bytes = qkv.numel() * 2 + B * 785 * 384 * 2  # q, k, v read + o write (fp16)
-    local_achieved = local_bytes / t_local / 1e9
-    # the routing op on the same shard (routing HBM GB/s)
-    x_embed = torch.randn(B, 785, 384, device=dev)
-    metrics = (torch.randn(6, B, 785, 64, device=dev) * 1.3).half()
-    plan = model._plan(dev)
-    t_route = _time_kernel(lambda: plan(x_embed, metrics), stream)
-    route_bytes = B * (6 * 785 * 64 * 2 + 785 * 384 * 4 + 393 * 384 * 4 + 785 * 4 * 3 + 392 * 8)
-
+    kern = measure_kernels(model, B, dev, stream, args.kernel_keys)
     line = None
     if rank == 0:
         cpu_v, cpu_n, cpu_t = cpu_port_rate(MergeNetSmall().init_weights(0),
@@ -273,17 +413,8 @@ def run_b200(args):
                     "d2h_bytes_per_step": host_logits[0].numel() * host_logits.element_size(),
                     "overlap": "H2D of step i+1 on a copy stream during step i's forward"},
             "gpu_launches": ForwardGraph.library_launches(model) * args.steps,
-            "roofline": {"kernel": "attn_win_persistent_kernel<half> with the CLS row folded in (local attention, "
-                                   "window 16, 785 tokens, 6 heads, B=%d)" % B,
-                         "bound": "hbm", "achieved": local_achieved, "peak": peak, "unit": "GB/s",
-                         "frac": local_achieved / peak, "peak_kind": peak_kind, "traffic": TRAFFIC_LOCAL_ATTN * B,
-                         "algorithmic_bytes": local_bytes, "ms_per_launch": t_local * 1e3},
-            "latent_attention": {"kernel": "attn_tc_kernel<half,64,full,bias> (393 carriers, 6 heads)",
-                                 "ms_per_call": t_attn * 1e3, "algorithmic_bytes": attn_bytes,
-                                 "achieved_gbs": achieved, "frac": achieved / peak,
-                                 "traffic": TRAFFIC_LATENT_ATTN * B, "tflops": attn_flops / t_attn / 1e12},
-            "routing": {"ms_per_call": t_route * 1e3, "algorithmic_bytes": route_bytes,
-                        "achieved_gbs": route_bytes / t_route / 1e9, "frac": route_bytes / t_route / 1e9 / peak},
+            "roofline": kern.pop("roofline"),
+            **kern,
             "cpu_baseline": ({"value": cpu_v, "unit": "images/sec", "cores": os.cpu_count(), "kind": "port",
                               "sample": f"{cpu_n} images in {cpu_t:.1f} s, float32 CPU port (oracle/model_cpu.py)"}
                              if cpu_v is not None else None),
@@ -304,6 +435,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-sample", type=int, default=1)
+    ap.add_argument("--no-kernel-keys", dest="kernel_keys", action="store_false",
+                    help="skip the config-2/3 and reference-kernel keys")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

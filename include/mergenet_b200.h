@@ -257,11 +257,13 @@ int mn_attention(int batch, int nq, int nk, int heads, int head_dim, int dtype,
  * (the norm1/norm2 inputs of the LocalBlock / latent Block forward under fp16
  * autocast, opentome/timm/bias_local_attn.py:867-868): s = x + y (y fp16,
  * optional); x_out = s (fp32, optional, may alias x); h_ln = LayerNorm(s)
- * (fp16, optional; gamma/beta fp32); h_raw = fp16(s) (optional).
- * channels in {256, 384, 512, 768}. */
+ * (optional; gamma/beta fp32); h_raw = s rounded (optional).  y, h_ln and
+ * h_raw are 16-bit of type half_dtype (MN_F16, or MN_BF16 for bf16
+ * autocast).  channels in {256, 384, 512, 768}. */
 int mn_add_layernorm(int64_t rows, int channels, const float* x, const void* y,
                      const float* gamma, const float* beta, float eps,
-                     float* x_out, void* h_ln, void* h_raw, void* stream);
+                     float* x_out, void* h_ln, void* h_raw, int half_dtype,
+                     void* stream);
 
 /* Patch unfold for the patch-embedding GEMM (timm PatchEmbed's stride-p
  * p x p convolution, opentome/models/mergenet/model.py:517-519):
@@ -285,18 +287,47 @@ int mn_gemm_f16(int M, int N, int K, const void* a, int64_t lda, const void* w,
                 int64_t ldw, const void* bias, int epilogue, void* out,
                 int64_t ldo, int* status, void* stream);
 
+/* Split-precision GEMM for the fp32 Linear layers of the recovery
+ * cross-attention (MyCrossAttention's q/k/v and out projections, which the
+ * reference runs in fp32 with autocast off,
+ * opentome/models/mergenet/model.py:140-145, :215-219):
+ *   out[M, N] = out_scale * (A . W^T) + bias[N]
+ * with the fp32 operands given as fp16 pairs, A = a_hi + a_lo (a_lo may be
+ * NULL when A is exactly fp16) and W = w_hi + w_lo, each split as
+ * hi = fp16(x), lo = fp16(x - hi) after an exact power-of-two scaling.
+ * Three tcgen05 MMAs per K step (A_hi.W_hi + A_hi.W_lo + A_lo.W_hi)
+ * accumulate in one fp32 accumulator: about 7e-7 relative error per product,
+ * against 6e-8 for an fp32 FMA.  bias fp32 [N] or NULL; out fp32 or fp16
+ * (out_dtype MN_F32 / MN_F16), row stride ldo.  K must be a multiple of 64,
+ * N of 128, strides multiples of 8 elements and pointers 16-byte aligned
+ * (else MN_ERR_UNSUPPORTED). */
+int mn_gemm_f32_split(int M, int N, int K, const void* a_hi, const void* a_lo,
+                      int64_t lda, const void* w_hi, const void* w_lo,
+                      int64_t ldw, const float* bias, float out_scale,
+                      void* out, int64_t ldo, int out_dtype, int* status,
+                      void* stream);
+
+/* fp32 LayerNorm of rows (MyCrossAttention's q_norm / kv_norm,
+ * opentome/models/mergenet/model.py:133-134) written as the fp16 pair the
+ * split GEMM takes: ys = LayerNorm(x) * scale (an exact power of two),
+ * hi = fp16(ys), lo = fp16(ys - hi).  channels in {256, 384, 512, 768}. */
+int mn_layernorm_split(int64_t rows, int channels, const float* x,
+                       const float* gamma, const float* beta, float eps,
+                       float scale, void* hi, void* lo, void* stream);
+
 /* Patch embedding finish fused with the first block's LayerNorm (timm
  * PatchEmbed + VisionTransformer._pos_embed, then blocks[0].norm1, as the
- * LocalEncoder runs them under fp16 autocast,
+ * LocalEncoder runs them under autocast,
  * opentome/models/mergenet/model.py:517-535): for image b and token t,
  * x_out[b, t] = cls + pos[0] (t == 0) or float(emb[b, t - 1]) + pos[t]
- * (fp32), h_ln[b, t] = LayerNorm(x_out[b, t]) (fp16).  emb is the fp16 patch
- * projection [batch, tokens - 1, channels]; pos fp32 [tokens, channels];
- * cls fp32 [channels].  channels in {256, 384, 512, 768}. */
+ * (fp32), h_ln[b, t] = LayerNorm(x_out[b, t]) (16-bit).  emb is the patch
+ * projection [batch, tokens - 1, channels]; emb and h_ln have type
+ * half_dtype (MN_F16 or MN_BF16); pos fp32 [tokens, channels]; cls fp32
+ * [channels].  channels in {256, 384, 512, 768}. */
 int mn_embed_layernorm(int batch, int tokens, int channels, const void* emb,
                        const float* pos, const float* cls, const float* gamma,
                        const float* beta, float eps, float* x_out, void* h_ln,
-                       void* stream);
+                       int half_dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -69,10 +69,13 @@ _SIGNATURES = {
                                    c_int, c_int, c_int, c_float, _P, c_int, _P, _P]),
     "mn_attention": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, _P, c_int64, c_int64, c_int64, _P, _P,
                              c_int64, c_int64, c_int64, c_int, c_float, _P, c_int, _P, _P]),
-    "mn_add_layernorm": (c_int, [c_int64, c_int, _P, _P, _P, _P, c_float, _P, _P, _P, _P]),
-    "mn_embed_layernorm": (c_int, [c_int, c_int, c_int, _P, _P, _P, _P, _P, c_float, _P, _P, _P]),
+    "mn_add_layernorm": (c_int, [c_int64, c_int, _P, _P, _P, _P, c_float, _P, _P, _P, c_int, _P]),
+    "mn_embed_layernorm": (c_int, [c_int, c_int, c_int, _P, _P, _P, _P, _P, c_float, _P, _P, c_int, _P]),
     "mn_patch_unfold": (c_int, [c_int, c_int, c_int, c_int, c_int, _P, _P, _P]),
     "mn_gemm_f16": (c_int, [c_int, c_int, c_int, _P, c_int64, _P, c_int64, _P, c_int, _P, c_int64, _P, _P]),
+    "mn_gemm_f32_split": (c_int, [c_int, c_int, c_int, _P, _P, c_int64, _P, _P, c_int64, _P, c_float, _P, c_int64,
+                                  c_int, _P, _P]),
+    "mn_layernorm_split": (c_int, [c_int64, c_int, _P, _P, _P, c_float, c_float, _P, _P, _P]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

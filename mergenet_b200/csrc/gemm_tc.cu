@@ -17,6 +17,17 @@
 //               of the accumulator columns, bias (+ GELU), fp16 stores.
 // The two accumulators let the epilogue of one tile overlap the main loop of
 // the next.  Every wait is bounded; a timeout sets MN_STATUS_TC_TIMEOUT.
+//
+// Split-precision mode (mn_gemm_f32_split): the fp32 operands arrive as fp16
+// pairs, x = x_hi + x_lo with x_hi = fp16(x) and x_lo = fp16(x - x_hi), the
+// weight scaled by an exact power of two first so both halves stay in fp16's
+// normal range.  Each 16-wide K step issues three MMAs into the same fp32
+// accumulator, A_hi.W_hi + A_hi.W_lo + A_lo.W_hi (the dropped A_lo.W_lo is
+// 2^-22 of a product); each operand half is exact to 2^-22 relative, so a
+// product is exact to about 3 * 2^-22 (7e-7) relative, against fp32's
+// 6e-8 per product and its accumulation error of a few 1e-7 over K = 384.
+// With an fp16-exact A (A_lo == 0) the A_lo term is skipped.  The epilogue
+// unscales, adds an fp32 bias and stores fp32 or fp16.
 
 #include <algorithm>
 #include <mutex>
@@ -33,26 +44,32 @@ constexpr int BK = 64;  // one 128-byte swizzle atom of fp16
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 
-// Each epilogue warp stages a 32-row x 32-column fp16 block (2 KB) in shared
-// memory and writes it with one TMA store; two buffers per warp let the next
-// block be staged while the previous store drains.
-constexpr uint32_t kStageOutBytes = 32 * 32 * 2;
-constexpr uint32_t kOutBytes = kEpiWarps * 2 * kStageOutBytes;
+// Each epilogue warp stages a 32-row x 32-column block in shared memory and
+// writes it with one TMA store; with fp16 output two buffers per warp let the
+// next block be staged while the previous store drains.
 
-template <int BN>
+// NA / NW: fp16 planes of A / W per stage (1 plain, 2 = hi and lo);
+// OUT32: fp32 output (32 x 32 x 4-byte staging blocks, one per warp).
+template <int BN, int NA = 1, int NW = 1, bool OUT32 = false>
 struct Cfg {
   static constexpr uint32_t kABytes = BM * BK * 2;
   static constexpr uint32_t kBBytes = BN * BK * 2;
-  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = std::min<int>(8, (227 * 1024 - kOutBytes - 2048) / kStageBytes);
+  static constexpr uint32_t kStageBytes = NA * kABytes + NW * kBBytes;
+  static constexpr uint32_t kBlockOutBytes = 32 * 32 * (OUT32 ? 4 : 2);
+  static constexpr int kOutBufs = OUT32 ? 1 : 2;
+  static constexpr uint32_t kOutTotal = kEpiWarps * kOutBufs * kBlockOutBytes;
+  static constexpr int kStages = std::min<int>(8, (227 * 1024 - kOutTotal - 2048) / kStageBytes);
   static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;  // two accumulators
   static constexpr uint32_t out_off = kStages * kStageBytes;
-  static constexpr uint32_t bar_off = out_off + kOutBytes;  // full[S], empty[S], acc_full[2], acc_empty[2], done
+  static constexpr uint32_t bar_off = out_off + kOutTotal;  // full[S], empty[S], acc_full[2], acc_empty[2], done
   static constexpr uint32_t slot_off = bar_off + (2 * kStages + 5) * 8;
   static constexpr uint32_t bytes = slot_off + 16 + 1024;  // + alignment slack
 };
 static_assert(Cfg<256>::bytes <= 227 * 1024 && Cfg<192>::bytes <= 227 * 1024 && Cfg<128>::bytes <= 227 * 1024,
               "shared memory");
+static_assert(Cfg<128, 2, 2, true>::bytes <= 227 * 1024 && Cfg<128, 2, 2, true>::kStages >= 2 &&
+                  Cfg<128, 2, 2, false>::bytes <= 227 * 1024 && Cfg<128, 1, 2, true>::kStages >= 3,
+              "shared memory (split precision)");
 
 // GELU(x) = 0.5 x (1 + erf(x / sqrt 2)) on a pair, packed fp32x2.  erf(z) is
 // z * P(z^2) with |z| clamped to 2.9: P of degree 9, fitted by
@@ -82,13 +99,18 @@ __device__ __forceinline__ float2 gelu2(float2 x) {
   return ffma2(h, e, h);
 }
 
-template <int BN, int EPI>
+// EPI: 0 bias, 1 bias + GELU (fp16 bias), 2 scale * acc + fp32 bias (split).
+template <int BN, int EPI, int NA = 1, int NW = 1, bool OUT32 = false>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                               const __grid_constant__ CUtensorMap tmap_w,
-                                                              const __grid_constant__ CUtensorMap tmap_o, int M,
-                                                              int N, int K, const __half* __restrict__ bias,
-                                                              int* __restrict__ err) {
-  using C = Cfg<BN>;
+                                                              const __grid_constant__ CUtensorMap tmap_o,
+                                                              const __grid_constant__ CUtensorMap tmap_a_lo,
+                                                              const __grid_constant__ CUtensorMap tmap_w_lo, int M,
+                                                              int N, int K, const void* __restrict__ bias_ptr,
+                                                              float out_scale, int* __restrict__ err) {
+  using C = Cfg<BN, NA, NW, OUT32>;
+  const __half* bias = EPI == 2 ? nullptr : static_cast<const __half*>(bias_ptr);
+  const float* bias32 = EPI == 2 ? static_cast<const float*>(bias_ptr) : nullptr;
   constexpr int S = C::kStages;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -118,6 +140,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_w)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_o)) : "memory");
+    if (NA == 2) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a_lo)) : "memory");
+    if (NW == 2) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_w_lo)) : "memory");
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -138,8 +162,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           if (!tc::mbar_wait(empty + stage, phase ^ 1u, err)) { ok = false; break; }
           const uint32_t sa = tc::smem_u32(base + stage * C::kStageBytes);
           tma::expect_tx(full + stage, C::kStageBytes);
+          // stage layout: A_hi [A_lo] W_hi [W_lo]
           tma::load_2d(sa, &tmap_a, kb * BK, mb * BM, full + stage);
-          tma::load_2d(sa + C::kABytes, &tmap_w, kb * BK, nb * BN, full + stage);
+          if (NA == 2) tma::load_2d(sa + C::kABytes, &tmap_a_lo, kb * BK, mb * BM, full + stage);
+          tma::load_2d(sa + NA * C::kABytes, &tmap_w, kb * BK, nb * BN, full + stage);
+          if (NW == 2) tma::load_2d(sa + NA * C::kABytes + C::kBBytes, &tmap_w_lo, kb * BK, nb * BN, full + stage);
           last_phase[stage] = (int)phase;
           if (++stage == S) { stage = 0; phase ^= 1u; }
         }
@@ -165,11 +192,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           if (!tc::mbar_wait(full + stage, phase, err)) { ok = false; break; }
           tc::fence_after_sync();
           const uint32_t sa = tc::smem_u32(base + stage * C::kStageBytes);
-          const uint32_t sb = sa + C::kABytes;
+          const uint32_t sa_lo = sa + C::kABytes;
+          const uint32_t sb = sa + NA * C::kABytes;
+          const uint32_t sb_lo = sb + C::kBBytes;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
+          for (int k = 0; k < BK / 16; ++k) {
             tc::mma_f16_ss(d, tc::sw128_desc(sa + k * 32, 16), tc::sw128_desc(sb + k * 32, 16), idesc,
                            (kb > 0 || k > 0) ? 1u : 0u);
+            if (NW == 2)
+              tc::mma_f16_ss(d, tc::sw128_desc(sa + k * 32, 16), tc::sw128_desc(sb_lo + k * 32, 16), idesc, 1u);
+            if (NA == 2)
+              tc::mma_f16_ss(d, tc::sw128_desc(sa_lo + k * 32, 16), tc::sw128_desc(sb + k * 32, 16), idesc, 1u);
+          }
           tc::mma_commit(empty + stage);  // the stage is free once these MMAs have read it
           if (++stage == S) { stage = 0; phase ^= 1u; }
         }
@@ -188,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     const int quad = warp & 3;  // TMEM lanes this warp may access
     const int col_half = ew >> 2;
     const uint32_t lane_sel = (uint32_t)(quad * 32) << 16;
-    uint8_t* stage_out = base + C::out_off + ew * 2 * kStageOutBytes;
+    uint8_t* stage_out = base + C::out_off + ew * C::kOutBufs * C::kBlockOutBytes;
     int acc = 0, buf = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -206,36 +240,56 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           __syncwarp();
           if (lane == 0) tma::arrive(acc_empty + acc);
         }
-        uint4 bq[4];
-        if (brow) {
-          const uint4* b4 = reinterpret_cast<const uint4*>(brow + c * 32);
+        if (EPI == 2) {  // split precision: unscale, fp32 bias
+          const float* b32 = bias32 ? bias32 + nb * BN + c * 32 : nullptr;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) bq[q] = __ldg(b4 + q);
+          for (int i = 0; i < 32; i += 4) {
+            const float4 bb = b32 ? __ldg(reinterpret_cast<const float4*>(b32 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[i] = fmaf(v[i], out_scale, bb.x);
+            v[i + 1] = fmaf(v[i + 1], out_scale, bb.y);
+            v[i + 2] = fmaf(v[i + 2], out_scale, bb.z);
+            v[i + 3] = fmaf(v[i + 3], out_scale, bb.w);
+          }
         }
-        const __half2* bh = reinterpret_cast<const __half2*>(bq);
-        uint4 packed[4];
+        uint4 packed[OUT32 ? 8 : 4];
         uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
+        if (OUT32) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float2 p = make_float2(v[2 * i], v[2 * i + 1]);
-          if (brow) p = fadd2(p, __half22float2(bh[i]));
-          if (EPI == 1) p = gelu2(__half22float2(__float22half2_rn(p)));  // GELU of the fp16 linear output
-          __half2 h = __float22half2_rn(p);
-          pw[i] = *reinterpret_cast<uint32_t*>(&h);
+          for (int i = 0; i < 32; ++i) pw[i] = __float_as_uint(v[i]);
+        } else {
+          uint4 bq[4];
+          if (brow) {
+            const uint4* b4 = reinterpret_cast<const uint4*>(brow + c * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) bq[q] = __ldg(b4 + q);
+          }
+          const __half2* bh = reinterpret_cast<const __half2*>(bq);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float2 p = make_float2(v[2 * i], v[2 * i + 1]);
+            if (brow) p = fadd2(p, __half22float2(bh[i]));
+            if (EPI == 1) p = gelu2(__half22float2(__float22half2_rn(p)));  // GELU of the fp16 linear output
+            __half2 h = __float22half2_rn(p);
+            pw[i] = *reinterpret_cast<uint32_t*>(&h);
+          }
         }
         // stage this warp's 32 x 32 block (row = lane) and store it with TMA
-        if (lane == 0) tma::bulk_wait_read<1>();  // the buffer's previous store has read it
+        if (lane == 0) {  // the buffer's previous store has read it
+          if (C::kOutBufs == 2) tma::bulk_wait_read<1>();
+          else tma::bulk_wait_read<0>();
+        }
         __syncwarp();
-        uint8_t* sb = stage_out + buf * kStageOutBytes;
+        uint8_t* sb = stage_out + buf * C::kBlockOutBytes;
+        constexpr int kRowBytes = OUT32 ? 128 : 64;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(sb + lane * 64 + q * 16) = packed[q];
+        for (int q = 0; q < kRowBytes / 16; ++q) *reinterpret_cast<uint4*>(sb + lane * kRowBytes + q * 16) = packed[q];
         tc::fence_async_smem();
         __syncwarp();
         if (lane == 0) {
           tma::store_2d(&tmap_o, tc::smem_u32(sb), nb * BN + c * 32, mb * BM + quad * 32);
           tma::bulk_commit();
         }
-        buf ^= 1;
+        if (C::kOutBufs == 2) buf ^= 1;
       }
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
@@ -274,7 +328,36 @@ static int launch(int M, int N, int K, const void* a, int64_t lda, const void* w
   const int grid = std::max(1, std::min(tiles, sms));
   auto kern = gemm_tc_kernel<BN, EPI>;
   if (!ensure_smem(kern, Cfg<BN>::bytes)) return MN_ERR_LAUNCH;
-  kern<<<grid, kThreads, Cfg<BN>::bytes, st>>>(ma, mw, mo, M, N, K, static_cast<const __half*>(bias), status);
+  kern<<<grid, kThreads, Cfg<BN>::bytes, st>>>(ma, mw, mo, ma, mw, M, N, K, bias, 1.0f, status);
+  return MN_OK;
+}
+
+// Split-precision launch: A = a_hi (+ a_lo), W = w_hi + w_lo, BN = 128.
+template <int NA, bool OUT32>
+static int launch_split(int M, int N, int K, const void* a_hi, const void* a_lo, int64_t lda, const void* w_hi,
+                        const void* w_lo, int64_t ldw, const float* bias, float out_scale, void* out, int64_t ldo,
+                        int* status, cudaStream_t st) {
+  constexpr int BN = 128;
+  CUtensorMap ma, mal, mw, mwl, mo;
+  const cuuint64_t odims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+  const cuuint64_t ostr[1] = {(cuuint64_t)ldo * (OUT32 ? 4 : 2)};
+  const cuuint32_t obox[2] = {32, 32};
+  if (!make_map(&ma, a_hi, M, K, lda, BM, BK, true) || !make_map(&mw, w_hi, N, K, ldw, BN, BK, true) ||
+      !make_map(&mwl, w_lo, N, K, ldw, BN, BK, true) ||
+      (NA == 2 && !make_map(&mal, a_lo, M, K, lda, BM, BK, true)) ||
+      !tma::encode_dt(&mo, OUT32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, out, odims,
+                      ostr, obox, false))
+    return MN_ERR_UNSUPPORTED;
+  if (NA != 2) mal = ma;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int tiles = ((M + BM - 1) / BM) * (N / BN);
+  const int grid = std::max(1, std::min(tiles, sms));
+  using C = Cfg<BN, NA, 2, OUT32>;
+  auto kern = gemm_tc_kernel<BN, 2, NA, 2, OUT32>;
+  if (!ensure_smem(kern, C::bytes)) return MN_ERR_LAUNCH;
+  kern<<<grid, kThreads, C::bytes, st>>>(ma, mw, mo, mal, mwl, M, N, K, bias, out_scale, status);
   return MN_OK;
 }
 
@@ -306,6 +389,31 @@ extern "C" int mn_gemm_f16(int M, int N, int K, const void* a, int64_t lda, cons
   else if (N % 128 == 0)
     rc = gelu ? gemm::launch<128, 1>(M, N, K, a, lda, w, ldw, bias, out, ldo, status, st)
               : gemm::launch<128, 0>(M, N, K, a, lda, w, ldw, bias, out, ldo, status, st);
+  if (rc != MN_OK) return rc;
+  return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
+}
+
+extern "C" int mn_gemm_f32_split(int M, int N, int K, const void* a_hi, const void* a_lo, int64_t lda,
+                                 const void* w_hi, const void* w_lo, int64_t ldw, const float* bias,
+                                 float out_scale, void* out, int64_t ldo, int out_dtype, int* status, void* stream) {
+  if (M < 0 || N <= 0 || K <= 0 || !a_hi || !w_hi || !w_lo || !out) return MN_ERR_ARG;
+  if (out_dtype != MN_F32 && out_dtype != MN_F16) return MN_ERR_ARG;
+  if (M == 0) return MN_OK;
+  auto al16 = [](const void* p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  if (K % gemm::BK != 0 || N % 128 != 0 || lda < K || ldw < K || lda % 8 != 0 || ldw % 8 != 0 || ldo < N ||
+      ldo % 8 != 0 || !al16(a_hi) || !al16(a_lo) || !al16(w_hi) || !al16(w_lo) || !al16(out) || !al16(bias))
+    return MN_ERR_UNSUPPORTED;
+  cudaGetLastError();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc;
+  if (a_lo)
+    rc = out_dtype == MN_F32
+             ? gemm::launch_split<2, true>(M, N, K, a_hi, a_lo, lda, w_hi, w_lo, ldw, bias, out_scale, out, ldo, status, st)
+             : gemm::launch_split<2, false>(M, N, K, a_hi, a_lo, lda, w_hi, w_lo, ldw, bias, out_scale, out, ldo, status, st);
+  else
+    rc = out_dtype == MN_F32
+             ? gemm::launch_split<1, true>(M, N, K, a_hi, nullptr, lda, w_hi, w_lo, ldw, bias, out_scale, out, ldo, status, st)
+             : gemm::launch_split<1, false>(M, N, K, a_hi, nullptr, lda, w_hi, w_lo, ldw, bias, out_scale, out, ldo, status, st);
   if (rc != MN_OK) return rc;
   return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
 }

@@ -88,6 +88,18 @@ inline EncodeTiledFn encoder() {
 // 16-bit elements, box `box`, zero fill out of bounds.  L2 promotion is 256 B
 // unless `promote128`: a box whose rows are 128 B inside wider rows (one head
 // of a packed q/k/v row) would otherwise pull its neighbours' bytes too.
+inline bool encode_dt(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* ptr, const cuuint64_t* dims,
+                      const cuuint64_t* strides_bytes, const cuuint32_t* box, bool swizzle128,
+                      bool promote128 = false) {
+  EncodeTiledFn enc = encoder();
+  if (!enc) return false;
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return enc(map, dt, (cuuint32_t)rank, const_cast<void*>(ptr), dims, strides_bytes, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE,
+             swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+             promote128 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B : CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 inline bool encode(CUtensorMap* map, bool bf16, int rank, const void* ptr, const cuuint64_t* dims,
                    const cuuint64_t* strides_bytes, const cuuint32_t* box, bool swizzle128, bool promote128 = false) {
   EncodeTiledFn enc = encoder();

@@ -109,8 +109,18 @@ class MergeNetSmall(nn.Module):
 
     def __init__(self, img_size=224, patch_size=8, embed_dim=384, num_heads=6, mlp_ratio=4.0, local_depth=6,
                  latent_depth=6, num_classes=1000, metric_dim=64, spatial_radius=3.0, local_window=16,
-                 lambda_local=2.0):
+                 lambda_local=2.0, compute_dtype=torch.float16):
         super().__init__()
+        if compute_dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError(f"compute_dtype must be float16 or bfloat16 (the autocast types), got {compute_dtype}")
+        # the autocast type: GEMM outputs, attention operands and metric heads
+        # (fp16 autocast for the canonical model, bf16 for the 384/p8 config)
+        self.compute_dtype = compute_dtype
+        # the recovery cross-attention's fp32 projections: "split" runs them on
+        # the tensor cores as split-precision products (errors about 1e-6 of
+        # the largest output, 1.2-2.5x IEEE fp32's); "ieee" as IEEE fp32
+        # cuBLAS GEMMs (TF32 off), several times slower
+        self.cross_precision = "split"
         self.img_size, self.patch_size = img_size, patch_size
         self.embed_dim, self.num_heads = embed_dim, num_heads
         self.local_window = local_window
@@ -177,7 +187,7 @@ class MergeNetSmall(nn.Module):
     def _weights16(self):
         """fp16 copies of the GEMM weights autocast would cast on every call."""
         if self._half is None:
-            self._half = {n: p.detach().half() for n, p in self.named_parameters()
+            self._half = {n: p.detach().to(self.compute_dtype) for n, p in self.named_parameters()
                           if "pos_embed" not in n and "cls_token" not in n and "norm" not in n}
         return self._half
 
@@ -200,7 +210,7 @@ class MergeNetSmall(nn.Module):
 
     def _linear16(self, x, name, lin):
         w16 = self._weights16()
-        return F.linear(x.half(), w16[name + ".weight"], w16[name + ".bias"])
+        return F.linear(x.to(self.compute_dtype), w16[name + ".weight"], w16[name + ".bias"])
 
     def _metric(self, h_raw, i, metrics, w16):
         lin = self.local.metric_layers[i]
@@ -231,27 +241,64 @@ class MergeNetSmall(nn.Module):
 
     def _cross(self, topk_x, x_embed):
         """MyCrossAttention (model.py:122-221) as the reference runs it under
-        fp16 autocast: fp32 LayerNorms, q/k/v projections in true fp32 (the
-        reference turns autocast off for them, :140-145; TF32 is switched off
-        here), the attention on fp16 operands (SDPA autocasts them, :178-186)
-        with an fp16 context widened to fp32, and the out-projection in fp32
-        (:215-219)."""
+        fp16 autocast: fp32 LayerNorms, q/k/v projections in fp32 (autocast
+        off, :140-145), the attention on fp16 operands (SDPA autocasts them,
+        :178-186) with an fp16 context widened to fp32, and the
+        out-projection in fp32 (:215-219).  The fp32 GEMMs run on the tensor
+        cores as split-precision products (fp16 hi/lo pairs, three MMAs into
+        an fp32 accumulator, about 7e-7 relative per product); the q/k/v
+        results are rounded to fp16 as the reference rounds them for SDPA."""
+        from .linear import SplitWeight, layernorm_split, linear_f32_split
         ca = self.encode_cross_attention
         b, nq, c = topk_x.shape
         nk = x_embed.shape[1]
         hd = c // self.num_heads
-        qn = F.layer_norm(topk_x, (c,), ca.q_norm.weight, ca.q_norm.bias, ca.q_norm.eps)
-        kvn = F.layer_norm(x_embed, (c,), ca.kv_norm.weight, ca.kv_norm.bias, ca.kv_norm.eps)
-        if self._kv32 is None:
-            self._kv32 = (torch.cat([ca.k_proj.weight, ca.v_proj.weight]).contiguous(),
-                          torch.cat([ca.k_proj.bias, ca.v_proj.bias]).contiguous())
-        with _true_fp32_matmul():
-            q = F.linear(qn, ca.q_proj.weight, ca.q_proj.bias).half()
-            kv = F.linear(kvn, *self._kv32).half().view(b, nk, 2, self.num_heads, hd)
-            ctx = cross_attention(q.view(b, nq, self.num_heads, hd), kv[:, :, 0], kv[:, :, 1],
-                                  out_dtype=torch.float16)
-            out = F.linear(ctx.view(b, nq, c).float(), ca.out_proj.weight, ca.out_proj.bias)
-        return out
+        if self._kv32 is None or self._kv32[0].hi.device != topk_x.device:
+            self._kv32 = (SplitWeight(ca.q_proj.weight, ca.q_proj.bias),
+                          SplitWeight(torch.cat([ca.k_proj.weight, ca.v_proj.weight]),
+                                      torch.cat([ca.k_proj.bias, ca.v_proj.bias])),
+                          SplitWeight(ca.out_proj.weight, ca.out_proj.bias))
+        if self.cross_precision == "ieee":
+            return self._cross_ieee(topk_x, x_embed)
+        wq, wkv, wo = self._kv32
+        q_hi, q_lo = layernorm_split(topk_x, ca.q_norm)
+        kv_hi, kv_lo = layernorm_split(x_embed, ca.kv_norm)
+        cd = self.compute_dtype
+        if cd == torch.float16:
+            q = linear_f32_split(q_hi, q_lo, wq, out_dtype=torch.float16)
+            kv = linear_f32_split(kv_hi, kv_lo, wkv, out_dtype=torch.float16)
+        else:  # the GEMM writes fp32 or fp16; bf16 autocast rounds the fp32 result
+            q = linear_f32_split(q_hi, q_lo, wq).to(cd)
+            kv = linear_f32_split(kv_hi, kv_lo, wkv).to(cd)
+        kv = kv.view(b, nk, 2, self.num_heads, hd)
+        ctx = cross_attention(q.view(b, nq, self.num_heads, hd), kv[:, :, 0], kv[:, :, 1], out_dtype=cd)
+        ctx = ctx.view(b, nq, c)
+        if cd == torch.float16:  # an fp16 context is its own hi plane
+            return linear_f32_split(ctx, None, wo, a_scale=1.0, out_dtype=torch.float32)
+        c_hi = ctx.half()  # a bf16 value in fp16: hi plus the (tiny) remainder
+        c_lo = (ctx.float() - c_hi.float()).half()
+        return linear_f32_split(c_hi, c_lo, wo, a_scale=1.0, out_dtype=torch.float32)
+
+    def _cross_ieee(self, topk_x, x_embed):
+        """The same recovery cross-attention with IEEE fp32 cuBLAS GEMMs."""
+        ca = self.encode_cross_attention
+        b, nq, c = topk_x.shape
+        nk = x_embed.shape[1]
+        hd = c // self.num_heads
+        cd = self.compute_dtype
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        try:
+            qn = F.layer_norm(topk_x, (c,), ca.q_norm.weight, ca.q_norm.bias, ca.q_norm.eps)
+            kvn = F.layer_norm(x_embed, (c,), ca.kv_norm.weight, ca.kv_norm.bias, ca.kv_norm.eps)
+            q = F.linear(qn, ca.q_proj.weight, ca.q_proj.bias).to(cd)
+            k = F.linear(kvn, ca.k_proj.weight, ca.k_proj.bias).to(cd)
+            v = F.linear(kvn, ca.v_proj.weight, ca.v_proj.bias).to(cd)
+            ctx = cross_attention(q.view(b, nq, self.num_heads, hd), k.view(b, nk, self.num_heads, hd),
+                                  v.view(b, nk, self.num_heads, hd), out_dtype=cd)
+            return F.linear(ctx.view(b, nq, c).float(), ca.out_proj.weight, ca.out_proj.bias)
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev
 
     def _embed(self, images, w16, norm1):
         """timm PatchEmbed + _pos_embed, then the first block's norm1: the
@@ -262,11 +309,13 @@ class MergeNetSmall(nn.Module):
         b, ch, hh, ww = images.shape
         p = self.patch_size
         gh, gw = hh // p, ww // p
-        patches = torch.empty(b, gh, gw, ch, p, p, device=images.device, dtype=torch.float16)
+        patches = torch.empty(b, gh, gw, ch, p, p, device=images.device, dtype=self.compute_dtype)
         from . import _lib as L
         img = images if images.dtype == torch.float32 and images.is_contiguous() else images.float().contiguous()
-        rc = L.lib().mn_patch_unfold(b, ch, hh, ww, p, L.ptr(img), L.ptr(patches), L.stream_of(img))
-        if rc == L.MN_ERR_UNSUPPORTED:  # patch sizes that are not a multiple of 8
+        rc = L.MN_ERR_UNSUPPORTED
+        if self.compute_dtype == torch.float16:  # the unfold kernel writes fp16
+            rc = L.lib().mn_patch_unfold(b, ch, hh, ww, p, L.ptr(img), L.ptr(patches), L.stream_of(img))
+        if rc == L.MN_ERR_UNSUPPORTED:  # bf16, or patch sizes that are not a multiple of 8
             patches.copy_(images.view(b, ch, gh, p, gw, p).permute(0, 2, 4, 1, 3, 5))
         else:
             L.check(rc, "mn_patch_unfold")
@@ -291,25 +340,26 @@ class MergeNetSmall(nn.Module):
         if not images.is_cuda:
             raise RuntimeError("MergeNetSmall runs on CUDA (there is no CPU path)")
         w16 = self._weights16()
+        cd = self.compute_dtype
         vit = self.local.vit
         b = images.shape[0]
         x, h0 = self._embed(images, w16, vit.blocks[0].norm1)
         n, c = x.shape[1], x.shape[2]
         depth = len(vit.blocks)
         metrics = torch.empty(depth, b, n, self.local.metric_layers[0].out_features, device=x.device,
-                              dtype=torch.float16)
+                              dtype=self.compute_dtype)
         y = None
         for i, blk in enumerate(vit.blocks):
             # x <- x + y (previous MLP), h = LN1(x); fp16(x) feeds the previous metric head
             if i == 0:
                 h = h0
             else:
-                _, h, raw = add_layernorm(x, y, blk.norm1, x_out=x, want_raw=True)
+                _, h, raw = add_layernorm(x, y, blk.norm1, x_out=x, want_raw=True, dtype=cd)
                 self._metric(raw, i - 1, metrics, w16)
             p = self._attn_local(h, i, blk)
-            _, h, _ = add_layernorm(x, p, blk.norm2, x_out=x)
+            _, h, _ = add_layernorm(x, p, blk.norm2, x_out=x, dtype=cd)
             y = self._mlp(h, f"local.vit.blocks.{i}", blk)
-        _, _, raw = add_layernorm(x, y, None, x_out=x, want_ln=False, want_raw=True)
+        _, _, raw = add_layernorm(x, y, None, x_out=x, want_ln=False, want_raw=True, dtype=cd)
         self._metric(raw, depth - 1, metrics, w16)
         x_embed = x
         route = self._plan(x.device)(x_embed, metrics, check=False)
@@ -320,9 +370,9 @@ class MergeNetSmall(nn.Module):
         log_size = route.topk_size.log()
         y = None
         for i, blk in enumerate(self.latent.vit.blocks):
-            _, h, _ = add_layernorm(x_trace, y, blk.norm1, x_out=x_trace if y is not None else None)
+            _, h, _ = add_layernorm(x_trace, y, blk.norm1, x_out=x_trace if y is not None else None, dtype=cd)
             p = self._attn_latent(h, i, blk, log_size)
-            _, h, _ = add_layernorm(x_trace, p, blk.norm2, x_out=x_trace)
+            _, h, _ = add_layernorm(x_trace, p, blk.norm2, x_out=x_trace, dtype=cd)
             y = self._mlp(h, f"latent.vit.blocks.{i}", blk)
         lv = self.latent.vit
         # the latent encoder's final norm over every carrier row (fp32 under
@@ -461,20 +511,6 @@ class ForwardGraph:
         return 1 + (2 * nl + 1 + 2 + 2 * nt) + (nl + nt + 1) + 4
 
 
-class _true_fp32_matmul:
-    """fp32 GEMMs in IEEE fp32 (no TF32) inside the block, whatever the
-    process-wide setting; restores it on exit."""
-
-    def __enter__(self):
-        self.prev = torch.backends.cuda.matmul.allow_tf32
-        torch.backends.cuda.matmul.allow_tf32 = False
-        return self
-
-    def __exit__(self, *exc):
-        torch.backends.cuda.matmul.allow_tf32 = self.prev
-        return False
-
-
 def embed_layernorm(emb, pos, cls, ln):
     """x = [cls + pos[0]; float(emb) + pos[1:]] per image (fp32) and its fp16
     LayerNorm, in one pass of the library's fused kernel.  emb [B, T-1, C]
@@ -482,29 +518,32 @@ def embed_layernorm(emb, pos, cls, ln):
     from . import _lib as L
     b, t1, c = emb.shape
     x = torch.empty(b, t1 + 1, c, device=emb.device, dtype=torch.float32)
-    h = torch.empty(b, t1 + 1, c, device=emb.device, dtype=torch.float16)
+    h = torch.empty(b, t1 + 1, c, device=emb.device, dtype=emb.dtype)
     emb = emb.contiguous()
     pos = pos.contiguous().float()
     cls = cls.contiguous().float()
     L.check(L.lib().mn_embed_layernorm(b, t1 + 1, c, L.ptr(emb), L.ptr(pos), L.ptr(cls), L.ptr(ln.weight),
-                                       L.ptr(ln.bias), float(ln.eps), L.ptr(x), L.ptr(h), L.stream_of(emb)),
+                                       L.ptr(ln.bias), float(ln.eps), L.ptr(x), L.ptr(h), L.dtype_code(emb.dtype),
+                                       L.stream_of(emb)),
             "mn_embed_layernorm")
     return x, h
 
 
-def add_layernorm(x, y, ln, x_out=None, want_ln=True, want_raw=False):
+def add_layernorm(x, y, ln, x_out=None, want_ln=True, want_raw=False, dtype=None):
     """(x + y [fp32], LayerNorm(x + y) [fp16], fp16(x + y)) in one pass of the
     library's fused kernel; y (fp16) may be None, outputs not wanted are None."""
     from . import _lib as L
     c = x.shape[-1]
     rows = x.numel() // c
-    h_ln = torch.empty(x.shape, device=x.device, dtype=torch.float16) if want_ln else None
-    h_raw = torch.empty(x.shape, device=x.device, dtype=torch.float16) if want_raw else None
-    if y is not None and y.dtype != torch.float16:
-        y = y.half()
+    dtype = dtype or (y.dtype if y is not None and y.dtype in (torch.float16, torch.bfloat16) else torch.float16)
+    h_ln = torch.empty(x.shape, device=x.device, dtype=dtype) if want_ln else None
+    h_raw = torch.empty(x.shape, device=x.device, dtype=dtype) if want_raw else None
+    if y is not None and y.dtype != dtype:
+        y = y.to(dtype)
     L.check(L.lib().mn_add_layernorm(rows, c, L.ptr(x), L.ptr(y), L.ptr(ln.weight) if want_ln else None,
                                      L.ptr(ln.bias) if want_ln else None, float(ln.eps) if want_ln else 0.0,
-                                     L.ptr(x_out), L.ptr(h_ln), L.ptr(h_raw), L.stream_of(x)), "mn_add_layernorm")
+                                     L.ptr(x_out), L.ptr(h_ln), L.ptr(h_raw), L.dtype_code(dtype), L.stream_of(x)),
+            "mn_add_layernorm")
     return x_out, h_ln, h_raw
 
 
@@ -534,14 +573,16 @@ _FIXED = {
 }
 
 
-def mergenet_small_cls(pretrained=False, **kwargs):
+def mergenet_small_cls(pretrained=False, compute_dtype=torch.float16, **kwargs):
     """The reference's ``mergenet_small_cls`` factory
     (opentome/models/mergenet/model.py:1602-1607) on the B200 kernels: the
     same keyword arguments and canonical defaults, and a module whose state
     dict has the reference's parameter names and shapes.  Pretrained weights
     are loaded with ``load_state_dict`` from a reference checkpoint
     (downloading them is not supported).  Keyword values that select paths
-    other than the canonical inference path raise ``NotImplementedError``."""
+    other than the canonical inference path raise ``NotImplementedError``.
+    ``compute_dtype`` is the autocast type the reference would run under
+    (float16, or bfloat16 as for the 384 x 384 / patch-8 configuration)."""
     if pretrained:
         raise NotImplementedError("load a reference checkpoint with load_state_dict(strict=True) instead")
     cfg = dict(MERGENET_SMALL_CANONICAL_KWARGS)
@@ -558,7 +599,7 @@ def mergenet_small_cls(pretrained=False, **kwargs):
     return MergeNetSmall(img_size=cfg["img_size"], patch_size=cfg["patch_size"], local_depth=cfg["local_depth"],
                          latent_depth=cfg["latent_depth"], num_classes=num_classes, metric_dim=cfg["dtem_feat_dim"],
                          spatial_radius=float(cfg["dtem_spatial_radius"]), local_window=cfg["local_block_window"],
-                         lambda_local=cfg["lambda_local"])
+                         lambda_local=cfg["lambda_local"], compute_dtype=compute_dtype)
 
 
 try:  # register under the reference's name when timm is importable

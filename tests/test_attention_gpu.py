@@ -307,21 +307,23 @@ def test_latent_proportional_attention(dev, n):
     assert mn.attention.attention_status(dev) == 0
 
 
-@pytest.mark.parametrize("rows,y", [(785 * 3, True), (393 * 2, False), (7, True)])
-def test_add_layernorm(dev, rows, y):
+@pytest.mark.parametrize("rows,y,dtype", [(785 * 3, True, torch.float16), (393 * 2, False, torch.float16),
+                                          (7, True, torch.float16), (785 * 2, True, torch.bfloat16)])
+def test_add_layernorm(dev, rows, y, dtype):
     from mergenet_b200.model import add_layernorm
     torch.manual_seed(rows)
     x = torch.randn(rows, 384, device=dev) * 3
-    yy = torch.randn(rows, 384, device=dev).half() if y else None
+    yy = torch.randn(rows, 384, device=dev).to(dtype) if y else None
     ln = torch.nn.LayerNorm(384, eps=1e-6).to(dev)
     torch.nn.init.normal_(ln.weight)
     torch.nn.init.normal_(ln.bias)
     s = x + (yy.float() if y else 0)
     xo = torch.empty_like(x)
-    _, h, raw = add_layernorm(x, yy, ln, x_out=xo, want_raw=True)
+    _, h, raw = add_layernorm(x, yy, ln, x_out=xo, want_raw=True, dtype=dtype)
     assert torch.equal(xo, s)
-    assert torch.equal(raw, s.half())
-    torch.testing.assert_close(h.float(), ln(s).half().float(), atol=2e-3, rtol=2e-3)
+    assert torch.equal(raw, s.to(dtype))
+    tol = 2e-3 if dtype == torch.float16 else 1.6e-2
+    torch.testing.assert_close(h.float(), ln(s).to(dtype).float(), atol=tol, rtol=tol)
 
 
 @pytest.mark.parametrize("batch,tokens", [(3, 785), (1, 2), (2, 1)])
@@ -354,3 +356,20 @@ def test_patch_unfold_exact(dev, b, c, hw, p):
     L.check(L.lib().mn_patch_unfold(b, c, hw, hw, p, L.ptr(img), L.ptr(out), L.stream_of(img)), "unfold")
     want = img.view(b, c, gh, p, gh, p).permute(0, 2, 4, 1, 3, 5).half()
     assert torch.equal(out, want)
+
+
+def test_window_attention_matches_flash_attention(dev):
+    """The reference's windowed attention IS FlashAttention-2's
+    flash_attn_func(window_size=(w, w)) (bias_local_attn.py:560-567); the
+    flash_attn library is installed, so compare with it directly on the
+    canonical shape (785 tokens, 6 heads of 64, window 16), q/k/v read from
+    the packed projection."""
+    fa = pytest.importorskip("flash_attn")
+    import mergenet_b200 as mn
+    torch.manual_seed(21)
+    b, n, h, d = 4, 785, 6, 64
+    qkv = (torch.randn(b, n, 3 * h * d, device=dev) * 0.5).half()
+    view = qkv.view(b, n, 3, h, d)
+    want = fa.flash_attn_func(view[:, :, 0], view[:, :, 1], view[:, :, 2], window_size=(16, 16))
+    got = mn.local_attention_packed(qkv, h, 16, cls_global=False).view(b, n, h, d)
+    torch.testing.assert_close(got.float(), want.float(), atol=5e-3, rtol=5e-3)

@@ -100,3 +100,20 @@ def test_oracle_attention_matches_reference_naive(golden_dir):
         np.testing.assert_allclose(local_attention(q, k, v, w, scale=1.0), g[f"unbiased{i}"], rtol=1e-5, atol=1e-5)
         np.testing.assert_allclose(local_attention(q, k, v, w, bias=bias, scale=1.0), g[f"biased{i}"],
                                    rtol=1e-5, atol=1e-5)
+
+
+def test_timed_port_routing_matches_the_oracle():
+    """The batched torch routing of the timed CPU baseline (model_cpu.route_torch)
+    gives the oracle's carriers, masses and features."""
+    import torch
+    from oracle import model_cpu
+    grid = (28, 28)
+    r_list = canonical_r_list(grid)
+    x, metrics = routing_inputs(3, 2, grid, 32, 64)
+    geom = O.Geometry(grid, 3.0)
+    ref = O.route_and_gather(x, metrics, r_list, geom)
+    tx, ts, ti = model_cpu.route_torch(torch.from_numpy(x), [torch.from_numpy(m.astype(np.float32)) for m in metrics],
+                                       r_list, geom)
+    np.testing.assert_array_equal(ti.numpy(), ref["topk_idx"])
+    np.testing.assert_allclose(ts.numpy(), ref["topk_size"], rtol=3e-5, atol=3e-5)
+    np.testing.assert_allclose(tx.numpy(), ref["topk_x"], rtol=1e-4, atol=1e-4)
