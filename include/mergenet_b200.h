@@ -287,6 +287,14 @@ int mn_gemm_f16(int M, int N, int K, const void* a, int64_t lda, const void* w,
                 int64_t ldw, const void* bias, int epilogue, void* out,
                 int64_t ldo, int* status, void* stream);
 
+/* Self-test of the bounded wait the tensor-core kernels share (no
+ * counterpart in the reference): one CTA allocates tensor memory, waits on a
+ * barrier phase that nothing completes, gives up after limit_ms (0.001 ..
+ * 1000), ORs MN_STATUS_TC_TIMEOUT into *status and frees its tensor memory,
+ * leaving the context usable.  It shows that a stuck copy or MMA ends in an
+ * error status rather than a hang. */
+int mn_tc_wait_selftest(int* status, double limit_ms, void* stream);
+
 /* Split-precision GEMM for the fp32 Linear layers of the recovery
  * cross-attention (MyCrossAttention's q/k/v and out projections, which the
  * reference runs in fp32 with autocast off,

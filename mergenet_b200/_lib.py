@@ -76,6 +76,7 @@ _SIGNATURES = {
     "mn_gemm_f32_split": (c_int, [c_int, c_int, c_int, _P, _P, c_int64, _P, _P, c_int64, _P, c_float, _P, c_int64,
                                   c_int, _P, _P]),
     "mn_layernorm_split": (c_int, [c_int64, c_int, _P, _P, _P, c_float, c_float, _P, _P, _P]),
+    "mn_tc_wait_selftest": (c_int, [_P, c_double, _P]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

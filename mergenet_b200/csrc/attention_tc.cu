@@ -1239,3 +1239,37 @@ bool attention_tc(int dtype, const void* q, int64_t qb, int64_t qn, int64_t qh, 
 }
 
 }  // namespace mn
+
+// ---------------------------------------------------------------------------
+// Self-test of the bounded wait every tensor-core kernel here relies on: one
+// CTA allocates TMEM as the kernels do, waits on an mbarrier phase that
+// nothing completes, gives up after limit_ns, records MN_STATUS_TC_TIMEOUT
+// and frees its TMEM -- the exit path a stuck copy or MMA would take.
+// ---------------------------------------------------------------------------
+namespace mn {
+__global__ void __launch_bounds__(128, 1) tc_wait_selftest_kernel(int* status, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_slot;
+  if (threadIdx.x < 32) tc::tmem_alloc(&tmem_slot, 32);
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (threadIdx.x == 0 && !tc::mbar_wait(&bar, 0, nullptr, limit_ns) && status)
+    atomicOr(status, MN_STATUS_TC_TIMEOUT);
+  tc::fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x < 32) tc::tmem_dealloc(tmem_slot, 32);
+}
+}  // namespace mn
+
+extern "C" int mn_tc_wait_selftest(int* status, double limit_ms, void* stream) {
+  if (!status || !(limit_ms >= 0.001 && limit_ms <= 1000.0)) return MN_ERR_ARG;
+  cudaGetLastError();
+  mn::tc_wait_selftest_kernel<<<1, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      status, (unsigned long long)(limit_ms * 1e6));
+  return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
+}

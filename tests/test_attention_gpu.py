@@ -373,3 +373,29 @@ def test_window_attention_matches_flash_attention(dev):
     want = fa.flash_attn_func(view[:, :, 0], view[:, :, 1], view[:, :, 2], window_size=(16, 16))
     got = mn.local_attention_packed(qkv, h, 16, cls_global=False).view(b, n, h, d)
     torch.testing.assert_close(got.float(), want.float(), atol=5e-3, rtol=5e-3)
+
+
+def test_bounded_wait_gives_up_and_the_context_survives(dev):
+    """A tensor-core wait that nothing completes ends after its limit with
+    MN_STATUS_TC_TIMEOUT in the status word (mn_tc_wait_selftest: TMEM
+    allocated and freed as in the kernels), and the next attention call on
+    the same context runs clean and correct."""
+    import time
+    from mergenet_b200 import _lib as L
+    import mergenet_b200 as mn
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    t0 = time.perf_counter()
+    L.check(L.lib().mn_tc_wait_selftest(L.ptr(status), 20.0, L.stream_of(status)), "mn_tc_wait_selftest")
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    assert int(status.item()) & L.MN_STATUS_TC_TIMEOUT
+    assert elapsed < 5.0
+    torch.manual_seed(2)
+    qkv = (torch.randn(2, 785, 1152, device=dev) * 0.5).half()
+    out = mn.local_attention_packed(qkv, 6, 16, cls_global=True)
+    view = qkv.view(2, 785, 3, 6, 64)
+    q, k, v = (view[:, :, i].transpose(1, 2) for i in range(3))
+    exp = reference_bhnd(q, k, v, None, 16)
+    exp[:, :, :1] = torch.softmax(q[:, :, :1].float() @ k.float().transpose(-1, -2) / 8.0, -1) @ v.float()
+    torch.testing.assert_close(out.float(), exp.transpose(1, 2).reshape(2, 785, 384), atol=5e-3, rtol=5e-3)
+    assert mn.attention.attention_status(dev) == 0

@@ -252,6 +252,33 @@ def test_select_infeasible_budget_fails_closed(dev):
         mn.dtem_select(1, scores, allowed)
 
 
+def test_select_degenerate_range_fails_closed(dev):
+    """Equal scores everywhere give every donor row the same energy, so the
+    ThreTopK range (global max - min, thetopk.py:12-13) is zero and the
+    reference divides by it; the kernel flags MN_STATUS_DEGENERATE_RANGE
+    (and only that bit) and the host raises instead of returning NaNs."""
+    import mergenet_b200 as mn
+    from mergenet_b200 import _lib as L
+    scores = torch.full((2, 50, 9), 0.3, device=dev)
+    allowed = torch.ones(2, 50, 9, dtype=torch.bool, device=dev)
+    with pytest.raises(RuntimeError, match="range"):
+        mn.dtem_select(10, scores, allowed)
+    s = scores.contiguous()
+    out = torch.empty_like(s)
+    wsb = L.lib().mn_dtem_select_workspace_bytes(2, 50)
+    ws = torch.empty(int(wsb), dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    L.check(L.lib().mn_dtem_select(2, 50, 9, L.ptr(s), L.ptr(allowed.to(torch.uint8)), 10, 1.0, 30.0, L.ptr(out),
+                                   L.ptr(ws), wsb, L.ptr(status), L.stream_of(s)), "mn_dtem_select")
+    assert int(status.item()) == L.MN_STATUS_DEGENERATE_RANGE
+    # a well-posed call on the same context afterwards is unaffected
+    gen = torch.Generator().manual_seed(3)
+    good = torch.randn(2, 50, 9, generator=gen)
+    got = mn.dtem_select(10, good.to(dev), allowed).cpu().numpy()
+    want, _, _ = O.select(10, good.numpy(), np.ones((2, 50, 9), dtype=bool))
+    np.testing.assert_allclose(got, want, rtol=0, atol=2e-6)
+
+
 def test_select_empty_rows_stay_finite(dev):
     """tests/test_dtem_spatial_mask.py:205-239: an isolated donor keeps its mass."""
     import mergenet_b200 as mn
