@@ -1182,6 +1182,13 @@ static bool launch_win_persistent(const void* q, int64_t qb, int64_t qn, int64_t
 #define MN_TC_BLOCK_KEYS 64  // key block of the multi-block paths: 64 or 128
 #endif
 
+#ifndef MN_TC_FULL_WS
+#define MN_TC_FULL_WS 1  // no window: the warp-specialised kernel (attention_ws.cu)
+#endif
+bool attention_ws(int dtype, const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v,
+                  int64_t kb, int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, float scale, const void* bias,
+                  int bias_dtype, void* out, int out_dtype, int* err, cudaStream_t st);
+
 template <typename ET>
 static bool dispatch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const void* k, const void* v, int64_t kb,
                         int64_t kn, int64_t kh, int B, int Nq, int Nk, int H, int window, float scale,
@@ -1198,6 +1205,9 @@ static bool dispatch_tc(const void* q, int64_t qb, int64_t qn, int64_t qh, const
   if (window >= 0)
     return launch_tc<ET, NBM, true>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
                                     out, out_dtype, err, st, cls_global, cls_done);
+  if (MN_TC_FULL_WS)
+    return attention_ws(std::is_same<ET, __half>::value ? MN_F16 : MN_BF16, q, qb, qn, qh, k, v, kb, kn, kh, B, Nq,
+                        Nk, H, scale, bias, bias_dtype, out, out_dtype, err, st);
   return launch_tc<ET, NBM, false>(q, qb, qn, qh, k, v, kb, kn, kh, B, Nq, Nk, H, window, scale, bias, bias_dtype,
                                    out, out_dtype, err, st, cls_global, cls_done);
 }
