@@ -10,7 +10,8 @@ a profiler can skip the first iteration's launches and capture the second's.
 
 * ``attention``: windowed local attention with the CLS row (packed qkv
   [B, 785, 1152] fp16, window 16), latent attention over 393 tokens with a
-  per-key log-size bias, and the 393 x 785 recovery cross-attention.
+  per-key log-size bias, and the 393 x 785 recovery cross-attention (the
+  last two on the warp-specialised kernel).
 * ``routing``: the fused six-layer routing and carrier gather on x_embed
   [B, 785, 384] fp32 and metrics [6, B, 785, 64] fp16.
 * ``gemm``: the MLP GEMMs of one local block on B x 785 token rows: fc1 with
