@@ -275,6 +275,9 @@ __global__ void __launch_bounds__(kLaneScoreThreads, 2) route_score_lane_kernel(
     float a[CM];
     load_metric_row<CM>(mbase + (int64_t)(1 + 2 * d + dp) * CM, a);
     normalise_row<CM>(a);
+    float2 a2[CM / 2];
+#pragma unroll
+    for (int i = 0; i < CM / 2; ++i) a2[i] = make_float2(a[2 * i], a[2 * i + 1]);
     const int32_t* srx = pt.slot_rx + (int64_t)d * kc;
     float sc[kMaxKc];
 #pragma unroll
@@ -288,16 +291,16 @@ __global__ void __launch_bounds__(kLaneScoreThreads, 2) route_score_lane_kernel(
         continue;
       }
       const float4* rv = reinterpret_cast<const float4*>(nrm + (int64_t)(sidx - s_lo) * RS);
-      float acc4[4] = {0.f, 0.f, 0.f, 0.f};
+      // four accumulators over channels i mod 4, two per fp32x2 FMA (each
+      // lane bitwise the scalar FMA)
+      float2 acc01 = make_float2(0.f, 0.f), acc23 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int w = 0; w < CM / 4; ++w) {
         const float4 r4 = rv[w];
-        acc4[0] = fmaf(a[4 * w], r4.x, acc4[0]);
-        acc4[1] = fmaf(a[4 * w + 1], r4.y, acc4[1]);
-        acc4[2] = fmaf(a[4 * w + 2], r4.z, acc4[2]);
-        acc4[3] = fmaf(a[4 * w + 3], r4.w, acc4[3]);
+        acc01 = ffma2(a2[2 * w], make_float2(r4.x, r4.y), acc01);
+        acc23 = ffma2(a2[2 * w + 1], make_float2(r4.z, r4.w), acc23);
       }
-      const float acc = (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
+      const float acc = (acc01.x + acc01.y) + (acc23.x + acc23.y);
       // logits = scores / tau1 (dtem.py:1557); exact without a division at tau1 == 1
       sc[c] = unit_tau ? acc : acc / tau1;
     }

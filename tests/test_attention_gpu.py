@@ -399,3 +399,37 @@ def test_bounded_wait_gives_up_and_the_context_survives(dev):
     exp[:, :, :1] = torch.softmax(q[:, :, :1].float() @ k.float().transpose(-1, -2) / 8.0, -1) @ v.float()
     torch.testing.assert_close(out.float(), exp.transpose(1, 2).reshape(2, 785, 384), atol=5e-3, rtol=5e-3)
     assert mn.attention.attention_status(dev) == 0
+
+
+@pytest.mark.parametrize("b,nq,nk,h,dtype,biased", [
+    (48, 393, 393, 6, torch.float16, True),    # latent shape, several tiles per query stream
+    (48, 393, 393, 6, torch.bfloat16, True),
+    (48, 393, 785, 6, torch.float16, False),   # cross shape, several tiles per query stream
+    (1, 1000, 2000, 2, torch.bfloat16, False),
+    (300, 9, 64, 1, torch.float16, False),     # one key block, many tiny items
+])
+def test_warp_specialised_many_items(dev, b, nq, nk, h, dtype, biased):
+    """The warp-specialised kernel (latent and cross) when each of its query
+    streams walks many (tile, head, image) items: Q stages and the K/V / S
+    rings wrap many times.  Checked against an fp32 restatement, and run
+    twice to check the result is bit-for-bit repeatable."""
+    import mergenet_b200 as mn
+    g = torch.Generator(device="cpu").manual_seed(b * 1000 + nq + nk)
+    q = (torch.randn(b, nq, h, 64, generator=g) * 0.5).to(dev, dtype)
+    k = (torch.randn(b, nk, h, 64, generator=g) * 0.5).to(dev, dtype)
+    v = torch.randn(b, nk, h, 64, generator=g).to(dev, dtype)
+    bias = (torch.rand(b, nk, generator=g) * 3 + 0.05).log().to(dev) if biased else None
+    if biased:
+        qkv = torch.stack([q, k, v], dim=2).reshape(b, nq, 3 * h * 64)
+        run = lambda: mn.local_attention_packed(qkv, h, -1, cls_global=False, bias=bias).view(b, nq, h, 64)
+    else:
+        run = lambda: mn.cross_attention(q, k, v)
+    out1, out2 = run(), run()
+    s = torch.einsum("bqhd,bkhd->bhqk", q.float(), k.float()) / 8.0
+    if biased:
+        s = s + bias.to(dtype).float()[:, None, None, :]
+    exp = torch.einsum("bhqk,bkhd->bqhd", torch.softmax(s, -1), v.float())
+    tol = 2e-2 if dtype == torch.bfloat16 else 5e-3
+    torch.testing.assert_close(out1.float(), exp, atol=tol, rtol=tol)
+    assert torch.equal(out1, out2)
+    assert mn.attention.attention_status(dev) == 0
