@@ -16,11 +16,12 @@
 //     thread) read S(g), keep the row's running maximum and sum, and write
 //     P(g) as packed fp16 / bf16 pairs over the first half of S(g)'s columns.
 //
-// S(g+2) is issued as soon as P.V(g) is, so the tensor core computes the
-// next scores while the softmax warps work, and the two
-// slots interleave on the SM's tensor core, special-function units and
-// issue slots.  All hand-offs are mbarriers; every wait is bounded in time
-// and gives up early once any CTA has recorded an error.
+// S(g+2) is issued right after P.V(g) (its buffer held P(g-1), so it waits
+// for P.V(g-1) to complete), so the tensor core computes the next scores
+// while the softmax warps work, and the two slots interleave on the SM's
+// tensor core, special-function units and issue slots.  All hand-offs are
+// mbarriers; every wait is bounded in time and gives up early once any CTA
+// has recorded an error.
 #include <algorithm>
 
 #include "common.cuh"
