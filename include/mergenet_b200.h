@@ -253,6 +253,14 @@ int mn_attention(int batch, int nq, int nk, int heads, int head_dim, int dtype,
                  int64_t kv_sh, int window, float scale, void* out,
                  int out_dtype, int* status, void* stream);
 
+/* LayerNorm(x + y) written in fp32 (y 16-bit of type half_dtype, optional):
+ * the latent encoder's final norm over every carrier row, which fp16 / bf16
+ * autocast runs in fp32 (opentome/models/mergenet/model.py:1195-1198),
+ * fused with the residual add before it.  channels in {256, 384, 512, 768}. */
+int mn_add_layernorm_f32(int64_t rows, int channels, const float* x, const void* y,
+                         const float* gamma, const float* beta, float eps, float* out,
+                         int half_dtype, void* stream);
+
 /* Residual add + LayerNorm + fp16 cast over rows of a fp32 residual stream
  * (the norm1/norm2 inputs of the LocalBlock / latent Block forward under fp16
  * autocast, opentome/timm/bias_local_attn.py:867-868): s = x + y (y fp16,

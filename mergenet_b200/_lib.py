@@ -70,6 +70,7 @@ _SIGNATURES = {
     "mn_attention": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, _P, c_int64, c_int64, c_int64, _P, _P,
                              c_int64, c_int64, c_int64, c_int, c_float, _P, c_int, _P, _P]),
     "mn_add_layernorm": (c_int, [c_int64, c_int, _P, _P, _P, _P, c_float, _P, _P, _P, c_int, _P]),
+    "mn_add_layernorm_f32": (c_int, [c_int64, c_int, _P, _P, _P, _P, c_float, _P, c_int, _P]),
     "mn_embed_layernorm": (c_int, [c_int, c_int, c_int, _P, _P, _P, _P, _P, c_float, _P, _P, c_int, _P]),
     "mn_patch_unfold": (c_int, [c_int, c_int, c_int, c_int, c_int, _P, _P, _P]),
     "mn_gemm_f16": (c_int, [c_int, c_int, c_int, _P, c_int64, _P, c_int64, _P, c_int, _P, c_int64, _P, _P]),

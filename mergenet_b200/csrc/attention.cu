@@ -30,8 +30,9 @@ extern "C" int mn_attention(int batch, int nq, int nk, int heads, int head_dim, 
                             int64_t q_sb, int64_t q_sn, int64_t q_sh, const void* k, const void* v, int64_t kv_sb,
                             int64_t kv_sn, int64_t kv_sh, int window, float scale, void* out, int out_dtype,
                             int* status, void* stream) {
-  if (batch < 0 || nq < 0 || nk <= 0 || heads <= 0 || head_dim <= 0 || !out) return MN_ERR_ARG;
-  if ((int64_t)batch * nq == 0) return MN_OK;
+  if (batch < 0 || nq < 0 || nk <= 0 || heads <= 0 || head_dim <= 0) return MN_ERR_ARG;
+  if ((int64_t)batch * nq == 0) return MN_OK;  // nothing to compute (empty tensors may have null pointers)
+  if (!out) return MN_ERR_ARG;
   if (!q || !k || !v || dtype < 0 || dtype > 2 || out_dtype < 0 || out_dtype > 2) return MN_ERR_ARG;
   if (!attention_tc_supported(dtype, q, q_sb, q_sn, q_sh, k, v, kv_sb, kv_sn, kv_sh, nq, nk, head_dim, window, false))
     return MN_ERR_UNSUPPORTED;
@@ -48,8 +49,9 @@ extern "C" int mn_local_attention(int batch, int tokens, int heads, int head_dim
                                   const void* k, const void* v, int64_t s_b, int64_t s_n, int64_t s_h,
                                   const void* bias, int bias_dtype, int window, int cls_global, float scale,
                                   void* out, int out_dtype, int* status, void* stream) {
-  if (batch < 0 || tokens < 0 || heads <= 0 || head_dim <= 0 || !out) return MN_ERR_ARG;
-  if ((int64_t)batch * tokens == 0) return MN_OK;
+  if (batch < 0 || tokens < 0 || heads <= 0 || head_dim <= 0) return MN_ERR_ARG;
+  if ((int64_t)batch * tokens == 0) return MN_OK;  // nothing to compute (empty tensors may have null pointers)
+  if (!out) return MN_ERR_ARG;
   if (!q || !k || !v) return MN_ERR_ARG;
   if (dtype < 0 || dtype > 2 || out_dtype < 0 || out_dtype > 2 || (bias && (bias_dtype < 0 || bias_dtype > 2)))
     return MN_ERR_ARG;

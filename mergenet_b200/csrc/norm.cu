@@ -93,6 +93,59 @@ __global__ void __launch_bounds__(256) add_layernorm_kernel(const float* __restr
   if (h_ln) layernorm_row_store<C, HT>(v, gamma, beta, eps, h_ln + row * C, lane);
 }
 
+// LayerNorm(x + y) of one row per warp, written in fp32: the latent
+// encoder's final norm, which autocast runs in fp32 (model.py:1195-1198).
+template <int C, typename HT>
+__global__ void __launch_bounds__(256) add_layernorm_f32_kernel(const float* __restrict__ x,
+                                                                const HT* __restrict__ y,
+                                                                const float* __restrict__ gamma,
+                                                                const float* __restrict__ beta, float eps,
+                                                                int64_t rows, float* __restrict__ out) {
+  constexpr int V = C / 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * C);
+  float v[V][4];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const float4 a = xr[lane + 32 * i];
+    v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+  }
+  if (y) {
+    const uint2* yr = reinterpret_cast<const uint2*>(y + row * C);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      float f[4];
+      unpack4<HT>(yr[lane + 32 * i], f);
+      v[i][0] += f[0]; v[i][1] += f[1];
+      v[i][2] += f[2]; v[i][3] += f[3];
+    }
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) s += (v[i][0] + v[i][1]) + (v[i][2] + v[i][3]);
+  const float mean = warp_sum(s) * (1.0f / C);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d = v[i][j] - mean;
+      q = fmaf(d, d, q);
+    }
+  const float rstd = rsqrtf(warp_sum(q) * (1.0f / C) + eps);
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
+  float4* o = reinterpret_cast<float4*>(out + row * C);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const float4 g = g4[lane + 32 * i], bb = b4[lane + 32 * i];
+    o[lane + 32 * i] = make_float4((v[i][0] - mean) * rstd * g.x + bb.x, (v[i][1] - mean) * rstd * g.y + bb.y,
+                                   (v[i][2] - mean) * rstd * g.z + bb.z, (v[i][3] - mean) * rstd * g.w + bb.w);
+  }
+}
+
 // fp32 LayerNorm of one row per warp, written as two fp16 planes for the
 // split-precision GEMM: ys = LayerNorm(x) * scale (scale an exact power of
 // two), hi = fp16(ys), lo = fp16(ys - hi), so hi + lo carries ys to 2^-22.
@@ -323,5 +376,29 @@ extern "C" int mn_layernorm_split(int64_t rows, int channels, const float* x, co
     case 768: layernorm_split_kernel<768><<<grid, 256, 0, st>>>(x, gamma, beta, eps, scale, rows, h, l); break;
     default: return MN_ERR_UNSUPPORTED;
   }
+  return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
+}
+
+extern "C" int mn_add_layernorm_f32(int64_t rows, int channels, const float* x, const void* y, const float* gamma,
+                                    const float* beta, float eps, float* out, int half_dtype, void* stream) {
+  if (rows < 0 || !x || !gamma || !beta || !out) return MN_ERR_ARG;
+  if (rows == 0) return MN_OK;
+  if (half_dtype != MN_F16 && half_dtype != MN_BF16) return MN_ERR_ARG;
+  cudaGetLastError();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  auto run = [&](auto tag) -> bool {
+    using HT = decltype(tag);
+    const HT* yh = static_cast<const HT*>(y);
+    switch (channels) {
+      case 384: add_layernorm_f32_kernel<384, HT><<<grid, 256, 0, st>>>(x, yh, gamma, beta, eps, rows, out); return true;
+      case 256: add_layernorm_f32_kernel<256, HT><<<grid, 256, 0, st>>>(x, yh, gamma, beta, eps, rows, out); return true;
+      case 512: add_layernorm_f32_kernel<512, HT><<<grid, 256, 0, st>>>(x, yh, gamma, beta, eps, rows, out); return true;
+      case 768: add_layernorm_f32_kernel<768, HT><<<grid, 256, 0, st>>>(x, yh, gamma, beta, eps, rows, out); return true;
+      default: return false;
+    }
+  };
+  const bool ok = half_dtype == MN_F16 ? run(__half{}) : run(__nv_bfloat16{});
+  if (!ok) return MN_ERR_UNSUPPORTED;
   return cudaGetLastError() == cudaSuccess ? MN_OK : MN_ERR_LAUNCH;
 }

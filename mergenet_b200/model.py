@@ -377,7 +377,7 @@ class MergeNetSmall(nn.Module):
         lv = self.latent.vit
         # the latent encoder's final norm over every carrier row (fp32 under
         # autocast); the head reads the CLS row (model.py:1195-1198)
-        x_latent = F.layer_norm(torch.add(x_trace, y), (c,), lv.norm.weight, lv.norm.bias, lv.norm.eps)
+        x_latent = add_layernorm_f32(x_trace, y, lv.norm)
         cls = x_latent[:, 0]
         logits = self._linear16(cls, "head", self.head)
         aux = {
@@ -503,12 +503,15 @@ class ForwardGraph:
     def library_launches(model):
         """Library (mn_*) kernels one forward launches: the patch unfold; two
         fused add+LayerNorm per block (the first one fused with the
-        embedding) plus the closing one and the two cross norms; one windowed
-        attention per local block (its CLS row computed by the same kernel);
-        one attention per latent block and for the recovery cross-attention;
-        and the four routing kernels."""
+        embedding) plus the closing one and the latent encoder's final norm;
+        one windowed attention per local block (its CLS row computed by the
+        same kernel); one attention per latent block and for the recovery
+        cross-attention; with split-precision cross projections, their two
+        LayerNorms and three GEMMs (q, k/v, output); and the four routing
+        kernels."""
         nl, nt = len(model.local.vit.blocks), len(model.latent.vit.blocks)
-        return 1 + (2 * nl + 1 + 2 + 2 * nt) + (nl + nt + 1) + 4
+        cross = 5 if getattr(model, "cross_precision", "split") == "split" else 0  # 2 split norms + 3 GEMMs
+        return 1 + (2 * nl + 1 + 2 * nt + 1) + (nl + nt + 1) + cross + 4
 
 
 def embed_layernorm(emb, pos, cls, ln):
@@ -545,6 +548,20 @@ def add_layernorm(x, y, ln, x_out=None, want_ln=True, want_raw=False, dtype=None
                                      L.ptr(x_out), L.ptr(h_ln), L.ptr(h_raw), L.dtype_code(dtype), L.stream_of(x)),
             "mn_add_layernorm")
     return x_out, h_ln, h_raw
+
+
+def add_layernorm_f32(x, y, ln):
+    """LayerNorm(x + y) in fp32 (y fp16 / bf16, may be None) in one pass of the
+    library's kernel: the latent encoder's final norm (fp32 under autocast)."""
+    from . import _lib as L
+    c = x.shape[-1]
+    rows = x.numel() // c
+    out = torch.empty(x.shape, device=x.device, dtype=torch.float32)
+    hd = y.dtype if y is not None else torch.float16
+    L.check(L.lib().mn_add_layernorm_f32(rows, c, L.ptr(x), L.ptr(y), L.ptr(ln.weight), L.ptr(ln.bias),
+                                         float(ln.eps), L.ptr(out), L.dtype_code(hd), L.stream_of(x)),
+            "mn_add_layernorm_f32")
+    return out
 
 
 # The reference factory's canonical kwargs (opentome/models/mergenet/model.py:

@@ -433,3 +433,35 @@ def test_warp_specialised_many_items(dev, b, nq, nk, h, dtype, biased):
     torch.testing.assert_close(out1.float(), exp, atol=tol, rtol=tol)
     assert torch.equal(out1, out2)
     assert mn.attention.attention_status(dev) == 0
+
+
+def test_empty_batch_attention(dev):
+    """Zero images: every attention entry point returns an empty result and
+    launches nothing (the reference returns empty tensors for an empty batch)."""
+    import mergenet_b200 as mn
+    qkv = torch.zeros(0, 785, 1152, device=dev, dtype=torch.float16)
+    assert mn.local_attention_packed(qkv, 6, 16, cls_global=True).shape == (0, 785, 384)
+    assert mn.local_attention_packed(qkv[:, :393], 6, -1, cls_global=False,
+                                     bias=torch.zeros(0, 393, device=dev)).shape == (0, 393, 384)
+    q = torch.zeros(0, 393, 6, 64, device=dev, dtype=torch.float16)
+    kv = torch.zeros(0, 785, 6, 64, device=dev, dtype=torch.float16)
+    assert mn.cross_attention(q, kv, kv).shape == (0, 393, 6, 64)
+    assert mn.attention.attention_status(dev) == 0
+
+
+@pytest.mark.parametrize("rows,y,dtype", [(393 * 3, True, torch.float16), (393 * 2, True, torch.bfloat16),
+                                          (5, False, torch.float16)])
+def test_add_layernorm_f32(dev, rows, y, dtype):
+    """The latent encoder's final norm: LayerNorm(x + y) in fp32 (autocast runs
+    layer_norm in fp32, model.py:1195-1198), fused with the residual add."""
+    from mergenet_b200.model import add_layernorm_f32
+    torch.manual_seed(rows)
+    x = torch.randn(rows, 384, device=dev) * 3
+    yy = torch.randn(rows, 384, device=dev).to(dtype) if y else None
+    ln = torch.nn.LayerNorm(384, eps=1e-6).to(dev)
+    torch.nn.init.normal_(ln.weight)
+    torch.nn.init.normal_(ln.bias)
+    out = add_layernorm_f32(x, yy, ln)
+    exp = torch.nn.functional.layer_norm(x + (yy.float() if y else 0), (384,), ln.weight, ln.bias, ln.eps)
+    assert out.dtype == torch.float32
+    torch.testing.assert_close(out, exp, atol=2e-5, rtol=2e-5)
