@@ -47,7 +47,7 @@ constexpr float kRescaleLog2 = 8.0f;
 // per-slot barriers
 enum : int {
   kQFull = 0,                    // [2] Q stage landed
-  kKFull = 2,                    // [3] K stage landed (+ bias staged)
+  kKFull = 2,                    // [3] K stage landed
   kVFull = kKFull + kStages,     // [3] V stage landed
   kSFull = kVFull + kStages,     // [3] S(g) complete (+ bias of block g staged)
   kPFull = kSFull + kStages,     // [3] P(g) in TMEM (one arrival per softmax warp)
