@@ -81,10 +81,71 @@ def _as_u8(t):
     return t.view(torch.uint8) if t.dtype == torch.bool else t
 
 
+def _neighbor_dot_grads(ctx, a, b, ridx, rval, grad_scores):
+    """Gradients of scores[d, k] = a[d] . b[r(d, k)] (dtem.py:667-676):
+    grad_b is the transport of grad_scores * a into the receivers (the same
+    edge-ordered, atomics-free sum as sparse_weighted_transport, which is the
+    reference's sequential scatter-add), grad_a the transport adjoint's
+    per-donor gather of grad_scores * b.  Invalid slots contribute nothing."""
+    g = grad_scores.to(a.dtype).contiguous()
+    grad_a = grad_b = None
+    if ctx.needs_input_grad[0]:
+        grad_a = sparse_transport_adjoint(g, a, ridx, rval, b)[1]
+    if ctx.needs_input_grad[1]:
+        grad_b = sparse_weighted_transport(g, a, ridx, rval, b.shape[1])
+    return grad_a, grad_b
+
+
+class _SparseNeighborDotFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, b, receiver_indices, receiver_valid):
+        out = _sparse_neighbor_dot(a, b, receiver_indices, receiver_valid)
+        ctx.save_for_backward(a.contiguous(), b.contiguous(), receiver_indices.long().contiguous(),
+                              receiver_valid.bool().contiguous())
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_scores):
+        a, b, ridx, rval = ctx.saved_tensors
+        grad_a, grad_b = _neighbor_dot_grads(ctx, a, b, ridx, rval, grad_scores)
+        return grad_a, grad_b, None, None
+
+
+class _SparseSpatialScoreFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, b, neighbor_patch_indices, neighbor_patch_valid, donor_patch_indices,
+                receiver_patch_indices):
+        scores, ridx, rval = _sparse_spatial_score(a, b, neighbor_patch_indices, neighbor_patch_valid,
+                                                   donor_patch_indices, receiver_patch_indices)
+        ctx.save_for_backward(a.contiguous(), b.contiguous(), ridx, rval)
+        ctx.mark_non_differentiable(ridx, rval)
+        return scores, ridx, rval
+
+    @staticmethod
+    def backward(ctx, grad_scores, _grad_indices, _grad_valid):
+        a, b, ridx, rval = ctx.saved_tensors
+        grad_a, grad_b = _neighbor_dot_grads(ctx, a, b, ridx, rval, grad_scores)
+        return grad_a, grad_b, None, None, None, None
+
+
+def _wants_grad(*tensors):
+    return torch.is_grad_enabled() and any(t.requires_grad for t in tensors)
+
+
 def sparse_spatial_score(a, b, neighbor_patch_indices, neighbor_patch_valid, donor_patch_indices,
                          receiver_patch_indices):
     """(scores [B,Na,K], receiver_indices int64 [B,Na,K], receiver_valid bool
-    [B,Na,K]) exactly as dtem.py:813-848; receivers must be sorted per row."""
+    [B,Na,K]) exactly as dtem.py:813-848; receivers must be sorted per row.
+    Differentiable in a and b (_SparseSpatialScore.backward, dtem.py:768-810)."""
+    if _wants_grad(a, b):
+        return _SparseSpatialScoreFn.apply(a, b, neighbor_patch_indices, neighbor_patch_valid, donor_patch_indices,
+                                           receiver_patch_indices)
+    return _sparse_spatial_score(a, b, neighbor_patch_indices, neighbor_patch_valid, donor_patch_indices,
+                                 receiver_patch_indices)
+
+
+def _sparse_spatial_score(a, b, neighbor_patch_indices, neighbor_patch_valid, donor_patch_indices,
+                          receiver_patch_indices):
     dev = L.require_cuda(a, b, neighbor_patch_indices, neighbor_patch_valid, donor_patch_indices,
                          receiver_patch_indices)
     if a.ndim != 3 or b.ndim != 3 or a.shape[0] != b.shape[0] or a.shape[-1] != b.shape[-1]:
@@ -110,7 +171,14 @@ def sparse_spatial_score(a, b, neighbor_patch_indices, neighbor_patch_valid, don
 
 
 def sparse_neighbor_dot(a, b, receiver_indices, receiver_valid):
-    """Indexed donor/receiver dot products (dtem.py:680-687)."""
+    """Indexed donor/receiver dot products (dtem.py:680-687), differentiable in
+    a and b (_SparseNeighborDot.backward, dtem.py:633-677)."""
+    if _wants_grad(a, b):
+        return _SparseNeighborDotFn.apply(a, b, receiver_indices, receiver_valid)
+    return _sparse_neighbor_dot(a, b, receiver_indices, receiver_valid)
+
+
+def _sparse_neighbor_dot(a, b, receiver_indices, receiver_valid):
     dev = L.require_cuda(a, b, receiver_indices, receiver_valid)
     if a.dtype != b.dtype:
         raise ValueError("a and b must share a dtype")

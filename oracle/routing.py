@@ -143,6 +143,24 @@ def sparse_neighbor_dot(a, b, receiver_indices, receiver_valid):
     return (s * np.asarray(receiver_valid).astype(F32)).astype(F32)
 
 
+def sparse_neighbor_dot_backward(a, b, receiver_indices, receiver_valid, grad_scores):
+    """Gradients of sparse_neighbor_dot (the torch path of
+    _SparseNeighborDot.backward, dtem.py:667-676): grad_a[d] = sum_k g[d,k]
+    b[r(d,k)]; grad_b[s] += g[d,k] a[d] scatter-added over the flattened
+    donor-major edge list (np.add.at applies the edges in that order)."""
+    a = np.asarray(a, dtype=F32)
+    b = np.asarray(b, dtype=F32)
+    ridx = np.asarray(receiver_indices)
+    g = (np.asarray(grad_scores, dtype=F32) * np.asarray(receiver_valid).astype(F32)).astype(F32)
+    bidx = np.arange(a.shape[0])[:, None, None]
+    grad_a = (g[..., None] * b[bidx, ridx]).sum(axis=2, dtype=F32).astype(F32)
+    grad_b = np.zeros_like(b)
+    contrib = (g[..., None] * a[:, :, None, :]).astype(F32)
+    for i in range(a.shape[0]):
+        np.add.at(grad_b[i], ridx[i].reshape(-1), contrib[i].reshape(-1, a.shape[-1]))
+    return grad_a, grad_b
+
+
 def sparse_weighted_transport(assignment, values, receiver_indices, receiver_valid, num_receivers):
     """out[b,s,:] = sum over (d,k) with slot s of assignment*values, in (d,k) order.
 

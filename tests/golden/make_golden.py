@@ -41,6 +41,7 @@ from opentome.timm.dtem import (  # noqa: E402
     DTEMBlock,
     adjacency_to_padded_neighbors,
     build_patch_spatial_adjacency,
+    sparse_neighbor_dot,
     sparse_spatial_score,
     sparse_weighted_transport,
 )
@@ -213,6 +214,32 @@ def transport_case():
                         receivers=receivers, out=out.numpy())
 
 
+def neighbor_dot_backward_case():
+    """Gradients of the reference's sparse_neighbor_dot (the score of
+    sparse_spatial_score too) through its own autograd Function
+    (opentome/timm/dtem.py:597-677): grad_a gathers, grad_b scatter-adds
+    over the edges in donor-major order.  Random edge lists with repeated
+    receivers and invalid slots, as the reference's tests draw them."""
+    rng = np.random.default_rng(20261202)
+    cases = {}
+    for i, (batch, donors, receivers, neighbors, channels) in enumerate(
+            [(2, 50, 57, 13, 24), (3, 392, 392, 29, 64)]):
+        a = rng.standard_normal((batch, donors, channels), dtype=np.float32)
+        b = rng.standard_normal((batch, receivers, channels), dtype=np.float32)
+        ridx = rng.integers(0, receivers, (batch, donors, neighbors))
+        rvalid = rng.random((batch, donors, neighbors)) > 0.2
+        gs = rng.standard_normal((batch, donors, neighbors), dtype=np.float32)
+        ta = torch.from_numpy(a).requires_grad_(True)
+        tb = torch.from_numpy(b).requires_grad_(True)
+        scores = sparse_neighbor_dot(ta, tb, torch.from_numpy(ridx), torch.from_numpy(rvalid))
+        scores.backward(torch.from_numpy(gs))
+        cases.update({f"a{i}": a, f"b{i}": b, f"receiver_indices{i}": ridx.astype(np.int32),
+                      f"receiver_valid{i}": rvalid, f"grad_scores{i}": gs,
+                      f"scores{i}": scores.detach().numpy(), f"grad_a{i}": ta.grad.numpy(),
+                      f"grad_b{i}": tb.grad.numpy()})
+    np.savez_compressed(HERE / "neighbor_dot_backward.npz", **cases)
+
+
 def attention_case():
     """The reference's own CPU unfold implementations of the windowed
     attention (opentome/timm/bias_local_attn.py:46-240), BNHD layout."""
@@ -232,7 +259,14 @@ def attention_case():
 
 
 def main():
+    # `make_golden.py <case> ...` regenerates only the named cases
+    only = set(sys.argv[1:])
+    if only:
+        for name in only:
+            globals()[name]()
+        return
     attention_case()
+    neighbor_dot_backward_case()
     thre_topk_case()
     select_case()
     transport_case()

@@ -117,3 +117,15 @@ def test_timed_port_routing_matches_the_oracle():
     np.testing.assert_array_equal(ti.numpy(), ref["topk_idx"])
     np.testing.assert_allclose(ts.numpy(), ref["topk_size"], rtol=3e-5, atol=3e-5)
     np.testing.assert_allclose(tx.numpy(), ref["topk_x"], rtol=1e-4, atol=1e-4)
+
+
+def test_oracle_neighbor_dot_backward(golden_dir):
+    """The restated gradients against the reference's own autograd run."""
+    g = load(golden_dir, "neighbor_dot_backward")
+    for i in range(2):
+        ga, gb = O.sparse_neighbor_dot_backward(g[f"a{i}"], g[f"b{i}"], g[f"receiver_indices{i}"],
+                                                g[f"receiver_valid{i}"], g[f"grad_scores{i}"])
+        np.testing.assert_allclose(ga, g[f"grad_a{i}"], rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(gb, g[f"grad_b{i}"], rtol=1e-5, atol=1e-5)
+        s = O.sparse_neighbor_dot(g[f"a{i}"], g[f"b{i}"], g[f"receiver_indices{i}"], g[f"receiver_valid{i}"])
+        np.testing.assert_allclose(s, g[f"scores{i}"], rtol=1e-5, atol=1e-5)

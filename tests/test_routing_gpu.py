@@ -317,3 +317,43 @@ def test_empty_batches(dev):
     assert s.shape == (0, 7, nbr.shape[1])
     out = mn.sparse_weighted_transport(torch.empty(0, 7, nbr.shape[1], device=dev), a, ri, rv, 8)
     assert out.shape == (0, 8, 9)
+
+
+def test_neighbor_dot_backward_matches_reference(dev, golden_dir):
+    """Gradients of sparse_neighbor_dot against the reference's own autograd
+    run (_SparseNeighborDot.backward, dtem.py:633-677, torch path): grad_b is
+    summed in the reference's edge order, so it matches bit for bit."""
+    import mergenet_b200 as mn
+    g = np.load(golden_dir / "neighbor_dot_backward.npz")
+    for i in range(2):
+        a = torch.from_numpy(g[f"a{i}"]).to(dev).requires_grad_(True)
+        b = torch.from_numpy(g[f"b{i}"]).to(dev).requires_grad_(True)
+        ridx = torch.from_numpy(g[f"receiver_indices{i}"]).to(dev)
+        rval = torch.from_numpy(g[f"receiver_valid{i}"]).to(dev)
+        scores = mn.sparse_neighbor_dot(a, b, ridx, rval)
+        scores.backward(torch.from_numpy(g[f"grad_scores{i}"]).to(dev))
+        np.testing.assert_allclose(scores.detach().cpu().numpy(), g[f"scores{i}"], rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(a.grad.cpu().numpy(), g[f"grad_a{i}"], rtol=1e-5, atol=1e-5)
+        np.testing.assert_array_equal(b.grad.cpu().numpy(), g[f"grad_b{i}"])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_spatial_score_backward(dev, golden_dir, dtype):
+    """sparse_spatial_score is differentiable in a and b, with the receiver
+    slots it returns (dtem.py:768-810): checked against the oracle's
+    neighbor-dot gradients on those slots."""
+    import mergenet_b200 as mn
+    g = np.load(golden_dir / "select_g3x5.npz")
+    nbr, val = mn.build_patch_spatial_neighbors((3, 5), 2, device=dev)
+    a = torch.from_numpy(g["a"]).to(dev, dtype).requires_grad_(True)
+    b = torch.from_numpy(g["b"]).to(dev, dtype).requires_grad_(True)
+    scores, ridx, rval = mn.sparse_spatial_score(a, b, nbr, val, torch.from_numpy(g["a_idx"] - 1).to(dev),
+                                                 torch.from_numpy(g["b_idx"] - 1).to(dev))
+    assert not ridx.requires_grad and not rval.requires_grad
+    gs = torch.randn(scores.shape, generator=torch.Generator().manual_seed(3)).to(dev, dtype)
+    scores.backward(gs)
+    want_a, want_b = O.sparse_neighbor_dot_backward(g["a"], g["b"], ridx.cpu().numpy(), rval.cpu().numpy(),
+                                                    gs.float().cpu().numpy())
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    np.testing.assert_allclose(a.grad.float().cpu().numpy(), want_a, rtol=tol, atol=tol)
+    np.testing.assert_allclose(b.grad.float().cpu().numpy(), want_b, rtol=tol, atol=tol)
