@@ -182,6 +182,17 @@ int mn_thre_topk(int rows, int n, const float* x, int k, float temperature,
                  float* y, void* workspace, size_t workspace_bytes,
                  int* status, void* stream);
 
+/* Gradient of ThreTopK with respect to x (the reference differentiates
+ * opentome/utils/thetopk.py:4-43 by autograd): grad_y f32 [rows, n] ->
+ * grad_x f32 [rows, n], including the path through the global range, whose
+ * gradient is split evenly over tied maxima and minima.
+ * workspace: mn_thre_topk_backward_workspace_bytes(rows, n) bytes. */
+size_t mn_thre_topk_backward_workspace_bytes(int rows, int n);
+int mn_thre_topk_backward(int rows, int n, const float* x, int k,
+                          float temperature, const float* grad_y,
+                          float* grad_x, void* workspace,
+                          size_t workspace_bytes, int* status, void* stream);
+
 /* Soft-k-max block of DTEMBlock._select with the sparse spatial mask,
  * opentome/timm/dtem.py:1551-1580: scores f32 [B,Na,K] + allowed uint8 ->
  * assignment f32 [B,Na,K].  Returns MN_INFEASIBLE_BUDGET through the device

@@ -20,6 +20,7 @@ from .routing import (  # noqa: F401
     sparse_transport_adjoint,
     sparse_weighted_transport,
     sparse_weighted_transport_pair,
+    thre_topk_backward,
 )
 from .dtem import DTEMMergeBlock, build_eval_group_indices, make_merge_block  # noqa: F401
 from .attention import (  # noqa: F401

@@ -61,6 +61,8 @@ _SIGNATURES = {
                                             _P, _P]),
     "mn_thre_topk_workspace_bytes": (c_size_t, [c_int, c_int]),
     "mn_thre_topk": (c_int, [c_int, c_int, _P, c_int, c_float, _P, _P, c_size_t, _P, _P]),
+    "mn_thre_topk_backward_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "mn_thre_topk_backward": (c_int, [c_int, c_int, _P, c_int, c_float, _P, _P, _P, c_size_t, _P, _P]),
     "mn_dtem_select_workspace_bytes": (c_size_t, [c_int, c_int]),
     "mn_dtem_select": (c_int, [c_int, c_int, c_int, _P, _P, c_int, c_float, c_float, _P, _P, c_size_t, _P, _P]),
     "mn_dtem_select_noalloc": (c_int, [c_int, c_int, c_int, _P, _P, c_int, c_float, c_float, _P, _P, _P]),

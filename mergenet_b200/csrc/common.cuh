@@ -137,6 +137,19 @@ __device__ __forceinline__ void block_minmax(float& vmin, float& vmax, float* sc
   __syncthreads();
 }
 
+// Block-wide sum of one float per thread (fixed order: warp trees, then the
+// warps' sums in warp order).  scratch: >= 32 floats.  Result in every thread.
+__device__ __forceinline__ float block_sum(float v, float* scratch) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  v = warp_sum((lane < nw) ? scratch[lane] : 0.f);
+  __syncthreads();
+  return v;
+}
+
 __device__ __forceinline__ int block_min_int(int v, int* scratch) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   v = warp_min_int(v);

@@ -244,6 +244,113 @@ __global__ void __launch_bounds__(512) thre_topk_rows_kernel(const float* __rest
   for (int i = threadIdx.x; i < n; i += blockDim.x) y[(int64_t)blockIdx.x * n + i] = thre_topk_map(xrow[i], lam);
 }
 
+// Gradient of ThreTopK with respect to x: the closed form of the reference's
+// autograd through thetopk.py:4-43.  Per row (one CTA): recompute
+// x~ = x / R * T, the sorted scans and the bracket b, then
+//   dx~_i = f'(d_i) g_i + [x~_i <= xs_b] dlse1 e^{x~_i - lse1_b}
+//           - [x~_i > xs_b] dL e^{-x~_i - lse2_b}
+// with dlambda = -sum_i f'(d_i) g_i, dL the path through |term_b|,
+// dlse1 = dlambda + dL; dx = dx~ T / R.  The row's share of
+// dR = -sum_i dx~_i x_i T / R^2 goes to rpart[row] (thre_topk_grad_range_kernel
+// adds dR to the maximum and -dR to the minimum elements).
+__global__ void __launch_bounds__(512) thre_topk_grad_rows_kernel(const float* __restrict__ x,
+                                                                  const float* __restrict__ gy, int n, int k,
+                                                                  float temperature, const float* partials,
+                                                                  int nparts, float* __restrict__ gx,
+                                                                  float* __restrict__ rpart, int* status) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red[64];
+  const int np = next_pow2(n);
+  RowScratch rs = carve_row_scratch(smem_raw, np);
+  float* xrow = reinterpret_cast<float*>(smem_raw + row_scratch_bytes(np));
+  const float range = reduce_range(partials, nparts, red, status);
+  const int64_t row = blockIdx.x;
+  const float* xr = x + row * n;
+  const float* gr = gy + row * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) xrow[i] = xr[i] / range * temperature;
+  __syncthreads();
+  int b = 0;
+  const float lam = thre_topk_lambda(xrow, n, np, k, rs, &b);
+  const float xs_b = rs.xs[b], lse1_b = rs.lse1[b];
+  const float lse2_b = b + 1 < n ? (float)(-(double)rs.xs[0] + log(rs.dbuf[n - 2 - b])) : -INFINITY;
+  const float km = (float)(k - (n - 1 - b));
+  const float el = expf(lse1_b + lse2_b);
+  const float term = sqrtf(km * km + el) + km;
+  auto fprime = [&](float v) {
+    const float dv = v - lam;
+    return dv > 0.f ? 0.5f * expf(-dv) : 0.5f * expf(dv);
+  };
+  float sdd = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) sdd += gr[i] * fprime(xrow[i]);
+  sdd = block_sum(sdd, red);
+  const float dlam = -sdd;
+  const float sgn = term > 0.f ? 1.f : (term < 0.f ? -1.f : 0.f);
+  const float dterm = -dlam / (fabsf(term) + 1e-8f) * sgn;
+  const float dl = el > 0.f ? dterm * 0.5f / sqrtf(km * km + el) * el : 0.f;
+  const float dlse1 = dlam + dl;
+  const float inv_r = temperature / range;
+  // elements equal to xs_b take their side from their place in the stable
+  // sort: below_b values lie under xs_b, and ties rank by index after them
+  int below_b = 0;
+  for (int hi = b; below_b < hi;) {
+    const int mid = (below_b + hi) >> 1;
+    if (rs.xs[mid] < xs_b) below_b = mid + 1;
+    else hi = mid;
+  }
+  float part = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = xrow[i];
+    float dxt = gr[i] * fprime(v);
+    bool low = v < xs_b;
+    if (v == xs_b) {
+      int pos = below_b;
+      for (int j = 0; j < i; ++j) pos += xrow[j] == xs_b;
+      low = pos <= b;
+    }
+    if (low) dxt += dlse1 * expf(v - lse1_b);
+    else if (b + 1 < n) dxt -= dl * expf(-v - lse2_b);
+    gx[row * n + i] = dxt * inv_r;
+    part += dxt * xr[i];
+  }
+  part = block_sum(part, red);
+  if (threadIdx.x == 0) rpart[row] = -part * inv_r / range;
+}
+
+// The range's share of the ThreTopK gradient: dR (the sum of the rows'
+// partials) to every maximum element and -dR to every minimum element, split
+// evenly over ties as the reference's autograd splits max() / min().
+__global__ void __launch_bounds__(1024) thre_topk_grad_range_kernel(const float* __restrict__ x, int64_t total,
+                                                                   const float* __restrict__ rpart, int rows,
+                                                                   const float* partials, int nparts,
+                                                                   float* __restrict__ gx) {
+  __shared__ float red[64];
+  __shared__ int cnt[2];
+  float lo = INFINITY, hi = -INFINITY;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+    lo = fminf(lo, partials[2 * i]);
+    hi = fmaxf(hi, partials[2 * i + 1]);
+  }
+  block_minmax(lo, hi, red);
+  float dr = 0.f;
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) dr += rpart[r];
+  dr = block_sum(dr, red);
+  if (threadIdx.x == 0) cnt[0] = cnt[1] = 0;
+  __syncthreads();
+  int nmax = 0, nmin = 0;
+  for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+    nmax += x[i] == hi;
+    nmin += x[i] == lo;
+  }
+  atomicAdd(&cnt[0], nmax);  // integer counts: order-independent
+  atomicAdd(&cnt[1], nmin);
+  __syncthreads();
+  const float add_max = dr / (float)max(cnt[0], 1), add_min = dr / (float)max(cnt[1], 1);
+  for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+    if (x[i] == hi) gx[i] += add_max;
+    if (x[i] == lo) gx[i] -= add_min;
+  }
+}
+
 // Row energies of the masked scores (dtem.py:1557-1567): one warp per row.
 __global__ void __launch_bounds__(256) select_energy_kernel(const float* __restrict__ scores,
                                                             const uint8_t* __restrict__ allowed, int rows,
@@ -462,6 +569,32 @@ extern "C" int mn_thre_topk(int rows, int n, const float* x, int k, float temper
   if (!ensure_smem(thre_topk_rows_kernel, smem)) return MN_ERR_LAUNCH;
   minmax_partials_kernel<<<parts, 256, 0, st>>>(x, (int64_t)rows * n, partials);
   thre_topk_rows_kernel<<<rows, 512, smem, st>>>(x, n, k, temperature, partials, parts, y, status);
+  return launch_status();
+}
+
+extern "C" size_t mn_thre_topk_backward_workspace_bytes(int rows, int n) {
+  if (rows <= 0 || n <= 0) return 0;
+  return mn_thre_topk_workspace_bytes(rows, n) + (size_t)rows * sizeof(float);
+}
+
+extern "C" int mn_thre_topk_backward(int rows, int n, const float* x, int k, float temperature, const float* grad_y,
+                                     float* grad_x, void* workspace, size_t workspace_bytes, int* status,
+                                     void* stream) {
+  if (rows <= 0 || n <= 0 || !x || !grad_y || !grad_x || !workspace) return MN_ERR_ARG;
+  if (n > 4096) return MN_ERR_UNSUPPORTED;
+  if (workspace_bytes < mn_thre_topk_backward_workspace_bytes(rows, n)) return MN_ERR_WORKSPACE;
+  cudaGetLastError();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int parts = thre_topk_parts((int64_t)rows * n);
+  float* partials = static_cast<float*>(workspace);
+  float* rpart = partials + 2 * parts;
+  const int np = next_pow2(n);
+  const size_t smem = row_scratch_bytes(np) + (size_t)n * sizeof(float);
+  if (!ensure_smem(thre_topk_grad_rows_kernel, smem)) return MN_ERR_LAUNCH;
+  minmax_partials_kernel<<<parts, 256, 0, st>>>(x, (int64_t)rows * n, partials);
+  thre_topk_grad_rows_kernel<<<rows, 512, smem, st>>>(x, grad_y, n, k, temperature, partials, parts, grad_x, rpart,
+                                                      status);
+  thre_topk_grad_range_kernel<<<1, 1024, 0, st>>>(x, (int64_t)rows * n, rpart, rows, partials, parts, grad_x);
   return launch_status();
 }
 

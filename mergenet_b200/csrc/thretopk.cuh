@@ -43,7 +43,11 @@ __device__ __forceinline__ RowScratch carve_row_scratch(unsigned char* base, int
 // x: the n scaled values of this row, readable by every thread (shared or
 // global).  Returns lambda in every thread.  np = next_pow2(n) and the block
 // size must divide np (np >= blockDim.x) or be larger than np.
-__device__ __noinline__ static float thre_topk_lambda(const float* x, int n, int np, int k, RowScratch s) {
+// *bracket (when given) receives the chosen bracket b: lambda = xlamb[b].
+// The scratch keeps the sorted row (xs), lse1 and the suffix sums (dbuf)
+// after the call, for the gradient.
+__device__ __noinline__ static float thre_topk_lambda(const float* x, int n, int np, int k, RowScratch s,
+                                                      int* bracket = nullptr) {
   const int tid = threadIdx.x;
   const int per_thread = np / (int)blockDim.x;
   if (np % (int)blockDim.x == 0 && (per_thread == 1 || per_thread == 2 || per_thread == 4) && blockDim.x >= 32) {
@@ -115,6 +119,7 @@ __device__ __noinline__ static float thre_topk_lambda(const float* x, int n, int
   }
   int idx = block_min_int(cand, s.iscr);
   if (idx == INT_MAX) idx = 0;
+  if (bracket) *bracket = idx;
   float lam = s.xlamb[idx];
   __syncthreads();
   return lam;

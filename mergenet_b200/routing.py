@@ -270,7 +270,48 @@ def _default_check(check):
 
 def ThreTopK(x, k, temperature=30.0):  # noqa: N802 - reference name
     """Threshold soft top-k (opentome/utils/thetopk.py:4-43): one global
-    max - min range over the whole input, per-row threshold."""
+    max - min range over the whole input, per-row threshold.  Differentiable
+    in x (thre_topk_backward)."""
+    if _wants_grad(x):
+        return _ThreTopKFn.apply(x, int(k), float(temperature))
+    return _thre_topk(x, k, temperature)
+
+
+class _ThreTopKFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, k, temperature):
+        ctx.save_for_backward(x)
+        ctx.k, ctx.temperature = k, temperature
+        return _thre_topk(x, k, temperature)
+
+    @staticmethod
+    def backward(ctx, grad_y):
+        (x,) = ctx.saved_tensors
+        return thre_topk_backward(x, ctx.k, grad_y, ctx.temperature), None, None
+
+
+def thre_topk_backward(x, k, grad_y, temperature=30.0):
+    """d ThreTopK(x) / dx applied to grad_y, as the reference's autograd
+    differentiates thetopk.py:4-43: through the threshold lambda of the
+    row's bracket (its lse1, lse2 and |term|), the two-sided map, the scaled
+    input x / R * T and the global range R = max - min, whose gradient is
+    split evenly over tied maxima and minima.  Returns grad_x shaped and
+    typed like x."""
+    dev = L.require_cuda(x, grad_y)
+    x32 = x.float().contiguous()
+    if x32.dim() == 1:
+        x32 = x32.unsqueeze(0)
+    rows, n = x32.shape
+    g32 = grad_y.float().contiguous().reshape(rows, n)
+    gx = torch.empty_like(x32)
+    wsb = L.lib().mn_thre_topk_backward_workspace_bytes(rows, n)
+    ws = torch.empty(max(int(wsb), 16), dtype=torch.uint8, device=dev)
+    L.check(L.lib().mn_thre_topk_backward(rows, n, L.ptr(x32), int(k), float(temperature), L.ptr(g32), L.ptr(gx),
+                                          L.ptr(ws), wsb, None, L.stream_of(x32)), "ThreTopK backward")
+    return gx.reshape(x.shape).to(x.dtype)
+
+
+def _thre_topk(x, k, temperature):
     dev = L.require_cuda(x)
     if x.dim() == 1:
         x = x.unsqueeze(0)

@@ -235,6 +235,57 @@ def thre_topk(x, k, temperature=30.0):
 # --------------------------------------------------------------------------
 # Select  (dtem.py:1464-1580, soft-k-max branch with the sparse spatial mask)
 # --------------------------------------------------------------------------
+
+def thre_topk_backward(x, k, grad_y, temperature=30.0):
+    """Gradient of ThreTopK with respect to x, in float64: the closed form of
+    what the reference's autograd computes through thetopk.py:4-43.  With
+    x~ = x / R * T (R = max - min over the whole input), b the row's bracket
+    and lambda = lse1[b] - log(|term[b]| + 1e-8):
+    dx~_i = f'(d_i) g_i + [s(i) <= b] dlse1 e^{x~_i - lse1[b]}
+            - [s(i) > b] dL e^{-x~_i - lse2[b]},
+    with dlambda = -sum_i f'(d_i) g_i, dL = d|term|/dL * (-dlambda / (|term| + 1e-8)),
+    dlse1 = dlambda + dL; then dx = dx~ T / R, and dR = -sum dx~_i x_i T / R^2
+    goes to the maximum (+) and minimum (-) elements, split evenly over ties.
+    s(i) is i's position in the row's stable ascending sort."""
+    x = np.asarray(x, np.float64)
+    g = np.asarray(grad_y, np.float64)
+    squeeze = x.ndim == 1
+    if squeeze:
+        x, g = x[None], g[None]
+    r_range = x.max() - x.min()
+    xt = x / r_range * temperature
+    rows, n = x.shape
+    dxt = np.zeros_like(xt)
+    for r in range(rows):
+        perm = np.argsort(xt[r], kind="stable")
+        xs = xt[r, perm]
+        lse1 = xs[-1] + np.log(np.cumsum(np.exp(xs - xs[-1])))
+        suffix = np.cumsum(np.exp(xs[0] - xs)[::-1])[::-1]
+        lse2 = np.concatenate([-xs[0] + np.log(suffix[1:]), [-np.inf]])
+        km = k - (n - 1 - np.arange(n))
+        big_l = lse1 + lse2
+        term = np.sqrt(km * km + np.exp(big_l)) + km
+        xl = lse1 - np.log(np.abs(term) + 1e-8)
+        mask = (xl >= xs) & (xl <= np.concatenate([xs[1:], [np.inf]]))
+        b = int(np.argmax(mask)) if mask.any() else 0
+        d = xt[r] - xl[b]
+        dd = g[r] * np.where(d > 0, 0.5 * np.exp(-d), 0.5 * np.exp(d))
+        dlam = -dd.sum()
+        el = np.exp(big_l[b])
+        dl = -dlam / (np.abs(term[b]) + 1e-8) * np.sign(term[b]) * 0.5 / np.sqrt(km[b] ** 2 + el) * el
+        dxs = np.zeros(n)
+        dxs[:b + 1] = (dlam + dl) * np.exp(xs[:b + 1] - lse1[b])
+        if b < n - 1:
+            dxs[b + 1:] = -dl * np.exp(-xs[b + 1:] - lse2[b])
+        dxt[r] = dd
+        dxt[r, perm] += dxs
+    dx = dxt * temperature / r_range
+    d_range = (dxt * (-x * temperature / r_range ** 2)).sum()
+    is_max, is_min = x == x.max(), x == x.min()
+    dx[is_max] += d_range / is_max.sum()
+    dx[is_min] -= d_range / is_min.sum()
+    return dx[0] if squeeze else dx
+
 def _softmax_lastdim(x):
     """exp(x - max) * (1 / sum) like the CPU softmax kernel."""
     mx = x.max(axis=-1, keepdims=True)

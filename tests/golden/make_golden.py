@@ -174,6 +174,33 @@ def thre_topk_case():
     np.savez_compressed(HERE / "thre_topk.npz", **cases)
 
 
+def thre_topk_backward_case():
+    """Gradients of the reference's ThreTopK through its own autograd
+    (sort, logcumsumexp, the bracket gather and the global max - min range,
+    opentome/utils/thetopk.py:4-43) for random upstream gradients."""
+    rng = np.random.default_rng(17)
+    cases = {}
+    shapes = [((4, 37), 9), ((3, 64), 20), ((2, 392), 65), ((1, 50), 49), ((5, 8), 1)]
+    for i, (shape, k) in enumerate(shapes):
+        x = (rng.standard_normal(shape, dtype=np.float32) * 2 + 5).astype(np.float32)
+        g = rng.standard_normal(shape, dtype=np.float32)
+        tx = torch.from_numpy(x).requires_grad_(True)
+        y = ThreTopK(tx, k, 30.0)
+        y.backward(torch.from_numpy(g))
+        cases.update({f"x{i}": x, f"k{i}": k, f"g{i}": g, f"y{i}": y.detach().numpy(), f"dx{i}": tx.grad.numpy()})
+    # integer-valued rows: ties everywhere, at the bracket and at the global
+    # maximum and minimum
+    for i, (shape, k) in enumerate([((3, 40), 10), ((2, 64), 31)], start=len(shapes)):
+        x = np.round(rng.standard_normal(shape, dtype=np.float32) * 2 + 5).astype(np.float32)
+        g = rng.standard_normal(shape, dtype=np.float32)
+        tx = torch.from_numpy(x).requires_grad_(True)
+        y = ThreTopK(tx, k, 30.0)
+        y.backward(torch.from_numpy(g))
+        cases.update({f"x{i}": x, f"k{i}": k, f"g{i}": g, f"y{i}": y.detach().numpy(), f"dx{i}": tx.grad.numpy()})
+    cases["count"] = np.int64(len(shapes) + 2)
+    np.savez_compressed(HERE / "thre_topk_backward.npz", **cases)
+
+
 def select_case():
     """The reference test's (3,5) R=2 geometry with per-sample partitions
     (tests/test_dtem_spatial_sparse.py:179-227)."""
@@ -268,6 +295,7 @@ def main():
     attention_case()
     neighbor_dot_backward_case()
     thre_topk_case()
+    thre_topk_backward_case()
     select_case()
     transport_case()
     route_case("route_g3x6", 101, 2, (3, 6), 2.0, 7, 5, [3, 3], capture=True)

@@ -129,3 +129,12 @@ def test_oracle_neighbor_dot_backward(golden_dir):
         np.testing.assert_allclose(gb, g[f"grad_b{i}"], rtol=1e-5, atol=1e-5)
         s = O.sparse_neighbor_dot(g[f"a{i}"], g[f"b{i}"], g[f"receiver_indices{i}"], g[f"receiver_valid{i}"])
         np.testing.assert_allclose(s, g[f"scores{i}"], rtol=1e-5, atol=1e-5)
+
+
+def test_oracle_thre_topk_backward(golden_dir):
+    """The closed-form ThreTopK gradient against the reference's autograd."""
+    g = load(golden_dir, "thre_topk_backward")
+    for i in range(int(g["count"])):
+        dx = O.thre_topk_backward(g[f"x{i}"], int(g[f"k{i}"]), g[f"g{i}"])
+        ref = g[f"dx{i}"]
+        assert np.abs(dx - ref).max() <= 2e-5 * np.abs(ref).max()

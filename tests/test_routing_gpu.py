@@ -244,6 +244,37 @@ def test_thre_topk_matches_reference(dev, golden_dir):
         np.testing.assert_allclose(y.cpu().numpy().reshape(g[f"y{i}"].shape), g[f"y{i}"], rtol=0, atol=2e-6)
 
 
+def test_thre_topk_backward_matches_reference(dev, golden_dir):
+    """x.grad through mn.ThreTopK against the reference's own autograd
+    (thetopk.py:4-43), tied rows included (their bracket side follows the
+    stable sort; the range gradient is split over tied maxima / minima)."""
+    import mergenet_b200 as mn
+    g = np.load(golden_dir / "thre_topk_backward.npz")
+    for i in range(int(g["count"])):
+        x = torch.from_numpy(g[f"x{i}"]).to(dev).requires_grad_(True)
+        y = mn.ThreTopK(x, int(g[f"k{i}"]), 30.0)
+        np.testing.assert_allclose(y.detach().cpu().numpy(), g[f"y{i}"], rtol=0, atol=2e-6)
+        y.backward(torch.from_numpy(g[f"g{i}"]).to(dev))
+        ref = g[f"dx{i}"]
+        err = np.abs(x.grad.cpu().numpy() - ref).max()
+        assert err <= 1e-4 * np.abs(ref).max(), (i, err)
+
+
+@pytest.mark.parametrize("rows,n,k", [(64, 392, 196), (8, 1000, 37), (3, 4096, 2048)])
+def test_thre_topk_backward_large_rows(dev, rows, n, k):
+    """Row lengths of the donor sets and the kernel's maximum against the
+    float64 closed form of the oracle (rel. 1e-4 of the largest entry)."""
+    import mergenet_b200 as mn
+    from oracle import routing as O
+    gen = torch.Generator().manual_seed(rows * 7 + n)
+    x = torch.randn(rows, n, generator=gen) * 3 + 1
+    gy = torch.randn(rows, n, generator=gen)
+    ref = O.thre_topk_backward(x.numpy(), k, gy.numpy())
+    gx = mn.thre_topk_backward(x.to(dev), k, gy.to(dev))
+    err = np.abs(gx.cpu().numpy() - ref).max()
+    assert err <= 1e-4 * np.abs(ref).max(), err
+
+
 def test_select_infeasible_budget_fails_closed(dev):
     import mergenet_b200 as mn
     scores = torch.randn(1, 2, 3, device=dev)
