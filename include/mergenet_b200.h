@@ -203,6 +203,21 @@ int mn_dtem_select(int batch, int num_donors, int k_slots, const float* scores,
                    float* assignment, void* workspace, size_t workspace_bytes,
                    int* status, void* stream);
 
+/* Gradient of that select block with respect to scores (the reference
+ * differentiates dtem.py:1551-1580 by autograd): grad_assignment f32
+ * [B,Na,K] -> grad_scores f32 [B,Na,K], through the masked row softmax, the
+ * logsumexp row energies and ThreTopK over the batch (its range included);
+ * the over-unity renormalisation divides by a detached total.  Masked slots
+ * and rows with no allowed slot get zero.
+ * workspace: mn_dtem_select_backward_workspace_bytes(batch, num_donors). */
+size_t mn_dtem_select_backward_workspace_bytes(int batch, int num_donors);
+int mn_dtem_select_backward(int batch, int num_donors, int k_slots,
+                            const float* scores, const uint8_t* allowed, int k,
+                            float tau1, float tau2,
+                            const float* grad_assignment, float* grad_scores,
+                            void* workspace, size_t workspace_bytes,
+                            int* status, void* stream);
+
 /* Soft-k-max select without any device allocation by the caller.  No
  * counterpart in the reference: it exists for callers that cannot allocate
  * device memory (no allocator of their own, or no cudaMalloc allowed on

@@ -14,6 +14,7 @@ from .routing import (  # noqa: F401
     carrier_scatter,
     check_status,
     dtem_select,
+    dtem_select_backward,
     route_and_gather,
     sparse_neighbor_dot,
     sparse_spatial_score,

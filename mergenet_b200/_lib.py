@@ -65,6 +65,9 @@ _SIGNATURES = {
     "mn_thre_topk_backward": (c_int, [c_int, c_int, _P, c_int, c_float, _P, _P, _P, c_size_t, _P, _P]),
     "mn_dtem_select_workspace_bytes": (c_size_t, [c_int, c_int]),
     "mn_dtem_select": (c_int, [c_int, c_int, c_int, _P, _P, c_int, c_float, c_float, _P, _P, c_size_t, _P, _P]),
+    "mn_dtem_select_backward_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "mn_dtem_select_backward": (c_int, [c_int, c_int, c_int, _P, _P, c_int, c_float, c_float, _P, _P, _P, c_size_t,
+                                        _P, _P]),
     "mn_dtem_select_noalloc": (c_int, [c_int, c_int, c_int, _P, _P, c_int, c_float, c_float, _P, _P, _P]),
     "mn_carrier_scatter": (c_int, [c_int, c_int, c_int, c_int, c_int, _P, _P, _P, _P]),
     "mn_local_attention": (c_int, [c_int, c_int, c_int, c_int, c_int, _P, _P, _P, c_int64, c_int64, c_int64, _P,

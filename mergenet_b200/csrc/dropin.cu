@@ -245,32 +245,21 @@ __global__ void __launch_bounds__(512) thre_topk_rows_kernel(const float* __rest
 }
 
 // Gradient of ThreTopK with respect to x: the closed form of the reference's
-// autograd through thetopk.py:4-43.  Per row (one CTA): recompute
-// x~ = x / R * T, the sorted scans and the bracket b, then
-//   dx~_i = f'(d_i) g_i + [x~_i <= xs_b] dlse1 e^{x~_i - lse1_b}
-//           - [x~_i > xs_b] dL e^{-x~_i - lse2_b}
-// with dlambda = -sum_i f'(d_i) g_i, dL the path through |term_b|,
-// dlse1 = dlambda + dL; dx = dx~ T / R.  The row's share of
-// dR = -sum_i dx~_i x_i T / R^2 goes to rpart[row] (thre_topk_grad_range_kernel
-// adds dR to the maximum and -dR to the minimum elements).
-__global__ void __launch_bounds__(512) thre_topk_grad_rows_kernel(const float* __restrict__ x,
-                                                                  const float* __restrict__ gy, int n, int k,
-                                                                  float temperature, const float* partials,
-                                                                  int nparts, float* __restrict__ gx,
-                                                                  float* __restrict__ rpart, int* status) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ float red[64];
-  const int np = next_pow2(n);
-  RowScratch rs = carve_row_scratch(smem_raw, np);
-  float* xrow = reinterpret_cast<float*>(smem_raw + row_scratch_bytes(np));
-  const float range = reduce_range(partials, nparts, red, status);
-  const int64_t row = blockIdx.x;
-  const float* xr = x + row * n;
-  const float* gr = gy + row * n;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) xrow[i] = xr[i] / range * temperature;
-  __syncthreads();
-  int b = 0;
-  const float lam = thre_topk_lambda(xrow, n, np, k, rs, &b);
+// autograd through thetopk.py:4-43.  Per row (one CTA), after
+// thre_topk_lambda has left the sorted row and its scans in rs and returned
+// lambda and the bracket b:
+//   dx~_i = f'(d_i) g_i + [s(i) <= b] dlse1 e^{x~_i - lse1_b}
+//           - [s(i) > b] dL e^{-x~_i - lse2_b}
+// with s(i) the place of i in the stable ascending sort, dlambda =
+// -sum_i f'(d_i) g_i, dL the path through |term_b|, dlse1 = dlambda + dL.
+// Writes gx[i] = dx~_i T / R and returns (in every thread) the row's share
+// of dR = -sum_i dx~_i x_i T / R^2, which thre_topk_grad_range_kernel adds
+// to the maximum and subtracts from the minimum elements.
+// xrow: the row's scaled values x~ (shared); xr: its unscaled values; g:
+// the upstream gradient (readable by every thread).
+__device__ float thre_topk_row_grad(const float* xrow, const float* xr, const float* g, int n, int k, float lam,
+                                    int b, float range, float temperature, const RowScratch& rs, float* red,
+                                    float* __restrict__ gx) {
   const float xs_b = rs.xs[b], lse1_b = rs.lse1[b];
   const float lse2_b = b + 1 < n ? (float)(-(double)rs.xs[0] + log(rs.dbuf[n - 2 - b])) : -INFINITY;
   const float km = (float)(k - (n - 1 - b));
@@ -281,7 +270,7 @@ __global__ void __launch_bounds__(512) thre_topk_grad_rows_kernel(const float* _
     return dv > 0.f ? 0.5f * expf(-dv) : 0.5f * expf(dv);
   };
   float sdd = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) sdd += gr[i] * fprime(xrow[i]);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) sdd += g[i] * fprime(xrow[i]);
   sdd = block_sum(sdd, red);
   const float dlam = -sdd;
   const float sgn = term > 0.f ? 1.f : (term < 0.f ? -1.f : 0.f);
@@ -300,7 +289,7 @@ __global__ void __launch_bounds__(512) thre_topk_grad_rows_kernel(const float* _
   float part = 0.f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const float v = xrow[i];
-    float dxt = gr[i] * fprime(v);
+    float dxt = g[i] * fprime(v);
     bool low = v < xs_b;
     if (v == xs_b) {
       int pos = below_b;
@@ -309,11 +298,33 @@ __global__ void __launch_bounds__(512) thre_topk_grad_rows_kernel(const float* _
     }
     if (low) dxt += dlse1 * expf(v - lse1_b);
     else if (b + 1 < n) dxt -= dl * expf(-v - lse2_b);
-    gx[row * n + i] = dxt * inv_r;
+    gx[i] = dxt * inv_r;
     part += dxt * xr[i];
   }
   part = block_sum(part, red);
-  if (threadIdx.x == 0) rpart[row] = -part * inv_r / range;
+  return -part * inv_r / range;
+}
+
+__global__ void __launch_bounds__(512) thre_topk_grad_rows_kernel(const float* __restrict__ x,
+                                                                  const float* __restrict__ gy, int n, int k,
+                                                                  float temperature, const float* partials,
+                                                                  int nparts, float* __restrict__ gx,
+                                                                  float* __restrict__ rpart, int* status) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red[64];
+  const int np = next_pow2(n);
+  RowScratch rs = carve_row_scratch(smem_raw, np);
+  float* xrow = reinterpret_cast<float*>(smem_raw + row_scratch_bytes(np));
+  const float range = reduce_range(partials, nparts, red, status);
+  const int64_t row = blockIdx.x;
+  const float* xr = x + row * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) xrow[i] = xr[i] / range * temperature;
+  __syncthreads();
+  int b = 0;
+  const float lam = thre_topk_lambda(xrow, n, np, k, rs, &b);
+  const float part = thre_topk_row_grad(xrow, xr, gy + row * n, n, k, lam, b, range, temperature, rs, red,
+                                        gx + row * n);
+  if (threadIdx.x == 0) rpart[row] = part;
 }
 
 // The range's share of the ThreTopK gradient: dR (the sum of the rows'
@@ -375,7 +386,7 @@ __global__ void __launch_bounds__(256) select_energy_kernel(const float* __restr
   }
   if (lane == 0) {
     energy[row] = e;
-    if (m != -INFINITY) atomicAdd(&valid_count[row / Na], 1);
+    if (valid_count && m != -INFINITY) atomicAdd(&valid_count[row / Na], 1);
   }
 }
 
@@ -423,6 +434,117 @@ __global__ void __launch_bounds__(512) select_rows_kernel(const float* __restric
     }
     const float tmp = fmaxf(ks - 1.0f, 0.0f) + 1.0f;
     for (int c = 0; c < K; ++c) out[c] = out[c] / tmp;
+  }
+}
+
+// Select backward, part 1 (one CTA per batch row): recompute lambda over
+// the row energies, then per donor row the masked softmax p, y = ThreTopK
+// (times the valid-row flag) and t = max(sum_j p_j y - 1, 0) + 1 (detached
+// in the reference), the upstream gradient of y, dy = sum_j G_j p_j / t,
+// and through thre_topk_row_grad the energies' gradient (before the range
+// share) and the batch row's share of dR.  y and t go to the workspace for
+// part 2.
+__global__ void __launch_bounds__(512) select_grad_rows_kernel(const float* __restrict__ scores,
+                                                               const uint8_t* __restrict__ allowed,
+                                                               const float* __restrict__ grad_assign, int Na,
+                                                               int K, int k, float tau1, float tau2,
+                                                               const float* __restrict__ energy,
+                                                               const float* partials, int nparts,
+                                                               float* __restrict__ yrow_out,
+                                                               float* __restrict__ trow_out,
+                                                               float* __restrict__ grad_energy,
+                                                               float* __restrict__ rpart, int* status) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red[64];
+  const int np = next_pow2(Na);
+  RowScratch rs = carve_row_scratch(smem_raw, np);
+  float* xrow = reinterpret_cast<float*>(smem_raw + row_scratch_bytes(np));
+  float* dy = xrow + Na;
+  const int bb = blockIdx.x;
+  const float range = reduce_range(partials, nparts, red, status);
+  const float* e = energy + (int64_t)bb * Na;
+  for (int i = threadIdx.x; i < Na; i += blockDim.x) xrow[i] = e[i] / range * tau2;
+  __syncthreads();
+  int b = 0;
+  const float lam = thre_topk_lambda(xrow, Na, np, k, rs, &b);
+  for (int d = threadIdx.x; d < Na; d += blockDim.x) {
+    const int64_t row = (int64_t)bb * Na + d;
+    const float* s = scores + row * K;
+    const uint8_t* al = allowed + row * K;
+    const float* g = grad_assign + row * K;
+    float m = -INFINITY;
+    for (int c = 0; c < K; ++c)
+      if (al[c]) m = fmaxf(m, s[c] / tau1);
+    float y = 0.f, t = 1.f, gy = 0.f;
+    if (m != -INFINITY) {
+      y = thre_topk_map(xrow[d], lam);
+      float sum = 0.f;
+      for (int c = 0; c < K; ++c)
+        if (al[c]) sum += expf(s[c] / tau1 - m);
+      const float inv = 1.0f / sum;
+      float ks = 0.f, gp = 0.f;
+      for (int c = 0; c < K; ++c) {
+        if (!al[c]) continue;
+        const float pc = expf(s[c] / tau1 - m) * inv;
+        ks += pc * y;
+        gp += g[c] * pc;
+      }
+      t = fmaxf(ks - 1.0f, 0.0f) + 1.0f;
+      gy = gp / t;
+    }
+    dy[d] = gy;
+    yrow_out[row] = y;
+    trow_out[row] = t;
+  }
+  __syncthreads();
+  const float part = thre_topk_row_grad(xrow, e, dy, Na, k, lam, b, range, tau2, rs, red,
+                                        grad_energy + (int64_t)bb * Na);
+  if (threadIdx.x == 0) rpart[bb] = part;
+}
+
+// Select backward, part 2 (one warp per donor row): with dp_j = G_j y / t,
+// dscores_j = p_j (dp_j - sum_l dp_l p_l + dE E) / tau1 on allowed slots of
+// valid rows (the softmax's and the logsumexp's backward), zero elsewhere.
+__global__ void __launch_bounds__(256) select_grad_out_kernel(const float* __restrict__ scores,
+                                                              const uint8_t* __restrict__ allowed,
+                                                              const float* __restrict__ grad_assign, int rows,
+                                                              int K, float tau1, const float* __restrict__ energy,
+                                                              const float* __restrict__ grad_energy,
+                                                              const float* __restrict__ yrow,
+                                                              const float* __restrict__ trow,
+                                                              float* __restrict__ grad_scores) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* s = scores + row * K;
+  const uint8_t* al = allowed + row * K;
+  const float* g = grad_assign + row * K;
+  float* out = grad_scores + row * K;
+  float m = -INFINITY;
+  for (int c = lane; c < K; c += 32)
+    if (al[c]) m = fmaxf(m, s[c] / tau1);
+  m = warp_max(m);
+  if (m == -INFINITY) {
+    for (int c = lane; c < K; c += 32) out[c] = 0.f;
+    return;
+  }
+  float sum = 0.f;
+  for (int c = lane; c < K; c += 32)
+    if (al[c]) sum += expf(s[c] / tau1 - m);
+  const float inv = 1.0f / warp_sum(sum);
+  const float scale = yrow[row] / trow[row];
+  float inner = 0.f;
+  for (int c = lane; c < K; c += 32)
+    if (al[c]) inner += g[c] * scale * (expf(s[c] / tau1 - m) * inv);
+  inner = warp_sum(inner);
+  const float dlse = grad_energy[row] * energy[row];
+  for (int c = lane; c < K; c += 32) {
+    float v = 0.f;
+    if (al[c]) {
+      const float pc = expf(s[c] / tau1 - m) * inv;
+      v = pc * (g[c] * scale - inner + dlse) / tau1;
+    }
+    out[c] = v;
   }
 }
 
@@ -628,6 +750,48 @@ extern "C" int mn_dtem_select(int batch, int num_donors, int k_slots, const floa
   minmax_partials_kernel<<<parts, 256, 0, st>>>(energy, rows, partials);
   select_rows_kernel<<<batch, 512, smem, st>>>(scores, allowed, num_donors, k_slots, k, tau1, tau2, energy, counts,
                                                partials, parts, assignment, status);
+  return launch_status();
+}
+
+extern "C" size_t mn_dtem_select_backward_workspace_bytes(int batch, int num_donors) {
+  if (batch <= 0 || num_donors <= 0) return 0;
+  const int64_t rows = (int64_t)batch * num_donors;
+  return (size_t)rows * 4 * sizeof(float) + (size_t)thre_topk_parts(rows) * 2 * sizeof(float) +
+         (size_t)batch * sizeof(float) + 64;
+}
+
+extern "C" int mn_dtem_select_backward(int batch, int num_donors, int k_slots, const float* scores,
+                                       const uint8_t* allowed, int k, float tau1, float tau2,
+                                       const float* grad_assignment, float* grad_scores, void* workspace,
+                                       size_t workspace_bytes, int* status, void* stream) {
+  if (batch <= 0 || num_donors <= 0 || k_slots <= 0 || !scores || !allowed || !grad_assignment || !grad_scores ||
+      !workspace)
+    return MN_ERR_ARG;
+  if (num_donors > 4096) return MN_ERR_UNSUPPORTED;
+  if (workspace_bytes < mn_dtem_select_backward_workspace_bytes(batch, num_donors)) return MN_ERR_WORKSPACE;
+  cudaGetLastError();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t rows = (int64_t)batch * num_donors;
+  const int parts = thre_topk_parts(rows);
+  float* energy = static_cast<float*>(workspace);
+  float* grad_energy = energy + rows;
+  float* yrow = grad_energy + rows;
+  float* trow = yrow + rows;
+  float* partials = trow + rows;
+  float* rpart = partials + 2 * parts;
+  const int np = next_pow2(num_donors);
+  const size_t smem = row_scratch_bytes(np) + (size_t)2 * num_donors * sizeof(float);
+  if (!ensure_smem(select_grad_rows_kernel, smem)) return MN_ERR_LAUNCH;
+  select_energy_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(scores, allowed, (int)rows, k_slots, tau1,
+                                                                   energy, nullptr, num_donors);
+  minmax_partials_kernel<<<parts, 256, 0, st>>>(energy, rows, partials);
+  select_grad_rows_kernel<<<batch, 512, smem, st>>>(scores, allowed, grad_assignment, num_donors, k_slots, k, tau1,
+                                                    tau2, energy, partials, parts, yrow, trow, grad_energy, rpart,
+                                                    status);
+  thre_topk_grad_range_kernel<<<1, 1024, 0, st>>>(energy, rows, rpart, batch, partials, parts, grad_energy);
+  select_grad_out_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(scores, allowed, grad_assignment, (int)rows,
+                                                                     k_slots, tau1, energy, grad_energy, yrow, trow,
+                                                                     grad_scores);
   return launch_status();
 }
 

@@ -327,7 +327,50 @@ def _thre_topk(x, k, temperature):
 
 def dtem_select(k, scores, allowed, tau1=1.0, tau2=30.0, check=True):
     """Soft-k-max block of DTEMBlock._select with the sparse mask
-    (dtem.py:1536-1580): scores/allowed [B,Na,K] -> assignment [B,Na,K]."""
+    (dtem.py:1536-1580): scores/allowed [B,Na,K] -> assignment [B,Na,K].
+    Differentiable in scores (dtem_select_backward)."""
+    if _wants_grad(scores):
+        return _DtemSelectFn.apply(scores, allowed, int(k), float(tau1), float(tau2), check)
+    return _dtem_select(k, scores, allowed, tau1, tau2, check)
+
+
+class _DtemSelectFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, scores, allowed, k, tau1, tau2, check):
+        out = _dtem_select(k, scores, allowed, tau1, tau2, check)
+        ctx.save_for_backward(scores, allowed)
+        ctx.args = (k, tau1, tau2)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_assignment):
+        scores, allowed = ctx.saved_tensors
+        k, tau1, tau2 = ctx.args
+        return dtem_select_backward(k, scores, allowed, grad_assignment, tau1, tau2), None, None, None, None, None
+
+
+def dtem_select_backward(k, scores, allowed, grad_assignment, tau1=1.0, tau2=30.0):
+    """Gradient of the sparse soft-k-max select with respect to its scores,
+    as the reference's autograd differentiates dtem.py:1551-1580: through
+    the masked row softmax, the logsumexp row energies and ThreTopK over the
+    batch's energies (its range included); the over-unity renormalisation
+    divides by a detached total.  Rows with no allowed slot and masked slots
+    get zero.  Returns grad_scores shaped and typed like scores."""
+    dev = L.require_cuda(scores, allowed, grad_assignment)
+    s = scores.float().contiguous()
+    al = allowed.bool().contiguous()
+    g = grad_assignment.float().contiguous()
+    bsz, na, kk = s.shape
+    out = torch.empty_like(s)
+    wsb = L.lib().mn_dtem_select_backward_workspace_bytes(bsz, na)
+    ws = torch.empty(int(wsb), dtype=torch.uint8, device=dev)
+    L.check(L.lib().mn_dtem_select_backward(bsz, na, kk, L.ptr(s), L.ptr(_as_u8(al)), int(k), float(tau1),
+                                            float(tau2), L.ptr(g), L.ptr(out), L.ptr(ws), wsb, None,
+                                            L.stream_of(s)), "dtem_select backward")
+    return out.to(scores.dtype)
+
+
+def _dtem_select(k, scores, allowed, tau1, tau2, check):
     dev = L.require_cuda(scores, allowed)
     s = scores.float().contiguous()
     al = allowed.bool().contiguous()

@@ -286,6 +286,36 @@ def thre_topk_backward(x, k, grad_y, temperature=30.0):
     dx[is_min] -= d_range / is_min.sum()
     return dx[0] if squeeze else dx
 
+def select_backward(k, scores, allowed, grad_assign, tau1=1.0, tau2=30.0):
+    """Gradient of the sparse soft-k-max select (dtem.py:1551-1580) with
+    respect to its scores, in float64, as the reference's autograd takes it.
+    Per valid donor row (any allowed slot), with p the masked softmax of
+    scores / tau1, E = exp(logsumexp), y = ThreTopK(E over the batch) and
+    t = max(sum_j p_j y - 1, 0) + 1 (detached):
+      dp_j = G_j y / t,   dy = sum_j G_j p_j / t,
+      dE = thre_topk_backward(E, k, dy) (invalid rows: E = 0, no gradient),
+      dscores_j = p_j (dp_j - sum_l dp_l p_l + dE E) / tau1 on allowed slots."""
+    s = np.asarray(scores, np.float64)
+    al = np.asarray(allowed, np.bool_)
+    g = np.asarray(grad_assign, np.float64)
+    valid = al.any(-1)
+    logits = np.where(al, s / tau1, -np.inf)
+    m = np.where(valid, logits.max(-1), 0.0)
+    e = np.where(al, np.exp(logits - m[..., None]), 0.0)
+    tot = np.where(valid, e.sum(-1), 1.0)
+    p = e / tot[..., None]
+    energy = np.where(valid, np.exp(np.log(tot) + m), 0.0)
+    y = thre_topk(energy.astype(F32), k, tau2).astype(np.float64).reshape(energy.shape) * valid
+    t = np.maximum((p * y[..., None]).sum(-1) - 1.0, 0.0) + 1.0
+    gt = g / t[..., None]
+    dp = gt * y[..., None]
+    dy = (gt * p).sum(-1) * valid
+    de = thre_topk_backward(energy, k, dy, tau2).reshape(energy.shape) * valid
+    inner = (dp * p).sum(-1)
+    ds = p * (dp - inner[..., None] + (de * energy)[..., None]) / tau1
+    return np.where(al & valid[..., None], ds, 0.0)
+
+
 def _softmax_lastdim(x):
     """exp(x - max) * (1 / sum) like the CPU softmax kernel."""
     mx = x.max(axis=-1, keepdims=True)

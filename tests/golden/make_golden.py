@@ -241,6 +241,72 @@ def transport_case():
                         receivers=receivers, out=out.numpy())
 
 
+def select_backward_case():
+    """Gradients through the reference's sparse soft-k-max select,
+    DTEMBlock._select (opentome/timm/dtem.py:1464-1580): sparse scores,
+    masked logsumexp row energies, ThreTopK over the batch, the row softmax
+    and the (detached) over-unity renormalisation.  The scores' own gradient
+    is observed by wrapping the module's sparse_spatial_score (the call
+    itself is the reference's, unchanged) so the select block can be checked
+    apart from the score's backward."""
+    import opentome.timm.dtem as ref_dtem
+    rng = np.random.default_rng(20261203)
+    cases = {}
+    seen = {}
+    original = ref_dtem.sparse_spatial_score
+
+    def observed(*args, **kwargs):
+        scores, ridx, rvalid = original(*args, **kwargs)
+        scores.retain_grad()
+        seen["scores"] = scores
+        return scores, ridx, rvalid
+
+    def partition(grid, batch, mode):
+        n = grid[0] * grid[1]
+        a_rows, b_rows = [], []
+        for bi in range(batch):
+            if mode == "alternating":
+                tokens = np.arange(n)
+                a_tok, b_tok = tokens[(tokens + bi) % 2 == 0], tokens[(tokens + bi) % 2 == 1]
+            else:
+                perm = rng.permutation(n)
+                a_tok, b_tok = np.sort(perm[: n // 2]), np.sort(perm[n // 2:])
+            a_rows.append(a_tok + 1)
+            b_rows.append(b_tok + 1)
+        return torch.from_numpy(np.stack(a_rows)), torch.from_numpy(np.stack(b_rows))
+
+    ref_dtem.sparse_spatial_score = observed
+    try:
+        for i, (grid, radius, batch, k, channels, mode) in enumerate(
+                [((3, 5), 2, 2, 3, 9, "reference_test"), ((8, 8), 3, 2, 16, 16, "alternating"),
+                 ((6, 7), 1, 3, 3, 8, "random")]):
+            if mode == "reference_test":  # tests/test_dtem_spatial_sparse.py:179-227
+                a_idx = torch.tensor([[1, 3, 5, 7, 9, 11, 13], [2, 4, 6, 8, 10, 12, 14]])
+                b_idx = torch.tensor([[2, 4, 6, 8, 10, 12, 14, 15], [1, 3, 5, 7, 9, 11, 13, 15]])
+            else:
+                a_idx, b_idx = partition(grid, batch, mode)
+            na, nb = a_idx.shape[1], b_idx.shape[1]
+            a = (rng.standard_normal((batch, na, channels), dtype=np.float32) * 0.5).astype(np.float32)
+            b = (rng.standard_normal((batch, nb, channels), dtype=np.float32) * 0.5).astype(np.float32)
+            block = make_block(grid, radius, "sparse")
+            ta = torch.from_numpy(a).requires_grad_(True)
+            tb = torch.from_numpy(b).requires_grad_(True)
+            assign, _ = block._select(k, ta, tb, a_idx, b_idx)
+            g = rng.standard_normal(tuple(assign.shape), dtype=np.float32)
+            assign.backward(torch.from_numpy(g))
+            scores = seen["scores"]
+            cases.update({f"grid{i}": np.array(grid), f"radius{i}": radius, f"k{i}": k,
+                          f"a{i}": a, f"b{i}": b, f"a_idx{i}": a_idx.numpy(), f"b_idx{i}": b_idx.numpy(),
+                          f"grad_assign{i}": g, f"assign{i}": assign.detach().numpy(),
+                          f"scores{i}": scores.detach().numpy(), f"grad_scores{i}": scores.grad.numpy(),
+                          f"allowed{i}": block._tome_info["assign_valid_mask"].numpy(),
+                          f"grad_a{i}": ta.grad.numpy(), f"grad_b{i}": tb.grad.numpy()})
+    finally:
+        ref_dtem.sparse_spatial_score = original
+    cases["count"] = np.int64(3)
+    np.savez_compressed(HERE / "select_backward.npz", **cases)
+
+
 def neighbor_dot_backward_case():
     """Gradients of the reference's sparse_neighbor_dot (the score of
     sparse_spatial_score too) through its own autograd Function
@@ -297,6 +363,7 @@ def main():
     thre_topk_case()
     thre_topk_backward_case()
     select_case()
+    select_backward_case()
     transport_case()
     route_case("route_g3x6", 101, 2, (3, 6), 2.0, 7, 5, [3, 3], capture=True)
     route_case("route_g4x4", 102, 3, (4, 4), 1.5, 16, 8, [2, 2, 2], capture=True)

@@ -138,3 +138,13 @@ def test_oracle_thre_topk_backward(golden_dir):
         dx = O.thre_topk_backward(g[f"x{i}"], int(g[f"k{i}"]), g[f"g{i}"])
         ref = g[f"dx{i}"]
         assert np.abs(dx - ref).max() <= 2e-5 * np.abs(ref).max()
+
+
+def test_oracle_select_backward(golden_dir):
+    """The select block's score gradient against the reference's autograd
+    through DTEMBlock._select (observed at its sparse_spatial_score call)."""
+    g = load(golden_dir, "select_backward")
+    for i in range(int(g["count"])):
+        ds = O.select_backward(int(g[f"k{i}"]), g[f"scores{i}"], g[f"allowed{i}"], g[f"grad_assign{i}"])
+        ref = g[f"grad_scores{i}"]
+        assert np.abs(ds - ref).max() <= 2e-5 * np.abs(ref).max(), i

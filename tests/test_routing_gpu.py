@@ -265,7 +265,6 @@ def test_thre_topk_backward_large_rows(dev, rows, n, k):
     """Row lengths of the donor sets and the kernel's maximum against the
     float64 closed form of the oracle (rel. 1e-4 of the largest entry)."""
     import mergenet_b200 as mn
-    from oracle import routing as O
     gen = torch.Generator().manual_seed(rows * 7 + n)
     x = torch.randn(rows, n, generator=gen) * 3 + 1
     gy = torch.randn(rows, n, generator=gen)
@@ -388,3 +387,45 @@ def test_spatial_score_backward(dev, golden_dir, dtype):
     tol = 1e-5 if dtype == torch.float32 else 2e-2
     np.testing.assert_allclose(a.grad.float().cpu().numpy(), want_a, rtol=tol, atol=tol)
     np.testing.assert_allclose(b.grad.float().cpu().numpy(), want_b, rtol=tol, atol=tol)
+
+
+def test_select_backward_matches_reference(dev, golden_dir):
+    """Metric gradients through the sparse score and the soft-k-max select
+    against the reference's autograd through DTEMBlock._select
+    (dtem.py:1464-1580), and the select block's own score gradient; one case
+    has donor rows with no allowed receiver."""
+    import mergenet_b200 as mn
+    g = np.load(golden_dir / "select_backward.npz")
+    for i in range(int(g["count"])):
+        nbr, val = mn.build_patch_spatial_neighbors(tuple(int(v) for v in g[f"grid{i}"]), float(g[f"radius{i}"]),
+                                                    device=dev)
+        a = torch.from_numpy(g[f"a{i}"]).to(dev).requires_grad_(True)
+        b = torch.from_numpy(g[f"b{i}"]).to(dev).requires_grad_(True)
+        scores, ridx, rval = mn.sparse_spatial_score(a, b, nbr, val, torch.from_numpy(g[f"a_idx{i}"] - 1).to(dev),
+                                                     torch.from_numpy(g[f"b_idx{i}"] - 1).to(dev))
+        scores.retain_grad()
+        assign = mn.dtem_select(int(g[f"k{i}"]), scores, rval)
+        np.testing.assert_allclose(assign.detach().cpu().numpy(), g[f"assign{i}"], rtol=0, atol=2e-6)
+        assign.backward(torch.from_numpy(g[f"grad_assign{i}"]).to(dev))
+        for name, got in (("grad_scores", scores.grad), ("grad_a", a.grad), ("grad_b", b.grad)):
+            ref = g[f"{name}{i}"]
+            err = np.abs(got.cpu().numpy() - ref).max()
+            assert err <= 1e-4 * np.abs(ref).max(), (i, name, err)
+
+
+@pytest.mark.parametrize("batch,na,k_slots,k", [(4, 392, 29, 196), (2, 1000, 13, 300)])
+def test_select_backward_against_oracle(dev, batch, na, k_slots, k):
+    """Donor-set sizes of the 28x28 grid (radius 3: 29 slots) and a longer
+    row against the oracle's float64 closed form; about a tenth of the slots
+    and a few whole rows are masked."""
+    import mergenet_b200 as mn
+    gen = torch.Generator().manual_seed(na + k)
+    scores = torch.randn(batch, na, k_slots, generator=gen) * 0.3
+    allowed = torch.rand(batch, na, k_slots, generator=gen) > 0.1
+    allowed[:, ::97] = False
+    ga = torch.randn(batch, na, k_slots, generator=gen)
+    ref = O.select_backward(k, scores.numpy(), allowed.numpy(), ga.numpy())
+    got = mn.dtem_select_backward(k, scores.to(dev), allowed.to(dev), ga.to(dev))
+    err = np.abs(got.cpu().numpy() - ref).max()
+    assert err <= 1e-4 * np.abs(ref).max(), err
+    assert int(torch.count_nonzero(got.cpu()[~allowed])) == 0
