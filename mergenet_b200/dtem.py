@@ -18,13 +18,21 @@ signatures, return values and ``_tome_info`` side effects:
 The scoring, the select block and both transports run on the library's CUDA
 kernels (``sparse_spatial_score``, ``dtem_select``,
 ``sparse_weighted_transport``); the remaining elementwise steps are PyTorch
-on the same device.  It covers the inference path the canonical model uses:
-eval mode, global candidates with a 2-D spatial radius on the sparse backend,
-soft-k-max selection, and ``source_trace_mode`` "center" or "none".  Other
-configurations (training, flat windows, the dense backend, dense source
-matrices) raise ``NotImplementedError`` before any device work.  For the
-whole six-layer loop plus the carrier block in a handful of launches, use
-``RoutePlan`` instead.
+on the same device.  It covers the configuration the canonical model uses:
+global candidates with a 2-D spatial radius on the sparse backend, soft-k-max
+selection, and ``source_trace_mode`` "center" or "none", in eval mode and in
+training mode.  Training is differentiable end to end in x, size and the
+metric: the score, select and transport kernels have CUDA backward passes,
+and the donors' mass update keeps the reference's straight-through form
+``wa * (tmp + (clamp(tmp, 0, 1) - tmp).detach())``.  Training groups tokens
+as the reference does (dtem.py:1755-1800): ``train_grouping``
+"random_per_sample" (the default) draws ``torch.rand(B, n - 1)`` on the
+tokens' device and splits its argsort; the deterministic modes use
+``build_eval_group_indices`` with ``train_grouping_seed``.  Other
+configurations (flat windows, the dense backend, dense source matrices)
+raise ``NotImplementedError`` before any device work.  For the whole
+six-layer inference loop plus the carrier block in a handful of launches,
+use ``RoutePlan`` instead.
 """
 from __future__ import annotations
 
@@ -106,8 +114,6 @@ class DTEMMergeBlock(torch.nn.Module):
     # ------------------------------------------------------------- checks
     def _check_supported(self):
         info = self._tome_info
-        if self.training:
-            raise NotImplementedError("DTEMMergeBlock implements the inference path (call .eval())")
         window = info.get("window_size")
         if window is not None and window > 0:
             raise NotImplementedError("flat-window DTEM candidates are not on the B200 path")
@@ -150,9 +156,27 @@ class DTEMMergeBlock(torch.nn.Module):
         return assign.to(scores.dtype), None
 
     # -------------------------------------------------------------- merge
-    @torch.no_grad()
+    def _groups(self, n_tokens, bsz, dev):
+        """Donor / receiver positions (before the prefix offset) and whether
+        they are the strided parity split (dtem.py:1755-1812)."""
+        info = self._tome_info
+        layer = info.get("merge_layer_index", 0)
+        if self.training:
+            grouping = info.get("train_grouping", "random_per_sample")
+            if grouping == "random_per_sample":
+                perm = torch.argsort(torch.rand(bsz, n_tokens, device=dev), dim=1)
+                nd = n_tokens // 2
+                return perm[:, :nd], perm[:, nd:], False
+            seed = info.get("train_grouping_seed", 0)
+        else:
+            grouping = info.get("eval_grouping", "alternating_per_layer")
+            seed = info.get("eval_grouping_seed", 0)
+        a_idx, b_idx = build_eval_group_indices(n_tokens, bsz, dev, grouping, seed, layer)
+        return a_idx, b_idx, grouping == "alternating_per_layer_fast" and n_tokens % 2 == 0
+
     def _merge_train(self, x, size, r, n, metric, source_matrix=None):
-        """One soft merge layer (dtem.py:1687-2223), inference path."""
+        """One soft merge layer (dtem.py:1687-2223); differentiable when
+        autograd records it, with the centre tracking outside the graph."""
         self._check_supported()
         info = self._tome_info
         m = metric["metric"].float()
@@ -168,10 +192,8 @@ class DTEMMergeBlock(torch.nn.Module):
         offset = 1 if info.get("class_token", True) else 0
         n_tokens = n - offset
         layer = info.get("merge_layer_index", 0)
-        grouping = info.get("eval_grouping", "alternating_per_layer")
-        a_idx, b_idx = build_eval_group_indices(n_tokens, bsz, dev, grouping, info.get("eval_grouping_seed", 0), layer)
+        a_idx, b_idx, strided = self._groups(n_tokens, bsz, dev)
         a_idx, b_idx = a_idx + offset, b_idx + offset
-        strided = grouping == "alternating_per_layer_fast" and n_tokens % 2 == 0
         if strided:
             donor_parity = 0 if layer % 2 else 1
             ds = slice(offset + donor_parity, offset + n_tokens, 2)
@@ -188,7 +210,7 @@ class DTEMMergeBlock(torch.nn.Module):
             a, b = gather(m, a_sorted).contiguous(), gather(m, b_sorted).contiguous()
             wa = torch.gather(size[..., 0], 1, a_sorted).float()
             wb = torch.gather(size[..., 0], 1, b_sorted).float()
-        wa0, wb0 = wa.clone(), wb.clone()
+        wa0, wb0 = wa.detach().clone(), wb.detach().clone()
         if trace_center:
             tc = info.get("token_center")
             if tc is None:
@@ -206,13 +228,14 @@ class DTEMMergeBlock(torch.nn.Module):
         xb = wb[..., None] * xb + xb_contrib
         wb = wb + wb_contrib
         tmp = 1 - assign.sum(dim=-1)
-        wa = wa * torch.clamp(tmp, 0.0, 1.0)  # the straight-through form's forward value
+        wa = wa * (tmp + (torch.clamp(tmp, 0.0, 1.0) - tmp).detach())
         wb_safe = torch.clamp(wb, min=torch.finfo(wb.dtype).eps)
         xb = xb / wb_safe[..., None]
         if trace_center:
-            c_contrib = sparse_weighted_transport(assign, (wa0 * ca.float()).unsqueeze(-1).contiguous(), ridx, rvalid,
-                                                  nb)[..., 0]
-            cb_new = (wb0 * cb.float() + c_contrib) / wb_safe
+            with torch.no_grad():
+                c_contrib = sparse_weighted_transport(assign, (wa0 * ca.float()).unsqueeze(-1).contiguous(), ridx,
+                                                      rvalid, nb)[..., 0]
+                cb_new = (wb0 * cb.float() + c_contrib) / wb_safe
         x_out = torch.empty_like(x)
         size_out = torch.empty_like(size)
         if offset:
@@ -234,20 +257,26 @@ class DTEMMergeBlock(torch.nn.Module):
             x_out[:, n:] = x[:, n:]
             size_out[:, n:] = size[:, n:]
         if trace_center:
-            old = info.get("token_center")
-            center = torch.empty(bsz, t_tokens, device=dev, dtype=torch.float32)
-            if offset:
-                center[:, :offset] = 0 if old is None else old[:, :offset]
-            if n < t_tokens:
-                center[:, n:] = tc[:, n:]
-            if strided:
-                center[:, ds] = ca.float()
-                center[:, rs] = cb_new
-            else:
-                center.scatter_(1, a_sorted, ca.float())
-                center.scatter_(1, b_sorted, cb_new)
-            info["token_center"] = center
+            self._store_center(info, tc, ca, cb_new, a_sorted, b_sorted, ds if strided else None,
+                               rs if strided else None, offset, n, bsz, t_tokens, dev)
         return x_out, size_out, n, None, None  # _select's out dict is None on the soft-k-max path
+
+    @torch.no_grad()
+    def _store_center(self, info, tc, ca, cb_new, a_sorted, b_sorted, ds, rs, offset, n, bsz, t_tokens, dev):
+        """token_center after the layer (dtem.py:2031-2044 and the restore)."""
+        old = info.get("token_center")
+        center = torch.empty(bsz, t_tokens, device=dev, dtype=torch.float32)
+        if offset:
+            center[:, :offset] = 0 if old is None else old[:, :offset]
+        if n < t_tokens:
+            center[:, n:] = tc[:, n:]
+        if ds is not None:
+            center[:, ds] = ca.float()
+            center[:, rs] = cb_new
+        else:
+            center.scatter_(1, a_sorted, ca.float())
+            center.scatter_(1, b_sorted, cb_new)
+        info["token_center"] = center
 
 
 def make_merge_block(grid_size, radius=3.0, device=None, eval_grouping="alternating_per_layer_fast", **kwargs):

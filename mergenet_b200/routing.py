@@ -196,7 +196,35 @@ def _sparse_neighbor_dot(a, b, receiver_indices, receiver_valid):
 
 def sparse_weighted_transport(assignment, values, receiver_indices, receiver_valid, num_receivers):
     """out[b, s] = sum of assignment * values over edges into receiver s
-    (dtem.py:1035-1067), accumulated in edge order without atomics."""
+    (dtem.py:1035-1067), accumulated in edge order without atomics.
+    Differentiable in assignment and values like the reference's
+    _SparseTransport (dtem.py:934-974): the backward is
+    sparse_transport_adjoint."""
+    if _wants_grad(assignment, values):
+        return _SparseTransportFn.apply(assignment, values, receiver_indices, receiver_valid, int(num_receivers))
+    return _sparse_weighted_transport(assignment, values, receiver_indices, receiver_valid, num_receivers)
+
+
+class _SparseTransportFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, assignment, values, receiver_indices, receiver_valid, num_receivers):
+        out = _sparse_weighted_transport(assignment, values, receiver_indices, receiver_valid, num_receivers)
+        a = assignment.contiguous()
+        ctx.save_for_backward(a, values.to(a.dtype).contiguous(), receiver_indices.long().contiguous(),
+                              receiver_valid.bool().contiguous())
+        ctx.values_dtype = values.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        a, v, ridx, rval = ctx.saved_tensors
+        gw, gv = sparse_transport_adjoint(a, v, ridx, rval, grad_output.to(v.dtype))
+        grad_a = gw if ctx.needs_input_grad[0] else None
+        grad_v = gv.to(ctx.values_dtype) if ctx.needs_input_grad[1] else None
+        return grad_a, grad_v, None, None, None
+
+
+def _sparse_weighted_transport(assignment, values, receiver_indices, receiver_valid, num_receivers):
     dev = L.require_cuda(assignment, values, receiver_indices, receiver_valid)
     num_receivers = int(num_receivers)
     if assignment.dtype != values.dtype:

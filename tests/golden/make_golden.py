@@ -307,6 +307,43 @@ def select_backward_case():
     np.savez_compressed(HERE / "select_backward.npz", **cases)
 
 
+def merge_train_backward_case():
+    """One training-mode soft merge layer of the reference,
+    DTEMBlock._merge_train (opentome/timm/dtem.py:1687-2223), differentiated
+    by its own autograd: gradients of random upstream gradients on the
+    output tokens and masses with respect to x, size and the metric.  The
+    deterministic train groupings make the partition reproducible: the
+    strided parity split and a seeded permutation (the generic gather /
+    scatter path)."""
+    rng = np.random.default_rng(20261204)
+    cases = {}
+    specs = [((8, 8), 3.0, 2, 16, 8, 12, "alternating_per_layer_fast", 1),
+             ((6, 7), 2.0, 3, 12, 6, 9, "seeded", 0)]
+    for i, (grid, radius, batch, channels, metric_dim, r, grouping, layer) in enumerate(specs):
+        t = grid[0] * grid[1] + 1
+        x = rng.standard_normal((batch, t, channels), dtype=np.float32)
+        metric = rng.standard_normal((batch, t, metric_dim), dtype=np.float32)
+        size = (1.0 + 2.0 * rng.random((batch, t, 1))).astype(np.float32)
+        block = make_block(grid, radius, "sparse")
+        block.train()
+        block._tome_info.update({"train_grouping": grouping, "train_grouping_seed": 7, "merge_layer_index": layer})
+        tx = torch.from_numpy(x).requires_grad_(True)
+        tm = torch.from_numpy(metric).requires_grad_(True)
+        ts = torch.from_numpy(size).requires_grad_(True)
+        x_out, size_out, _, _, _ = block._merge_train(tx, ts, r, t, {"metric": tm})
+        gx = rng.standard_normal(tuple(x_out.shape), dtype=np.float32)
+        gs = rng.standard_normal(tuple(size_out.shape), dtype=np.float32)
+        torch.autograd.backward([x_out, size_out], [torch.from_numpy(gx), torch.from_numpy(gs)])
+        cases.update({f"grid{i}": np.array(grid), f"radius{i}": radius, f"r{i}": r, f"grouping{i}": grouping,
+                      f"layer{i}": layer, f"x{i}": x, f"metric{i}": metric, f"size{i}": size,
+                      f"x_out{i}": x_out.detach().numpy(), f"size_out{i}": size_out.detach().numpy(),
+                      f"center{i}": block._tome_info["token_center"].numpy(),
+                      f"grad_x_out{i}": gx, f"grad_size_out{i}": gs, f"grad_x{i}": tx.grad.numpy(),
+                      f"grad_metric{i}": tm.grad.numpy(), f"grad_size{i}": ts.grad.numpy()})
+    cases["count"] = np.int64(len(specs))
+    np.savez_compressed(HERE / "merge_train_backward.npz", **cases)
+
+
 def neighbor_dot_backward_case():
     """Gradients of the reference's sparse_neighbor_dot (the score of
     sparse_spatial_score too) through its own autograd Function
@@ -364,6 +401,7 @@ def main():
     thre_topk_backward_case()
     select_case()
     select_backward_case()
+    merge_train_backward_case()
     transport_case()
     route_case("route_g3x6", 101, 2, (3, 6), 2.0, 7, 5, [3, 3], capture=True)
     route_case("route_g4x4", 102, 3, (4, 4), 1.5, 16, 8, [2, 2, 2], capture=True)

@@ -127,3 +127,62 @@ def test_local_attention_module(dev, dtype, cls_global):
     tol = 2e-2 if dtype == torch.bfloat16 else 1e-2
     assert ((out.float() - want).abs().max() / want.abs().max()).item() <= tol
     assert sorted(n for n, _ in mod.named_parameters()) == ["proj.bias", "proj.weight", "qkv.bias", "qkv.weight"]
+
+
+@pytest.mark.parametrize("case", [0, 1])
+def test_merge_block_training_gradients_match_reference(dev, golden_dir, case):
+    """A training-mode merge layer (dtem.py:1687-2223) forward and backward
+    against the reference's own autograd: output tokens, masses and centres,
+    then the gradients with respect to x, size and the metric, which run
+    through the transport adjoint, the select backward (ThreTopK included)
+    and the neighbour-dot backward, and the straight-through mass update."""
+    import mergenet_b200 as mn
+    g = np.load(golden_dir / "merge_train_backward.npz")
+    i = case
+    grid = tuple(int(v) for v in g[f"grid{i}"])
+    block = mn.make_merge_block(grid, float(g[f"radius{i}"]), device=dev).train()
+    block._tome_info.update({"train_grouping": str(g[f"grouping{i}"]), "train_grouping_seed": 7,
+                             "merge_layer_index": int(g[f"layer{i}"])})
+    x = torch.from_numpy(g[f"x{i}"]).to(dev).requires_grad_(True)
+    metric = torch.from_numpy(g[f"metric{i}"]).to(dev).requires_grad_(True)
+    size = torch.from_numpy(g[f"size{i}"]).to(dev).requires_grad_(True)
+    t = x.shape[1]
+    x_out, size_out, n, _, _ = block._merge_train(x, size, int(g[f"r{i}"]), t, {"metric": metric})
+    assert n == t
+    np.testing.assert_allclose(x_out.detach().cpu().numpy(), g[f"x_out{i}"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(size_out.detach().cpu().numpy(), g[f"size_out{i}"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(block._tome_info["token_center"].cpu().numpy(), g[f"center{i}"], rtol=0, atol=1e-3)
+    torch.autograd.backward([x_out, size_out], [torch.from_numpy(g[f"grad_x_out{i}"]).to(dev),
+                                                torch.from_numpy(g[f"grad_size_out{i}"]).to(dev)])
+    for name, got in (("grad_x", x.grad), ("grad_size", size.grad), ("grad_metric", metric.grad)):
+        ref = g[f"{name}{i}"]
+        err = np.abs(got.cpu().numpy() - ref).max()
+        assert err <= 1e-4 * np.abs(ref).max(), (name, err)
+
+
+def test_merge_block_training_random_groups(dev):
+    """The default train grouping ("random_per_sample", dtem.py:1763-1770):
+    each image gets its own donor / receiver split from torch.rand on the
+    device, mass is conserved, the same generator state gives the same
+    layer, and the backward reaches x, size and the metric."""
+    import mergenet_b200 as mn
+    grid = (14, 14)
+    gen = torch.Generator().manual_seed(11)
+    x = torch.randn(4, 197, 32, generator=gen).to(dev).requires_grad_(True)
+    metric = torch.randn(4, 197, 16, generator=gen).to(dev).requires_grad_(True)
+    size = torch.ones(4, 197, 1, device=dev, requires_grad=True)
+    outs = []
+    for _ in range(2):
+        block = mn.make_merge_block(grid, 3.0, device=dev).train()
+        torch.cuda.manual_seed(1234)
+        outs.append(block._merge_train(x, size, 40, 197, {"metric": metric}))
+    (x0, s0, _, _, _), (x1, s1, _, _, _) = outs
+    assert torch.equal(x0, x1) and torch.equal(s0, s1)
+    torch.testing.assert_close(s0.double().sum(1), size.double().sum(1), rtol=1e-6, atol=1e-4)
+    # different images, different splits: the masses left on the donors differ in position
+    moved = (s0[..., 0] != 1).cpu()
+    assert any(not torch.equal(moved[0], moved[j]) for j in range(1, 4))
+    (x0 * torch.randn_like(x0)).sum().add((s0 * 0.5).sum()).backward()
+    for t in (x, size, metric):
+        assert t.grad is not None and bool(torch.isfinite(t.grad).all())
+    assert float(metric.grad.abs().sum()) > 0

@@ -170,14 +170,15 @@ def test_attention_shapes_outside_the_kernels_are_refused():
 
 
 def test_merge_block_refuses_paths_it_does_not_implement():
-    """DTEMMergeBlock covers the inference path only; the others are refused
-    before any device work."""
+    """DTEMMergeBlock covers the sparse spatial soft-k-max path in eval and
+    training mode; the other paths, and train groupings the reference does
+    not have, are refused before any device work."""
     import mergenet_b200 as mn
     block = mn.DTEMMergeBlock({"window_size": 0, "dtem_spatial_radius": 3.0, "dtem_spatial_backend": "sparse",
-                               "tau2": 30.0})
+                               "tau2": 30.0, "train_grouping": "random"})
     x = torch.zeros(1, 5, 8)
     size = torch.ones(1, 5, 1)
-    with pytest.raises(NotImplementedError, match="inference"):
+    with pytest.raises(ValueError, match="grouping"):
         block.train()._merge_train(x, size, 1, 5, {"metric": torch.ones(1, 5, 4)})
     block.eval()
     block._tome_info["dtem_spatial_backend"] = "dense"

@@ -234,6 +234,11 @@ def test_sparse_transport_pair_and_adjoint(dev, dtype, channels):
     np.testing.assert_allclose(gw.float().cpu().numpy(), gw_ref.numpy(), rtol=tol, atol=tol * max(1, channels ** 0.5))
     np.testing.assert_allclose(gv.float().cpu().numpy(), gv_ref.numpy(), rtol=tol, atol=tol)
     assert int(torch.count_nonzero(gw.cpu()[~valid])) == 0
+    # autograd through sparse_weighted_transport runs the same adjoint
+    wd = w.to(dtype).to(dev).requires_grad_()
+    vd = v.to(dtype).to(dev).requires_grad_()
+    mn.sparse_weighted_transport(wd, vd, idx.to(dev), valid.to(dev), receivers).backward(probe.to(dtype).to(dev))
+    assert torch.equal(wd.grad, gw) and torch.equal(vd.grad, gv)
 
 
 def test_thre_topk_matches_reference(dev, golden_dir):
