@@ -40,6 +40,12 @@ __device__ __forceinline__ void store_2d(const CUtensorMap* map, uint32_t src, i
                "r"(x), "r"(y), "r"(src)
                : "memory");
 }
+__device__ __forceinline__ void store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(src)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // wait until at most N committed store groups may still read shared memory
 template <int N>
