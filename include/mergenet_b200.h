@@ -193,6 +193,38 @@ int mn_thre_topk_backward(int rows, int n, const float* x, int k,
                           float* grad_x, void* workspace,
                           size_t workspace_bytes, int* status, void* stream);
 
+/* The carrier block's soft-top-k training terms
+ * (opentome/models/mergenet/model.py:1163-1206).
+ *
+ * mn_soft_topk_aux: aux f32 [B, C] = sum_i x[b, i, :] * soft_sel[b, i] /
+ * max(sum_j soft_sel[b, j], 1e-6) over the n patch rows of x (element
+ * strides x_batch_stride, x_row_stride; channels contiguous), the auxiliary
+ * representation of model.py:1196-1198.  mn_soft_topk_aux_backward: its
+ * gradients, grad_x [B, n, C] (x's dtype, contiguous) and grad_sel f32
+ * [B, n]; workspace mn_soft_topk_aux_backward_workspace_bytes(B, n).
+ * mn_carrier_ste_backward: the gradient that the straight-through carrier
+ * weights topk_x * (1 + (w - w.detach())), w = soft_sel[b, topk_idx[b, j]]
+ * (model.py:1176-1179), send to soft_sel: grad_sel f32 [B, n] is zeroed and
+ * grad_sel[b, topk_idx[b, j]] = grad_out[b, j, :] . topk_x[b, j, :]; the
+ * features' own gradient is grad_out itself.  An index outside [0, n) is
+ * skipped and sets MN_STATUS_TOO_MANY_EDGES in *status. */
+int mn_soft_topk_aux(int batch, int n, int channels, int dtype, const void* x,
+                     int64_t x_batch_stride, int64_t x_row_stride,
+                     const float* soft_sel, float* aux, void* stream);
+size_t mn_soft_topk_aux_backward_workspace_bytes(int batch, int n);
+int mn_soft_topk_aux_backward(int batch, int n, int channels, int dtype,
+                              const void* x, int64_t x_batch_stride,
+                              int64_t x_row_stride, const float* soft_sel,
+                              const float* grad_aux, void* grad_x,
+                              float* grad_sel, void* workspace,
+                              size_t workspace_bytes, void* stream);
+int mn_carrier_ste_backward(int batch, int k, int channels, int dtype,
+                            const void* topk_x, int64_t x_batch_stride,
+                            int64_t x_row_stride, const void* grad_out,
+                            int64_t g_batch_stride, int64_t g_row_stride,
+                            const int64_t* topk_idx, int n, float* grad_sel,
+                            int* status, void* stream);
+
 /* Soft-k-max block of DTEMBlock._select with the sparse spatial mask,
  * opentome/timm/dtem.py:1551-1580: scores f32 [B,Na,K] + allowed uint8 ->
  * assignment f32 [B,Na,K].  Returns MN_INFEASIBLE_BUDGET through the device

@@ -12,6 +12,7 @@ from .routing import (  # noqa: F401
     build_patch_spatial_adjacency,
     build_patch_spatial_neighbors,
     carrier_scatter,
+    carrier_ste,
     check_status,
     dtem_select,
     dtem_select_backward,
@@ -20,6 +21,7 @@ from .routing import (  # noqa: F401
     sparse_spatial_score,
     sparse_transport_adjoint,
     sparse_weighted_transport,
+    soft_topk_aux_repr,
     sparse_weighted_transport_pair,
     thre_topk_backward,
 )

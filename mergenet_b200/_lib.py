@@ -61,6 +61,12 @@ _SIGNATURES = {
                                             _P, _P]),
     "mn_thre_topk_workspace_bytes": (c_size_t, [c_int, c_int]),
     "mn_thre_topk": (c_int, [c_int, c_int, _P, c_int, c_float, _P, _P, c_size_t, _P, _P]),
+    "mn_soft_topk_aux": (c_int, [c_int, c_int, c_int, c_int, _P, c_int64, c_int64, _P, _P, _P]),
+    "mn_soft_topk_aux_backward_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "mn_soft_topk_aux_backward": (c_int, [c_int, c_int, c_int, c_int, _P, c_int64, c_int64, _P, _P, _P, _P, _P,
+                                          c_size_t, _P]),
+    "mn_carrier_ste_backward": (c_int, [c_int, c_int, c_int, c_int, _P, c_int64, c_int64, _P, c_int64, c_int64, _P,
+                                        c_int, _P, _P, _P]),
     "mn_thre_topk_backward_workspace_bytes": (c_size_t, [c_int, c_int]),
     "mn_thre_topk_backward": (c_int, [c_int, c_int, _P, c_int, c_float, _P, _P, _P, c_size_t, _P, _P]),
     "mn_dtem_select_workspace_bytes": (c_size_t, [c_int, c_int]),

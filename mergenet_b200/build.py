@@ -23,7 +23,7 @@ INCLUDE = ROOT / "include"
 BUILD = ROOT / "_build"
 LIB = PKG / "libmergenet_b200.so"
 
-SOURCES = ["tables.cpp", "route.cu", "dropin.cu", "attention.cu", "attention_tc.cu", "attention_ws.cu", "norm.cu", "gemm_tc.cu"]
+SOURCES = ["tables.cpp", "route.cu", "dropin.cu", "attention.cu", "attention_tc.cu", "attention_ws.cu", "norm.cu", "gemm_tc.cu", "carrier_train.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
               "-Xptxas", "-warn-spills"]

@@ -525,6 +525,107 @@ def route_and_gather(x_embed, metrics, grid_size, radius=3.0, r_list=None):
     return plan(x_embed, metrics)
 
 
+# --------------------------------------------------------------------------
+# The carrier block's soft-top-k training terms (model.py:1163-1206)
+# --------------------------------------------------------------------------
+def carrier_ste(topk_x_trace, soft_sel, sorted_topk_indices):
+    """The straight-through carrier weights of model.py:1176-1179:
+    ``topk_x_trace * (1 + (w - w.detach()))[..., None]`` with
+    ``w = soft_sel.gather(1, sorted_topk_indices)``.  The value is
+    topk_x_trace; under autograd soft_sel receives, at each carrier's patch,
+    the dot product of the carrier's gradient and its features
+    (``mn_carrier_ste_backward``) and topk_x_trace the gradient unchanged."""
+    if _wants_grad(topk_x_trace, soft_sel):
+        return _CarrierSteFn.apply(topk_x_trace, soft_sel, sorted_topk_indices)
+    L.require_cuda(topk_x_trace, soft_sel, sorted_topk_indices)
+    return topk_x_trace
+
+
+class _CarrierSteFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, topk_x_trace, soft_sel, sorted_topk_indices):
+        L.require_cuda(topk_x_trace, soft_sel, sorted_topk_indices)
+        ctx.save_for_backward(topk_x_trace, sorted_topk_indices.long().contiguous())
+        ctx.sel_shape, ctx.sel_dtype = soft_sel.shape, soft_sel.dtype
+        return topk_x_trace.clone()
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        x, idx = ctx.saved_tensors
+        grad_sel = None
+        if ctx.needs_input_grad[1]:
+            g = grad_out.to(x.dtype)
+            if g.stride(-1) != 1:
+                g = g.contiguous()
+            xc = x if x.stride(-1) == 1 else x.contiguous()
+            bsz, k, c = xc.shape
+            n = ctx.sel_shape[1]
+            grad_sel = torch.empty(bsz, n, device=x.device, dtype=torch.float32)
+            status = _status(x.device)
+            L.check(L.lib().mn_carrier_ste_backward(bsz, k, c, L.dtype_code(xc.dtype), L.ptr(xc), xc.stride(0),
+                                                    xc.stride(1), L.ptr(g), g.stride(0), g.stride(1), L.ptr(idx), n,
+                                                    L.ptr(grad_sel), L.ptr(status), L.stream_of(xc)),
+                    "carrier_ste backward")
+            if int(status.item()):
+                raise ValueError("carrier_ste: carrier patch index out of range")
+            grad_sel = grad_sel.to(ctx.sel_dtype)
+        return grad_out, grad_sel, None
+
+
+def soft_topk_aux_repr(x_patches, soft_sel):
+    """The soft-top-k auxiliary representation of model.py:1196-1198:
+    ``(x_patches * (soft_sel / soft_sel.sum(1, keepdim=True).clamp(min=1e-6))
+    [..., None]).sum(1)`` -> float32 [B, C] (``mn_soft_topk_aux``; the
+    model's head GEMM on it stays the caller's).  x_patches [B, n, C] may be
+    a strided view such as ``x_local[:, 1:]`` (channels contiguous);
+    soft_sel [B, n].  Differentiable in both (``mn_soft_topk_aux_backward``)."""
+    if _wants_grad(x_patches, soft_sel):
+        return _SoftTopkAuxFn.apply(x_patches, soft_sel)
+    return _soft_topk_aux(x_patches, soft_sel.float().contiguous())
+
+
+def _aux_operands(x_patches):
+    if x_patches.dim() != 3:
+        raise ValueError("x_patches must be [B, n, C]")
+    return x_patches if x_patches.stride(-1) == 1 else x_patches.contiguous()
+
+
+def _soft_topk_aux(x_patches, sel32):
+    L.require_cuda(x_patches, sel32)
+    x = _aux_operands(x_patches)
+    bsz, n, c = x.shape
+    if sel32.shape != (bsz, n):
+        raise ValueError("soft_sel must be [B, n] for x_patches [B, n, C]")
+    aux = torch.empty(bsz, c, device=x.device, dtype=torch.float32)
+    L.check(L.lib().mn_soft_topk_aux(bsz, n, c, L.dtype_code(x.dtype), L.ptr(x), x.stride(0), x.stride(1),
+                                     L.ptr(sel32), L.ptr(aux), L.stream_of(x)), "soft_topk_aux_repr")
+    return aux
+
+
+class _SoftTopkAuxFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x_patches, soft_sel):
+        sel32 = soft_sel.float().contiguous()
+        ctx.save_for_backward(x_patches, sel32)
+        ctx.sel_dtype = soft_sel.dtype
+        return _soft_topk_aux(x_patches, sel32)
+
+    @staticmethod
+    def backward(ctx, grad_aux):
+        x_patches, sel32 = ctx.saved_tensors
+        x = _aux_operands(x_patches)
+        bsz, n, c = x.shape
+        g = grad_aux.float().contiguous()
+        grad_x = torch.empty(bsz, n, c, device=x.device, dtype=x.dtype)
+        grad_sel = torch.empty(bsz, n, device=x.device, dtype=torch.float32)
+        wsb = L.lib().mn_soft_topk_aux_backward_workspace_bytes(bsz, n)
+        ws = torch.empty(max(int(wsb), 16), dtype=torch.uint8, device=x.device)
+        L.check(L.lib().mn_soft_topk_aux_backward(bsz, n, c, L.dtype_code(x.dtype), L.ptr(x), x.stride(0), x.stride(1),
+                                                  L.ptr(sel32), L.ptr(g), L.ptr(grad_x), L.ptr(grad_sel), L.ptr(ws),
+                                                  wsb, L.stream_of(x)), "soft_topk_aux_repr backward")
+        return grad_x, grad_sel.to(ctx.sel_dtype)
+
+
 def carrier_scatter(topk_x, topk_idx, num_patches):
     """Transpose of the carrier gather: [B, k+1, C] -> [B, P, C], carrier i at
     patch topk_idx[b, i], zeros elsewhere."""
