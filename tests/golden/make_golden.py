@@ -344,6 +344,46 @@ def merge_train_backward_case():
     np.savez_compressed(HERE / "merge_train_backward.npz", **cases)
 
 
+def merge_train_chain_backward_case():
+    """The six training-mode merge layers chained as LocalEncoder.forward
+    chains them (model.py:574-590; merge_layer_index per layer, sizes and
+    token centres carried), then the carrier block's mass top-k and gather
+    (model.py:1157-1183), differentiated by the reference's autograd:
+    gradients of random upstream gradients on the final tokens, the final
+    masses and the gathered carriers with respect to the input tokens and
+    every layer's metric."""
+    rng = np.random.default_rng(20261205)
+    grid, radius, batch, channels, metric_dim = (8, 8), 3.0, 2, 16, 8
+    r_list = canonical_r_list(grid)
+    t = grid[0] * grid[1] + 1
+    x = rng.standard_normal((batch, t, channels), dtype=np.float32)
+    metrics = rng.standard_normal((len(r_list), batch, t, metric_dim), dtype=np.float32)
+    block = make_block(grid, radius, "sparse")
+    block.train()
+    block._tome_info.update({"train_grouping": "alternating_per_layer_fast", "train_grouping_seed": 0})
+    tx = torch.from_numpy(x).requires_grad_(True)
+    tm = torch.from_numpy(metrics).requires_grad_(True)
+    xs, size, n = tx, torch.ones(batch, t, 1), t
+    for i, r in enumerate(r_list):
+        block._tome_info["merge_layer_index"] = i
+        xs, size, n, _, _ = block._merge_train(xs, size, r, n, {"metric": tm[i]})
+    k = t - sum(r_list) - 1
+    strength = size[..., 0][:, 1:]
+    idx = torch.topk(strength.detach(), k, dim=1, largest=True, sorted=False).indices
+    order = torch.argsort(torch.gather(block._tome_info["token_center"][:, 1:], 1, idx), dim=1)
+    topk = torch.gather(idx, 1, order)
+    carriers = torch.gather(xs, 1, (topk + 1).unsqueeze(-1).expand(-1, -1, channels))
+    gx = rng.standard_normal(tuple(xs.shape), dtype=np.float32)
+    gs = rng.standard_normal(tuple(size.shape), dtype=np.float32)
+    gc = rng.standard_normal(tuple(carriers.shape), dtype=np.float32)
+    torch.autograd.backward([xs, size, carriers], [torch.from_numpy(gx), torch.from_numpy(gs), torch.from_numpy(gc)])
+    np.savez_compressed(HERE / "merge_train_chain_backward.npz", grid=np.array(grid), radius=radius,
+                        r_list=np.array(r_list), x=x, metrics=metrics, x_out=xs.detach().numpy(),
+                        size_out=size.detach().numpy(), topk_idx=topk.numpy(),
+                        center=block._tome_info["token_center"].numpy(), grad_x_out=gx, grad_size_out=gs,
+                        grad_carriers=gc, grad_x=tx.grad.numpy(), grad_metrics=tm.grad.numpy())
+
+
 def neighbor_dot_backward_case():
     """Gradients of the reference's sparse_neighbor_dot (the score of
     sparse_spatial_score too) through its own autograd Function
@@ -402,6 +442,7 @@ def main():
     select_case()
     select_backward_case()
     merge_train_backward_case()
+    merge_train_chain_backward_case()
     transport_case()
     route_case("route_g3x6", 101, 2, (3, 6), 2.0, 7, 5, [3, 3], capture=True)
     route_case("route_g4x4", 102, 3, (4, 4), 1.5, 16, 8, [2, 2, 2], capture=True)

@@ -188,3 +188,39 @@ def test_merge_block_training_random_groups(dev):
     for t in (x, size, metric):
         assert t.grad is not None and bool(torch.isfinite(t.grad).all())
     assert float(metric.grad.abs().sum()) > 0
+
+
+def test_merge_chain_training_gradients_match_reference(dev, golden_dir):
+    """Six training-mode merge layers chained as LocalEncoder.forward chains
+    them (model.py:574-590), then the carrier top-k and gather
+    (model.py:1157-1183), against the reference's own autograd of the same
+    chain: outputs, carriers, centres, and the gradients with respect to the
+    input tokens and all six metrics."""
+    import mergenet_b200 as mn
+    g = np.load(golden_dir / "merge_train_chain_backward.npz")
+    grid = tuple(int(v) for v in g["grid"])
+    r_list = [int(v) for v in g["r_list"]]
+    block = mn.make_merge_block(grid, float(g["radius"]), device=dev).train()
+    block._tome_info.update({"train_grouping": "alternating_per_layer_fast", "train_grouping_seed": 0})
+    x = torch.from_numpy(g["x"]).to(dev).requires_grad_(True)
+    metrics = torch.from_numpy(g["metrics"]).to(dev).requires_grad_(True)
+    bsz, t, c = x.shape
+    xs, size, n = x, torch.ones(bsz, t, 1, device=dev), t
+    for i, r in enumerate(r_list):
+        block._tome_info["merge_layer_index"] = i
+        xs, size, n, _, _ = block._merge_train(xs, size, r, n, {"metric": metrics[i]})
+    k = t - sum(r_list) - 1
+    idx = torch.topk(size[..., 0][:, 1:].detach(), k, dim=1, largest=True, sorted=False).indices
+    order = torch.argsort(torch.gather(block._tome_info["token_center"][:, 1:], 1, idx), dim=1)
+    topk = torch.gather(idx, 1, order)
+    np.testing.assert_array_equal(topk.cpu().numpy(), g["topk_idx"])
+    carriers = torch.gather(xs, 1, (topk + 1).unsqueeze(-1).expand(-1, -1, c))
+    np.testing.assert_allclose(xs.detach().cpu().numpy(), g["x_out"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(size.detach().cpu().numpy(), g["size_out"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(block._tome_info["token_center"].cpu().numpy(), g["center"], rtol=0, atol=2e-3)
+    torch.autograd.backward([xs, size, carriers], [torch.from_numpy(g[k_]).to(dev) for k_ in
+                                                   ("grad_x_out", "grad_size_out", "grad_carriers")])
+    for name, got in (("grad_x", x.grad), ("grad_metrics", metrics.grad)):
+        ref = g[name]
+        err = np.abs(got.cpu().numpy() - ref).max()
+        assert err <= 1e-3 * np.abs(ref).max(), (name, err)
