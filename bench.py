@@ -296,7 +296,42 @@ def measure_kernels(model, B, dev, stream, extra=True):
         q.transpose(1, 2), kv[:, :, 0].transpose(1, 2), kv[:, :, 1].transpose(1, 2)), stream) * 1e3
     out["reference_gpu_kernels"] = ref
     out["config5_highres_bf16"] = config5(dev, stream, peak)
+    try:
+        out["training_merge_layer"] = training_merge_layer(B, dev, stream)
+    except Exception as exc:  # noqa: BLE001 - report, do not fail the bench
+        out["training_merge_layer"] = f"unavailable: {type(exc).__name__}: {exc}"
     return out
+
+
+def training_merge_layer(B, dev, stream):
+    """One training-mode DTEM merge layer (DTEMMergeBlock._merge_train, the
+    reference's dtem.py:1687-2223 with autograd) forward and backward at the
+    model's shape: x fp32 [B, 785, 384], metric [B, 785, 64], r = 65, the
+    strided parity grouping.  The backward runs the library's transport
+    adjoint, select, ThreTopK and neighbour-dot gradients."""
+    import mergenet_b200
+    block = mergenet_b200.make_merge_block((28, 28), 3.0, device=dev).train()
+    block._tome_info.update({"train_grouping": "alternating_per_layer_fast", "merge_layer_index": 1})
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn(B, 785, 384, device=dev, generator=g).requires_grad_(True)
+    metric = torch.randn(B, 785, 64, device=dev, generator=g).requires_grad_(True)
+    size = torch.ones(B, 785, 1, device=dev)
+    gx = torch.randn(B, 785, 384, device=dev, generator=g)
+    gs = torch.randn(B, 785, 1, device=dev, generator=g)
+
+    def fwd():
+        block._tome_info["token_center"] = None
+        return block._merge_train(x, size, 65, 785, {"metric": metric})
+
+    def fwd_bwd():
+        xo, so, _, _, _ = fwd()
+        torch.autograd.backward([xo, so], [gx, gs])
+
+    with torch.no_grad():
+        t_eval = _time_kernel(fwd, stream)
+    t_train = _time_kernel(fwd_bwd, stream)
+    return {"workload": f"one merge layer, x [{B}, 785, 384] fp32, metric 64, r=65, train mode",
+            "ms_forward_no_grad": t_eval * 1e3, "ms_forward_backward": t_train * 1e3}
 
 
 def config5(dev, stream, peak, batch=64, steps=5):

@@ -104,66 +104,97 @@ __global__ void __launch_bounds__(512) transport_kernel(
     ET* __restrict__ out, int* status) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int* start = reinterpret_cast<int*>(smem_raw);  // [Nb + 1]
-  int* cursor = start + Nb + 1;                   // [Nb]
-  int* list = cursor + Nb;                        // [Na*K]
+  int* list = start + Nb + 1;                     // [Na*K]
+  int* wcount = list + Na * K;                    // [nw][Nb]: per-warp counts, then per-warp cursors
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int bb = blockIdx.x;
   const int c0 = blockIdx.y * CC;
   const int E = Na * K;
   const int64_t eb = (int64_t)bb * E;
-  for (int i = threadIdx.x; i < Nb + 1; i += blockDim.x) start[i] = 0;
-  __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+  // stable counting sort by receiver: warp w takes the contiguous edge
+  // segment [w * seg, (w + 1) * seg), counts its receivers, and after a
+  // prefix over (receiver, warp) places its edges in ascending edge order
+  const int seg = (E + nw - 1) / nw;
+  const int e_lo = min(E, warp * seg), e_hi = min(E, e_lo + seg);
+  int* mycount = wcount + warp * Nb;
+  for (int i = lane; i < Nb; i += 32) mycount[i] = 0;
+  __syncwarp();
+  auto key_of = [&](int e) -> int {
     const int64_t r = ridx[eb + e];
-    if (rvalid[eb + e] && r >= 0 && r < Nb) atomicAdd(&start[r + 1], 1);
-    else if (rvalid[eb + e] && status) atomicOr(status, MN_STATUS_TOO_MANY_EDGES);
+    return (rvalid[eb + e] && r >= 0 && r < Nb) ? (int)r : -1;
+  };
+  for (int base = e_lo; base < e_hi; base += 32) {
+    const int e = base + lane;
+    const int key = e < e_hi ? key_of(e) : -1;
+    if (e < e_hi && key < 0 && rvalid[eb + e] && status) atomicOr(status, MN_STATUS_TOO_MANY_EDGES);
+    const unsigned peers = __match_any_sync(MN_FULL_MASK, key);
+    if (key >= 0 && lane == __ffs(peers) - 1) mycount[key] += __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+  // start[r] = edges of receivers < r; each warp's cursor for r begins after
+  // the lower warps' edges into r
+  for (int r = threadIdx.x; r < Nb; r += blockDim.x) {
+    int tot = 0;
+    for (int ww = 0; ww < nw; ++ww) {
+      const int cnt = wcount[ww * Nb + r];
+      wcount[ww * Nb + r] = tot;
+      tot += cnt;
+    }
+    start[r + 1] = tot;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    start[0] = 0;
     for (int i = 0; i < Nb; ++i) start[i + 1] += start[i];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < Nb; i += blockDim.x) cursor[i] = start[i];
-  __syncthreads();
-  if (threadIdx.x < 32) {  // stable fill by one warp, 32 edges at a time
-    const int lane = threadIdx.x;
-    for (int base = 0; base < E; base += 32) {
-      const int e = base + lane;
-      int key = -1;
-      if (e < E) {
-        const int64_t r = ridx[eb + e];
-        if (rvalid[eb + e] && r >= 0 && r < Nb) key = (int)r;
-      }
-      const unsigned peers = __match_any_sync(MN_FULL_MASK, key);
-      const int rank = __popc(peers & ((1u << lane) - 1u));
-      int pos = 0;
-      if (key >= 0) pos = cursor[key] + rank;
-      __syncwarp();
-      if (key >= 0) {
-        list[pos] = e;
-        if (rank == 0) cursor[key] += __popc(peers);
-      }
-      __syncwarp();
-    }
+  for (int base = e_lo; base < e_hi; base += 32) {
+    const int e = base + lane;
+    const int key = e < e_hi ? key_of(e) : -1;
+    const unsigned peers = __match_any_sync(MN_FULL_MASK, key);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (key >= 0) list[start[key] + mycount[key] + rank] = e;
+    __syncwarp();
+    if (key >= 0 && lane == __ffs(peers) - 1) mycount[key] += __popc(peers);
+    __syncwarp();
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  // gather: a lane accumulates up to four channels (32 apart) of one
+  // receiver, each in ascending edge order (the reference's sequential
+  // scatter order: mul, then add, no fused multiply-add)
   const ET* wb = w + eb;
   const ET* vb = v + (int64_t)bb * Na * C;
+  const int c_end = min(C, c0 + CC);
   for (int r = warp; r < Nb; r += nw) {
-    for (int c = c0 + lane; c < min(C, c0 + CC); c += 32) {
-      float acc = 0.f;
-      for (int j = start[r]; j < start[r + 1]; ++j) {
+    const int j0 = start[r], j1 = start[r + 1];
+    for (int cb = c0; cb < c_end; cb += 128) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int j = j0; j < j1; ++j) {
         const int e = list[j];
-        const int d = e / K;
-        acc = __fadd_rn(acc, __fmul_rn(to_f32(wb[e]), to_f32(vb[(int64_t)d * C + c])));
+        const float we = to_f32(wb[e]);
+        const ET* vrow = vb + (int64_t)(e / K) * C;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = cb + q * 32 + lane;
+          if (c < c_end) acc[q] = __fadd_rn(acc[q], __fmul_rn(we, to_f32(vrow[c])));
+        }
       }
-      out[((int64_t)bb * Nb + r) * C + c] = from_f32<ET>(acc);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int c = cb + q * 32 + lane;
+        if (c < c_end) out[((int64_t)bb * Nb + r) * C + c] = from_f32<ET>(acc[q]);
+      }
     }
   }
 }
 
-// Adjoint of the transport (dtem.py:962-973): a gather per donor.
-template <typename ET>
+// Adjoint of the transport (dtem.py:962-973): a gather per donor, one warp
+// per donor row.  G > 0: the donor's value row and its gradient row live in
+// registers (G channel groups of 32 per lane, C <= 32 G), and every
+// receiver row is read once for both the assignment's gradient (a dot
+// product) and the values' gradient.  G == 0: any C, two passes.
+template <typename ET, int G>
 __global__ void __launch_bounds__(256) transport_adjoint_kernel(
     const ET* __restrict__ w, const ET* __restrict__ v, const int64_t* __restrict__ ridx,
     const uint8_t* __restrict__ rvalid, const ET* __restrict__ g, int B, int Na, int Nb, int K, int C,
@@ -173,26 +204,63 @@ __global__ void __launch_bounds__(256) transport_adjoint_kernel(
   if (row >= (int64_t)B * Na) return;
   const int bb = (int)(row / Na);
   const ET* vrow = v + row * C;
-  for (int k = 0; k < K; ++k) {
-    const int64_t o = row * K + k;
-    const int64_t s = ridx[o];
-    float acc = 0.f;
-    if (rvalid[o] && s >= 0 && s < Nb) {
-      const ET* grow = g + ((int64_t)bb * Nb + s) * C;
-      for (int c = lane; c < C; c += 32) acc = fmaf(to_f32(grow[c]), to_f32(vrow[c]), acc);
-      acc = warp_sum(acc);
+  if constexpr (G > 0) {
+    float vr[G], gv[G];
+#pragma unroll
+    for (int q = 0; q < G; ++q) {
+      const int c = q * 32 + lane;
+      vr[q] = c < C ? to_f32(vrow[c]) : 0.f;
+      gv[q] = 0.f;
     }
-    if (lane == 0) grad_w[o] = from_f32<ET>(acc);
-  }
-  for (int c = lane; c < C; c += 32) {
-    float acc = 0.f;
     for (int k = 0; k < K; ++k) {
       const int64_t o = row * K + k;
       const int64_t s = ridx[o];
-      if (rvalid[o] && s >= 0 && s < Nb)
-        acc = fmaf(to_f32(w[o]), to_f32(g[((int64_t)bb * Nb + s) * C + c]), acc);
+      float dot = 0.f;
+      if (rvalid[o] && s >= 0 && s < Nb) {
+        const ET* grow = g + ((int64_t)bb * Nb + s) * C;
+        const float wk = to_f32(w[o]);
+        float gr[G];
+#pragma unroll
+        for (int q = 0; q < G; ++q) {
+          const int c = q * 32 + lane;
+          gr[q] = c < C ? to_f32(grow[c]) : 0.f;
+        }
+#pragma unroll
+        for (int q = 0; q < G; ++q) {
+          dot = fmaf(gr[q], vr[q], dot);
+          gv[q] = fmaf(wk, gr[q], gv[q]);
+        }
+        dot = warp_sum(dot);
+      }
+      if (lane == 0) grad_w[o] = from_f32<ET>(dot);
     }
-    grad_v[row * C + c] = from_f32<ET>(acc);
+#pragma unroll
+    for (int q = 0; q < G; ++q) {
+      const int c = q * 32 + lane;
+      if (c < C) grad_v[row * C + c] = from_f32<ET>(gv[q]);
+    }
+  } else {
+    for (int k = 0; k < K; ++k) {
+      const int64_t o = row * K + k;
+      const int64_t s = ridx[o];
+      float acc = 0.f;
+      if (rvalid[o] && s >= 0 && s < Nb) {
+        const ET* grow = g + ((int64_t)bb * Nb + s) * C;
+        for (int c = lane; c < C; c += 32) acc = fmaf(to_f32(grow[c]), to_f32(vrow[c]), acc);
+        acc = warp_sum(acc);
+      }
+      if (lane == 0) grad_w[o] = from_f32<ET>(acc);
+    }
+    for (int c = lane; c < C; c += 32) {
+      float acc = 0.f;
+      for (int k = 0; k < K; ++k) {
+        const int64_t o = row * K + k;
+        const int64_t s = ridx[o];
+        if (rvalid[o] && s >= 0 && s < Nb)
+          acc = fmaf(to_f32(w[o]), to_f32(g[((int64_t)bb * Nb + s) * C + c]), acc);
+      }
+      grad_v[row * C + c] = from_f32<ET>(acc);
+    }
   }
 }
 
@@ -633,7 +701,8 @@ extern "C" int mn_sparse_weighted_transport(int batch, int num_donors, int num_r
     return launch_status();
   }
   if (!assignment || !values || !receiver_indices || !receiver_valid) return MN_ERR_ARG;
-  const size_t smem = ((size_t)2 * num_receivers + 1 + (size_t)num_donors * k) * sizeof(int);
+  // edge starts, the edge list and 16 warps' per-receiver counts
+  const size_t smem = ((size_t)num_receivers + 1 + (size_t)num_donors * k + (size_t)16 * num_receivers) * sizeof(int);
   if (smem > 200 * 1024) return MN_ERR_UNSUPPORTED;
   const int CC = 128;
   const dim3 grid(batch, (channels + CC - 1) / CC);
@@ -662,10 +731,20 @@ extern "C" int mn_sparse_transport_adjoint(int batch, int num_donors, int num_re
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc = dispatch_dtype(dtype, [&](auto tag) {
     using ET = decltype(tag);
-    transport_adjoint_kernel<ET><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
-        static_cast<const ET*>(assignment), static_cast<const ET*>(values), receiver_indices, receiver_valid,
-        static_cast<const ET*>(grad_out), batch, num_donors, num_receivers, k, channels,
-        static_cast<ET*>(grad_assignment), static_cast<ET*>(grad_values));
+    auto launch = [&](auto kern) {
+      kern<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+          static_cast<const ET*>(assignment), static_cast<const ET*>(values), receiver_indices, receiver_valid,
+          static_cast<const ET*>(grad_out), batch, num_donors, num_receivers, k, channels,
+          static_cast<ET*>(grad_assignment), static_cast<ET*>(grad_values));
+    };
+    const int groups = (channels + 31) / 32;
+    if (groups <= 1) launch(transport_adjoint_kernel<ET, 1>);
+    else if (groups <= 2) launch(transport_adjoint_kernel<ET, 2>);
+    else if (groups <= 4) launch(transport_adjoint_kernel<ET, 4>);
+    else if (groups <= 8) launch(transport_adjoint_kernel<ET, 8>);
+    else if (groups <= 12) launch(transport_adjoint_kernel<ET, 12>);
+    else if (groups <= 16) launch(transport_adjoint_kernel<ET, 16>);
+    else launch(transport_adjoint_kernel<ET, 0>);
   });
   return rc != MN_OK ? rc : launch_status();
 }
