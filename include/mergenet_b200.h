@@ -228,7 +228,8 @@ int mn_carrier_ste_backward(int batch, int k, int channels, int dtype,
 /* Soft-k-max block of DTEMBlock._select with the sparse spatial mask,
  * opentome/timm/dtem.py:1551-1580: scores f32 [B,Na,K] + allowed uint8 ->
  * assignment f32 [B,Na,K].  Returns MN_INFEASIBLE_BUDGET through the device
- * status when a batch row has fewer than k valid donor rows. */
+ * status when a batch row has fewer than k valid donor rows.  Limits:
+ * num_donors <= 4096, k_slots <= 160 (MN_ERR_UNSUPPORTED beyond). */
 size_t mn_dtem_select_workspace_bytes(int batch, int num_donors);
 int mn_dtem_select(int batch, int num_donors, int k_slots, const float* scores,
                    const uint8_t* allowed, int k, float tau1, float tau2,
@@ -254,7 +255,7 @@ int mn_dtem_select_backward(int batch, int num_donors, int k_slots,
  * counterpart in the reference: it exists for callers that cannot allocate
  * device memory (no allocator of their own, or no cudaMalloc allowed on
  * their path).  Same inputs, outputs and results as mn_dtem_select; its
- * scratch is a fixed array inside the library (about 1.3 MB per GPU, held
+ * scratch is a fixed array inside the library (about 1.5 MB per GPU, held
  * until exit).  Limits: batch * num_donors <= 262144, batch <= 65536,
  * num_donors <= 4096 (MN_ERR_UNSUPPORTED beyond).  Calls that overlap on one
  * GPU share the scratch and race; order them on a single stream.  The first

@@ -458,13 +458,14 @@ __global__ void __launch_bounds__(256) select_energy_kernel(const float* __restr
   }
 }
 
-__global__ void __launch_bounds__(512) select_rows_kernel(const float* __restrict__ scores,
-                                                          const uint8_t* __restrict__ allowed, int Na, int K,
-                                                          int k, float tau1, float tau2,
-                                                          const float* __restrict__ energy,
-                                                          const int* __restrict__ valid_count,
-                                                          const float* partials, int nparts,
-                                                          float* __restrict__ assign, int* status) {
+// The select's per-image threshold: one CTA per image computes lambda of
+// ThreTopK over the image's row energies (thetopk.py:4-43) and flags an
+// infeasible budget; select_rows_kernel then forms every donor row.
+__global__ void __launch_bounds__(512) select_lambda_kernel(int Na, int k, float tau2,
+                                                            const float* __restrict__ energy,
+                                                            const int* __restrict__ valid_count,
+                                                            const float* partials, int nparts,
+                                                            float* __restrict__ lam_out, int* status) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ float red[64];
   const int np = next_pow2(Na);
@@ -477,32 +478,63 @@ __global__ void __launch_bounds__(512) select_rows_kernel(const float* __restric
   for (int i = threadIdx.x; i < Na; i += blockDim.x) xrow[i] = e[i] / range * tau2;
   __syncthreads();
   const float lam = thre_topk_lambda(xrow, Na, np, k, rs);
-  for (int d = threadIdx.x; d < Na; d += blockDim.x) {
-    const int64_t row = (int64_t)bb * Na + d;
-    const float* s = scores + row * K;
-    const uint8_t* al = allowed + row * K;
-    float* out = assign + row * K;
+  if (threadIdx.x == 0) lam_out[bb] = lam;
+}
+
+// Every donor row of the select (dtem.py:1557-1579), one thread per row:
+// the masked softmax x the row's k-hot y = map(E / range * tau2, lambda),
+// then the clamp-normalise.  The CTA's 256 rows of scores and mask are
+// staged in shared memory with coalesced loads (a row is K values apart per
+// thread), and the assignment leaves the same way.
+__global__ void __launch_bounds__(256) select_rows_kernel(const float* __restrict__ scores,
+                                                          const uint8_t* __restrict__ allowed, int rows, int Na,
+                                                          int K, float tau1, float tau2,
+                                                          const float* __restrict__ energy,
+                                                          const float* partials, int nparts,
+                                                          const float* __restrict__ lam_in,
+                                                          float* __restrict__ assign) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red[64];
+  float* sbuf = reinterpret_cast<float*>(smem_raw);                        // [256 * K]
+  uint8_t* abuf = reinterpret_cast<uint8_t*>(sbuf + (size_t)blockDim.x * K);  // [256 * K]
+  const float range = reduce_range(partials, nparts, red, nullptr);
+  const int64_t row0 = (int64_t)blockIdx.x * blockDim.x;
+  const int nrows = (int)(rows - row0 < (int64_t)blockDim.x ? rows - row0 : (int64_t)blockDim.x);
+  const int64_t base = row0 * K;
+  for (int i = threadIdx.x; i < nrows * K; i += blockDim.x) {
+    sbuf[i] = scores[base + i];
+    abuf[i] = allowed[base + i];
+  }
+  __syncthreads();
+  const int r = threadIdx.x;
+  if (r < nrows) {
+    const int64_t row = row0 + r;
+    const float* s = sbuf + r * K;
+    const uint8_t* al = abuf + r * K;
+    float* out = sbuf + r * K;  // the row's assignment replaces its scores
     float m = -INFINITY;
     for (int c = 0; c < K; ++c)
       if (al[c]) m = fmaxf(m, s[c] / tau1);
     if (m == -INFINITY) {
       for (int c = 0; c < K; ++c) out[c] = 0.f;
-      continue;
+    } else {
+      const float y = thre_topk_map(energy[row] / range * tau2, lam_in[row / Na]);
+      float sum = 0.f;
+      for (int c = 0; c < K; ++c)
+        if (al[c]) sum += expf(s[c] / tau1 - m);
+      const float inv = 1.0f / sum;
+      float ks = 0.f;
+      for (int c = 0; c < K; ++c) {
+        const float kh = al[c] ? (expf(s[c] / tau1 - m) * inv) * y : 0.f;
+        out[c] = kh;
+        ks += kh;
+      }
+      const float tmp = fmaxf(ks - 1.0f, 0.0f) + 1.0f;
+      for (int c = 0; c < K; ++c) out[c] = out[c] / tmp;
     }
-    const float y = thre_topk_map(xrow[d], lam);
-    float sum = 0.f;
-    for (int c = 0; c < K; ++c)
-      if (al[c]) sum += expf(s[c] / tau1 - m);
-    const float inv = 1.0f / sum;
-    float ks = 0.f;
-    for (int c = 0; c < K; ++c) {
-      const float kh = al[c] ? (expf(s[c] / tau1 - m) * inv) * y : 0.f;
-      out[c] = kh;
-      ks += kh;
-    }
-    const float tmp = fmaxf(ks - 1.0f, 0.0f) + 1.0f;
-    for (int c = 0; c < K; ++c) out[c] = out[c] / tmp;
   }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nrows * K; i += blockDim.x) assign[base + i] = sbuf[i];
 }
 
 // Select backward, part 1 (one CTA per batch row): recompute lambda over
@@ -803,7 +835,18 @@ extern "C" size_t mn_dtem_select_workspace_bytes(int batch, int num_donors) {
   if (batch <= 0 || num_donors <= 0) return 0;
   const int64_t rows = (int64_t)batch * num_donors;
   return (size_t)rows * sizeof(float) + (size_t)batch * sizeof(int) +
-         (size_t)thre_topk_parts(rows) * 2 * sizeof(float) + 64;
+         (size_t)thre_topk_parts(rows) * 2 * sizeof(float) + (size_t)batch * sizeof(float) + 64;
+}
+
+// The select after the row energies and their min/max partials: lambda per
+// image, then every donor row.
+static void launch_select(int batch, int num_donors, int k_slots, const float* scores, const uint8_t* allowed, int k,
+                          float tau1, float tau2, const float* energy, const int* counts, const float* partials,
+                          int parts, float* lam, size_t smem, float* assignment, int* status, cudaStream_t st) {
+  const int64_t rows = (int64_t)batch * num_donors;
+  select_lambda_kernel<<<batch, 512, smem, st>>>(num_donors, k, tau2, energy, counts, partials, parts, lam, status);
+  select_rows_kernel<<<(unsigned)((rows + 255) / 256), 256, (size_t)256 * k_slots * 5, st>>>(
+      scores, allowed, (int)rows, num_donors, k_slots, tau1, tau2, energy, partials, parts, lam, assignment);
 }
 
 extern "C" int mn_dtem_select(int batch, int num_donors, int k_slots, const float* scores, const uint8_t* allowed,
@@ -820,15 +863,18 @@ extern "C" int mn_dtem_select(int batch, int num_donors, int k_slots, const floa
   int* counts = reinterpret_cast<int*>(energy + rows);
   float* partials = reinterpret_cast<float*>(counts + batch);
   const int parts = thre_topk_parts(rows);
+  float* lam = partials + 2 * parts;
   const int np = next_pow2(num_donors);
   const size_t smem = row_scratch_bytes(np) + (size_t)num_donors * sizeof(float);
-  if (!ensure_smem(select_rows_kernel, smem)) return MN_ERR_LAUNCH;
+  if (k_slots > 160) return MN_ERR_UNSUPPORTED;  // the row kernel stages 256 rows of K slots
+  if (!ensure_smem(select_lambda_kernel, smem) || !ensure_smem(select_rows_kernel, (size_t)256 * k_slots * 5))
+    return MN_ERR_LAUNCH;
   cudaMemsetAsync(counts, 0, (size_t)batch * sizeof(int), st);
   select_energy_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(scores, allowed, (int)rows, k_slots, tau1,
                                                                    energy, counts, num_donors);
   minmax_partials_kernel<<<parts, 256, 0, st>>>(energy, rows, partials);
-  select_rows_kernel<<<batch, 512, smem, st>>>(scores, allowed, num_donors, k_slots, k, tau1, tau2, energy, counts,
-                                               partials, parts, assignment, status);
+  launch_select(batch, num_donors, k_slots, scores, allowed, k, tau1, tau2, energy, counts, partials, parts, lam, smem,
+                assignment, status, st);
   return launch_status();
 }
 
@@ -900,13 +946,13 @@ extern "C" int mn_carrier_scatter(int batch, int k, int num_patches, int channel
 // synchronisation and unpredictable latency of an allocation, or a process
 // whose device memory is already carved up by another runtime).  This
 // variant keeps its scratch (row energies, per-batch valid-row counts,
-// energy min/max partials) in a fixed array compiled into the library, so
-// the caller passes only inputs and outputs.
+// energy min/max partials, per-image thresholds) in a fixed array compiled
+// into the library, so the caller passes only inputs and outputs.
 //
 // The array holds at most kNoAllocMaxRows donor rows (batch * num_donors)
 // and kNoAllocMaxBatch batch rows; larger calls are rejected with
 // MN_ERR_UNSUPPORTED before anything is launched.  Every GPU that loads the
-// library carries the array (about 1.3 MB) until the process exits.  All
+// library carries the array (about 1.5 MB) until the process exits.  All
 // calls on a device share it: calls whose kernels overlap on that device
 // (different streams without ordering) race and corrupt each other, so
 // order them on one stream.  The valid-row counters start from zero on every
@@ -926,7 +972,7 @@ constexpr int kNoAllocMaxBatch = 65536;
 constexpr int kNoAllocMaxParts = 1024;
 constexpr size_t kNoAllocScratchBytes =
     (size_t)kNoAllocMaxRows * sizeof(float) + (size_t)kNoAllocMaxBatch * sizeof(int) +
-    (size_t)kNoAllocMaxParts * 2 * sizeof(float);
+    (size_t)kNoAllocMaxParts * 2 * sizeof(float) + (size_t)kNoAllocMaxBatch * sizeof(float);
 static __device__ __align__(256) unsigned char g_select_scratch[kNoAllocScratchBytes];
 
 std::mutex g_scratch_mu;
@@ -990,14 +1036,17 @@ extern "C" int mn_dtem_select_noalloc(int batch, int num_donors, int k_slots, co
   float* energy = static_cast<float*>(scratch);
   int* counts = reinterpret_cast<int*>(energy + rows);
   float* partials = reinterpret_cast<float*>(counts + batch);
+  float* lam = partials + 2 * parts;
   const int np = next_pow2(num_donors);
   const size_t smem = row_scratch_bytes(np) + (size_t)num_donors * sizeof(float);
-  if (!ensure_smem(select_rows_kernel, smem)) return MN_ERR_LAUNCH;
+  if (k_slots > 160) return MN_ERR_UNSUPPORTED;  // the row kernel stages 256 rows of K slots
+  if (!ensure_smem(select_lambda_kernel, smem) || !ensure_smem(select_rows_kernel, (size_t)256 * k_slots * 5))
+    return MN_ERR_LAUNCH;
   cudaMemsetAsync(counts, 0, (size_t)batch * sizeof(int), st);
   select_energy_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(scores, allowed, (int)rows, k_slots, tau1,
                                                                    energy, counts, num_donors);
   minmax_partials_kernel<<<parts, 256, 0, st>>>(energy, rows, partials);
-  select_rows_kernel<<<batch, 512, smem, st>>>(scores, allowed, num_donors, k_slots, k, tau1, tau2, energy, counts,
-                                               partials, parts, assignment, status);
+  launch_select(batch, num_donors, k_slots, scores, allowed, k, tau1, tau2, energy, counts, partials, parts, lam, smem,
+                assignment, status, st);
   return launch_status();
 }
