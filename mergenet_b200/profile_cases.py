@@ -2,6 +2,7 @@
 
     python -m mergenet_b200.profile_cases attention [--batch 128] [--iters 2]
     python -m mergenet_b200.profile_cases routing   [--batch 128] [--iters 2]
+    python -m mergenet_b200.profile_cases training  [--batch 128] [--iters 2]
 
 Each case runs ``iters`` identical iterations on ``cuda:0`` with seeded
 synthetic inputs of the mergenet_small_cls shapes (224x224 images, patch 8:
@@ -16,6 +17,10 @@ a profiler can skip the first iteration's launches and capture the second's.
   [B, 785, 384] fp32 and metrics [6, B, 785, 64] fp16.
 * ``gemm``: the MLP GEMMs of one local block on B x 785 token rows: fc1 with
   the GELU epilogue (384 -> 1536), then fc2 (1536 -> 384).
+* ``training``: one training-mode merge layer (DTEMMergeBlock, x [B, 785,
+  384] fp32, metric 64, r = 65, the strided parity grouping) forward and
+  backward: the drop-in score, select and transport kernels and their
+  gradients.
 """
 from __future__ import annotations
 
@@ -71,13 +76,34 @@ def gemm(batch, iters):
     print("gemm status", gemm_status(dev))
 
 
+def training(batch, iters):
+    from .dtem import make_merge_block
+    from .routing import check_status  # noqa: F401  (the library must load)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    block = make_merge_block((28, 28), 3.0, device=dev).train()
+    block._tome_info.update({"train_grouping": "alternating_per_layer_fast", "merge_layer_index": 1})
+    x = torch.randn(batch, 785, 384, device=dev, generator=g).requires_grad_(True)
+    metric = torch.randn(batch, 785, 64, device=dev, generator=g).requires_grad_(True)
+    size = torch.ones(batch, 785, 1, device=dev)
+    gx = torch.randn(batch, 785, 384, device=dev, generator=g)
+    gs = torch.randn(batch, 785, 1, device=dev, generator=g)
+    for _ in range(iters):
+        block._tome_info["token_center"] = None
+        xo, so, _, _, _ = block._merge_train(x, size, 65, 785, {"metric": metric})
+        torch.autograd.backward([xo, so], [gx, gs])
+    torch.cuda.synchronize()
+    print("training grads finite", bool(torch.isfinite(x.grad).all() and torch.isfinite(metric.grad).all()))
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["attention", "routing", "gemm"])
+    ap.add_argument("case", choices=["attention", "routing", "gemm", "training"])
     ap.add_argument("--batch", type=int, default=128)
     ap.add_argument("--iters", type=int, default=2)
     args = ap.parse_args()
-    {"attention": attention, "routing": routing, "gemm": gemm}[args.case](args.batch, args.iters)
+    {"attention": attention, "routing": routing, "gemm": gemm, "training": training}[args.case](args.batch,
+                                                                                               args.iters)
 
 
 if __name__ == "__main__":
