@@ -160,24 +160,52 @@ __global__ void __launch_bounds__(512) transport_kernel(
     __syncwarp();
   }
   __syncthreads();
-  // gather: a lane accumulates up to four channels (32 apart) of one
-  // receiver, each in ascending edge order (the reference's sequential
-  // scatter order: mul, then add, no fused multiply-add)
+  // gather, every (receiver, channel) sum in ascending edge order (the
+  // reference's sequential scatter order: mul, then add, no fused
+  // multiply-add)
   const ET* wb = w + eb;
   const ET* vb = v + (int64_t)bb * Na * C;
   const int c_end = min(C, c0 + CC);
+  if (c_end - c0 <= 8) {
+    // few channels (the masses and centres): a thread per receiver
+    for (int r = threadIdx.x; r < Nb; r += blockDim.x) {
+      const int j0 = start[r], j1 = start[r + 1];
+      for (int c = c0; c < c_end; ++c) {
+        float acc = 0.f;
+        for (int j = j0; j < j1; ++j) {
+          const int e = list[j];
+          acc = __fadd_rn(acc, __fmul_rn(to_f32(wb[e]), to_f32(vb[(int64_t)(e / K) * C + c])));
+        }
+        out[((int64_t)bb * Nb + r) * C + c] = from_f32<ET>(acc);
+      }
+    }
+    return;
+  }
+  // a lane accumulates up to four channels (32 apart) of one receiver; the
+  // loads of four edges are in flight before their products are added
   for (int r = warp; r < Nb; r += nw) {
     const int j0 = start[r], j1 = start[r + 1];
     for (int cb = c0; cb < c_end; cb += 128) {
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int j = j0; j < j1; ++j) {
-        const int e = list[j];
-        const float we = to_f32(wb[e]);
-        const ET* vrow = vb + (int64_t)(e / K) * C;
+      for (int j = j0; j < j1; j += 4) {
+        float we[4], vv[4][4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int c = cb + q * 32 + lane;
-          if (c < c_end) acc[q] = __fadd_rn(acc[q], __fmul_rn(we, to_f32(vrow[c])));
+        for (int u = 0; u < 4; ++u) {
+          const bool has = j + u < j1;
+          const int e = list[has ? j + u : j0];
+          we[u] = has ? to_f32(wb[e]) : 0.f;
+          const ET* vrow = vb + (int64_t)(e / K) * C;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int c = cb + q * 32 + lane;
+            vv[u][q] = (has && c < c_end) ? to_f32(vrow[c]) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (j + u >= j1) break;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[q] = __fadd_rn(acc[q], __fmul_rn(we[u], vv[u][q]));
         }
       }
 #pragma unroll
