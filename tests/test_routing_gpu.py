@@ -434,3 +434,29 @@ def test_select_backward_against_oracle(dev, batch, na, k_slots, k):
     err = np.abs(got.cpu().numpy() - ref).max()
     assert err <= 1e-4 * np.abs(ref).max(), err
     assert int(torch.count_nonzero(got.cpu()[~allowed])) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_half_precision_gradients_follow_the_input_dtype(dev, dtype):
+    """Autocast-style 16-bit inputs: ThreTopK and the select compute in fp32
+    (as the reference's float32 energies and scores do) and hand back
+    gradients in the input's dtype, equal to the fp32 gradients rounded."""
+    import mergenet_b200 as mn
+    gen = torch.Generator().manual_seed(21)
+    x = (torch.randn(6, 392, generator=gen) * 2 + 4).to(dtype)
+    gy = torch.randn(6, 392, generator=gen)
+    xh = x.to(dev).requires_grad_(True)
+    mn.ThreTopK(xh, 196).backward(gy.to(dev).to(dtype))
+    want = mn.thre_topk_backward(x.float().to(dev), 196, gy.to(dtype).float().to(dev))
+    assert xh.grad.dtype == dtype
+    torch.testing.assert_close(xh.grad, want.to(dtype), rtol=0, atol=0)
+    scores = (torch.randn(2, 300, 13, generator=gen) * 0.3).to(dtype)
+    allowed = torch.rand(2, 300, 13, generator=gen) > 0.1
+    ga = torch.randn(2, 300, 13, generator=gen)
+    sh = scores.to(dev).requires_grad_(True)
+    assign = mn.dtem_select(100, sh, allowed.to(dev))
+    assert assign.dtype == dtype
+    assign.backward(ga.to(dev).to(dtype))
+    want = mn.dtem_select_backward(100, scores.float().to(dev), allowed.to(dev), ga.to(dtype).float().to(dev))
+    assert sh.grad.dtype == dtype
+    torch.testing.assert_close(sh.grad, want.to(dtype), rtol=0, atol=0)
