@@ -100,24 +100,27 @@ __global__ void __launch_bounds__(256) neighbor_dot_kernel(
 template <typename ET>
 __global__ void __launch_bounds__(512) transport_kernel(
     const ET* __restrict__ w, const ET* __restrict__ v, const int64_t* __restrict__ ridx,
-    const uint8_t* __restrict__ rvalid, int Na, int Nb, int K, int C, int CC,
+    const uint8_t* __restrict__ rvalid, int Na, int Nb, int K, int C, int CC, int sort_warps,
     ET* __restrict__ out, int* status) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int* start = reinterpret_cast<int*>(smem_raw);  // [Nb + 1]
   int* list = start + Nb + 1;                     // [Na*K]
-  int* wcount = list + Na * K;                    // [nw][Nb]: per-warp counts, then per-warp cursors
+  int* wcount = list + Na * K;                    // [sort_warps][Nb]: per-warp counts, then cursors
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int bb = blockIdx.x;
   const int c0 = blockIdx.y * CC;
   const int E = Na * K;
   const int64_t eb = (int64_t)bb * E;
-  // stable counting sort by receiver: warp w takes the contiguous edge
-  // segment [w * seg, (w + 1) * seg), counts its receivers, and after a
+  // stable counting sort by receiver: sort warp w (of sort_warps <= nw, as
+  // many as the shared memory holds count rows for) takes the contiguous
+  // edge segment [w * seg, (w + 1) * seg), counts its receivers, and after a
   // prefix over (receiver, warp) places its edges in ascending edge order
-  const int seg = (E + nw - 1) / nw;
-  const int e_lo = min(E, warp * seg), e_hi = min(E, e_lo + seg);
-  int* mycount = wcount + warp * Nb;
-  for (int i = lane; i < Nb; i += 32) mycount[i] = 0;
+  const int seg = (E + sort_warps - 1) / sort_warps;
+  const bool sorter = warp < sort_warps;
+  const int e_lo = sorter ? min(E, warp * seg) : E, e_hi = sorter ? min(E, e_lo + seg) : E;
+  int* mycount = wcount + (sorter ? warp : 0) * Nb;
+  if (sorter)
+    for (int i = lane; i < Nb; i += 32) mycount[i] = 0;
   __syncwarp();
   auto key_of = [&](int e) -> int {
     const int64_t r = ridx[eb + e];
@@ -136,7 +139,7 @@ __global__ void __launch_bounds__(512) transport_kernel(
   // the lower warps' edges into r
   for (int r = threadIdx.x; r < Nb; r += blockDim.x) {
     int tot = 0;
-    for (int ww = 0; ww < nw; ++ww) {
+    for (int ww = 0; ww < sort_warps; ++ww) {
       const int cnt = wcount[ww * Nb + r];
       wcount[ww * Nb + r] = tot;
       tot += cnt;
@@ -761,9 +764,12 @@ extern "C" int mn_sparse_weighted_transport(int batch, int num_donors, int num_r
     return launch_status();
   }
   if (!assignment || !values || !receiver_indices || !receiver_valid) return MN_ERR_ARG;
-  // edge starts, the edge list and 16 warps' per-receiver counts
-  const size_t smem = ((size_t)num_receivers + 1 + (size_t)num_donors * k + (size_t)16 * num_receivers) * sizeof(int);
-  if (smem > 200 * 1024) return MN_ERR_UNSUPPORTED;
+  // edge starts, the edge list and up to 16 sort warps' per-receiver counts
+  const size_t base_ints = (size_t)num_receivers + 1 + (size_t)num_donors * k;
+  const size_t cap_ints = 200 * 1024 / sizeof(int);
+  if (base_ints + num_receivers > cap_ints) return MN_ERR_UNSUPPORTED;
+  const int sort_warps = (int)std::min<size_t>(16, (cap_ints - base_ints) / num_receivers);
+  const size_t smem = (base_ints + (size_t)sort_warps * num_receivers) * sizeof(int);
   const int CC = 128;
   const dim3 grid(batch, (channels + CC - 1) / CC);
   int rc = dispatch_dtype(dtype, [&](auto tag) {
@@ -771,7 +777,7 @@ extern "C" int mn_sparse_weighted_transport(int batch, int num_donors, int num_r
     if (!ensure_smem(transport_kernel<ET>, smem)) return;  // reported by launch_status below
     transport_kernel<ET><<<grid, 512, smem, st>>>(static_cast<const ET*>(assignment), static_cast<const ET*>(values),
                                                   receiver_indices, receiver_valid, num_donors, num_receivers, k,
-                                                  channels, CC, static_cast<ET*>(out), status);
+                                                  channels, CC, sort_warps, static_cast<ET*>(out), status);
   });
   return rc != MN_OK ? rc : launch_status();
 }

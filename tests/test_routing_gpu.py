@@ -460,3 +460,22 @@ def test_half_precision_gradients_follow_the_input_dtype(dev, dtype):
     want = mn.dtem_select_backward(100, scores.float().to(dev), allowed.to(dev), ga.to(dtype).float().to(dev))
     assert sh.grad.dtype == dtype
     torch.testing.assert_close(sh.grad, want.to(dtype), rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("channels", [1, 8, 40, 384])
+def test_transport_at_the_48x48_grid_size(dev, channels):
+    """The drop-in transport at the 384x384 / patch-8 size (1,152 donors and
+    receivers, 29 slots): its edge list and sort counts fit the shared
+    memory, and every (receiver, channel) sum is the oracle's sequential
+    donor-major scatter, bit for bit, on the narrow (thread per receiver)
+    and wide (four channels per lane) paths."""
+    import mergenet_b200 as mn
+    gen = torch.Generator().manual_seed(48 + channels)
+    b, na, nb, k = 2, 1152, 1152, 29
+    w = torch.rand(b, na, k, generator=gen)
+    v = torch.randn(b, na, channels, generator=gen)
+    ridx = torch.randint(nb, (b, na, k), generator=gen)
+    rvalid = torch.rand(b, na, k, generator=gen) > 0.4
+    got = mn.sparse_weighted_transport(w.to(dev), v.to(dev), ridx.to(dev), rvalid.to(dev), nb)
+    want = O.sparse_weighted_transport(w.numpy(), v.numpy(), ridx.numpy(), rvalid.numpy(), nb)
+    np.testing.assert_array_equal(got.cpu().numpy(), want)
