@@ -13,7 +13,7 @@ import pytest
 import torch
 
 from conftest import carrier_mismatches, rel_err
-from inputs import routing_inputs
+from inputs import canonical_r_list, routing_inputs
 
 pytestmark = pytest.mark.gpu
 
@@ -224,3 +224,22 @@ def test_merge_chain_training_gradients_match_reference(dev, golden_dir):
         ref = g[name]
         err = np.abs(got.cpu().numpy() - ref).max()
         assert err <= 1e-3 * np.abs(ref).max(), (name, err)
+
+
+def test_merge_block_loop_at_the_48x48_grid(dev):
+    """The drop-in merge block driven through the six-layer loop at the
+    384x384 / patch-8 size (2,305 tokens, radius 3) gives the fused route's
+    carriers, masses and centres on the same inputs."""
+    import mergenet_b200 as mn
+    grid = (48, 48)
+    r_list = canonical_r_list(grid)
+    x, metrics = routing_inputs(17, 2, grid, 24, 64, layers=6, metric_dtype=np.float32)
+    xt, mt = torch.from_numpy(x).to(dev), torch.from_numpy(metrics).to(dev)
+    block = mn.make_merge_block(grid, 3.0, device=dev)
+    _, size, center, topk, topk_x = run_reference_loop(block, xt, mt, r_list)
+    res = mn.RoutePlan(grid, 3.0, r_list, device=dev)(xt, mt)
+    mism = carrier_mismatches(topk.cpu().numpy(), res.topk_idx.cpu().numpy(), res.center.cpu().numpy())
+    assert not mism, mism
+    np.testing.assert_allclose(size.cpu().numpy(), res.size.cpu().numpy(), rtol=3e-5, atol=3e-5)
+    np.testing.assert_allclose(center.cpu().numpy(), res.center.cpu().numpy(), rtol=0, atol=2e-3)
+    assert rel_err(topk_x.cpu().numpy(), res.topk_x.cpu().numpy()) <= 2e-3
