@@ -42,7 +42,7 @@ IMG = 224
 # of a B=128 launch) of the windowed attention kernel with its CLS row and of
 # the latent attention kernel, per image; the traffic grows in proportion to
 # the batch
-TRAFFIC_LOCAL_ATTN = 317.5e6 / 128  # ncu DRAM read + write per image, B=128 one-kernel capture (TMA-stored O)
+TRAFFIC_LOCAL_ATTN = 317.5e6 / 128
 TRAFFIC_LATENT_ATTN = 156.8e6 / 128
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 
