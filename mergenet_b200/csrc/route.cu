@@ -765,10 +765,27 @@ __global__ void __launch_bounds__(256) route_transport_kernel(
 // The next row's coefficient lines are prefetched into L1 one row ahead.
 // ---------------------------------------------------------------------------
 constexpr int kPairThreads = 256;
-constexpr int kPairSplits = 4;
+#ifndef MN_ROUTE_SPLITS
+#define MN_ROUTE_SPLITS 10
+#endif
+#ifndef MN_ROUTE_NARROW_THREADS
+#define MN_ROUTE_NARROW_THREADS 512
+#endif
+constexpr int kPairSplits = MN_ROUTE_SPLITS;
+// Launch bound of the stencil: 32-channel tiles run two CTAs per SM; a
+// narrower tile (grids whose token tile does not fit twice, e.g. 48 x 48)
+// runs one CTA per SM with up to 512 threads, its rows split ten ways
+// (48 x 48, B=64: 819 us for the routing call against 952 us with 256
+// threads and four splits; 768 or 1024 threads were slower)
+template <int CT>
+struct StencilBound {
+  static constexpr int kThreads = CT == 32 ? kPairThreads : MN_ROUTE_NARROW_THREADS;
+  static constexpr int kBlocks = CT == 32 ? 2 : 1;
+};
 
 template <typename XT, int CT, int DY1, int DY3>
-__global__ void __launch_bounds__(kPairThreads, 2) route_transport_stencil_kernel(
+__global__ void __launch_bounds__(StencilBound<CT>::kThreads, StencilBound<CT>::kBlocks)
+    route_transport_stencil_kernel(
     const XT* __restrict__ x, int B, int T, int C, int grid_h, int grid_w, int half, int L, int k,
     int row_splits, RouteWs ws, XT* __restrict__ topk_x) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -966,7 +983,7 @@ static bool launch_stencil_ct(const void* x, int B, int T, int C, const mn_route
                               const RouteWs& ws, void* topk_x, cudaStream_t st) {
   const int half_w = d->grid_w / 2;
   const int per_split = (CT / 4) * ((half_w + 1) / 2);  // threads per row split
-  int splits = std::max(1, std::min(d->grid_h, kPairThreads / per_split));  // <= the kernel's launch bound
+  int splits = std::max(1, std::min(d->grid_h, StencilBound<CT>::kThreads / per_split));  // <= the launch bound
   splits = std::min(splits, kPairSplits);
   const int threads = ((per_split * splits + 31) / 32) * 32;
   const size_t smem = (size_t)(T + 1) * CT * sizeof(float);  // tile + zero row
@@ -978,19 +995,23 @@ static bool launch_stencil_ct(const void* x, int B, int T, int C, const mn_route
   return true;
 }
 
+#ifndef MN_ROUTE_NARROW_CT
+#define MN_ROUTE_NARROW_CT 16  // 8-channel tiles measured slower (1013 against 952 us at 48 x 48)
+#endif
 template <typename XT>
 static bool launch_stencil(int variant, const void* x, int B, int T, int C, const mn_route_dims* d, int L, int k,
                            const RouteWs& ws, void* topk_x, cudaStream_t st) {
   const bool wide = (size_t)T * 32 * sizeof(float) <= 200 * 1024;
+  constexpr int NCT = MN_ROUTE_NARROW_CT;
   if (variant == 1) {
     if (wide) return launch_stencil_ct<XT, 32, 2, 0>(x, B, T, C, d, L, k, ws, topk_x, st);
-    else return launch_stencil_ct<XT, 16, 2, 0>(x, B, T, C, d, L, k, ws, topk_x, st);
+    else return launch_stencil_ct<XT, NCT, 2, 0>(x, B, T, C, d, L, k, ws, topk_x, st);
   } else if (variant == 2) {
     if (wide) return launch_stencil_ct<XT, 32, 1, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
-    else return launch_stencil_ct<XT, 16, 1, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
+    else return launch_stencil_ct<XT, NCT, 1, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
   } else {
     if (wide) return launch_stencil_ct<XT, 32, 0, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
-    else return launch_stencil_ct<XT, 16, 0, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
+    else return launch_stencil_ct<XT, NCT, 0, -1>(x, B, T, C, d, L, k, ws, topk_x, st);
   }
 }
 
