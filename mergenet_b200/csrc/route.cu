@@ -777,10 +777,16 @@ constexpr int kPairSplits = MN_ROUTE_SPLITS;
 // runs one CTA per SM with up to 512 threads, its rows split ten ways
 // (48 x 48, B=64: 819 us for the routing call against 952 us with 256
 // threads and four splits; 768 or 1024 threads were slower)
+#ifndef MN_ROUTE_WIDE_THREADS
+#define MN_ROUTE_WIDE_THREADS 256  // one CTA per SM with 448 or 512 threads: 847-852 against 745 us at 28 x 28
+#endif
+#ifndef MN_ROUTE_WIDE_BLOCKS
+#define MN_ROUTE_WIDE_BLOCKS 2
+#endif
 template <int CT>
 struct StencilBound {
-  static constexpr int kThreads = CT == 32 ? kPairThreads : MN_ROUTE_NARROW_THREADS;
-  static constexpr int kBlocks = CT == 32 ? 2 : 1;
+  static constexpr int kThreads = CT == 32 ? MN_ROUTE_WIDE_THREADS : MN_ROUTE_NARROW_THREADS;
+  static constexpr int kBlocks = CT == 32 ? MN_ROUTE_WIDE_BLOCKS : 1;
 };
 
 template <typename XT, int CT, int DY1, int DY3>
