@@ -137,6 +137,29 @@ def test_cpu_tensors_are_rejected():
         mn.unbiased_local_attention(torch.rand(1, 5, 2, 64), torch.rand(1, 5, 2, 64), torch.rand(1, 5, 2, 64), 1)
 
 
+def test_training_functions_refuse_host_tensors():
+    """The gradient entry points and the carrier block's training terms have
+    no CPU path either: host tensors, with or without autograd, raise before
+    any kernel is launched."""
+    import mergenet_b200 as mn
+    x = torch.rand(2, 8)
+    with pytest.raises(RuntimeError):
+        mn.thre_topk_backward(x, 3, torch.rand(2, 8))
+    with pytest.raises(RuntimeError):
+        mn.ThreTopK(x.clone().requires_grad_(True), 3)
+    scores, allowed = torch.rand(1, 4, 3), torch.ones(1, 4, 3, dtype=torch.bool)
+    with pytest.raises(RuntimeError):
+        mn.dtem_select_backward(2, scores, allowed, torch.rand(1, 4, 3))
+    with pytest.raises(RuntimeError):
+        mn.dtem_select(2, scores.clone().requires_grad_(True), allowed)
+    with pytest.raises(RuntimeError):
+        mn.soft_topk_aux_repr(torch.rand(2, 8, 4), x)
+    with pytest.raises(RuntimeError):
+        mn.carrier_ste(torch.rand(2, 3, 4), x, torch.zeros(2, 3, dtype=torch.long))
+    with pytest.raises(RuntimeError):
+        mn.carrier_ste(torch.rand(2, 3, 4), x.clone().requires_grad_(True), torch.zeros(2, 3, dtype=torch.long))
+
+
 def test_attention_argument_checks_precede_any_launch():
     """A per-key bias that is not (B, N) and a packed width that is not
     3 x heads x head_dim are refused before the device is touched, so the
