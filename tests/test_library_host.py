@@ -255,3 +255,29 @@ def test_factory_accepts_the_reference_kwargs_and_refuses_other_paths():
         mergenet_small_cls(dtem_window_size=8)
     with pytest.raises(TypeError):
         mergenet_small_cls(not_an_argument=1)
+
+
+def test_merge_block_groupings_follow_the_mode():
+    """DTEMMergeBlock picks its donor / receiver split as dtem.py:1755-1812
+    does: eval mode from eval_grouping / eval_grouping_seed, training mode
+    from train_grouping / train_grouping_seed (the strided split only for
+    alternating_per_layer_fast with an even token count), and the default
+    training grouping draws a fresh permutation per image."""
+    import mergenet_b200 as mn
+    block = mn.DTEMMergeBlock({"eval_grouping": "seeded", "eval_grouping_seed": 3, "train_grouping": "seeded",
+                               "train_grouping_seed": 9, "merge_layer_index": 2})
+    a_e, b_e, strided = block.eval()._groups(10, 2, "cpu")
+    want_a, want_b = mn.build_eval_group_indices(10, 2, "cpu", "seeded", seed=3, layer_index=2)
+    assert not strided and torch.equal(a_e, want_a) and torch.equal(b_e, want_b)
+    a_t, b_t, strided = block.train()._groups(10, 2, "cpu")
+    want_a, want_b = mn.build_eval_group_indices(10, 2, "cpu", "seeded", seed=9, layer_index=2)
+    assert not strided and torch.equal(a_t, want_a) and torch.equal(b_t, want_b)
+    block._tome_info["train_grouping"] = "alternating_per_layer_fast"
+    assert block._groups(10, 2, "cpu")[2] and not block._groups(9, 2, "cpu")[2]
+    block._tome_info["train_grouping"] = "random_per_sample"
+    torch.manual_seed(0)
+    a_r, b_r, strided = block._groups(10, 3, "cpu")
+    assert not strided and a_r.shape == (3, 5) and b_r.shape == (3, 5)
+    for i in range(3):  # each image's halves partition the tokens
+        assert sorted(torch.cat([a_r[i], b_r[i]]).tolist()) == list(range(10))
+    assert any(not torch.equal(a_r[0], a_r[i]) for i in (1, 2))
