@@ -267,7 +267,8 @@ int mn_dtem_select_noalloc(int batch, int num_donors, int k_slots,
                            int* status, void* stream);
 
 /* Transpose of the carrier gather: out [B,P,C] (dtype) gets carrier row i+1
- * of topk_x [B,k+1,C] at patch topk_idx[b,i]; other rows are zero. */
+ * of topk_x [B,k+1,C] at patch topk_idx[b,i]; other rows are zero (a patch
+ * listed twice gets the later carrier; B <= 65535). */
 int mn_carrier_scatter(int batch, int k, int num_patches, int channels,
                        int dtype, const void* topk_x, const int64_t* topk_idx,
                        void* out, void* stream);

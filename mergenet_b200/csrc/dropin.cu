@@ -679,17 +679,48 @@ __global__ void __launch_bounds__(256) select_grad_out_kernel(const float* __res
   }
 }
 
+// Transpose of the carrier gather, one pass over the output: a CTA owns
+// kScatterRows patch rows of one image, maps each to its carrier through an
+// inverse table of the image's carrier indices (built in shared memory; if a
+// patch is listed twice the later carrier wins) and writes every row once,
+// the carrier's features or zeros, with 16-byte stores when the rows allow.
+constexpr int kScatterRows = 64;
+
 template <typename ET>
 __global__ void __launch_bounds__(256) carrier_scatter_kernel(const ET* __restrict__ topk_x,
                                                               const int64_t* __restrict__ idx, int k, int P,
                                                               int C, ET* __restrict__ out) {
-  const int64_t row = blockIdx.x;  // b * k + i
-  const int bb = (int)(row / k), i = (int)(row % k);
-  const int64_t p = idx[row];
-  if (p < 0 || p >= P) return;
-  const ET* src = topk_x + ((int64_t)bb * (k + 1) + 1 + i) * C;
-  ET* dst = out + ((int64_t)bb * P + p) * C;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) dst[c] = src[c];
+  __shared__ int inv[kScatterRows];
+  const int bb = blockIdx.y;
+  const int p0 = blockIdx.x * kScatterRows;
+  const int nrows = min(kScatterRows, P - p0);
+  for (int r = threadIdx.x; r < nrows; r += blockDim.x) inv[r] = -1;
+  __syncthreads();
+  const int64_t* ib = idx + (int64_t)bb * k;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const int64_t p = ib[i];
+    if (p >= p0 && p < p0 + nrows) atomicMax(&inv[p - p0], i);
+  }
+  __syncthreads();
+  const ET* src_b = topk_x + ((int64_t)bb * (k + 1) + 1) * C;
+  ET* dst_b = out + ((int64_t)bb * P + p0) * C;
+  const bool vec = (C * (int)sizeof(ET)) % 16 == 0 && (reinterpret_cast<uintptr_t>(topk_x) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  if (vec) {
+    const int vpr = C * (int)sizeof(ET) / 16;  // 16-byte vectors per row
+    for (int e = threadIdx.x; e < nrows * vpr; e += blockDim.x) {
+      const int r = e / vpr, v = e % vpr;
+      const int i = inv[r];
+      const uint4 val = i >= 0 ? reinterpret_cast<const uint4*>(src_b + (int64_t)i * C)[v] : make_uint4(0, 0, 0, 0);
+      reinterpret_cast<uint4*>(dst_b + (int64_t)r * C)[v] = val;
+    }
+  } else {
+    for (int e = threadIdx.x; e < nrows * C; e += blockDim.x) {
+      const int r = e / C, c = e % C;
+      const int i = inv[r];
+      dst_b[(int64_t)r * C + c] = i >= 0 ? src_b[(int64_t)i * C + c] : from_f32<ET>(0.f);
+    }
+  }
 }
 
 template <typename F>
@@ -960,13 +991,18 @@ extern "C" int mn_carrier_scatter(int batch, int k, int num_patches, int channel
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t elem = dtype == MN_F32 ? 4 : 2;
   cudaGetLastError();
-  cudaMemsetAsync(out, 0, (size_t)batch * num_patches * channels * elem, st);
-  if ((int64_t)batch * k == 0) return launch_status();
+  if (batch == 0) return launch_status();
+  if (k == 0) {
+    cudaMemsetAsync(out, 0, (size_t)batch * num_patches * channels * elem, st);
+    return launch_status();
+  }
   if (!topk_x || !topk_idx) return MN_ERR_ARG;
+  if (batch > 65535) return MN_ERR_UNSUPPORTED;
+  const dim3 grid((unsigned)((num_patches + kScatterRows - 1) / kScatterRows), (unsigned)batch);
   int rc = dispatch_dtype(dtype, [&](auto tag) {
     using ET = decltype(tag);
-    carrier_scatter_kernel<ET><<<(unsigned)((int64_t)batch * k), 128, 0, st>>>(
-        static_cast<const ET*>(topk_x), topk_idx, k, num_patches, channels, static_cast<ET*>(out));
+    carrier_scatter_kernel<ET><<<grid, 256, 0, st>>>(static_cast<const ET*>(topk_x), topk_idx, k, num_patches,
+                                                     channels, static_cast<ET*>(out));
   });
   return rc != MN_OK ? rc : launch_status();
 }

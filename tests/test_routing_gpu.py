@@ -342,6 +342,26 @@ def test_carrier_scatter_is_gather_transpose(dev):
     assert int(torch.count_nonzero(full[mask])) == 0
 
 
+@pytest.mark.parametrize("dtype,channels", [(torch.float16, 384), (torch.float32, 13), (torch.bfloat16, 8)])
+def test_carrier_scatter_one_pass(dev, dtype, channels):
+    """The scatter writes every patch row once: the carrier's features at its
+    patch, zeros elsewhere (config-2 shapes: 392 of 784 patches), on the
+    16-byte path and the element path; a patch listed twice takes the later
+    carrier."""
+    import mergenet_b200 as mn
+    gen = torch.Generator().manual_seed(channels)
+    b, p, k = 4, 784, 392
+    idx = torch.stack([torch.randperm(p, generator=gen)[:k] for _ in range(b)])
+    idx[3, 10] = idx[3, 3]  # patch listed twice: carrier 10 wins over carrier 3
+    topk_x = torch.randn(b, k + 1, channels, generator=gen).to(dtype)
+    want = torch.zeros(b, p, channels, dtype=dtype)
+    for i in range(b):
+        for j in range(k):
+            want[i, idx[i, j]] = topk_x[i, 1 + j]
+    got = mn.carrier_scatter(topk_x.to(dev), idx.to(dev), p)
+    assert torch.equal(got.cpu(), want)
+
+
 def test_empty_batches(dev):
     import mergenet_b200 as mn
     nbr, val = mn.build_patch_spatial_neighbors((3, 5), 2, device=dev)
