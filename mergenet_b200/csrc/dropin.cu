@@ -17,7 +17,10 @@ namespace mn {
 // binary search in the sorted receiver list (static-invalid slots map to 0),
 // then the warp computes each valid slot's fp32 dot product.
 // --------------------------------------------------------------------------
-template <typename ET>
+// QUAD: rows of whole 64-byte groups, 16-byte aligned: four lanes share a
+// slot's dot product (lane q takes the row's 16-byte vectors q, q + 4, ...)
+// and a warp scores eight slots at a time.
+template <typename ET, bool QUAD>
 __global__ void __launch_bounds__(256) sparse_score_kernel(
     const ET* __restrict__ a, const ET* __restrict__ b, const int64_t* __restrict__ nbr,
     const uint8_t* __restrict__ nbr_valid, const int64_t* __restrict__ donor_patch,
@@ -48,20 +51,52 @@ __global__ void __launch_bounds__(256) sparse_score_kernel(
       }
     }
     const int kmax = min(32, K - k0);
-    for (int j = 0; j < kmax; ++j) {
-      const int64_t s = __shfl_sync(MN_FULL_MASK, slot, j);
-      const bool v = __shfl_sync(MN_FULL_MASK, ok, j);
-      float acc = 0.f;
-      if (v) {
-        const ET* brow = b + ((int64_t)bb * Nb + s) * C;
-        for (int c = lane; c < C; c += 32) acc = fmaf(to_f32(arow[c]), to_f32(brow[c]), acc);
-        acc = warp_sum(acc);
+    if constexpr (QUAD) {
+      constexpr int E = 16 / sizeof(ET);  // elements per 16-byte vector
+      const int vpr = C / E;              // vectors per row, a multiple of 4
+      const int q = lane & 3;
+      for (int g = 0; g < kmax; g += 8) {
+        const int j = g + (lane >> 2);
+        const int jj = min(j, kmax - 1);
+        const int64_t s = __shfl_sync(MN_FULL_MASK, slot, jj);
+        const bool v = __shfl_sync(MN_FULL_MASK, ok, jj) && j < kmax;
+        float acc = 0.f;
+        if (v) {
+          const uint4* av = reinterpret_cast<const uint4*>(arow);
+          const uint4* bv = reinterpret_cast<const uint4*>(b + ((int64_t)bb * Nb + s) * C);
+          for (int t = q; t < vpr; t += 4) {
+            const uint4 ua = av[t], ub = bv[t];
+            const ET* ea = reinterpret_cast<const ET*>(&ua);
+            const ET* eb = reinterpret_cast<const ET*>(&ub);
+#pragma unroll
+            for (int e = 0; e < E; ++e) acc = fmaf(to_f32(ea[e]), to_f32(eb[e]), acc);
+          }
+        }
+        acc += __shfl_xor_sync(MN_FULL_MASK, acc, 1);
+        acc += __shfl_xor_sync(MN_FULL_MASK, acc, 2);
+        if (q == 0 && j < kmax) {
+          const int64_t o = row * K + k0 + j;
+          scores[o] = from_f32<ET>(acc);
+          ridx_out[o] = s;
+          rvalid_out[o] = v ? 1 : 0;
+        }
       }
-      if (lane == 0) {
-        const int64_t o = row * K + k0 + j;
-        scores[o] = from_f32<ET>(acc);
-        ridx_out[o] = s;
-        rvalid_out[o] = v ? 1 : 0;
+    } else {
+      for (int j = 0; j < kmax; ++j) {
+        const int64_t s = __shfl_sync(MN_FULL_MASK, slot, j);
+        const bool v = __shfl_sync(MN_FULL_MASK, ok, j);
+        float acc = 0.f;
+        if (v) {
+          const ET* brow = b + ((int64_t)bb * Nb + s) * C;
+          for (int c = lane; c < C; c += 32) acc = fmaf(to_f32(arow[c]), to_f32(brow[c]), acc);
+          acc = warp_sum(acc);
+        }
+        if (lane == 0) {
+          const int64_t o = row * K + k0 + j;
+          scores[o] = from_f32<ET>(acc);
+          ridx_out[o] = s;
+          rvalid_out[o] = v ? 1 : 0;
+        }
       }
     }
   }
@@ -754,10 +789,12 @@ extern "C" int mn_sparse_spatial_score(int batch, int num_donors, int num_receiv
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc = dispatch_dtype(dtype, [&](auto tag) {
     using ET = decltype(tag);
-    sparse_score_kernel<ET><<<grid, 256, 0, st>>>(
-        static_cast<const ET*>(a), static_cast<const ET*>(b), neighbor_indices, neighbor_valid, donor_patch,
-        receiver_patch, batch, num_donors, num_receivers, num_patches, k, channels, static_cast<ET*>(scores),
-        receiver_indices, receiver_valid);
+    const bool quad = (channels * (int)sizeof(ET)) % 64 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(b) & 15) == 0;
+    auto kern = quad ? sparse_score_kernel<ET, true> : sparse_score_kernel<ET, false>;
+    kern<<<grid, 256, 0, st>>>(static_cast<const ET*>(a), static_cast<const ET*>(b), neighbor_indices, neighbor_valid,
+                               donor_patch, receiver_patch, batch, num_donors, num_receivers, num_patches, k, channels,
+                               static_cast<ET*>(scores), receiver_indices, receiver_valid);
   });
   return rc != MN_OK ? rc : launch_status();
 }
