@@ -103,7 +103,8 @@ __global__ void __launch_bounds__(256) sparse_score_kernel(
 }
 
 // sparse_neighbor_dot (dtem.py:286-315): same dot with precomputed slots.
-template <typename ET>
+// QUAD as in sparse_score_kernel: four lanes per slot, eight slots a pass.
+template <typename ET, bool QUAD>
 __global__ void __launch_bounds__(256) neighbor_dot_kernel(
     const ET* __restrict__ a, const ET* __restrict__ b, const int64_t* __restrict__ ridx,
     const uint8_t* __restrict__ rvalid, int B, int Na, int Nb, int K, int C, ET* __restrict__ scores) {
@@ -112,17 +113,44 @@ __global__ void __launch_bounds__(256) neighbor_dot_kernel(
   if (row >= (int64_t)B * Na) return;
   const int bb = (int)(row / Na);
   const ET* arow = a + row * C;
-  for (int k = 0; k < K; ++k) {
-    const int64_t o = row * K + k;
-    const bool v = rvalid[o] != 0;
-    const int64_t s = ridx[o];
-    float acc = 0.f;
-    if (v && s >= 0 && s < Nb) {
-      const ET* brow = b + ((int64_t)bb * Nb + s) * C;
-      for (int c = lane; c < C; c += 32) acc = fmaf(to_f32(arow[c]), to_f32(brow[c]), acc);
-      acc = warp_sum(acc);
+  if constexpr (QUAD) {
+    constexpr int E = 16 / sizeof(ET);
+    const int vpr = C / E;
+    const int q = lane & 3;
+    for (int g = 0; g < K; g += 8) {
+      const int k = g + (lane >> 2);
+      const int64_t o = row * K + min(k, K - 1);
+      const int64_t s = ridx[o];
+      const bool v = k < K && rvalid[o] != 0 && s >= 0 && s < Nb;
+      float acc = 0.f;
+      if (v) {
+        const uint4* av = reinterpret_cast<const uint4*>(arow);
+        const uint4* bv = reinterpret_cast<const uint4*>(b + ((int64_t)bb * Nb + s) * C);
+        for (int t = q; t < vpr; t += 4) {
+          const uint4 ua = av[t], ub = bv[t];
+          const ET* ea = reinterpret_cast<const ET*>(&ua);
+          const ET* eb = reinterpret_cast<const ET*>(&ub);
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc = fmaf(to_f32(ea[e]), to_f32(eb[e]), acc);
+        }
+      }
+      acc += __shfl_xor_sync(MN_FULL_MASK, acc, 1);
+      acc += __shfl_xor_sync(MN_FULL_MASK, acc, 2);
+      if (q == 0 && k < K) scores[row * K + k] = from_f32<ET>(acc);
     }
-    if (lane == 0) scores[o] = from_f32<ET>(acc);
+  } else {
+    for (int k = 0; k < K; ++k) {
+      const int64_t o = row * K + k;
+      const bool v = rvalid[o] != 0;
+      const int64_t s = ridx[o];
+      float acc = 0.f;
+      if (v && s >= 0 && s < Nb) {
+        const ET* brow = b + ((int64_t)bb * Nb + s) * C;
+        for (int c = lane; c < C; c += 32) acc = fmaf(to_f32(arow[c]), to_f32(brow[c]), acc);
+        acc = warp_sum(acc);
+      }
+      if (lane == 0) scores[o] = from_f32<ET>(acc);
+    }
   }
 }
 
@@ -810,7 +838,10 @@ extern "C" int mn_sparse_neighbor_dot(int batch, int num_donors, int num_receive
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc = dispatch_dtype(dtype, [&](auto tag) {
     using ET = decltype(tag);
-    neighbor_dot_kernel<ET><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+    const bool quad = (channels * (int)sizeof(ET)) % 64 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(b) & 15) == 0;
+    auto kern = quad ? neighbor_dot_kernel<ET, true> : neighbor_dot_kernel<ET, false>;
+    kern<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
         static_cast<const ET*>(a), static_cast<const ET*>(b), receiver_indices, receiver_valid, batch,
         num_donors, num_receivers, k, channels, static_cast<ET*>(scores));
   });
