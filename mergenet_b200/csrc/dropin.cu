@@ -288,6 +288,54 @@ __global__ void __launch_bounds__(512) transport_kernel(
 // registers (G channel groups of 32 per lane, C <= 32 G), and every
 // receiver row is read once for both the assignment's gradient (a dot
 // product) and the values' gradient.  G == 0: any C, two passes.
+// The same adjoint for narrow rows (C <= 8: masses, centres): one warp per
+// donor row with a lane per slot (slots 32 apart loop), so every slot's
+// receiver row is read at once; grad_w[k] = g[r_k] . v is the lane's own
+// sum, and grad_v[c] = sum_k w_k g[r_k][c] one warp reduction per channel.
+template <typename ET>
+__global__ void __launch_bounds__(256) transport_adjoint_narrow_kernel(
+    const ET* __restrict__ w, const ET* __restrict__ v, const int64_t* __restrict__ ridx,
+    const uint8_t* __restrict__ rvalid, const ET* __restrict__ g, int B, int Na, int Nb, int K, int C,
+    ET* __restrict__ grad_w, ET* __restrict__ grad_v) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= (int64_t)B * Na) return;
+  const int bb = (int)(row / Na);
+  float vr[8], gv[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    vr[c] = c < C ? to_f32(v[row * C + c]) : 0.f;
+    gv[c] = 0.f;
+  }
+  for (int k0 = 0; k0 < K; k0 += 32) {
+    const int k = k0 + lane;
+    float dot = 0.f;
+    if (k < K) {
+      const int64_t o = row * K + k;
+      const int64_t s = ridx[o];
+      if (rvalid[o] && s >= 0 && s < Nb) {
+        const ET* grow = g + ((int64_t)bb * Nb + s) * C;
+        const float wk = to_f32(w[o]);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          if (c < C) {
+            const float gc = to_f32(grow[c]);
+            dot = fmaf(gc, vr[c], dot);
+            gv[c] = fmaf(wk, gc, gv[c]);
+          }
+        }
+      }
+      grad_w[o] = from_f32<ET>(dot);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    if (c >= C) break;
+    const float t = warp_sum(gv[c]);
+    if (lane == 0) grad_v[row * C + c] = from_f32<ET>(t);
+  }
+}
+
 template <typename ET, int G>
 __global__ void __launch_bounds__(256) transport_adjoint_kernel(
     const ET* __restrict__ w, const ET* __restrict__ v, const int64_t* __restrict__ ridx,
@@ -903,7 +951,8 @@ extern "C" int mn_sparse_transport_adjoint(int batch, int num_donors, int num_re
           static_cast<ET*>(grad_assignment), static_cast<ET*>(grad_values));
     };
     const int groups = (channels + 31) / 32;
-    if (groups <= 1) launch(transport_adjoint_kernel<ET, 1>);
+    if (channels <= 8) launch(transport_adjoint_narrow_kernel<ET>);
+    else if (groups <= 1) launch(transport_adjoint_kernel<ET, 1>);
     else if (groups <= 2) launch(transport_adjoint_kernel<ET, 2>);
     else if (groups <= 4) launch(transport_adjoint_kernel<ET, 4>);
     else if (groups <= 8) launch(transport_adjoint_kernel<ET, 8>);
